@@ -1,0 +1,400 @@
+#!/usr/bin/env python
+"""Benchmark of the paged streaming hot path on B200.
+
+Workload: one isolated paged-attention step of the
+small model, bf16 - 80 streams x 17 layers, 8 heads of 64, chunk of 2 frames
+over 70 cached left-context frames (window 72), 16-frame pages, the free
+list a random permutation of the pool (seed 1), Q/K/V and the rel-pos
+projection N(0,1)/8.  A step is: page allocator (begin) -> paged append of
+the chunk's K/V for all 17 layers -> paged rel-pos attention for all 17
+layers -> counter update (end).  Streams are independent, so N GPUs run N
+replicas with no collective on the data path (weak scaling).
+
+Metric: paged-attn HBM GB/s = algorithmic bytes of the step / step time.
+Algorithmic bytes per stream-layer (bf16): append 8,192 (read new K,V,
+write K,V), attention 151,552 (read the 72-row K,V window, read Q, write O).
+
+``--impl reference`` times the reference's algorithm for the same step on
+the host cores (dense shift-append, index_select/index_copy_ pack/unpack,
+Python mask loop, numpy attention; oracle/baseline.py) - the reference has
+no GPU kernels for this path.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "parakeet-streaming_b200"))
+
+SHAPES = {
+    "small": dict(layers=17, dim=512, heads=8, att=(70, 1)),
+    "large": dict(layers=24, dim=1024, heads=8, att=(70, 13)),
+}
+PAGE = 16
+
+
+def alg_bytes(shape, es=2):
+    """Algorithmic bytes per stream-layer of each op (element size es)."""
+    c = SHAPES[shape]
+    D, left, T = c["dim"], c["att"][0], c["att"][1] + 1
+    W = left + T
+    return {
+        "append": 2 * (2 * T * D * es),
+        "attention": 2 * W * D * es + 2 * T * D * es,
+        "gather": 2 * (2 * W * D * es),
+        "conv": (2 * 8 + 3 * T) * D * es,   # cache in/out, GLU input [T, 2D], output [T, D]
+    }
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--model", choices=list(SHAPES), default="small")
+    ap.add_argument("--streams", type=int, default=80)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-breakdown", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.gpu)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+            return
+        self._t = threading.Thread(target=self._read, daemon=True)
+        self._t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self._t.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- reference arm
+def cpu_reference(args, seconds, steps=None):
+    """Time oracle/baseline.ReferenceStep; returns (GB/s, steps, seconds, threads, sample)."""
+    import numpy as np  # noqa: F401
+
+    from oracle.baseline import ReferenceStep
+    try:
+        from threadpoolctl import threadpool_info
+        threads = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
+    except Exception:
+        threads = os.cpu_count() or 1
+    c = SHAPES[args.model]
+    ref = ReferenceStep(c["layers"], c["dim"], c["heads"], c["att"], args.streams)
+    left, T = c["att"][0], c["att"][1] + 1
+    x = ref.inputs()
+    ref.step(x)  # warm (allocations, BLAS threads)
+    done, t0 = 0, time.perf_counter()
+    while True:
+        ref.step(x)
+        done += 1
+        el = time.perf_counter() - t0
+        if (steps is not None and done >= steps) or (steps is None and el >= seconds):
+            break
+    b = alg_bytes(args.model, es=2)
+    per_step = (b["append"] + b["attention"]) * args.streams * c["layers"]
+    sample = (f"{done} steps x {args.streams} streams x {c['layers']} layers "
+              f"(pack, mask loop, shift-append, attention, unpack), float32 numpy")
+    return per_step * done / el / 1e9, done, el, threads, sample
+
+
+def run_reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    K, W = args.steps, args.warmup
+    # each step is a bounded sample: at most ~1.5 s of CPU work per step
+    from oracle.baseline import ReferenceStep
+    c = SHAPES[args.model]
+    streams = args.streams
+    probe = ReferenceStep(c["layers"], c["dim"], c["heads"], c["att"], streams)
+    x = probe.inputs()
+    t0 = time.perf_counter()
+    probe.step(x)
+    one = time.perf_counter() - t0
+    budget = 150.0 / max(1, K + W)
+    sample_streams = streams
+    while one * sample_streams / streams > budget and sample_streams > 1:
+        sample_streams = max(1, sample_streams // 2)
+    args2 = argparse.Namespace(**vars(args))
+    args2.streams = sample_streams
+    gbs, done, el, threads, sample = cpu_reference(args2, 0, steps=K + W)
+    b = alg_bytes(args.model)
+    print(json.dumps({
+        "impl": "reference", "metric": "paged-attn HBM GB/s (append + attention, algorithmic bytes)",
+        "value": round(gbs, 4), "unit": "GB/s", "n_gpus": args.gpus, "steps": K, "warmup": W,
+        "ms_per_step": round(1e3 * el / done, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"configs[1] isolated paged-attention step, {args.model} model",
+                   "streams": sample_streams, "layers": c["layers"]},
+        "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": threads,
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "bytes_per_stream_layer": {"append": b["append"], "attention": b["attention"]},
+    }), flush=True)
+
+
+# ---------------------------------------------------------------- B200 arm
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference_arm(args)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    from parakeet_b200.ops import PagedKVPool, pages_per_stream
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    c = SHAPES[args.model]
+    L, D, H, att = c["layers"], c["dim"], c["heads"], c["att"]
+    left, T = att[0], att[1] + 1
+    W, P, dh = left + T, 2 * (left + T) - 1, D // H
+    B = args.streams
+    dt = torch.bfloat16
+    sc = 1.0 / dh ** 0.5
+
+    gen = torch.Generator().manual_seed(1)
+    n_pages = B * pages_per_stream(left, T, PAGE)
+    order = torch.randperm(n_pages, generator=gen)
+    pool = PagedKVPool(L, D, H, att, B, num_pages=n_pages, dtype=dt, device=dev, page_order=order)
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    rnd = lambda *s: (torch.randn(*s, generator=g, device=dev) * sc).to(dt)  # noqa: E731
+    pos = rnd(L, P, D)
+    bu, bv = rnd(L, H, dh), rnd(L, H, dh)
+    NBUF = 4
+    qkv = [rnd(L, B, T, 3 * D) for _ in range(NBUF)]
+    out = torch.empty(L, B, T, D, dtype=dt, device=dev)
+    slots = torch.arange(B, dtype=torch.int32, device=dev)
+    lengths = torch.full((B,), T, dtype=torch.int32, device=dev)
+    nb = alg_bytes(args.model)
+    units = B * L
+    step_bytes = (nb["append"] + nb["attention"]) * units
+
+    def step(buf, ev=None):
+        pool.begin_step(slots)
+        pool.append(0, buf[..., D:2 * D], buf[..., 2 * D:], slots)
+        if ev is not None:
+            ev[0].record()
+        pool.attention(0, buf[..., :D], pos, bu, bv, slots, lengths, out)
+        if ev is not None:
+            ev[1].record()
+        pool.end_step(slots, lengths)
+
+    # fill the 70-frame left context, then warm up
+    for i in range(-(-left // T)):
+        step(qkv[i % NBUF])
+    for i in range(args.warmup):
+        step(qkv[i % NBUF])
+    torch.cuda.synchronize()
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    t_soak = time.perf_counter()
+    while time.perf_counter() - t_soak < 1.0:   # bring clocks to load level, untimed
+        for i in range(50):
+            step(qkv[i % NBUF])
+        torch.cuda.synchronize()
+
+    K = args.steps
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(K)]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0.record()
+    for i in range(K):
+        step(qkv[i % NBUF], evs[i])
+    e1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = e0.elapsed_time(e1) / K
+    attn_ms = sum(a.elapsed_time(b) for a, b in evs) / K
+    clk = clocks.stop()
+    err = pool.read_error()
+
+    # ---- end to end through the public API: pinned host in, host out
+    hq = [b.cpu().pin_memory() for b in qkv]
+    hout = torch.empty(out.shape, dtype=dt).pin_memory()
+    dq = torch.empty_like(qkv[0])
+
+    def e2e_step(i):
+        dq.copy_(hq[i % NBUF], non_blocking=True)
+        step(dq)
+        hout.copy_(out, non_blocking=True)
+
+    for i in range(max(3, args.warmup)):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for i in range(K):
+        e2e_step(i)
+    f1.record()
+    torch.cuda.synchronize()
+    e2e_ms = f0.elapsed_time(f1) / K
+    if world > 1:
+        dist.barrier()
+
+    # ---- per-op breakdown (separate loops, same pool)
+    breakdown = {}
+    if not args.no_breakdown and rank == 0:
+        def timeit(fn, n=20):
+            for _ in range(3):
+                fn()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            a.record()
+            for _ in range(n):
+                fn()
+            b.record()
+            torch.cuda.synchronize()
+            return a.elapsed_time(b) / n
+        kv_out = [torch.empty(B, W, D, dtype=dt, device=dev) for _ in range(2)]
+        x2 = rnd(B, T, 2 * D)
+        wconv = rnd(D, 1, 9)
+        lnw, lnb = rnd(D) + 1, rnd(D)
+        yconv = torch.empty(B, T, D, dtype=dt, device=dev)
+        ops = {
+            "append": (lambda: pool.append(0, qkv[0][..., D:2 * D], qkv[0][..., 2 * D:], slots),
+                       nb["append"] * units, 1),
+            "attention": (lambda: pool.attention(0, qkv[0][..., :D], pos, bu, bv, slots, lengths, out),
+                          nb["attention"] * units, 1),
+            "gather": (lambda: [pool.gather(l, slots, *kv_out) for l in range(L)],
+                       nb["gather"] * units, L),
+            "conv": (lambda: [pool.conv_step(l, x2, wconv, slots, lengths, lnw, lnb, 1e-5, yconv)
+                              for l in range(L)], nb["conv"] * units, L),
+        }
+        hbm, _ = peaks()
+        for name, (fn, nbytes, launches) in ops.items():
+            t = timeit(fn)
+            breakdown[name] = {"ms": round(t, 4), "GB/s": round(nbytes / t / 1e6, 1),
+                               "frac": round(nbytes / t / 1e6 / hbm, 3), "launches": launches,
+                               "bytes_per_stream_layer": nb[name]}
+
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms, attn_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms, attn_ms = t.tolist()
+
+    if rank == 0:
+        hbm, kind = peaks()
+        attn_bytes = nb["attention"] * units
+        achieved = attn_bytes / (attn_ms * 1e-3) / 1e9
+        traffic = None
+        tp = os.path.join(REPO, "profiles", "attention_traffic.json")
+        if os.path.exists(tp):
+            tj = json.load(open(tp))
+            if tj.get("model") == args.model and tj.get("streams") == B:
+                traffic = tj.get("dram_bytes_per_launch")
+        cpu = None
+        if world == 1:
+            gbs, done, el, threads, sample = cpu_reference(args, args.cpu_seconds)
+            cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+                   "sample": sample}
+        value = step_bytes * world / (ms * 1e-3) / 1e9
+        e2e = step_bytes * world / (e2e_ms * 1e-3) / 1e9
+        line = {
+            "metric": "paged-attn HBM GB/s (append + attention, algorithmic bytes)",
+            "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": K,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"configs[1] isolated paged-attention step, {args.model} model",
+                       "streams_per_gpu": B, "layers": L, "heads": H, "head_dim": dh,
+                       "chunk": T, "left_context": left, "page_size": PAGE,
+                       "page_order": "randperm seed 1",
+                       "l2": f"inputs > L2: {pool.kv.numel() * 2 / 1e6:.0f} MB page pool, "
+                             f"{step_bytes / 1e6:.0f} MB read+written per step",
+                       "parallelism": f"{world} independent replicas (stream sharding)"},
+            "roofline": {"bound": "hbm", "kernel": "paged_attn_kernel",
+                         "achieved": round(achieved, 1), "peak": hbm, "peak_kind": kind,
+                         "unit": "GB/s", "frac": round(achieved / hbm, 3), "traffic": traffic,
+                         "alg_bytes_per_launch": attn_bytes, "avg_launch_ms": round(attn_ms, 4)},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e, 1), "unit": "GB/s",
+                    "h2d_bytes_per_step": qkv[0].numel() * 2, "d2h_bytes_per_step": out.numel() * 2,
+                    "ms_per_step": round(e2e_ms, 4)},
+            "gpu_launches": 4 * K,
+            "clocks": clk,
+            "device_error_word": err,
+            "ops": breakdown,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,178 @@
+/*
+ * pk.h - C ABI of libpk.so, the B200 (sm_100a) kernels for the streaming
+ * FastConformer hot path of odunola499/parakeet-streaming:
+ *
+ *   paged K/V append, page-table window gather, paged chunked rel-pos
+ *   self-attention, depthwise-conv time-cache step, and the device page
+ *   allocator that replaces the reference's dense per-slot pool.
+ *
+ * Every device buffer is allocated and owned by the caller; the library
+ * allocates no device memory.  Pointers are raw device addresses, strides
+ * are in elements, `stream` is a cudaStream_t (NULL = legacy default
+ * stream).  Every entry point returns PK_OK or a PK_E* status; argument
+ * errors are detected on the host before anything is launched.  Faults
+ * that only the device can see (pool exhausted, a page id out of range, a
+ * bounded wait that gave up) set bits in the caller's `error` word instead
+ * of trapping; read it with any device-to-host copy.
+ *
+ * Citations name the reference interface each entry point stands in for
+ * (paths inside the reference source tree).
+ */
+#ifndef PK_H
+#define PK_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define PK_OK 0
+#define PK_EINVAL 1   /* bad argument: shape, alignment, null pointer      */
+#define PK_ECUDA 2    /* a CUDA runtime call failed (see pk_last_error)    */
+#define PK_ENOTSUP 3  /* configuration this build does not handle          */
+
+/* element types */
+#define PK_DTYPE_F32 0
+#define PK_DTYPE_BF16 1
+
+/* bits of the device error word */
+#define PK_DEV_POOL_EXHAUSTED 1  /* a step asked for more pages than free  */
+#define PK_DEV_BAD_PAGE 2        /* a page-table entry outside the pool    */
+#define PK_DEV_TIMEOUT 4         /* a bounded wait on a TMA barrier ran out */
+#define PK_DEV_BAD_SLOT 8        /* a slot id outside [0, num_slots)       */
+
+/* per-slot counters, int32 [num_slots][PK_META_STRIDE] */
+#define PK_META_FIRST 0      /* oldest logical page held                   */
+#define PK_META_NEXT 1       /* next logical page to allocate              */
+#define PK_META_WRITTEN 2    /* rows written so far (chunk per step)       */
+#define PK_META_PROCESSED 3  /* StreamingState.processed_frames            */
+#define PK_META_CACHE_LEN 4  /* StreamingState.cache_lengths (<= left)     */
+#define PK_META_STRIDE 8
+
+/*
+ * Paged K/V window of every stream slot.  Replaces ModelCache.attn_k /
+ * attn_v (parakeet/modules/cache.py:24-29) and the slot pool's state
+ * tensors (parakeet/engine/scheduler.py:68-84).
+ */
+typedef struct pk_paged_kv_desc {
+    void *kv;             /* [num_pages][num_layers][2][page_size][dim]      */
+    int32_t *page_table;  /* [num_slots][ring], -1 = no page                 */
+    int32_t *free_ring;   /* [num_pages] FIFO of free page ids               */
+    int64_t *ring_ctr;    /* [2] monotonic head (pop) and tail (push)        */
+    int32_t *meta;        /* [num_slots][PK_META_STRIDE]                     */
+    int32_t *error;       /* [1] device error word (PK_DEV_* bits)           */
+    int32_t num_pages;
+    int32_t num_slots;
+    int32_t num_layers;
+    int32_t dim;          /* model width D                                   */
+    int32_t num_heads;    /* H, head_dim = dim / num_heads (64 or 128)       */
+    int32_t left;         /* left attention context (70)                     */
+    int32_t chunk;        /* frames per step T = right context + 1           */
+    int32_t page_size;    /* frames per page (16)                            */
+    int32_t ring;         /* page-table entries per slot (power of two)      */
+    int32_t dtype;        /* PK_DTYPE_*                                       */
+} pk_paged_kv_desc;
+
+typedef struct pk_paged_kv pk_paged_kv; /* opaque: desc + TMA descriptors */
+
+/* Validate `desc`, encode the pool's TMA descriptor, return a host handle.
+ * Replaces Scheduler.init_state_pool (parakeet/engine/scheduler.py:68-84). */
+int pk_paged_kv_create(const pk_paged_kv_desc *desc, pk_paged_kv **out);
+int pk_paged_kv_destroy(pk_paged_kv *kv);
+
+/* Page-table entries a stream needs at most / the ring size to give it. */
+int32_t pk_pages_per_stream(int32_t left, int32_t chunk, int32_t page_size);
+int32_t pk_ring_size(int32_t left, int32_t chunk, int32_t page_size);
+
+/* Reset the pool: every page free in `init_order` (device int32
+ * [num_pages], a permutation) or 0..num_pages-1 when NULL; every slot
+ * empty; error word cleared.  The free_ring order is the allocation order,
+ * like deque(range(pool)) in scheduler.py:84. */
+int pk_pages_reset(pk_paged_kv *kv, const int32_t *init_order, void *stream);
+
+/* Start of one batched step (one CTA, deterministic order):
+ *  0. return every page of the `released` slots (finished streams,
+ *     parakeet/engine/scheduler.py:101-104) and zero their counters;
+ *  1. per batch row, in order: free pages wholly left of the window;
+ *  2. per batch row, in order: allocate pages for rows [w, w + chunk).
+ * Replaces the pool half of Scheduler.pack_states (scheduler.py:128-170):
+ * nothing is gathered, the kernels read the pages in place. */
+int pk_pages_begin_step(pk_paged_kv *kv, const int32_t *slots, int32_t batch,
+                        const int32_t *released, int32_t num_released,
+                        void *stream);
+
+/* End of the step: written += chunk, processed += length,
+ * cache_len = min(cache_len + length, left) per batch row
+ * (parakeet/modules/encoder.py:257-260; unpack_states, scheduler.py:172-201,
+ * has nothing left to scatter). */
+int pk_pages_end_step(pk_paged_kv *kv, const int32_t *slots,
+                      const int32_t *lengths, int32_t batch, void *stream);
+
+/* Write this step's `chunk` new K and V rows of layers
+ * [layer0, layer0 + num_layers) into the pages.  key/value element
+ * (l, b, t, c) is at l*layer_stride + b*batch_stride + t*row_stride + c,
+ * e.g. the K and V thirds of the fused qkv GEMM output.
+ * Replaces ModelCache.update_attn_cache (parakeet/modules/cache.py:36-45). */
+int pk_append_kv(pk_paged_kv *kv, int32_t layer0, int32_t num_layers,
+                 const void *key, const void *value, int64_t layer_stride,
+                 int64_t batch_stride, int64_t row_stride,
+                 const int32_t *slots, int32_t batch, void *stream);
+
+/* Materialise the [batch][left + chunk][dim] K and V windows of one layer
+ * exactly as the reference's dense cache holds them (rows before a
+ * stream's first frame are zero).  Call after pk_append_kv of the step.
+ * Replaces the (K, V) return value of ModelCache.update_attn_cache
+ * (cache.py:45) and the index_select gather (scheduler.py:150-161). */
+int pk_gather_window(pk_paged_kv *kv, int32_t layer, const int32_t *slots,
+                     int32_t batch, void *k_out, void *v_out, void *stream);
+
+/* Chunked rel-pos multi-head self-attention over the paged window, for
+ * layers [layer0, layer0 + num_layers), after pk_append_kv of the step.
+ *   query  (l, b, t, c)  at l*q_layer_stride + b*q_batch_stride + t*q_row_stride + c
+ *   pos_proj (l, p, c)   at l*pos_layer_stride + p*dim + c, p < 2*(left+chunk)-1:
+ *                        linear_pos(pos_emb) of that layer (attention.py:102-106)
+ *   bias_u/v (l, h, d)   at l*bias_layer_stride + h*head_dim + d (pos_bias_u/v)
+ *   out    (l, b, t, c)  at l*out_layer_stride + b*out_batch_stride + t*out_row_stride + c
+ * The streaming mask is derived in-kernel from each slot's counters and
+ * `lengths` (parakeet/modules/encoder.py:167-227).  Output is the heads
+ * concatenated, before linear_out.
+ * Replaces ConformerAttention.forward lines 99-122
+ * (parakeet/modules/attention.py), i.e. rel_shift + bias + SDPA. */
+int pk_paged_attention(pk_paged_kv *kv, int32_t layer0, int32_t num_layers,
+                       const void *query, int64_t q_layer_stride,
+                       int64_t q_batch_stride, int64_t q_row_stride,
+                       const void *pos_proj, int64_t pos_layer_stride,
+                       const void *bias_u, const void *bias_v,
+                       int64_t bias_layer_stride, const int32_t *slots,
+                       const int32_t *lengths, int32_t batch, void *out,
+                       int64_t out_layer_stride, int64_t out_batch_stride,
+                       int64_t out_row_stride, void *stream);
+
+/* Depthwise causal conv step with its time cache, one layer:
+ *   GLU over the pw-conv1 output x (l=0: [batch][chunk][2*dim] with
+ *   x_batch_stride / x_row_stride) -> zero rows t >= length -> depthwise conv
+ *   over cat(cache, x) with weight [dim][kernel] -> cache = last kernel-1
+ *   frames -> if ln_weight: LayerNorm(eps) then SiLU -> y [batch][chunk][dim].
+ * conv_state is [num_slots][num_layers][dim][kernel-1] in the reference's
+ * own layout (ModelCache.conv, cache.py:30-34), updated in place by slot.
+ * Replaces ConformerConvolution.forward lines 153-159 with
+ * CausalConv1d.update_cache (parakeet/modules/convolution.py:37-52,150-162)
+ * and ModelCache.get/update_conv_cache (cache.py:47-53). */
+int pk_conv_step(void *conv_state, int32_t num_slots, int32_t num_layers,
+                 int32_t layer, int32_t dim, int32_t kernel, int32_t chunk,
+                 int32_t dtype, const void *x, int64_t x_batch_stride,
+                 int64_t x_row_stride, const void *weight,
+                 const void *ln_weight, const void *ln_bias, float ln_eps,
+                 const int32_t *slots, const int32_t *lengths, int32_t batch,
+                 void *y, int32_t *error, void *stream);
+
+/* Text of the last PK_ECUDA / PK_EINVAL cause seen by this thread. */
+const char *pk_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PK_H */

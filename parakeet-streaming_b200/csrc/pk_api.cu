@@ -1,0 +1,286 @@
+// C-ABI entry points of libpk.so (declared in include/pk.h): argument
+// checks on the host, TMA descriptor encoding, kernel dispatch.
+#include <cudaTypedefs.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <mutex>
+
+#include "pk_internal.h"
+
+namespace pk {
+
+static thread_local char g_err[512];
+
+void set_error(const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof(g_err), fmt, ap);
+    va_end(ap);
+}
+
+int cuda_status(cudaError_t e, const char *what) {
+    if (e == cudaSuccess) return PK_OK;
+    set_error("%s: %s", what, cudaGetErrorString(e));
+    return PK_ECUDA;
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000,
+                                             cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+int encode_tmap_3d(CUtensorMap *map, int dtype, const void *base, uint64_t d0, uint64_t d1,
+                   uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box0,
+                   uint32_t box1, uint32_t box2) {
+    auto fn = get_encode_fn();
+    if (!fn) {
+        set_error("cuTensorMapEncodeTiled unavailable from the driver");
+        return PK_ECUDA;
+    }
+    const cuuint64_t dims[3] = {d0, d1, d2};
+    const cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
+    const cuuint32_t box[3] = {box0, box1, box2};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(map, dtype == PK_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                    3, const_cast<void *>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error("cuTensorMapEncodeTiled failed (%d)", (int)r);
+        return PK_ECUDA;
+    }
+    return PK_OK;
+}
+
+}  // namespace pk
+
+using namespace pk;
+
+#define PK_CHECK(cond, ...)          \
+    do {                             \
+        if (!(cond)) {               \
+            pk::set_error(__VA_ARGS__); \
+            return PK_EINVAL;        \
+        }                            \
+    } while (0)
+
+static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+extern "C" {
+
+const char *pk_last_error(void) { return pk::g_err; }
+
+int32_t pk_pages_per_stream(int32_t left, int32_t chunk, int32_t page_size) {
+    if (left < 0 || chunk <= 0 || page_size <= 0) return -1;
+    const int span = left + chunk - 1;
+    return (span + page_size - 1) / page_size + 1;
+}
+
+int32_t pk_ring_size(int32_t left, int32_t chunk, int32_t page_size) {
+    const int n = pk_pages_per_stream(left, chunk, page_size);
+    if (n <= 0) return -1;
+    int r = 1;
+    while (r < n) r *= 2;
+    return r;
+}
+
+int pk_paged_kv_create(const pk_paged_kv_desc *desc, pk_paged_kv **out) {
+    PK_CHECK(desc && out, "null argument");
+    const pk_paged_kv_desc &d = *desc;
+    PK_CHECK(d.kv && d.page_table && d.free_ring && d.ring_ctr && d.meta && d.error,
+             "null device buffer in descriptor");
+    PK_CHECK(d.dtype == PK_DTYPE_F32 || d.dtype == PK_DTYPE_BF16, "bad dtype %d", d.dtype);
+    PK_CHECK(d.num_pages > 0 && d.num_slots > 0 && d.num_layers > 0, "empty pool");
+    PK_CHECK(d.num_heads > 0 && d.dim % d.num_heads == 0, "dim %% heads != 0");
+    PK_CHECK(d.left >= 0 && d.chunk > 0, "bad left/chunk");
+    PK_CHECK(d.page_size % 8 == 0 && d.page_size <= 256, "page_size must be a multiple of 8, <= 256");
+    PK_CHECK(d.ring >= pk_pages_per_stream(d.left, d.chunk, d.page_size) &&
+                 (d.ring & (d.ring - 1)) == 0,
+             "ring must be a power of two >= pk_pages_per_stream()");
+    PK_CHECK(aligned16(d.kv), "kv pool not 16-byte aligned");
+    const int esize = d.dtype == PK_DTYPE_BF16 ? 2 : 4;
+    PK_CHECK((d.dim * esize) % 128 == 0, "dim * element size must be a multiple of 128 bytes");
+    PK_CHECK(d.left + 2 * d.chunk - 1 <= 256, "left + 2*chunk - 1 must be <= 256");
+    pk_paged_kv *kv = static_cast<pk_paged_kv *>(calloc(1, sizeof(pk_paged_kv)));
+    if (!kv) return PK_EINVAL;
+    kv->d = d;
+    kv->esize = esize;
+    kv->head_dim = d.dim / d.num_heads;
+    const uint64_t row = (uint64_t)d.dim * esize;
+    int st = encode_tmap_3d(&kv->kv_map, d.dtype, d.kv, d.dim, d.page_size,
+                            (uint64_t)d.num_pages * d.num_layers * 2, row, row * d.page_size,
+                            128 / esize, d.page_size, 1);
+    if (st != PK_OK) {
+        free(kv);
+        return st;
+    }
+    *out = kv;
+    return PK_OK;
+}
+
+int pk_paged_kv_destroy(pk_paged_kv *kv) {
+    free(kv);
+    return PK_OK;
+}
+
+int pk_pages_reset(pk_paged_kv *kv, const int32_t *init_order, void *stream) {
+    PK_CHECK(kv, "null pool");
+    return launch_pages_reset(kv, init_order, static_cast<cudaStream_t>(stream));
+}
+
+int pk_pages_begin_step(pk_paged_kv *kv, const int32_t *slots, int32_t batch,
+                        const int32_t *released, int32_t num_released, void *stream) {
+    PK_CHECK(kv, "null pool");
+    PK_CHECK(batch >= 0 && num_released >= 0, "negative count");
+    PK_CHECK(batch == 0 || slots, "null slots");
+    PK_CHECK(num_released == 0 || released, "null released");
+    return launch_pages_begin(kv, slots, batch, released, num_released,
+                              static_cast<cudaStream_t>(stream));
+}
+
+int pk_pages_end_step(pk_paged_kv *kv, const int32_t *slots, const int32_t *lengths,
+                      int32_t batch, void *stream) {
+    PK_CHECK(kv, "null pool");
+    PK_CHECK(batch >= 0, "negative batch");
+    PK_CHECK(batch == 0 || (slots && lengths), "null slots/lengths");
+    return launch_pages_end(kv, slots, lengths, batch, static_cast<cudaStream_t>(stream));
+}
+
+int pk_append_kv(pk_paged_kv *kv, int32_t layer0, int32_t num_layers, const void *key,
+                 const void *value, int64_t layer_stride, int64_t batch_stride,
+                 int64_t row_stride, const int32_t *slots, int32_t batch, void *stream) {
+    PK_CHECK(kv, "null pool");
+    PK_CHECK(batch >= 0 && num_layers >= 0 && layer0 >= 0 &&
+                 layer0 + num_layers <= kv->d.num_layers,
+             "layer range [%d, %d) outside [0, %d)", layer0, layer0 + num_layers,
+             kv->d.num_layers);
+    if (batch == 0 || num_layers == 0) return PK_OK;
+    PK_CHECK(key && value && slots, "null pointer");
+    PK_CHECK(aligned16(key) && aligned16(value), "key/value not 16-byte aligned");
+    const int es = kv->esize;
+    PK_CHECK((layer_stride * es) % 16 == 0 && (batch_stride * es) % 16 == 0 &&
+                 (row_stride * es) % 16 == 0,
+             "strides must be multiples of 16 bytes");
+    return launch_append(kv, layer0, num_layers, key, value, layer_stride, batch_stride,
+                         row_stride, slots, batch, static_cast<cudaStream_t>(stream));
+}
+
+int pk_gather_window(pk_paged_kv *kv, int32_t layer, const int32_t *slots, int32_t batch,
+                     void *k_out, void *v_out, void *stream) {
+    PK_CHECK(kv, "null pool");
+    PK_CHECK(layer >= 0 && layer < kv->d.num_layers, "layer out of range");
+    PK_CHECK(batch >= 0, "negative batch");
+    if (batch == 0) return PK_OK;
+    PK_CHECK(slots && k_out && v_out, "null pointer");
+    PK_CHECK(aligned16(k_out) && aligned16(v_out), "outputs not 16-byte aligned");
+    return launch_gather(kv, layer, slots, batch, k_out, v_out, static_cast<cudaStream_t>(stream));
+}
+
+int pk_paged_attention(pk_paged_kv *kv, int32_t layer0, int32_t num_layers, const void *query,
+                       int64_t q_layer_stride, int64_t q_batch_stride, int64_t q_row_stride,
+                       const void *pos_proj, int64_t pos_layer_stride, const void *bias_u,
+                       const void *bias_v, int64_t bias_layer_stride, const int32_t *slots,
+                       const int32_t *lengths, int32_t batch, void *out,
+                       int64_t out_layer_stride, int64_t out_batch_stride,
+                       int64_t out_row_stride, void *stream) {
+    PK_CHECK(kv, "null pool");
+    PK_CHECK(batch >= 0 && num_layers >= 0 && layer0 >= 0 &&
+                 layer0 + num_layers <= kv->d.num_layers,
+             "layer range outside the pool");
+    if (batch == 0 || num_layers == 0) return PK_OK;
+    PK_CHECK(query && pos_proj && bias_u && bias_v && slots && lengths && out, "null pointer");
+    PK_CHECK(aligned16(pos_proj), "pos_proj not 16-byte aligned");
+    PK_CHECK(kv->head_dim == 64 || kv->head_dim == 128, "head_dim %d not handled", kv->head_dim);
+    PK_CHECK(out_row_stride % 2 == 0 && out_batch_stride % 2 == 0 && out_layer_stride % 2 == 0 &&
+                 (reinterpret_cast<uintptr_t>(out) % (2 * kv->esize)) == 0,
+             "out must allow 2-element stores");
+    const int es = kv->esize;
+    const int P = 2 * (kv->d.left + kv->d.chunk) - 1;
+    const int R = kv->d.left + 2 * kv->d.chunk - 1;
+    const uint64_t row = (uint64_t)kv->d.dim * es;
+    uint64_t lstride = (uint64_t)pos_layer_stride * es;
+    if (num_layers == 1) lstride = row * P;
+    PK_CHECK(lstride % 16 == 0 && lstride >= row * P, "bad pos_layer_stride");
+    CUtensorMap pos_map;
+    int st = encode_tmap_3d(&pos_map, kv->d.dtype, pos_proj, kv->d.dim, P, num_layers, row,
+                            lstride, 128 / es, R, 1);
+    if (st != PK_OK) return st;
+    AttnArgs a;
+    a.q = query;
+    a.q_ls = q_layer_stride;
+    a.q_bs = q_batch_stride;
+    a.q_rs = q_row_stride;
+    a.bias_u = bias_u;
+    a.bias_v = bias_v;
+    a.bias_ls = bias_layer_stride;
+    a.slots = slots;
+    a.lengths = lengths;
+    a.batch = batch;
+    a.out = out;
+    a.o_ls = out_layer_stride;
+    a.o_bs = out_batch_stride;
+    a.o_rs = out_row_stride;
+    a.layer0 = layer0;
+    a.nlayers = num_layers;
+    st = launch_attention(kv, pos_map, a, static_cast<cudaStream_t>(stream));
+    if (st == PK_ENOTSUP) pk::set_error("attention configuration not handled (smem or boxes)");
+    return st;
+}
+
+int pk_conv_step(void *conv_state, int32_t num_slots, int32_t num_layers, int32_t layer,
+                 int32_t dim, int32_t kernel, int32_t chunk, int32_t dtype, const void *x,
+                 int64_t x_batch_stride, int64_t x_row_stride, const void *weight,
+                 const void *ln_weight, const void *ln_bias, float ln_eps,
+                 const int32_t *slots, const int32_t *lengths, int32_t batch, void *y,
+                 int32_t *error, void *stream) {
+    PK_CHECK(dtype == PK_DTYPE_F32 || dtype == PK_DTYPE_BF16, "bad dtype");
+    PK_CHECK(layer >= 0 && layer < num_layers && num_slots > 0, "layer/slots out of range");
+    PK_CHECK(batch >= 0, "negative batch");
+    if (batch == 0) return PK_OK;
+    PK_CHECK(conv_state && x && weight && slots && lengths && y, "null pointer");
+    PK_CHECK((ln_weight == nullptr) == (ln_bias == nullptr), "ln_weight and ln_bias go together");
+    const int es = dtype == PK_DTYPE_BF16 ? 2 : 4;
+    PK_CHECK(dim % 4 == 0 && (reinterpret_cast<uintptr_t>(x) % (4 * es)) == 0 &&
+                 (x_batch_stride % 4) == 0 && (x_row_stride % 4) == 0 &&
+                 (reinterpret_cast<uintptr_t>(y) % (4 * es)) == 0,
+             "x/y must allow 4-element vector access");
+    ConvArgs a;
+    a.state = conv_state;
+    a.num_slots = num_slots;
+    a.num_layers = num_layers;
+    a.layer = layer;
+    a.dim = dim;
+    a.kernel = kernel;
+    a.chunk = chunk;
+    a.dtype = dtype;
+    a.x = x;
+    a.x_bs = x_batch_stride;
+    a.x_rs = x_row_stride;
+    a.w = weight;
+    a.ln_w = ln_weight;
+    a.ln_b = ln_bias;
+    a.eps = ln_eps;
+    a.slots = slots;
+    a.lengths = lengths;
+    a.batch = batch;
+    a.y = y;
+    a.error = error;
+    int st = launch_conv(a, static_cast<cudaStream_t>(stream));
+    if (st == PK_ENOTSUP) pk::set_error("conv configuration not handled (kernel 9, chunk <= 16)");
+    return st;
+}
+
+}  // extern "C"

@@ -1,0 +1,71 @@
+// Internal interfaces between the C-ABI layer (pk_api.cu) and the kernel
+// translation units.  Nothing here is exported.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "pk.h"
+
+struct pk_paged_kv {
+    pk_paged_kv_desc d;
+    CUtensorMap kv_map;  // 3-D view {dim, page_size, pages*layers*2}, 128B-swizzled boxes
+    int head_dim;
+    int esize;
+};
+
+namespace pk {
+
+void set_error(const char *fmt, ...);
+int cuda_status(cudaError_t e, const char *what);
+// Encode a tiled TMA descriptor (driver entry point fetched once via cudart).
+int encode_tmap_3d(CUtensorMap *map, int dtype, const void *base, uint64_t d0, uint64_t d1,
+                   uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box0,
+                   uint32_t box1, uint32_t box2);
+
+// pk_pages.cu
+int launch_pages_reset(const pk_paged_kv *kv, const int32_t *init_order, cudaStream_t s);
+int launch_pages_begin(const pk_paged_kv *kv, const int32_t *slots, int batch,
+                       const int32_t *released, int num_released, cudaStream_t s);
+int launch_pages_end(const pk_paged_kv *kv, const int32_t *slots, const int32_t *lengths,
+                     int batch, cudaStream_t s);
+
+// pk_kv.cu
+int launch_append(const pk_paged_kv *kv, int layer0, int nlayers, const void *key,
+                  const void *value, int64_t ls, int64_t bs, int64_t rs, const int32_t *slots,
+                  int batch, cudaStream_t s);
+int launch_gather(const pk_paged_kv *kv, int layer, const int32_t *slots, int batch,
+                  void *k_out, void *v_out, cudaStream_t s);
+
+// pk_attn.cu
+struct AttnArgs {
+    const void *q;
+    int64_t q_ls, q_bs, q_rs;
+    const void *bias_u, *bias_v;
+    int64_t bias_ls;
+    const int32_t *slots, *lengths;
+    int batch;
+    void *out;
+    int64_t o_ls, o_bs, o_rs;
+    int layer0, nlayers;
+};
+int launch_attention(const pk_paged_kv *kv, const CUtensorMap &pos_map, const AttnArgs &a,
+                     cudaStream_t s);
+
+// pk_conv.cu
+struct ConvArgs {
+    void *state;
+    int num_slots, num_layers, layer, dim, kernel, chunk, dtype;
+    const void *x;
+    int64_t x_bs, x_rs;
+    const void *w, *ln_w, *ln_b;
+    float eps;
+    const int32_t *slots, *lengths;
+    int batch;
+    void *y;
+    int32_t *error;
+};
+int launch_conv(const ConvArgs &a, cudaStream_t s);
+
+}  // namespace pk

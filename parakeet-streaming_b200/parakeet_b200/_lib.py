@@ -1,0 +1,102 @@
+"""ctypes binding of libpk.so (C ABI in include/pk.h).
+
+The library is built in-tree by ``python -m parakeet_b200.build``.  There is
+no fallback: if the shared object is missing or a call fails, an exception
+is raised.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libpk.so")
+HEADER = os.path.join(os.path.dirname(os.path.dirname(_HERE)), "include", "pk.h")
+
+PK_OK, PK_EINVAL, PK_ECUDA, PK_ENOTSUP = 0, 1, 2, 3
+PK_DTYPE_F32, PK_DTYPE_BF16 = 0, 1
+PK_DEV_POOL_EXHAUSTED, PK_DEV_BAD_PAGE, PK_DEV_TIMEOUT, PK_DEV_BAD_SLOT = 1, 2, 4, 8
+META_FIRST, META_NEXT, META_WRITTEN, META_PROCESSED, META_CACHE_LEN = 0, 1, 2, 3, 4
+META_STRIDE = 8
+
+
+class PKError(RuntimeError):
+    """A libpk entry point returned a non-zero status."""
+
+
+class PagedKVDesc(ctypes.Structure):
+    _fields_ = [
+        ("kv", ctypes.c_void_p),
+        ("page_table", ctypes.c_void_p),
+        ("free_ring", ctypes.c_void_p),
+        ("ring_ctr", ctypes.c_void_p),
+        ("meta", ctypes.c_void_p),
+        ("error", ctypes.c_void_p),
+        ("num_pages", ctypes.c_int32),
+        ("num_slots", ctypes.c_int32),
+        ("num_layers", ctypes.c_int32),
+        ("dim", ctypes.c_int32),
+        ("num_heads", ctypes.c_int32),
+        ("left", ctypes.c_int32),
+        ("chunk", ctypes.c_int32),
+        ("page_size", ctypes.c_int32),
+        ("ring", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+    ]
+
+
+_P = ctypes.c_void_p
+_I32 = ctypes.c_int32
+_I64 = ctypes.c_int64
+
+SIGNATURES = {
+    "pk_paged_kv_create": [ctypes.POINTER(PagedKVDesc), ctypes.POINTER(ctypes.c_void_p)],
+    "pk_paged_kv_destroy": [_P],
+    "pk_pages_per_stream": [_I32, _I32, _I32],
+    "pk_ring_size": [_I32, _I32, _I32],
+    "pk_pages_reset": [_P, _P, _P],
+    "pk_pages_begin_step": [_P, _P, _I32, _P, _I32, _P],
+    "pk_pages_end_step": [_P, _P, _P, _I32, _P],
+    "pk_append_kv": [_P, _I32, _I32, _P, _P, _I64, _I64, _I64, _P, _I32, _P],
+    "pk_gather_window": [_P, _I32, _P, _I32, _P, _P, _P],
+    "pk_paged_attention": [_P, _I32, _I32, _P, _I64, _I64, _I64, _P, _I64, _P, _P, _I64,
+                           _P, _P, _I32, _P, _I64, _I64, _I64, _P],
+    "pk_conv_step": [_P, _I32, _I32, _I32, _I32, _I32, _I32, _I32, _P, _I64, _I64, _P, _P, _P,
+                     ctypes.c_float, _P, _P, _I32, _P, _P, _P],
+    "pk_last_error": [],
+}
+RESTYPES = {"pk_last_error": ctypes.c_char_p}
+
+_lib = None
+
+
+def lib():
+    """The loaded libpk.so, with argument types set.  Raises if not built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise PKError(f"{LIB_PATH} is missing: build it with "
+                          "`python -m parakeet_b200.build` (needs nvcc)")
+        l = ctypes.CDLL(LIB_PATH)
+        for name, args in SIGNATURES.items():
+            fn = getattr(l, name)
+            fn.argtypes = args
+            fn.restype = RESTYPES.get(name, ctypes.c_int)
+        _lib = l
+    return _lib
+
+
+def check(status: int, what: str = "") -> None:
+    if status != PK_OK:
+        msg = lib().pk_last_error().decode(errors="replace")
+        kind = {PK_EINVAL: "invalid argument", PK_ECUDA: "CUDA error",
+                PK_ENOTSUP: "not supported"}.get(status, f"status {status}")
+        raise PKError(f"{what}: {kind}: {msg}")
+
+
+def declared_functions(header: str = HEADER) -> list[str]:
+    """Names of the functions include/pk.h declares."""
+    text = open(header).read()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?[a-z_0-9]+\s*\**\s*(pk_[a-z_0-9]+)\s*\(",
+                                 text, flags=re.M)))

@@ -1,0 +1,235 @@
+"""Torch-facing wrappers over the libpk C ABI.
+
+``PagedKVPool`` owns (as torch tensors) every device buffer the kernels use:
+the K/V pages, the page table, the free ring, per-slot counters, the error
+word and the conv time cache.  Each method checks shapes on the host, then
+makes one C call on the current CUDA stream.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+
+import torch
+
+from . import _lib
+from ._lib import check, lib
+
+DTYPES = {torch.float32: _lib.PK_DTYPE_F32, torch.bfloat16: _lib.PK_DTYPE_BF16}
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def pages_per_stream(left: int, chunk: int, page_size: int) -> int:
+    return int(lib().pk_pages_per_stream(left, chunk, page_size))
+
+
+def ring_size(left: int, chunk: int, page_size: int) -> int:
+    return int(lib().pk_ring_size(left, chunk, page_size))
+
+
+class PagedKVPool:
+    """Paged K/V window + conv cache for ``num_slots`` stream slots.
+
+    kv          [num_pages, L, 2, page_size, D]   model dtype
+    page_table  [num_slots, ring]                 int32, -1 = none
+    free_ring   [num_pages]                       int32
+    ring_ctr    [2]                               int64 head / tail
+    meta        [num_slots, 8]                    int32 counters (PK_META_*)
+    error       [1]                               int32 PK_DEV_* bits
+    conv        [num_slots, L, D, kernel - 1]     model dtype (ModelCache.conv layout)
+    """
+
+    def __init__(self, num_layers, dim, num_heads, att_context, num_slots, *, num_pages=None,
+                 page_size=16, conv_kernel=9, dtype=torch.bfloat16, device="cuda",
+                 page_order=None):
+        if dtype not in DTYPES:
+            raise TypeError(f"dtype {dtype} not handled (float32 or bfloat16)")
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise RuntimeError("PagedKVPool needs a CUDA device")
+        self.num_layers, self.dim, self.num_heads = num_layers, dim, num_heads
+        self.left, right = int(att_context[0]), int(att_context[1])
+        self.chunk = right + 1
+        self.window = self.left + self.chunk
+        self.page_size = page_size
+        self.num_slots = num_slots
+        self.dtype = dtype
+        self.conv_kernel = conv_kernel
+        self.per_stream = pages_per_stream(self.left, self.chunk, page_size)
+        self.ring = ring_size(self.left, self.chunk, page_size)
+        self.num_pages = int(num_pages or num_slots * self.per_stream)
+        dev = self.device
+        self.kv = torch.zeros((self.num_pages, num_layers, 2, page_size, dim), dtype=dtype, device=dev)
+        self.page_table = torch.full((num_slots, self.ring), -1, dtype=torch.int32, device=dev)
+        self.free_ring = torch.empty(self.num_pages, dtype=torch.int32, device=dev)
+        self.ring_ctr = torch.zeros(2, dtype=torch.int64, device=dev)
+        self.meta = torch.zeros((num_slots, _lib.META_STRIDE), dtype=torch.int32, device=dev)
+        self.error = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.conv = torch.zeros((num_slots, num_layers, dim, conv_kernel - 1), dtype=dtype, device=dev)
+        d = _lib.PagedKVDesc(
+            kv=self.kv.data_ptr(), page_table=self.page_table.data_ptr(),
+            free_ring=self.free_ring.data_ptr(), ring_ctr=self.ring_ctr.data_ptr(),
+            meta=self.meta.data_ptr(), error=self.error.data_ptr(), num_pages=self.num_pages,
+            num_slots=num_slots, num_layers=num_layers, dim=dim, num_heads=num_heads,
+            left=self.left, chunk=self.chunk, page_size=page_size, ring=self.ring,
+            dtype=DTYPES[dtype])
+        self._desc = d
+        h = ctypes.c_void_p()
+        check(lib().pk_paged_kv_create(ctypes.byref(d), ctypes.byref(h)), "pk_paged_kv_create")
+        self._h = h
+        self._lock = threading.Lock()
+        self.pending_release: list[int] = []
+        self.reset(page_order)
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h is not None and h.value:
+            try:
+                lib().pk_paged_kv_destroy(h)
+            except Exception:
+                pass
+            self._h = None
+
+    # ------------------------------------------------------------ allocator
+    def reset(self, page_order=None):
+        """All pages free in ``page_order`` (default 0..num_pages-1)."""
+        order = None
+        if page_order is not None:
+            order = torch.as_tensor(page_order, dtype=torch.int32).to(self.device)
+            if order.numel() != self.num_pages:
+                raise ValueError("page_order must list every page once")
+        self._order = order
+        check(lib().pk_pages_reset(self._h, _ptr(order), _stream(self.device)), "pk_pages_reset")
+        self.conv.zero_()
+
+    def release_slot(self, slot: int):
+        """Queue a finished stream's slot; its pages return to the free ring at
+        the start of the next step, before that step's frees and allocations."""
+        with self._lock:
+            self.pending_release.append(int(slot))
+
+    def begin_step(self, slots: torch.Tensor, released: torch.Tensor | None = None):
+        """Page releases, frees and allocations for one step of ``slots``
+        (int32 [B], distinct).  ``released`` defaults to the queued releases."""
+        if released is None:
+            with self._lock:
+                rel, self.pending_release = self.pending_release, []
+            if rel:
+                released = torch.tensor(rel, dtype=torch.int32).to(self.device)
+        n_rel = 0 if released is None else int(released.numel())
+        check(lib().pk_pages_begin_step(self._h, slots.data_ptr(), int(slots.numel()),
+                                        _ptr(released) if n_rel else None, n_rel,
+                                        _stream(self.device)), "pk_pages_begin_step")
+
+    def end_step(self, slots: torch.Tensor, lengths: torch.Tensor):
+        check(lib().pk_pages_end_step(self._h, slots.data_ptr(), lengths.data_ptr(),
+                                      int(slots.numel()), _stream(self.device)),
+              "pk_pages_end_step")
+
+    def zero_conv_slot(self, slot: int):
+        self.conv[slot].zero_()
+
+    def read_error(self) -> int:
+        return int(self.error.item())
+
+    # ------------------------------------------------------------ data path
+    def _check_rows(self, t: torch.Tensor, name: str):
+        if t.dtype != self.dtype or t.device != self.device:
+            raise TypeError(f"{name}: expected {self.dtype} on {self.device}, got {t.dtype} on {t.device}")
+        if t.stride(-1) != 1:
+            raise ValueError(f"{name}: last dimension must be contiguous")
+
+    def append(self, layer: int, key: torch.Tensor, value: torch.Tensor, slots: torch.Tensor):
+        """key/value [B, T, D] (any batch/row strides, e.g. qkv slices) or
+        [nl, B, T, D] for layers layer .. layer + nl - 1."""
+        if key.dim() == 3:
+            key, value = key.unsqueeze(0), value.unsqueeze(0)
+        self._check_rows(key, "key")
+        self._check_rows(value, "value")
+        nl, B, T, D = key.shape
+        if T != self.chunk or D != self.dim or value.shape != key.shape or key.stride() != value.stride():
+            raise ValueError(f"key/value shape {tuple(key.shape)} vs chunk {self.chunk}, dim {self.dim}")
+        check(lib().pk_append_kv(self._h, layer, nl, key.data_ptr(), value.data_ptr(),
+                                 key.stride(0), key.stride(1), key.stride(2), slots.data_ptr(), B,
+                                 _stream(self.device)), "pk_append_kv")
+
+    def gather(self, layer: int, slots: torch.Tensor, out_k=None, out_v=None):
+        B = int(slots.numel())
+        shape = (B, self.window, self.dim)
+        k = out_k if out_k is not None else torch.empty(shape, dtype=self.dtype, device=self.device)
+        v = out_v if out_v is not None else torch.empty(shape, dtype=self.dtype, device=self.device)
+        if not (k.is_contiguous() and v.is_contiguous() and tuple(k.shape) == shape):
+            raise ValueError("gather outputs must be contiguous [B, W, D]")
+        check(lib().pk_gather_window(self._h, layer, slots.data_ptr(), B, k.data_ptr(),
+                                     v.data_ptr(), _stream(self.device)), "pk_gather_window")
+        return k, v
+
+    def attention(self, layer: int, query: torch.Tensor, pos_proj: torch.Tensor,
+                  bias_u: torch.Tensor, bias_v: torch.Tensor, slots: torch.Tensor,
+                  lengths: torch.Tensor, out: torch.Tensor | None = None):
+        """query [B, T, D] or [nl, B, T, D]; pos_proj [P, D] or [nl, P, D];
+        bias_u/v [H, dh] or [nl, H, dh]; lengths int32 [B].  Returns out with
+        the query's leading shape (contiguous)."""
+        squeeze = query.dim() == 3
+        if squeeze:
+            query, pos_proj = query.unsqueeze(0), pos_proj.unsqueeze(0)
+            bias_u, bias_v = bias_u.unsqueeze(0), bias_v.unsqueeze(0)
+        self._check_rows(query, "query")
+        nl, B, T, D = query.shape
+        P = 2 * self.window - 1
+        if T != self.chunk or D != self.dim:
+            raise ValueError(f"query shape {tuple(query.shape)} vs chunk {self.chunk}, dim {self.dim}")
+        if tuple(pos_proj.shape) != (nl, P, D) or not pos_proj[0].is_contiguous():
+            raise ValueError(f"pos_proj must be [{nl}, {P}, {D}] with contiguous rows")
+        dh = D // self.num_heads
+        for t, n in ((bias_u, "bias_u"), (bias_v, "bias_v")):
+            if tuple(t.shape) != (nl, self.num_heads, dh) or not t[0].is_contiguous() or t.dtype != self.dtype:
+                raise ValueError(f"{n} must be [{nl}, {self.num_heads}, {dh}] {self.dtype}")
+        if bias_u.stride(0) != bias_v.stride(0):
+            raise ValueError("bias_u/bias_v layer strides differ")
+        if out is None:
+            out = torch.empty((nl, B, T, D), dtype=self.dtype, device=self.device)
+        elif out.dim() == 3:
+            out = out.unsqueeze(0)
+        check(lib().pk_paged_attention(
+            self._h, layer, nl, query.data_ptr(), query.stride(0), query.stride(1),
+            query.stride(2), pos_proj.data_ptr(), pos_proj.stride(0), bias_u.data_ptr(),
+            bias_v.data_ptr(), bias_u.stride(0), slots.data_ptr(), lengths.data_ptr(), B,
+            out.data_ptr(), out.stride(0), out.stride(1), out.stride(2), _stream(self.device)),
+            "pk_paged_attention")
+        return out[0] if squeeze else out
+
+    def conv_step(self, layer: int, x: torch.Tensor, weight: torch.Tensor, slots: torch.Tensor,
+                  lengths: torch.Tensor, ln_weight=None, ln_bias=None, eps=1e-5, out=None):
+        """x: pw-conv1 output [B, T, 2D]; weight [D, kernel] (or [D, 1, kernel]).
+        Returns [B, T, D]: the depthwise conv output, or SiLU(LayerNorm(.)) of it
+        when ln_weight/ln_bias are given.  Updates the slot conv caches."""
+        self._check_rows(x, "x")
+        B, T, D2 = x.shape
+        if T != self.chunk or D2 != 2 * self.dim:
+            raise ValueError(f"x shape {tuple(x.shape)}")
+        w = weight.reshape(self.dim, self.conv_kernel)
+        if not w.is_contiguous() or w.dtype != self.dtype:
+            raise ValueError("conv weight must be contiguous in the pool dtype")
+        if out is None:
+            out = torch.empty((B, T, self.dim), dtype=self.dtype, device=self.device)
+        check(lib().pk_conv_step(
+            self.conv.data_ptr(), self.num_slots, self.num_layers, layer, self.dim,
+            self.conv_kernel, T, DTYPES[self.dtype], x.data_ptr(), x.stride(0), x.stride(1),
+            w.data_ptr(), _ptr(ln_weight), _ptr(ln_bias), float(eps), slots.data_ptr(),
+            lengths.data_ptr(), B, out.data_ptr(), self.error.data_ptr(), _stream(self.device)),
+            "pk_conv_step")
+        return out
+
+    # ------------------------------------------------------------ views
+    def counters(self, slots: torch.Tensor):
+        """(processed_frames, cache_lengths) int64 of the given slots."""
+        m = self.meta.index_select(0, slots.long())
+        return (m[:, _lib.META_PROCESSED].long(), m[:, _lib.META_CACHE_LEN].long())

@@ -1,0 +1,62 @@
+"""Seeded random initialisation of the FastConformer encoder weights.
+
+No checkpoint is reachable offline, so every run (tests, golden vectors,
+benchmarks) uses synthetic weights.  Keys follow the reference's
+``ConformerEncoder.state_dict()`` layout (``layers.{i}.<module>.<param>``,
+see parakeet/modules/encoder.py:11-81 and parakeet/model.py:41-66 for the
+fused ``self_attn.qkv.weight``), so one state_dict feeds both the reference
+modules and this package.  numpy's PCG64 stream makes the values identical on
+every machine for a given seed.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+
+def _lin(rng, out_f, in_f):
+    return (rng.standard_normal((out_f, in_f)) / np.sqrt(in_f)).astype(np.float32)
+
+
+def _ln(rng, d):
+    return ((1.0 + 0.05 * rng.standard_normal(d)).astype(np.float32),
+            (0.05 * rng.standard_normal(d)).astype(np.float32))
+
+
+def random_layer_state_dict(rng, dim, heads, ff_mult=4, conv_kernel=9):
+    """One ConformerLayer's parameters (no biases: ``use_bias=False``,
+    parakeet/config.py:17), float32 numpy arrays."""
+    d_ff = dim * ff_mult
+    dh = dim // heads
+    sd = {}
+    for name in ("norm_feed_forward1", "norm_self_att", "norm_conv",
+                 "norm_feed_forward2", "norm_out"):
+        sd[f"{name}.weight"], sd[f"{name}.bias"] = _ln(rng, dim)
+    for ff in ("feed_forward1", "feed_forward2"):
+        sd[f"{ff}.linear1.weight"] = _lin(rng, d_ff, dim)
+        sd[f"{ff}.linear2.weight"] = _lin(rng, dim, d_ff)
+    sd["self_attn.qkv.weight"] = _lin(rng, 3 * dim, dim)
+    sd["self_attn.linear_pos.weight"] = _lin(rng, dim, dim)
+    sd["self_attn.linear_out.weight"] = _lin(rng, dim, dim)
+    sd["self_attn.pos_bias_u"] = (0.1 * rng.standard_normal((heads, dh))).astype(np.float32)
+    sd["self_attn.pos_bias_v"] = (0.1 * rng.standard_normal((heads, dh))).astype(np.float32)
+    sd["conv.pointwise_conv1.weight"] = _lin(rng, 2 * dim, dim)[:, :, None]
+    sd["conv.depthwise_conv.weight"] = (rng.standard_normal((dim, 1, conv_kernel))
+                                        / np.sqrt(conv_kernel)).astype(np.float32)
+    sd["conv.batch_norm.weight"], sd["conv.batch_norm.bias"] = _ln(rng, dim)
+    sd["conv.pointwise_conv2.weight"] = _lin(rng, dim, dim)[:, :, None]
+    return sd
+
+
+def random_encoder_layers(seed, num_layers, dim, heads, ff_mult=4, conv_kernel=9):
+    """``{"layers.{i}.<key>": array}`` for ``num_layers`` layers."""
+    rng = np.random.default_rng(seed)
+    sd = {}
+    for i in range(num_layers):
+        for k, v in random_layer_state_dict(rng, dim, heads, ff_mult, conv_kernel).items():
+            sd[f"layers.{i}.{k}"] = v
+    return sd
+
+
+def seeded_normal(seed, shape, scale=1.0, dtype=np.float32):
+    """Synthetic activations: N(0, 1) * scale from a PCG64 stream."""
+    return (np.random.default_rng(seed).standard_normal(shape) * scale).astype(dtype)

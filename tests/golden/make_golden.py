@@ -1,0 +1,233 @@
+"""Generate the golden vectors in this directory by running the reference.
+
+Runs odunola499/parakeet-streaming's own modules (imported from a source
+checkout given by ``--reference``) on seeded inputs and saves their outputs
+as small ``.npz`` fixtures.  The fixtures are committed; the GPU box never
+needs the reference.  Three shims make the reference importable offline:
+
+* ``librosa`` is not installed: a stub ``librosa.filters.mel`` returns
+  torchaudio's slaney mel bank (only the feature extractor uses it, which is
+  off the hot path);
+* weights come from ``parakeet_b200.weights`` (seeded numpy) and are loaded
+  with ``load_state_dict``, because HF downloads are impossible offline;
+* sequences are plain objects with an ``encoder_state`` slot id, which is all
+  ``Scheduler.pack_states`` reads (parakeet/engine/scheduler.py:136).
+
+Usage:  python tests/golden/make_golden.py --reference <path to reference>
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import sys
+import types
+from types import SimpleNamespace
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, os.path.join(REPO, "parakeet-streaming_b200"))
+from parakeet_b200.weights import random_encoder_layers, seeded_normal  # noqa: E402
+
+
+def install_librosa_stub():
+    import torchaudio
+
+    lib = types.ModuleType("librosa")
+    filters = types.ModuleType("librosa.filters")
+
+    def mel(sr, n_fft, n_mels, fmin, fmax, norm):
+        fb = torchaudio.functional.melscale_fbanks(
+            n_fft // 2 + 1, float(fmin), float(fmax), n_mels, sr,
+            norm=norm, mel_scale="slaney")
+        return fb.T.numpy()
+
+    filters.mel = mel
+    lib.filters = filters
+    sys.modules["librosa"] = lib
+    sys.modules["librosa.filters"] = filters
+
+
+# Streams used by the encoder fixtures: (name, acquire step, release step or
+# None, step whose chunk is short).  A stream runs in steps acquire <= s < release
+# and is released at the start of step ``release``; a short chunk (length 1 < T)
+# is only ever that stream's last step, like a final chunk.
+SMALL_SCHEDULE = dict(att=(70, 1), dim=512, heads=8, layers=2, steps=40, pool=4,
+                      seed=11, events=[("a", 0, None, None), ("b", 0, 21, None),
+                                       ("c", 6, None, None), ("d", 22, None, 39),
+                                       ("e", 25, None, None)],
+                      keep_steps=[0, 1, 2, 17, 34, 35, 36, 38, 39])
+LARGE_SCHEDULE = dict(att=(70, 13), dim=1024, heads=8, layers=1, steps=8, pool=3,
+                      seed=12, events=[("a", 0, None, None), ("b", 2, None, None)],
+                      keep_steps=[1, 6, 7])
+
+
+def encoder_stream_inputs(seed, step, batch, T, dim):
+    """Chunk input of one step: N(0,1) [batch, T, dim] from seed*1000+step."""
+    return seeded_normal(seed * 1000 + step, (batch, T, dim))
+
+
+def schedule_batches(cfg):
+    """Per step: [(stream name, length)] in acquisition order, which is the
+    order ``Scheduler.active`` (a deque, scheduler.py:24) hands them out."""
+    T = cfg["att"][1] + 1
+    steps = []
+    for s in range(cfg["steps"]):
+        live = [e for e in cfg["events"] if e[1] <= s and (e[2] is None or s < e[2])]
+        steps.append([(e[0], 1 if e[3] == s else T) for e in live])
+    return steps
+
+
+def run_encoder_fixture(ref, cfg):
+    from parakeet.modules import ConformerEncoder
+    from parakeet.engine.scheduler import Scheduler
+
+    left, right = cfg["att"]
+    T = right + 1
+    torch.manual_seed(0)
+    enc = ConformerEncoder(feat_in=128, hidden_size=cfg["dim"], ff_expansion_factor=4,
+                           num_layers=cfg["layers"], num_heads=cfg["heads"],
+                           subsampling_factor=8, pos_emb_max_len=5000,
+                           conv_kernel_size=9, att_context_size=cfg["att"],
+                           subsampling_conv_channels=256, use_bias=False)
+    sd = random_encoder_layers(cfg["seed"], cfg["layers"], cfg["dim"], cfg["heads"])
+    missing, unexpected = enc.load_state_dict({k: torch.from_numpy(v) for k, v in sd.items()},
+                                              strict=False)
+    assert not unexpected and all(not k.startswith("layers.") for k in missing), missing
+    enc.eval()
+    sched = Scheduler(max_active=cfg["pool"])
+    sched.init_state_pool(enc, torch.device("cpu"), torch.float32, cfg["pool"])
+    slot_of, acquired, released = {}, [], []
+    outs, lens, slots = {}, {}, {}
+    batches = schedule_batches(cfg)
+    for s, batch in enumerate(batches):
+        for name, acq, rel, _ in cfg["events"]:
+            if rel == s:
+                sched.release_state_slot(slot_of[name])
+                released.append((s, slot_of[name]))
+        for name, acq, rel, _ in cfg["events"]:
+            if acq == s:
+                slot_of[name] = sched.acquire_state_slot()
+                acquired.append((s, slot_of[name]))
+        seqs = [SimpleNamespace(encoder_state=slot_of[n]) for n, _ in batch]
+        x = torch.from_numpy(encoder_stream_inputs(cfg["seed"], s, len(batch), T, cfg["dim"]))
+        length = torch.tensor([n for _, n in batch], dtype=torch.int64)
+        st, idx = sched.pack_states(seqs)
+        with torch.inference_mode():
+            y, st = enc(x, st, length=length, bypass_pre_encode=True)
+        sched.unpack_states(st, idx)
+        if s in cfg["keep_steps"]:
+            outs[s] = y.numpy().astype(np.float32)
+            lens[s] = length.numpy()
+            slots[s] = idx.numpy()
+    fx = {"keep_steps": np.array(cfg["keep_steps"]),
+          "acquired": np.array(acquired, np.int64),
+          "released": np.array(released, np.int64).reshape(-1, 2),
+          "final_processed": sched._pool_state.processed_frames.numpy(),
+          "final_cache_len": sched._pool_state.cache_lengths.numpy(),
+          "final_conv_l0": sched._pool_state.cache.conv[:, 0].numpy(),
+          "final_k_l0_last": sched._pool_state.cache.attn_k[:, 0, -T:].numpy()}
+    for s in cfg["keep_steps"]:
+        fx[f"out_{s}"] = outs[s]
+        fx[f"len_{s}"] = lens[s]
+        fx[f"slots_{s}"] = slots[s]
+    return fx
+
+
+def cache_window_fixture(att, dim, steps, batch, layers, seed):
+    from parakeet.modules.cache import ModelCache
+
+    T = att[1] + 1
+    cache = ModelCache(layers, att, dim, 9, batch_size=batch, dtype=torch.float32)
+    rng = np.random.default_rng(seed)
+    keys = rng.standard_normal((steps, layers, batch, T, dim)).astype(np.float32)
+    vals = rng.standard_normal((steps, layers, batch, T, dim)).astype(np.float32)
+    wk = np.zeros((steps, layers, batch, att[0] + T, dim), np.float32)
+    wv = np.zeros_like(wk)
+    for s in range(steps):
+        for l in range(layers):
+            k, v = cache.update_attn_cache(l, torch.from_numpy(keys[s, l]),
+                                           torch.from_numpy(vals[s, l]))
+            wk[s, l], wv[s, l] = k.numpy(), v.numpy()
+    return {"keys": keys, "values": vals, "win_k": wk, "win_v": wv}
+
+
+def masks_fixture():
+    from parakeet.modules.encoder import ConformerEncoder
+
+    out = {}
+    rng = np.random.default_rng(5)
+    for tag, att in (("small", (70, 1)), ("large", (70, 13))):
+        T = att[1] + 1
+        cl, pf, ln = [], [], []
+        # aligned streams at every fill level, unaligned histories, short chunks
+        for proc in (0, 2, 14, 28, 68, 70, 72, 140, 1000):
+            cl.append(min(proc, 70)); pf.append(proc); ln.append(T)
+        for _ in range(12):
+            proc = int(rng.integers(0, 300))
+            cl.append(int(rng.integers(0, min(proc, 70) + 1))); pf.append(proc)
+            ln.append(int(rng.integers(1, T + 1)))
+        me = SimpleNamespace(att_context_size=att)
+        pad, mask = ConformerEncoder._create_streaming_masks(
+            me, T, torch.tensor(cl), torch.tensor(pf), torch.device("cpu"), torch.tensor(ln))
+        out[f"{tag}_cache_len"] = np.array(cl)
+        out[f"{tag}_processed"] = np.array(pf)
+        out[f"{tag}_lengths"] = np.array(ln)
+        out[f"{tag}_pad"] = pad.numpy()
+        out[f"{tag}_att"] = mask.numpy()
+    return out
+
+
+def scheduler_fixture():
+    """Slot ids returned by the reference Scheduler under seeded churn."""
+    from parakeet.engine.scheduler import Scheduler
+    from parakeet.modules.cache import ModelCache, StreamingState
+
+    class TinyEncoder:
+        def init_streaming_state(self, batch_size, device, dtype):
+            return StreamingState(ModelCache(1, (70, 1), 4, 9, batch_size, device, dtype),
+                                  torch.zeros(batch_size, dtype=torch.int64),
+                                  torch.zeros(batch_size, dtype=torch.int64))
+
+    sched = Scheduler()
+    sched.init_state_pool(TinyEncoder(), torch.device("cpu"), torch.float32, 8)
+    rng = np.random.default_rng(9)
+    held, ops = [], []
+    for _ in range(200):
+        if held and (rng.random() < 0.45 or len(held) == 8 and rng.random() < 0.5):
+            slot = held.pop(int(rng.integers(len(held))))
+            sched.release_state_slot(slot)
+            ops.append((1, slot))
+        else:
+            slot = sched.acquire_state_slot()
+            ops.append((0, -1 if slot is None else slot))
+            if slot is not None:
+                held.append(slot)
+    return {"ops": np.array(ops, np.int64)}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", required=True)
+    args = ap.parse_args()
+    install_librosa_stub()
+    sys.path.insert(0, os.path.abspath(args.reference))
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+
+    np.savez_compressed(os.path.join(HERE, "cache_window_small.npz"),
+                        **cache_window_fixture((70, 1), 16, 45, 3, 2, 21))
+    np.savez_compressed(os.path.join(HERE, "cache_window_large.npz"),
+                        **cache_window_fixture((70, 13), 8, 9, 2, 2, 22))
+    np.savez_compressed(os.path.join(HERE, "masks.npz"), **masks_fixture())
+    np.savez_compressed(os.path.join(HERE, "scheduler_slots.npz"), **scheduler_fixture())
+    np.savez_compressed(os.path.join(HERE, "encoder_small.npz"),
+                        **run_encoder_fixture(None, SMALL_SCHEDULE))
+    np.savez_compressed(os.path.join(HERE, "encoder_large.npz"),
+                        **run_encoder_fixture(None, LARGE_SCHEDULE))
+    print("golden vectors written to", HERE)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,205 @@
+"""Parity of the libpk kernels (called through the C ABI) with the CPU oracle.
+
+Page allocator: op-for-op equal to oracle.pages.PagePoolModel (page table,
+free ring order, counters).  Append + gather: bit-exact against the oracle's
+dense window, which equals the reference's (test_oracle_golden).  Attention
+and conv step: rel-L2 against the float64 oracle on valid rows, <= 1e-5 in
+fp32 and <= 1e-2 in bf16."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import pages, streaming
+from parakeet_b200 import _lib
+from parakeet_b200.engine.scheduler import SlotAllocator
+from parakeet_b200.ops import PagedKVPool
+from replay import rel_l2
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+TOL = {torch.float32: 1e-5, torch.bfloat16: 1e-2}
+SHAPES = {"small": dict(att=(70, 1), dim=512, heads=8), "large": dict(att=(70, 13), dim=1024, heads=8)}
+
+
+def pool_state(pool):
+    torch.cuda.synchronize()
+    head, tail = pool.ring_ctr.tolist()
+    ring = pool.free_ring.cpu().numpy()
+    free = [int(ring[i % pool.num_pages]) for i in range(head, tail)]
+    return pool.page_table.cpu().numpy(), pool.meta.cpu().numpy(), free
+
+
+def assert_pool_equals_model(pool, model):
+    table, meta, free = pool_state(pool)
+    assert np.array_equal(table, model.table)
+    assert np.array_equal(meta[:, _lib.META_FIRST], model.first)
+    assert np.array_equal(meta[:, _lib.META_NEXT], model.next)
+    assert np.array_equal(meta[:, _lib.META_WRITTEN], model.written)
+    assert np.array_equal(meta[:, _lib.META_PROCESSED], model.processed)
+    assert np.array_equal(meta[:, _lib.META_CACHE_LEN], model.cache_len)
+    assert free == list(model.free)
+
+
+@pytest.mark.parametrize("att,cap", [((70, 1), 0.6), ((70, 13), 0.6), ((70, 1), 1.0)])
+def test_page_allocator_matches_cpu_model(att, cap):
+    rng = np.random.default_rng(7)
+    left, T, ps, n_slots = att[0], att[1] + 1, 16, 24
+    per = pages.pages_per_stream(left, T, ps)
+    n_pages = int(cap * n_slots * per)
+    order = np.random.default_rng(1).permutation(n_pages)
+    pool = PagedKVPool(1, 128, 2, att, n_slots, num_pages=n_pages, dtype=torch.float32,
+                       device=DEV, page_order=order)
+    model = pages.PagePoolModel(n_pages, n_slots, left, T, ps, init_order=order)
+    alloc = SlotAllocator(n_slots, per, n_pages)
+    live = []
+    for step in range(160):
+        for _ in range(int(rng.integers(0, 3))):
+            if live and rng.random() < 0.3:
+                s = live.pop(int(rng.integers(len(live))))
+                alloc.release(s)
+                pool.release_slot(s)
+                model.release_slot(s)
+        for _ in range(int(rng.integers(0, 4))):
+            s = alloc.acquire()
+            if s is not None:
+                live.append(s)
+        batch = [s for s in live if rng.random() < 0.85]
+        lengths = [T if rng.random() < 0.9 else int(rng.integers(1, T + 1)) for _ in batch]
+        sl = torch.tensor(batch, dtype=torch.int32, device=DEV)
+        ln = torch.tensor(lengths, dtype=torch.int32, device=DEV)
+        assert model.begin_step(batch)
+        pool.begin_step(sl)
+        model.end_step(batch, lengths)
+        pool.end_step(sl, ln)
+        if step % 8 == 0 or step > 150:
+            assert_pool_equals_model(pool, model)
+    assert pool.read_error() == 0
+    assert_pool_equals_model(pool, model)
+
+
+def test_pool_exhaustion_sets_error_bit_and_allocates_nothing():
+    pool = PagedKVPool(1, 128, 2, (70, 1), 4, num_pages=2, dtype=torch.float32, device=DEV)
+    sl = torch.tensor([0, 1, 2], dtype=torch.int32, device=DEV)
+    pool.begin_step(sl)
+    torch.cuda.synchronize()
+    assert pool.read_error() & _lib.PK_DEV_POOL_EXHAUSTED
+    assert (pool.page_table == -1).all()
+    assert pool.ring_ctr.tolist() == [0, 2]
+
+
+def run_stream_steps(shape, dtype, steps, n_slots, seed, check_every=1, short_last=True):
+    """Staggered streams through append + gather + attention, against the
+    oracle's dense slot pool (pack -> update_attn_cache -> unpack) and masks."""
+    cfg = SHAPES[shape]
+    att, D, H = cfg["att"], cfg["dim"], cfg["heads"]
+    left, T = att[0], att[1] + 1
+    W, P, L = left + T, 2 * (left + T) - 1, 2
+    rng = np.random.default_rng(seed)
+    order = rng.permutation(n_slots * pages.pages_per_stream(left, T, 16))
+    pool = PagedKVPool(L, D, H, att, n_slots, dtype=dtype, device=DEV, page_order=order)
+    dense = streaming.SlotSchedulerModel(L, att, D, 9, n_slots)
+    start = {s: int(rng.integers(0, steps // 2)) if s else 0 for s in range(n_slots)}
+    pos = [rng.standard_normal((P, D)) / 8 for _ in range(L)]
+    bu = [rng.standard_normal((H, D // H)) / 8 for _ in range(L)]
+    bv = [rng.standard_normal((H, D // H)) / 8 for _ in range(L)]
+    to = lambda a: torch.tensor(np.asarray(a), dtype=dtype, device=DEV)  # noqa: E731
+    rd = lambda t: t.float().cpu().numpy().astype(np.float64)  # noqa: E731
+    pos_t, bu_t, bv_t = [to(p) for p in pos], [to(b) for b in bu], [to(b) for b in bv]
+    pos_r, bu_r, bv_r = [rd(t) for t in pos_t], [rd(t) for t in bu_t], [rd(t) for t in bv_t]
+    worst = 0.0
+    for step in range(steps):
+        batch = [s for s in range(n_slots) if start[s] <= step]
+        lengths = [T] * len(batch)
+        if short_last and step == steps - 1:
+            lengths[-1] = max(1, T // 2)
+        sl = torch.tensor(batch, dtype=torch.int32, device=DEV)
+        ln = torch.tensor(lengths, dtype=torch.int32, device=DEV)
+        pool.begin_step(sl)
+        st, idx = dense.pack_states(batch)
+        _, mask = streaming.streaming_masks(T, st.cache_lengths, st.processed_frames, lengths, att)
+        for l in range(L):
+            qkv = to(rng.standard_normal((len(batch), T, 3 * D)) / 8)
+            q, k, v = qkv[..., :D], qkv[..., D:2 * D], qkv[..., 2 * D:]
+            pool.append(l, k, v, sl)
+            kw_ref, vw_ref = st.cache.update_attn_cache(l, rd(k), rd(v))
+            out = pool.attention(l, q, pos_t[l], bu_t[l], bv_t[l], sl, ln)
+            if step % check_every == 0 or step == steps - 1:
+                kw, vw = pool.gather(l, sl)
+                assert np.array_equal(rd(kw), kw_ref), (step, l)
+                assert np.array_equal(rd(vw), vw_ref), (step, l)
+                ref = streaming.relpos_attention_core(rd(q), kw_ref, vw_ref, pos_r[l], bu_r[l],
+                                                      bv_r[l], mask, H)
+                got = rd(out)
+                rows = [(b, t) for b in range(len(batch)) for t in range(lengths[b])]
+                e = rel_l2(np.stack([got[b, t] for b, t in rows]), np.stack([ref[b, t] for b, t in rows]))
+                worst = max(worst, e)
+                assert e <= TOL[dtype], (step, l, e)
+        st.processed_frames += np.asarray(lengths)
+        st.cache_lengths = np.minimum(st.cache_lengths + np.asarray(lengths), left)
+        dense.unpack_states(st, idx)
+        pool.end_step(sl, ln)
+    assert pool.read_error() == 0
+    return worst
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_append_gather_attention_small(dtype):
+    run_stream_steps("small", dtype, steps=44, n_slots=5, seed=3, check_every=5)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_append_gather_attention_large(dtype):
+    run_stream_steps("large", dtype, steps=9, n_slots=3, seed=4)
+
+
+def conv_oracle(x2d, cache, w, lengths, g, b, eps=1e-5):
+    """GLU -> pad mask -> cached depthwise conv -> LayerNorm -> SiLU
+    (convolution.py:153-159) on float64."""
+    x = np.asarray(x2d, np.float64).transpose(0, 2, 1)          # [B, 2D, T]
+    y = streaming.glu_channels(x)
+    T = y.shape[-1]
+    pad = np.arange(T)[None, :] >= np.asarray(lengths)[:, None]
+    y = np.where(pad[:, None, :], 0.0, y)
+    y, nxt = streaming.causal_depthwise_conv(y, cache, w)
+    z = streaming.silu(streaming.layer_norm(y.transpose(0, 2, 1), g, b, eps))
+    return z, y.transpose(0, 2, 1), nxt
+
+
+@pytest.mark.parametrize("shape", ["small", "large"])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_conv_step_matches_oracle(shape, dtype):
+    cfg = SHAPES[shape]
+    D, T = cfg["dim"], cfg["att"][1] + 1
+    rng = np.random.default_rng(5)
+    n_slots, L, layer = 6, 3, 1
+    pool = PagedKVPool(L, D, cfg["heads"], cfg["att"], n_slots, dtype=dtype, device=DEV)
+    to = lambda a: torch.tensor(np.asarray(a), dtype=dtype, device=DEV)  # noqa: E731
+    rd = lambda t: t.float().cpu().numpy().astype(np.float64)  # noqa: E731
+    pool.conv.copy_(to(rng.standard_normal(pool.conv.shape)))
+    w = to(rng.standard_normal((D, 1, 9)) / 3)
+    g, b = to(1 + 0.1 * rng.standard_normal(D)), to(0.1 * rng.standard_normal(D))
+    for it in range(3):
+        batch = [4, 1, 3] if it != 1 else [0, 5]
+        lengths = [T] * len(batch)
+        lengths[0] = max(1, T - 1)
+        sl = torch.tensor(batch, dtype=torch.int32, device=DEV)
+        ln = torch.tensor(lengths, dtype=torch.int32, device=DEV)
+        x = to(rng.standard_normal((len(batch), T, 2 * D)))
+        others = [s for s in range(n_slots) if s not in batch]
+        untouched = pool.conv[others].clone()
+        cache_before = rd(pool.conv[sl.long(), layer])
+        ref_z, ref_y, ref_next = conv_oracle(rd(x), cache_before, rd(w), lengths, rd(g), rd(b))
+        raw = pool.conv_step(layer, x, w, sl, ln)                     # no LayerNorm
+        pool.conv[sl.long(), layer] = to(cache_before)                # rewind the cache
+        z = pool.conv_step(layer, x, w, sl, ln, g, b, 1e-5)
+        tol = TOL[dtype]
+        assert rel_l2(rd(raw), ref_y) <= tol
+        assert rel_l2(rd(z), ref_z) <= tol
+        got_next = rd(pool.conv[sl.long(), layer])
+        if dtype == torch.float32:
+            assert rel_l2(got_next, ref_next) <= tol
+        else:   # cache holds dtype-rounded GLU outputs: equal up to one rounding step
+            assert np.allclose(got_next, ref_next, rtol=1e-2, atol=1e-2)
+        assert torch.equal(pool.conv[others], untouched)
+    assert pool.read_error() == 0
