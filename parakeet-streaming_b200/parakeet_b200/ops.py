@@ -54,6 +54,8 @@ class PagedKVPool:
         self.device = torch.device(device)
         if self.device.type != "cuda":
             raise RuntimeError("PagedKVPool needs a CUDA device")
+        if self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
         self.num_layers, self.dim, self.num_heads = num_layers, dim, num_heads
         self.left, right = int(att_context[0]), int(att_context[1])
         self.chunk = right + 1
