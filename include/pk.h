@@ -57,7 +57,7 @@ extern "C" {
  * tensors (parakeet/engine/scheduler.py:68-84).
  */
 typedef struct pk_paged_kv_desc {
-    void *kv;             /* [num_pages][num_layers][2][page_size][dim]      */
+    void *kv;             /* [num_pages][num_layers][2][num_heads][page_size][head_dim] */
     int32_t *page_table;  /* [num_slots][ring], -1 = no page                 */
     int32_t *free_ring;   /* [num_pages] FIFO of free page ids               */
     int64_t *ring_ctr;    /* [2] monotonic head (pop) and tail (push)        */

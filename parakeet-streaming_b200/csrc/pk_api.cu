@@ -112,17 +112,19 @@ int pk_paged_kv_create(const pk_paged_kv_desc *desc, pk_paged_kv **out) {
              "ring must be a power of two >= pk_pages_per_stream()");
     PK_CHECK(aligned16(d.kv), "kv pool not 16-byte aligned");
     const int esize = d.dtype == PK_DTYPE_BF16 ? 2 : 4;
-    PK_CHECK((d.dim * esize) % 128 == 0, "dim * element size must be a multiple of 128 bytes");
+    PK_CHECK(((d.dim / d.num_heads) * esize) % 128 == 0,
+             "head_dim * element size must be a multiple of 128 bytes");
     PK_CHECK(d.left + 2 * d.chunk - 1 <= 256, "left + 2*chunk - 1 must be <= 256");
     pk_paged_kv *kv = static_cast<pk_paged_kv *>(calloc(1, sizeof(pk_paged_kv)));
     if (!kv) return PK_EINVAL;
     kv->d = d;
     kv->esize = esize;
     kv->head_dim = d.dim / d.num_heads;
-    const uint64_t row = (uint64_t)d.dim * esize;
-    int st = encode_tmap_3d(&kv->kv_map, d.dtype, d.kv, d.dim, d.page_size,
-                            (uint64_t)d.num_pages * d.num_layers * 2, row, row * d.page_size,
-                            128 / esize, d.page_size, 1);
+    // head-major planes: one (page, layer, K|V, head) is page_size x head_dim contiguous
+    const uint64_t row = (uint64_t)kv->head_dim * esize;
+    int st = encode_tmap_3d(&kv->kv_map, d.dtype, d.kv, kv->head_dim, d.page_size,
+                            (uint64_t)d.num_pages * d.num_layers * 2 * d.num_heads, row,
+                            row * d.page_size, 128 / esize, d.page_size, 1);
     if (st != PK_OK) {
         free(kv);
         return st;

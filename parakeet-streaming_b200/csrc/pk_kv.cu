@@ -12,9 +12,14 @@
 namespace pk {
 namespace {
 
-__device__ __forceinline__ int64_t page_row_offset(const pk_paged_kv_desc &d, int page, int layer,
-                                                   int kvi, int row) {
-    return ((((int64_t)page * d.num_layers + layer) * 2 + kvi) * d.page_size + row) * d.dim;
+// Element offset of (page, layer, K|V, row, model column) in the head-major
+// pool [pages][layers][2][heads][page_size][head_dim].
+__device__ __forceinline__ int64_t pool_offset(const pk_paged_kv_desc &d, int page, int layer,
+                                               int kvi, int row, int col) {
+    const int dh = d.dim / d.num_heads;
+    const int h = col / dh;
+    return (((((int64_t)page * d.num_layers + layer) * 2 + kvi) * d.num_heads + h) * d.page_size +
+            row) * dh + (col - h * dh);
 }
 
 // grid (batch, num_layers); every CTA moves T rows of K and of V of one
@@ -46,8 +51,9 @@ __global__ void __launch_bounds__(128)
         const char *src = (kvi ? value : key) +
                           ((int64_t)blockIdx.y * ls + (int64_t)b * bs + (int64_t)t * rs) * esize;
         const uint4 val = __ldg(reinterpret_cast<const uint4 *>(src) + v);
-        char *dst = pool + page_row_offset(d, page, l, kvi, a % d.page_size) * esize;
-        reinterpret_cast<uint4 *>(dst)[v] = val;
+        const int col = v * (16 / esize);
+        char *dst = pool + pool_offset(d, page, l, kvi, a % d.page_size, col) * esize;
+        *reinterpret_cast<uint4 *>(dst) = val;
     }
 }
 
@@ -76,8 +82,9 @@ __global__ void __launch_bounds__(256)
             const int page =
                 d.page_table[(int64_t)s * d.ring + ((a / d.page_size) & (d.ring - 1))];
             if (page >= 0 && page < d.num_pages) {
-                const char *src = pool + page_row_offset(d, page, layer, kvi, a % d.page_size) * esize;
-                val = __ldg(reinterpret_cast<const uint4 *>(src) + v);
+                const int col = v * (16 / esize);
+                const char *src = pool + pool_offset(d, page, layer, kvi, a % d.page_size, col) * esize;
+                val = __ldg(reinterpret_cast<const uint4 *>(src));
             } else {
                 raise(d.error, PK_DEV_BAD_PAGE);
             }

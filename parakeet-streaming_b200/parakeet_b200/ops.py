@@ -37,7 +37,7 @@ def ring_size(left: int, chunk: int, page_size: int) -> int:
 class PagedKVPool:
     """Paged K/V window + conv cache for ``num_slots`` stream slots.
 
-    kv          [num_pages, L, 2, page_size, D]   model dtype
+    kv          [num_pages, L, 2, H, page_size, dh] model dtype (head-major pages)
     page_table  [num_slots, ring]                 int32, -1 = none
     free_ring   [num_pages]                       int32
     ring_ctr    [2]                               int64 head / tail
@@ -68,7 +68,8 @@ class PagedKVPool:
         self.ring = ring_size(self.left, self.chunk, page_size)
         self.num_pages = int(num_pages or num_slots * self.per_stream)
         dev = self.device
-        self.kv = torch.zeros((self.num_pages, num_layers, 2, page_size, dim), dtype=dtype, device=dev)
+        self.kv = torch.zeros((self.num_pages, num_layers, 2, num_heads, page_size, dim // num_heads),
+                              dtype=dtype, device=dev)
         self.page_table = torch.full((num_slots, self.ring), -1, dtype=torch.int32, device=dev)
         self.free_ring = torch.empty(self.num_pages, dtype=torch.int32, device=dev)
         self.ring_ctr = torch.zeros(2, dtype=torch.int64, device=dev)
