@@ -36,7 +36,7 @@ struct AttnGeom {
     int W, R, max_boxes;
     uint32_t box_bytes;         // one page box: page_size rows x 128 bytes
     uint32_t pos_colbox_bytes;  // one column box of rel-pos rows (1024-aligned)
-    uint32_t off_v, off_pos, off_q, off_s, off_rows, off_zero, off_red;
+    uint32_t off_v, off_pos, off_q, off_s, off_rows, off_zero, off_red, off_mask;
     uint32_t p_stride;          // bytes per row of the bf16 probability tile
 };
 
@@ -366,6 +366,7 @@ __global__ void __launch_bounds__(MmaCfg<DH, NW>::THREADS)
     int *rowr = rowoff + 16 * KS_P;
     char *sZero = smem + g.off_zero;
     float *sRed = reinterpret_cast<float *>(smem + g.off_red);  // [2][NW][16]
+    uint32_t *sMask = reinterpret_cast<uint32_t *>(smem + g.off_mask);  // [16][4] key bits
 
     if (tid == 0)
         issue_window_loads<T, DH>(&kv_map, &pos_map, g, page_table, meta, error, a, h, b, lrel,
@@ -379,25 +380,44 @@ __global__ void __launch_bounds__(MmaCfg<DH, NW>::THREADS)
     }
 
     // Qu = q + pos_bias_u, Qv = q + pos_bias_v, rounded to bf16 as the reference's
-    // bf16 (query + pos_bias_*) is (attention.py:108-109); rows >= chunk are zero
+    // bf16 (query + pos_bias_*) is (attention.py:108-109).  Rows >= chunk of the
+    // m16 tile are left as they are: their scores are replaced by a constant
+    // below and their outputs are never stored, and MMA rows are independent.
     {
         const T *qb = static_cast<const T *>(a.q) + (int64_t)lrel * a.q_ls + (int64_t)b * a.q_bs + h * DH;
         const T *bu = static_cast<const T *>(a.bias_u) + (int64_t)lrel * a.bias_ls + h * DH;
         const T *bv = static_cast<const T *>(a.bias_v) + (int64_t)lrel * a.bias_ls + h * DH;
-        for (int idx = tid; idx < 16 * (DH / 2); idx += M::THREADS) {
+        for (int idx = tid; idx < chunk * (DH / 2); idx += M::THREADS) {
             const int t = idx / (DH / 2), d = 2 * (idx % (DH / 2));
-            __nv_bfloat162 u2 = __floats2bfloat162_rn(0.f, 0.f), v2 = u2;
-            if (t < chunk) {
-                const float2 q = __bfloat1622float2(
-                    *reinterpret_cast<const __nv_bfloat162 *>(qb + (int64_t)t * a.q_rs + d));
-                const float2 fu = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(bu + d));
-                const float2 fv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(bv + d));
-                u2 = __floats2bfloat162_rn(q.x + fu.x, q.y + fu.y);
-                v2 = __floats2bfloat162_rn(q.x + fv.x, q.y + fv.y);
-            }
+            const float2 q = __bfloat1622float2(
+                *reinterpret_cast<const __nv_bfloat162 *>(qb + (int64_t)t * a.q_rs + d));
+            const float2 fu = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(bu + d));
+            const float2 fv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(bv + d));
             const uint32_t off = (d >> 6) * 2048u + sw128(t, (d & 63) * 2);
-            *reinterpret_cast<__nv_bfloat162 *>(sQ + off) = u2;
-            *reinterpret_cast<__nv_bfloat162 *>(sQ + M::NCOL * 2048u + off) = v2;
+            *reinterpret_cast<__nv_bfloat162 *>(sQ + off) = __floats2bfloat162_rn(q.x + fu.x, q.y + fu.y);
+            *reinterpret_cast<__nv_bfloat162 *>(sQ + M::NCOL * 2048u + off) =
+                __floats2bfloat162_rn(q.x + fv.x, q.y + fv.y);
+        }
+        // streaming mask as bits: sMask[i][kb] bit (j % 32) set = key j allowed for query i
+        {
+            const int clen = ws.clen, n = ws.len, key_start = max(ws.proc - clen, 0);
+            const int off = g.left - clen, left_chunks = g.left / chunk;
+            for (int kb = warp; kb < 4; kb += NW) {
+                const int j = kb * 32 + lane;
+                bool key_ok = j < W && j >= off;
+                int kc = 0;
+                if (key_ok) {
+                    const int rr = j - off;
+                    key_ok = rr < clen || (rr - clen) < n;
+                    kc = (key_start + rr) / chunk;
+                }
+                for (int i = 0; i < chunk; ++i) {
+                    const int dc = (key_start + clen + i) / chunk - kc;
+                    const unsigned bits = __ballot_sync(0xffffffffu, key_ok && i < n && dc >= 0 &&
+                                                                         dc <= left_chunks);
+                    if (lane == 0) sMask[i * 4 + kb] = bits;
+                }
+            }
         }
         for (int j = tid; j < 16 * KS_P; j += M::THREADS) {
             const int av = ws.w - g.left + j;
@@ -477,9 +497,14 @@ __global__ void __launch_bounds__(MmaCfg<DH, NW>::THREADS)
 
     // scores, mask, row max (rows gq and gq + 8 of the fragment)
     const float scale = rsqrtf((float)DH);
-    const MaskCtx mk = make_mask(ws, g);
     float mx[2] = {-INFINITY, -INFINITY};
     {
+        uint32_t mrow[2][4];
+#pragma unroll
+        for (int r = 0; r < 2; ++r)
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                mrow[r][k] = (gq + 8 * r < chunk) ? sMask[(gq + 8 * r) * 4 + k] : 0u;
 #pragma unroll
         for (int t = 0; t < MAXT; ++t) {
             const int nt = warp + t * NW;
@@ -489,11 +514,13 @@ __global__ void __launch_bounds__(MmaCfg<DH, NW>::THREADS)
                 const int i = gq + (e >> 1) * 8, j = nt * 8 + 2 * tq + (e & 1);
                 float s;
                 if (j >= W) {
-                    s = -INFINITY;
-                } else if (i >= chunk || mk.masked(i, j)) {
-                    s = sc[t][e] * scale - 1e5f;
-                } else {
+                    s = -INFINITY;                        // key padding of the last tile
+                } else if (i >= chunk) {
+                    s = 0.f;                              // query padding of the m16 tile
+                } else if ((mrow[e >> 1][j >> 5] >> (j & 31)) & 1u) {
                     s = sc[t][e] * scale + sBD[i * RPAD + chunk - 1 - i + j] * scale;
+                } else {
+                    s = sc[t][e] * scale - 1e5f;          // masked_fill(-1e5), attention.py:115
                 }
                 sc[t][e] = s;
                 mx[e >> 1] = fmaxf(mx[e >> 1], s);
@@ -628,13 +655,15 @@ bool fill_geom(const pk_paged_kv *kv, AttnGeom &g, size_t &smem, bool mma) {
         g.off_rows = g.off_s + 16 * g.p_stride + ((d.chunk * RPAD * 4 + 15) & ~15);
         g.off_zero = g.off_rows + 2 * 16 * KS_P * 4;
         g.off_red = g.off_zero + 128;
-        smem = g.off_red + 2 * 8 * 16 * 4 + 1024;
+        g.off_mask = g.off_red + 2 * 8 * 16 * 4;
+        smem = g.off_mask + 16 * 4 * 4 + 1024;
     } else {
         g.off_s = g.off_q + 2 * d.chunk * DH * 4;
         g.p_stride = 0;
         g.off_rows = g.off_s + ((d.chunk * g.W * 4 + 15) & ~15);
         g.off_zero = g.off_rows + 2 * g.W * 4;
         g.off_red = g.off_zero;
+        g.off_mask = g.off_zero;
         smem = g.off_zero + 1024;
     }
     return smem <= 220 * 1024;
@@ -692,7 +721,7 @@ int launch_attention(const pk_paged_kv *kv, const CUtensorMap &pos_map, const At
     const bool bf16 = kv->d.dtype == PK_DTYPE_BF16;
     switch (kv->head_dim) {
         case 64:
-            return bf16 ? launch_bf16<64, 1>(kv, pos_map, a, s) : launch_f32<64>(kv, pos_map, a, s);
+            return bf16 ? launch_bf16<64, 4>(kv, pos_map, a, s) : launch_f32<64>(kv, pos_map, a, s);
         case 128:
             return bf16 ? launch_bf16<128, 4>(kv, pos_map, a, s) : launch_f32<128>(kv, pos_map, a, s);
         default:
