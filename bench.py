@@ -347,6 +347,7 @@ def main():
                               for l in range(L)], nb["conv"] * units, L),
         }
         hbm, _ = peaks()
+        pool.begin_step(slots)   # pages for this step's window; every op below re-runs it
         for name, (fn, nbytes, launches) in ops.items():
             t = timeit(fn)
             breakdown[name] = {"ms": round(t, 4), "GB/s": round(nbytes / t / 1e6, 1),

@@ -41,21 +41,24 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
     return fn;
 }
 
-int encode_tmap_3d(CUtensorMap *map, int dtype, const void *base, uint64_t d0, uint64_t d1,
-                   uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box0,
-                   uint32_t box1, uint32_t box2) {
+int encode_tmap(CUtensorMap *map, int dtype, const void *base, int rank, const uint64_t *dims,
+                const uint64_t *strides_bytes, const uint32_t *box) {
     auto fn = get_encode_fn();
     if (!fn) {
         set_error("cuTensorMapEncodeTiled unavailable from the driver");
         return PK_ECUDA;
     }
-    const cuuint64_t dims[3] = {d0, d1, d2};
-    const cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
-    const cuuint32_t box[3] = {box0, box1, box2};
-    const cuuint32_t estr[3] = {1, 1, 1};
+    cuuint64_t d[5], st[4];
+    cuuint32_t bx[5], estr[5];
+    for (int i = 0; i < rank; ++i) {
+        d[i] = dims[i];
+        bx[i] = box[i];
+        estr[i] = 1;
+        if (i + 1 < rank) st[i] = strides_bytes[i];
+    }
     CUresult r = fn(map, dtype == PK_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
-                    3, const_cast<void *>(base), dims, strides, box, estr,
+                    rank, const_cast<void *>(base), d, st, bx, estr,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
@@ -63,6 +66,15 @@ int encode_tmap_3d(CUtensorMap *map, int dtype, const void *base, uint64_t d0, u
         return PK_ECUDA;
     }
     return PK_OK;
+}
+
+int encode_tmap_3d(CUtensorMap *map, int dtype, const void *base, uint64_t d0, uint64_t d1,
+                   uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box0,
+                   uint32_t box1, uint32_t box2) {
+    const uint64_t dims[3] = {d0, d1, d2};
+    const uint64_t strides[2] = {stride1_bytes, stride2_bytes};
+    const uint32_t box[3] = {box0, box1, box2};
+    return encode_tmap(map, dtype, base, 3, dims, strides, box);
 }
 
 }  // namespace pk
@@ -220,6 +232,22 @@ int pk_paged_attention(pk_paged_kv *kv, int32_t layer0, int32_t num_layers, cons
     int st = encode_tmap_3d(&pos_map, kv->d.dtype, pos_proj, kv->d.dim, P, num_layers, row,
                             lstride, 128 / es, R, 1);
     if (st != PK_OK) return st;
+    // query rows of one head as 4-D tiles {head columns, chunk rows, stream, layer}
+    CUtensorMap q_map;
+    memset(&q_map, 0, sizeof(q_map));
+    if (kv->d.dtype == PK_DTYPE_BF16) {
+        PK_CHECK(aligned16(query) && (q_row_stride * es) % 16 == 0 &&
+                     (q_batch_stride * es) % 16 == 0 && (q_layer_stride * es) % 16 == 0,
+                 "query must be 16-byte aligned with 16-byte strides");
+        const uint64_t qb = (uint64_t)q_batch_stride * es;
+        const uint64_t ql = num_layers == 1 ? qb * batch : (uint64_t)q_layer_stride * es;
+        const uint64_t qdims[4] = {(uint64_t)kv->d.dim, (uint64_t)kv->d.chunk, (uint64_t)batch,
+                                   (uint64_t)num_layers};
+        const uint64_t qstr[3] = {(uint64_t)q_row_stride * es, qb, ql};
+        const uint32_t qbox[4] = {(uint32_t)(128 / es), (uint32_t)kv->d.chunk, 1, 1};
+        st = encode_tmap(&q_map, kv->d.dtype, query, 4, qdims, qstr, qbox);
+        if (st != PK_OK) return st;
+    }
     AttnArgs a;
     a.q = query;
     a.q_ls = q_layer_stride;
@@ -237,7 +265,7 @@ int pk_paged_attention(pk_paged_kv *kv, int32_t layer0, int32_t num_layers, cons
     a.o_rs = out_row_stride;
     a.layer0 = layer0;
     a.nlayers = num_layers;
-    st = launch_attention(kv, pos_map, a, static_cast<cudaStream_t>(stream));
+    st = launch_attention(kv, pos_map, q_map, a, static_cast<cudaStream_t>(stream));
     if (st == PK_ENOTSUP) pk::set_error("attention configuration not handled (smem or boxes)");
     return st;
 }

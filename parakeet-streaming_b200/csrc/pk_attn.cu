@@ -18,9 +18,9 @@
 // rel-pos rows complete on one mbarrier, V on a second, so the V load
 // overlaps the score computation.  All waits are bounded.
 //
-// Math: bf16 on tensor cores (mma.sync m16n8k16, fp32 accumulate; the
-// query chunk, T <= 16 frames, is one m16 tile), fp32 on CUDA cores (the
-// exact-parity path).
+// This file holds the fp32 path (CUDA cores, the exact-parity path) and the
+// dispatch; the bf16 path is the persistent tensor-core kernel of
+// pk_attn_bf16.cu.
 #include <math.h>
 
 #include "pk_common.cuh"
@@ -300,330 +300,6 @@ __global__ void __launch_bounds__(kF32Threads)
     }
 }
 
-// ------------------------------------------------------------------ bf16 path
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-                 : "r"(addr));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-                 : "r"(addr));
-}
-__device__ __forceinline__ void mma_bf16(float (&c)[4], const uint32_t (&a)[4], uint32_t b0,
-                                         uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, "
-        "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
-        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-template <int DH, int NW>
-struct MmaCfg {
-    static constexpr int NCOL = DH / 64;   // 128-byte column boxes per head (bf16)
-    static constexpr int KSTEPS = DH / 16;  // k-steps of the score MMAs
-    static constexpr int THREADS = NW * 32;
-    static constexpr int MAXT = (16 + NW - 1) / NW;  // 8-key tiles per warp: W <= 128
-};
-
-// shared-memory byte address of window row j, column `col` (a multiple of 8)
-// of the K or V box region; rows outside the window map to the zero row
-__device__ __forceinline__ uint32_t win_addr(uint32_t region, uint32_t zero, const int *rowoff,
-                                             const int *rowr, uint32_t box_bytes, int j, int col) {
-    const int ro = rowoff[j];
-    if (ro < 0) return zero + ((col & 63) * 2);
-    return region + ro + (col >> 6) * box_bytes + sw128(rowr[j], (col & 63) * 2);
-}
-
-template <int DH, int NW>
-__global__ void __launch_bounds__(MmaCfg<DH, NW>::THREADS)
-    paged_attn_bf16_kernel(const __grid_constant__ CUtensorMap kv_map,
-                           const __grid_constant__ CUtensorMap pos_map, const AttnGeom g,
-                           const int32_t *__restrict__ page_table,
-                           const int32_t *__restrict__ meta, int32_t *error, const AttnArgs a) {
-    using T = __nv_bfloat16;
-    using M = MmaCfg<DH, NW>;
-    extern __shared__ char smem_raw[];
-    char *smem = reinterpret_cast<char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                          ~uintptr_t(1023));
-    __shared__ WinShared ws;
-    const int h = blockIdx.x, b = blockIdx.y, lrel = blockIdx.z;
-    const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
-    const int gq = lane / 4, tq = lane % 4;  // mma fragment row group / column pair
-    const int chunk = g.chunk, W = g.W, ps = g.page_size;
-    const int NT_S = (W + 7) / 8;            // key tiles of 8
-    const int KS_P = (W + 15) / 16;          // key steps of 16 for P.V
-    const int NT_P = (g.R + 7) / 8;          // rel-pos tiles of 8
-    const int RPAD = NT_P * 8;
-
-    char *sK = smem, *sV = smem + g.off_v, *sP = smem + g.off_pos;
-    char *sQ = smem + g.off_q;                 // Qu then Qv: NCOL x (16 rows x 128 B) each
-    char *sPr = smem + g.off_s;                // probabilities, bf16 [16][p_stride]
-    float *sBD = reinterpret_cast<float *>(smem + g.off_s + 16 * g.p_stride);  // [chunk][RPAD]
-    int *rowoff = reinterpret_cast<int *>(smem + g.off_rows);
-    int *rowr = rowoff + 16 * KS_P;
-    char *sZero = smem + g.off_zero;
-    float *sRed = reinterpret_cast<float *>(smem + g.off_red);  // [2][NW][16]
-    uint32_t *sMask = reinterpret_cast<uint32_t *>(smem + g.off_mask);  // [16][4] key bits
-
-    if (tid == 0)
-        issue_window_loads<T, DH>(&kv_map, &pos_map, g, page_table, meta, error, a, h, b, lrel,
-                                  sK, sV, sP, ws);
-    __syncthreads();
-    T *out_base = static_cast<T *>(a.out) + (int64_t)lrel * a.o_ls + (int64_t)b * a.o_bs + h * DH;
-    if (!ws.ok) {
-        for (int idx = tid; idx < chunk * DH; idx += M::THREADS)
-            out_base[(int64_t)(idx / DH) * a.o_rs + idx % DH] = __float2bfloat16_rn(0.f);
-        return;
-    }
-
-    // Qu = q + pos_bias_u, Qv = q + pos_bias_v, rounded to bf16 as the reference's
-    // bf16 (query + pos_bias_*) is (attention.py:108-109).  Rows >= chunk of the
-    // m16 tile are left as they are: their scores are replaced by a constant
-    // below and their outputs are never stored, and MMA rows are independent.
-    {
-        const T *qb = static_cast<const T *>(a.q) + (int64_t)lrel * a.q_ls + (int64_t)b * a.q_bs + h * DH;
-        const T *bu = static_cast<const T *>(a.bias_u) + (int64_t)lrel * a.bias_ls + h * DH;
-        const T *bv = static_cast<const T *>(a.bias_v) + (int64_t)lrel * a.bias_ls + h * DH;
-        for (int idx = tid; idx < chunk * (DH / 2); idx += M::THREADS) {
-            const int t = idx / (DH / 2), d = 2 * (idx % (DH / 2));
-            const float2 q = __bfloat1622float2(
-                *reinterpret_cast<const __nv_bfloat162 *>(qb + (int64_t)t * a.q_rs + d));
-            const float2 fu = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(bu + d));
-            const float2 fv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(bv + d));
-            const uint32_t off = (d >> 6) * 2048u + sw128(t, (d & 63) * 2);
-            *reinterpret_cast<__nv_bfloat162 *>(sQ + off) = __floats2bfloat162_rn(q.x + fu.x, q.y + fu.y);
-            *reinterpret_cast<__nv_bfloat162 *>(sQ + M::NCOL * 2048u + off) =
-                __floats2bfloat162_rn(q.x + fv.x, q.y + fv.y);
-        }
-        // streaming mask as bits: sMask[i][kb] bit (j % 32) set = key j allowed for query i
-        {
-            const int clen = ws.clen, n = ws.len, key_start = max(ws.proc - clen, 0);
-            const int off = g.left - clen, left_chunks = g.left / chunk;
-            for (int kb = warp; kb < 4; kb += NW) {
-                const int j = kb * 32 + lane;
-                bool key_ok = j < W && j >= off;
-                int kc = 0;
-                if (key_ok) {
-                    const int rr = j - off;
-                    key_ok = rr < clen || (rr - clen) < n;
-                    kc = (key_start + rr) / chunk;
-                }
-                for (int i = 0; i < chunk; ++i) {
-                    const int dc = (key_start + clen + i) / chunk - kc;
-                    const unsigned bits = __ballot_sync(0xffffffffu, key_ok && i < n && dc >= 0 &&
-                                                                         dc <= left_chunks);
-                    if (lane == 0) sMask[i * 4 + kb] = bits;
-                }
-            }
-        }
-        for (int j = tid; j < 16 * KS_P; j += M::THREADS) {
-            const int av = ws.w - g.left + j;
-            if (j >= W || av < 0) {
-                rowoff[j] = -1;
-                rowr[j] = 0;
-            } else {
-                const int bi = av / ps - ws.nfirst;
-                rowoff[j] = bi * M::NCOL * g.box_bytes;
-                rowr[j] = av % ps - ws.start[bi];
-            }
-        }
-        for (int i = tid; i < 32; i += M::THREADS) reinterpret_cast<float *>(sZero)[i] = 0.f;
-    }
-    __syncthreads();
-
-    const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aP = smem_u32(sP);
-    const uint32_t aQ = smem_u32(sQ), aZ = smem_u32(sZero), aPr = smem_u32(sPr);
-
-    // A fragments of Qu and Qv (rows 0..15, all k-steps)
-    uint32_t fu[M::KSTEPS][4], fv[M::KSTEPS][4];
-#pragma unroll
-    for (int ks = 0; ks < M::KSTEPS; ++ks) {
-        const int col = ks * 16 + (lane / 16) * 8;
-        const uint32_t off = (col >> 6) * 2048u + sw128(lane % 16, (col & 63) * 2);
-        ldsm_x4(aQ + off, fu[ks]);
-        ldsm_x4(aQ + M::NCOL * 2048u + off, fv[ks]);
-    }
-
-    if (!mbar_wait_bounded(&ws.bar_k, 0, kWaitLimitNs)) {
-        if (tid == 0) raise(error, PK_DEV_TIMEOUT);
-        mbar_wait_bounded(&ws.bar_k, 0, kWaitLimitNs);
-        mbar_wait_bounded(&ws.bar_v, 0, kWaitLimitNs);
-        return;
-    }
-
-    // BD = Qv . P^T over rel-pos tiles; rows < chunk go to shared memory
-    for (int nt = warp; nt < NT_P; nt += NW) {
-        float c[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int kp = 0; kp < M::KSTEPS; kp += 2) {
-            const int col = kp * 16 + (lane / 8) * 8;
-            const int p = nt * 8 + (lane % 8);
-            uint32_t bb[4];
-            ldsm_x4(aP + (col >> 6) * g.pos_colbox_bytes + sw128(p, (col & 63) * 2), bb);
-            mma_bf16(c, fv[kp], bb[0], bb[1]);
-            mma_bf16(c, fv[kp + 1], bb[2], bb[3]);
-        }
-        const int p0 = nt * 8 + 2 * tq;
-        if (gq < chunk) *reinterpret_cast<float2 *>(sBD + gq * RPAD + p0) = make_float2(c[0], c[1]);
-        if (gq + 8 < chunk)
-            *reinterpret_cast<float2 *>(sBD + (gq + 8) * RPAD + p0) = make_float2(c[2], c[3]);
-    }
-
-    // S = Qu . K^T over this warp's key tiles (kept in registers)
-    constexpr int MAXT = M::MAXT;            // key tiles per warp held in registers
-    float sc[MAXT][4];
-#pragma unroll
-    for (int t = 0; t < MAXT; ++t) {
-        const int nt = warp + t * NW;
-        float c[4] = {0.f, 0.f, 0.f, 0.f};
-        if (nt < NT_S) {
-            const int j = nt * 8 + (lane % 8);
-#pragma unroll
-            for (int kp = 0; kp < M::KSTEPS; kp += 2) {
-                const int col = kp * 16 + (lane / 8) * 8;
-                uint32_t bb[4];
-                ldsm_x4(win_addr(aK, aZ, rowoff, rowr, g.box_bytes, j, col), bb);
-                mma_bf16(c, fu[kp], bb[0], bb[1]);
-                mma_bf16(c, fu[kp + 1], bb[2], bb[3]);
-            }
-        }
-#pragma unroll
-        for (int e = 0; e < 4; ++e) sc[t][e] = c[e];
-    }
-    __syncthreads();  // sBD complete
-
-    // scores, mask, row max (rows gq and gq + 8 of the fragment)
-    const float scale = rsqrtf((float)DH);
-    float mx[2] = {-INFINITY, -INFINITY};
-    {
-        uint32_t mrow[2][4];
-#pragma unroll
-        for (int r = 0; r < 2; ++r)
-#pragma unroll
-            for (int k = 0; k < 4; ++k)
-                mrow[r][k] = (gq + 8 * r < chunk) ? sMask[(gq + 8 * r) * 4 + k] : 0u;
-#pragma unroll
-        for (int t = 0; t < MAXT; ++t) {
-            const int nt = warp + t * NW;
-            if (nt >= NT_S) break;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int i = gq + (e >> 1) * 8, j = nt * 8 + 2 * tq + (e & 1);
-                float s;
-                if (j >= W) {
-                    s = -INFINITY;                        // key padding of the last tile
-                } else if (i >= chunk) {
-                    s = 0.f;                              // query padding of the m16 tile
-                } else if ((mrow[e >> 1][j >> 5] >> (j & 31)) & 1u) {
-                    s = sc[t][e] * scale + sBD[i * RPAD + chunk - 1 - i + j] * scale;
-                } else {
-                    s = sc[t][e] * scale - 1e5f;          // masked_fill(-1e5), attention.py:115
-                }
-                sc[t][e] = s;
-                mx[e >> 1] = fmaxf(mx[e >> 1], s);
-            }
-        }
-    }
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-        mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
-        mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
-    }
-    if (NW > 1) {
-        if (tq == 0) {
-            sRed[warp * 16 + gq] = mx[0];
-            sRed[warp * 16 + gq + 8] = mx[1];
-        }
-        __syncthreads();
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            float m = -INFINITY;
-            for (int w2 = 0; w2 < NW; ++w2) m = fmaxf(m, sRed[w2 * 16 + gq + r * 8]);
-            mx[r] = m;
-        }
-    }
-    float sum[2] = {0.f, 0.f};
-    {
-#pragma unroll
-        for (int t = 0; t < MAXT; ++t) {
-            const int nt = warp + t * NW;
-            if (nt >= NT_S) break;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float p = expf(sc[t][e] - mx[e >> 1]);
-                sc[t][e] = p;
-                sum[e >> 1] += p;
-            }
-            const int j0 = nt * 8 + 2 * tq;
-            *reinterpret_cast<__nv_bfloat162 *>(sPr + gq * g.p_stride + j0 * 2) =
-                __floats2bfloat162_rn(sc[t][0], sc[t][1]);
-            *reinterpret_cast<__nv_bfloat162 *>(sPr + (gq + 8) * g.p_stride + j0 * 2) =
-                __floats2bfloat162_rn(sc[t][2], sc[t][3]);
-        }
-    }
-    // zero probability columns between the last key tile and the last P.V step
-    for (int idx = tid; idx < 16 * (16 * KS_P - NT_S * 8); idx += M::THREADS) {
-        const int r = idx / (16 * KS_P - NT_S * 8), j = NT_S * 8 + idx % (16 * KS_P - NT_S * 8);
-        *reinterpret_cast<__nv_bfloat16 *>(sPr + r * g.p_stride + j * 2) = __float2bfloat16_rn(0.f);
-    }
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-        sum[r] += __shfl_xor_sync(0xffffffffu, sum[r], 1);
-        sum[r] += __shfl_xor_sync(0xffffffffu, sum[r], 2);
-    }
-    if (NW > 1) {
-        if (tq == 0) {
-            sRed[NW * 16 + warp * 16 + gq] = sum[0];
-            sRed[NW * 16 + warp * 16 + gq + 8] = sum[1];
-        }
-    }
-    __syncthreads();  // probabilities and partial sums visible
-    if (NW > 1) {
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            float s = 0.f;
-            for (int w2 = 0; w2 < NW; ++w2) s += sRed[NW * 16 + w2 * 16 + gq + r * 8];
-            sum[r] = s;
-        }
-    }
-
-    if (!mbar_wait_bounded(&ws.bar_v, 0, kWaitLimitNs)) {
-        if (tid == 0) raise(error, PK_DEV_TIMEOUT);
-        mbar_wait_bounded(&ws.bar_v, 0, kWaitLimitNs);
-        return;
-    }
-
-    // O = P . V: this warp's pairs of 8-column output tiles
-    const float inv0 = 1.f / sum[0], inv1 = 1.f / sum[1];
-    for (int np = warp; np < DH / 16; np += NW) {
-        float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int ks = 0; ks < KS_P; ++ks) {
-            uint32_t pa[4];
-            ldsm_x4(aPr + (lane % 16) * g.p_stride + (ks * 16 + (lane / 16) * 8) * 2, pa);
-            const int j = ks * 16 + (lane % 8) + ((lane / 8) & 1) * 8;
-            const int col = np * 16 + (lane / 16) * 8;
-            uint32_t vb[4];
-            ldsm_x4_t(win_addr(aV, aZ, rowoff, rowr, g.box_bytes, j, col), vb);
-            mma_bf16(c0, pa, vb[0], vb[1]);
-            mma_bf16(c1, pa, vb[2], vb[3]);
-        }
-        const int d0 = np * 16 + 2 * tq;
-        if (gq < chunk) {
-            T *o = out_base + (int64_t)gq * a.o_rs;
-            *reinterpret_cast<__nv_bfloat162 *>(o + d0) = __floats2bfloat162_rn(c0[0] * inv0, c0[1] * inv0);
-            *reinterpret_cast<__nv_bfloat162 *>(o + d0 + 8) = __floats2bfloat162_rn(c1[0] * inv0, c1[1] * inv0);
-        }
-        if (gq + 8 < chunk) {
-            T *o = out_base + (int64_t)(gq + 8) * a.o_rs;
-            *reinterpret_cast<__nv_bfloat162 *>(o + d0) = __floats2bfloat162_rn(c0[2] * inv1, c0[3] * inv1);
-            *reinterpret_cast<__nv_bfloat162 *>(o + d0 + 8) = __floats2bfloat162_rn(c1[2] * inv1, c1[3] * inv1);
-        }
-    }
-}
-
 // ------------------------------------------------------------------ launch
 template <typename T, int DH>
 bool fill_geom(const pk_paged_kv *kv, AttnGeom &g, size_t &smem, bool mma) {
@@ -680,23 +356,6 @@ int set_smem(K kernel, size_t smem, size_t &limit) {
     return PK_OK;
 }
 
-template <int DH, int NW>
-int launch_bf16(const pk_paged_kv *kv, const CUtensorMap &pos_map, const AttnArgs &a,
-                cudaStream_t s) {
-    AttnGeom g;
-    size_t smem;
-    if (kv->d.chunk > 16 || !fill_geom<__nv_bfloat16, DH>(kv, g, smem, true)) return PK_ENOTSUP;
-    if ((g.W + 7) / 8 > MmaCfg<DH, NW>::MAXT * NW) return PK_ENOTSUP;  // tiles in registers
-    static size_t limit = 48 * 1024;
-    int st = set_smem(paged_attn_bf16_kernel<DH, NW>, smem, limit);
-    if (st != PK_OK) return st;
-    dim3 grid(kv->d.num_heads, a.batch, a.nlayers);
-    paged_attn_bf16_kernel<DH, NW><<<grid, NW * 32, smem, s>>>(kv->kv_map, pos_map, g,
-                                                               kv->d.page_table, kv->d.meta,
-                                                               kv->d.error, a);
-    return cuda_status(cudaGetLastError(), "paged_attn_bf16_kernel");
-}
-
 template <int DH>
 int launch_f32(const pk_paged_kv *kv, const CUtensorMap &pos_map, const AttnArgs &a,
                cudaStream_t s) {
@@ -715,15 +374,15 @@ int launch_f32(const pk_paged_kv *kv, const CUtensorMap &pos_map, const AttnArgs
 
 }  // namespace
 
-int launch_attention(const pk_paged_kv *kv, const CUtensorMap &pos_map, const AttnArgs &a,
-                     cudaStream_t s) {
+int launch_attention(const pk_paged_kv *kv, const CUtensorMap &pos_map, const CUtensorMap &q_map,
+                     const AttnArgs &a, cudaStream_t s) {
     if (a.batch == 0 || a.nlayers == 0) return PK_OK;
-    const bool bf16 = kv->d.dtype == PK_DTYPE_BF16;
+    if (kv->d.dtype == PK_DTYPE_BF16) return launch_attention_bf16(kv, pos_map, q_map, a, s);
     switch (kv->head_dim) {
         case 64:
-            return bf16 ? launch_bf16<64, 4>(kv, pos_map, a, s) : launch_f32<64>(kv, pos_map, a, s);
+            return launch_f32<64>(kv, pos_map, a, s);
         case 128:
-            return bf16 ? launch_bf16<128, 4>(kv, pos_map, a, s) : launch_f32<128>(kv, pos_map, a, s);
+            return launch_f32<128>(kv, pos_map, a, s);
         default:
             return PK_ENOTSUP;
     }

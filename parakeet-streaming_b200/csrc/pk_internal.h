@@ -20,6 +20,8 @@ namespace pk {
 void set_error(const char *fmt, ...);
 int cuda_status(cudaError_t e, const char *what);
 // Encode a tiled TMA descriptor (driver entry point fetched once via cudart).
+int encode_tmap(CUtensorMap *map, int dtype, const void *base, int rank, const uint64_t *dims,
+                const uint64_t *strides_bytes, const uint32_t *box);
 int encode_tmap_3d(CUtensorMap *map, int dtype, const void *base, uint64_t d0, uint64_t d1,
                    uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box0,
                    uint32_t box1, uint32_t box2);
@@ -50,8 +52,11 @@ struct AttnArgs {
     int64_t o_ls, o_bs, o_rs;
     int layer0, nlayers;
 };
-int launch_attention(const pk_paged_kv *kv, const CUtensorMap &pos_map, const AttnArgs &a,
-                     cudaStream_t s);
+int launch_attention(const pk_paged_kv *kv, const CUtensorMap &pos_map, const CUtensorMap &q_map,
+                     const AttnArgs &a, cudaStream_t s);
+// pk_attn_bf16.cu
+int launch_attention_bf16(const pk_paged_kv *kv, const CUtensorMap &pos_map,
+                          const CUtensorMap &q_map, const AttnArgs &a, cudaStream_t s);
 
 // pk_conv.cu
 struct ConvArgs {
