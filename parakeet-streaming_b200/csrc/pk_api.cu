@@ -118,7 +118,8 @@ int pk_paged_kv_create(const pk_paged_kv_desc *desc, pk_paged_kv **out) {
     PK_CHECK(d.num_pages > 0 && d.num_slots > 0 && d.num_layers > 0, "empty pool");
     PK_CHECK(d.num_heads > 0 && d.dim % d.num_heads == 0, "dim %% heads != 0");
     PK_CHECK(d.left >= 0 && d.chunk > 0, "bad left/chunk");
-    PK_CHECK(d.page_size % 8 == 0 && d.page_size <= 256, "page_size must be a multiple of 8, <= 256");
+    PK_CHECK(d.page_size >= 8 && d.page_size <= 256 && (d.page_size & (d.page_size - 1)) == 0,
+             "page_size must be a power of two in [8, 256]");
     PK_CHECK(d.ring >= pk_pages_per_stream(d.left, d.chunk, d.page_size) &&
                  (d.ring & (d.ring - 1)) == 0,
              "ring must be a power of two >= pk_pages_per_stream()");
@@ -232,22 +233,10 @@ int pk_paged_attention(pk_paged_kv *kv, int32_t layer0, int32_t num_layers, cons
     int st = encode_tmap_3d(&pos_map, kv->d.dtype, pos_proj, kv->d.dim, P, num_layers, row,
                             lstride, 128 / es, R, 1);
     if (st != PK_OK) return st;
-    // query rows of one head as 4-D tiles {head columns, chunk rows, stream, layer}
-    CUtensorMap q_map;
-    memset(&q_map, 0, sizeof(q_map));
-    if (kv->d.dtype == PK_DTYPE_BF16) {
+    if (kv->d.dtype == PK_DTYPE_BF16)
         PK_CHECK(aligned16(query) && (q_row_stride * es) % 16 == 0 &&
                      (q_batch_stride * es) % 16 == 0 && (q_layer_stride * es) % 16 == 0,
                  "query must be 16-byte aligned with 16-byte strides");
-        const uint64_t qb = (uint64_t)q_batch_stride * es;
-        const uint64_t ql = num_layers == 1 ? qb * batch : (uint64_t)q_layer_stride * es;
-        const uint64_t qdims[4] = {(uint64_t)kv->d.dim, (uint64_t)kv->d.chunk, (uint64_t)batch,
-                                   (uint64_t)num_layers};
-        const uint64_t qstr[3] = {(uint64_t)q_row_stride * es, qb, ql};
-        const uint32_t qbox[4] = {(uint32_t)(128 / es), (uint32_t)kv->d.chunk, 1, 1};
-        st = encode_tmap(&q_map, kv->d.dtype, query, 4, qdims, qstr, qbox);
-        if (st != PK_OK) return st;
-    }
     AttnArgs a;
     a.q = query;
     a.q_ls = q_layer_stride;
@@ -265,7 +254,7 @@ int pk_paged_attention(pk_paged_kv *kv, int32_t layer0, int32_t num_layers, cons
     a.o_rs = out_row_stride;
     a.layer0 = layer0;
     a.nlayers = num_layers;
-    st = launch_attention(kv, pos_map, q_map, a, static_cast<cudaStream_t>(stream));
+    st = launch_attention(kv, pos_map, a, static_cast<cudaStream_t>(stream));
     if (st == PK_ENOTSUP) pk::set_error("attention configuration not handled (smem or boxes)");
     return st;
 }

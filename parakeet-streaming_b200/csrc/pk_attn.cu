@@ -374,10 +374,10 @@ int launch_f32(const pk_paged_kv *kv, const CUtensorMap &pos_map, const AttnArgs
 
 }  // namespace
 
-int launch_attention(const pk_paged_kv *kv, const CUtensorMap &pos_map, const CUtensorMap &q_map,
-                     const AttnArgs &a, cudaStream_t s) {
+int launch_attention(const pk_paged_kv *kv, const CUtensorMap &pos_map, const AttnArgs &a,
+                     cudaStream_t s) {
     if (a.batch == 0 || a.nlayers == 0) return PK_OK;
-    if (kv->d.dtype == PK_DTYPE_BF16) return launch_attention_bf16(kv, pos_map, q_map, a, s);
+    if (kv->d.dtype == PK_DTYPE_BF16) return launch_attention_bf16(kv, pos_map, a, s);
     switch (kv->head_dim) {
         case 64:
             return launch_f32<64>(kv, pos_map, a, s);

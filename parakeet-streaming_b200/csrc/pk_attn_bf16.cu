@@ -6,18 +6,22 @@
 // mask of parakeet/modules/encoder.py:167-227), organised for throughput:
 //
 // * one CTA per SM slot, looping over work items (layer, stream, head);
-// * a producer warp resolves each item's pages (slot counters -> page ring)
-//   and issues 128B-swizzled TMA tile loads (cp.async.bulk.tensor) of the
-//   K window, the rel-pos rows and the query rows on one mbarrier and of the
-//   V window on a second, into a ring of NS shared-memory stages; it also
-//   builds the item's row table and the streaming mask as bit rows;
+// * a producer warp resolves each item's pages (slot counters -> page ring),
+//   issues 128B-swizzled TMA tile loads (cp.async.bulk.tensor) of the K
+//   window and the rel-pos rows on one mbarrier and of the V window on a
+//   second, into a ring of NS shared-memory stages, and meanwhile builds the
+//   item's bf16 (q + pos_bias_u) and (q + pos_bias_v) tiles, its row table
+//   and its streaming mask as bit rows;
 // * four consumer warps compute BD = (q+v) P^T, S = (q+u) K^T, the masked
 //   softmax and O = P V with mma.sync m16n8k16 (bf16 in, fp32 accumulate;
-//   the query chunk, T <= 16 frames, is one m16 tile), then release the stage
-//   through an "empty" mbarrier;
-// * every wait is bounded (1 s); on a timeout the kernel records
-//   PK_DEV_TIMEOUT in the error word and leaves its loop.
+//   the query chunk, T <= 16 frames, is one m16 tile, and when T <= 8 the
+//   upper half of the tile is skipped), then release the stage through an
+//   "empty" mbarrier;
+// * every wait is bounded (1 s); a wait that gives up records
+//   PK_DEV_TIMEOUT in the error word and the CTA leaves its loop.
 #include <math.h>
+
+#include <algorithm>
 
 #include "pk_common.cuh"
 #include "pk_internal.h"
@@ -31,14 +35,14 @@ constexpr int kMaxBoxes = 16;
 constexpr int kMaxKeys = 128;               // window rows handled (16 * key steps)
 
 struct StageInfo {
-    int ok, w, proc, clen, len, nb, lrel, b, h;
+    int ok, lrel, b, h;
     int rowoff[kMaxKeys];   // byte offset of window row j's box, -1 = zero row
     int rowr[kMaxKeys];     // row inside that box
     uint32_t mask[16][4];   // bit j%32 of [i][j/32]: key j allowed for query i
 };
 
 struct PipeGeom {
-    int num_layers, num_heads, left, chunk, page_size, ring, num_pages, num_slots;
+    int num_layers, num_heads, left, chunk, page_size, ps_shift, ring, num_pages, num_slots;
     int W, R, max_boxes, items, batch;
     uint32_t box_bytes, pos_colbox_bytes;
     uint32_t st_k, st_v, st_pos, st_q, st_info, stage_bytes;  // offsets inside a stage
@@ -76,34 +80,38 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
 __device__ __forceinline__ void consumer_sync() {
     asm volatile("bar.sync 1, %0;" ::"n"(kCW * 32) : "memory");
 }
-__device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, uint64_t *bar,
-                                            int32_t c0, int32_t c1, int32_t c2, int32_t c3) {
-    asm volatile(
-        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
-        "r"(smem_u32(bar))
-        : "memory");
-}
 
-// window row j, column col (multiple of 8) of a K or V region -> smem address
-__device__ __forceinline__ uint32_t win_addr(uint32_t region, uint32_t zero, const StageInfo &in,
-                                             uint32_t box_bytes, int j, int col) {
+// Where window row j lives in a K or V region: its box base and row, or the
+// zero row when j is outside the window.
+struct RowRef {
+    uint32_t base;
+    uint32_t row;
+    bool zero;
+};
+__device__ __forceinline__ RowRef row_ref(uint32_t region, uint32_t zero, const StageInfo &in,
+                                          int j) {
     const int ro = in.rowoff[j];
-    if (ro < 0) return zero + ((col & 63) * 2);
-    return region + ro + (col >> 6) * box_bytes + sw128(in.rowr[j], (col & 63) * 2);
+    RowRef r;
+    r.zero = ro < 0;
+    r.base = r.zero ? zero : region + ro;
+    r.row = r.zero ? 0u : (uint32_t)in.rowr[j];
+    return r;
+}
+// 16-byte chunk `ch` (0..7) of column box `cb` of that row
+__device__ __forceinline__ uint32_t row_addr(const RowRef &r, uint32_t box_bytes, int cb, int ch) {
+    return r.zero ? r.base + ch * 16 : r.base + cb * box_bytes + sw128(r.row, ch * 16);
 }
 
-template <int DH, int NS>
+template <int DH, int NS, bool HI>
 __global__ void __launch_bounds__(kThreads)
     paged_attn_pipe_kernel(const __grid_constant__ CUtensorMap kv_map,
-                           const __grid_constant__ CUtensorMap pos_map,
-                           const __grid_constant__ CUtensorMap q_map, const PipeGeom g,
+                           const __grid_constant__ CUtensorMap pos_map, const PipeGeom g,
                            const int32_t *__restrict__ page_table,
                            const int32_t *__restrict__ meta, int32_t *error, const AttnArgs a) {
     constexpr int NCOL = DH / 64;       // 128-byte column boxes per head
     constexpr int KSTEPS = DH / 16;
     constexpr int MAXT = 4;             // key tiles of 8 per consumer warp (W <= 128)
+    constexpr int NE = HI ? 4 : 2;      // fragment elements per tile that can be live rows
     using T = __nv_bfloat16;
     extern __shared__ char smem_raw[];
     char *smem = reinterpret_cast<char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -112,12 +120,16 @@ __global__ void __launch_bounds__(kThreads)
     __shared__ int s_abort;
 
     const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
-    const int chunk = g.chunk, W = g.W, ps = g.page_size;
+    const int chunk = g.chunk, W = g.W;
     const int KS_P = (W + 15) / 16;
     const int NT_S = (W + 7) / 8;
     const int NT_P = (g.R + 7) / 8;
     const int RPAD = NT_P * 8;
 
+    // query tiles: rows >= chunk stay zero for the whole kernel
+    for (int s = 0; s < NS; ++s)
+        for (int i = tid; i < 2 * NCOL * 2048 / 16; i += kThreads)
+            reinterpret_cast<uint4 *>(smem + s * g.stage_bytes + g.st_q)[i] = make_uint4(0, 0, 0, 0);
     if (tid == 0) {
         for (int s = 0; s < NS; ++s) {
             mbar_init(&full_k[s], 1);
@@ -134,8 +146,8 @@ __global__ void __launch_bounds__(kThreads)
         if (lane == 0) {
             prefetch_tmap(&kv_map);
             prefetch_tmap(&pos_map);
-            prefetch_tmap(&q_map);
         }
+        const int ps = g.page_size, psh = g.ps_shift;
         int it = 0;
         int last_it[NS];
 #pragma unroll
@@ -179,14 +191,14 @@ __global__ void __launch_bounds__(kThreads)
             len = __shfl_sync(0xffffffffu, len, 0);
             ok = __shfl_sync(0xffffffffu, ok, 0);
             const int a_lo = max(w - g.left, 0), a_hi = w + chunk;
-            const int nfirst = a_lo / ps;
-            const int nb = (a_hi - 1) / ps - nfirst + 1;
+            const int nfirst = a_lo >> psh;
+            const int nb = ((a_hi - 1) >> psh) - nfirst + 1;
             if (nb > g.max_boxes) ok = 0;
             int page = 0, start = 0;
             if (ok && lane < nb) {
                 const int n = nfirst + lane;
                 page = page_table[(int64_t)slot * g.ring + (n & (g.ring - 1))];
-                const int lo = max(a_lo - n * ps, 0), hi = min(a_hi - n * ps, ps);
+                const int lo = max(a_lo - (n << psh), 0), hi = min(a_hi - (n << psh), ps);
                 start = lo > 0 ? lo : (hi < ps ? hi - ps : 0);
             }
             const bool bad = ok && lane < nb && (page < 0 || page >= g.num_pages);
@@ -194,39 +206,60 @@ __global__ void __launch_bounds__(kThreads)
                 if (lane == 0) raise(error, PK_DEV_BAD_PAGE);
                 ok = 0;
             }
-            if (lane == 0) {
-                if (ok) {
-                    const uint32_t kvb = nb * NCOL * g.box_bytes;
-                    mbar_expect_tx(&full_k[s], kvb + NCOL * (uint32_t)g.R * 128u +
-                                                   NCOL * (uint32_t)chunk * 128u);
-                    mbar_expect_tx(&full_v[s], kvb);
-                }
+            if (lane == 0 && ok) {
+                const uint32_t kvb = nb * NCOL * g.box_bytes;
+                mbar_expect_tx(&full_k[s], kvb + NCOL * (uint32_t)g.R * 128u);
+                mbar_expect_tx(&full_v[s], kvb);
             }
             __syncwarp();
             if (ok) {
-                // lane i issues the loads of page i; lane 31 the rel-pos and query rows
+                // lane i issues the loads of page i; lane 31 the rel-pos rows
                 if (lane < nb) {
                     const int kplane = ((page * g.num_layers + layer) * 2) * g.num_heads + h;
                     const int vplane = kplane + g.num_heads;
 #pragma unroll
-                    for (int cb = 0; cb < NCOL; ++cb) {
-                        const uint32_t off = (lane * NCOL + cb) * g.box_bytes;
-                        tma_load_3d(st + g.st_k + off, &kv_map, &full_k[s], cb * 64, start, kplane);
-                    }
+                    for (int cb = 0; cb < NCOL; ++cb)
+                        tma_load_3d(st + g.st_k + (lane * NCOL + cb) * g.box_bytes, &kv_map,
+                                    &full_k[s], cb * 64, start, kplane);
 #pragma unroll
-                    for (int cb = 0; cb < NCOL; ++cb) {
-                        const uint32_t off = (lane * NCOL + cb) * g.box_bytes;
-                        tma_load_3d(st + g.st_v + off, &kv_map, &full_v[s], cb * 64, start, vplane);
-                    }
+                    for (int cb = 0; cb < NCOL; ++cb)
+                        tma_load_3d(st + g.st_v + (lane * NCOL + cb) * g.box_bytes, &kv_map,
+                                    &full_v[s], cb * 64, start, vplane);
                 }
                 if (lane == 31) {
 #pragma unroll
-                    for (int cb = 0; cb < NCOL; ++cb) {
+                    for (int cb = 0; cb < NCOL; ++cb)
                         tma_load_3d(st + g.st_pos + cb * g.pos_colbox_bytes, &pos_map, &full_k[s],
                                     h * DH + cb * 64, 0, lrel);
-                        tma_load_4d(st + g.st_q + cb * 2048u, &q_map, &full_k[s], h * DH + cb * 64,
-                                    0, b, lrel);
+                }
+                // Qu = q + pos_bias_u, Qv = q + pos_bias_v in bf16 (the reference's bf16
+                // add, attention.py:108-109): 8 columns per lane per pass
+                const T *qb = static_cast<const T *>(a.q) + (int64_t)lrel * a.q_ls +
+                              (int64_t)b * a.q_bs + h * DH;
+                const T *bu = static_cast<const T *>(a.bias_u) + (int64_t)lrel * a.bias_ls + h * DH;
+                const T *bv = static_cast<const T *>(a.bias_v) + (int64_t)lrel * a.bias_ls + h * DH;
+                for (int idx = lane; idx < chunk * (DH / 8); idx += 32) {
+                    const int t = idx / (DH / 8), c8 = (idx % (DH / 8)) * 8;
+                    const uint4 q4 = *reinterpret_cast<const uint4 *>(qb + (int64_t)t * a.q_rs + c8);
+                    const uint4 u4 = __ldg(reinterpret_cast<const uint4 *>(bu + c8));
+                    const uint4 v4 = __ldg(reinterpret_cast<const uint4 *>(bv + c8));
+                    const __nv_bfloat162 *q2 = reinterpret_cast<const __nv_bfloat162 *>(&q4);
+                    const __nv_bfloat162 *u2 = reinterpret_cast<const __nv_bfloat162 *>(&u4);
+                    const __nv_bfloat162 *v2 = reinterpret_cast<const __nv_bfloat162 *>(&v4);
+                    uint4 ou, ov;
+                    __nv_bfloat162 *pu = reinterpret_cast<__nv_bfloat162 *>(&ou);
+                    __nv_bfloat162 *pv = reinterpret_cast<__nv_bfloat162 *>(&ov);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const float2 fq = __bfloat1622float2(q2[k]);
+                        const float2 fu = __bfloat1622float2(u2[k]);
+                        const float2 fv = __bfloat1622float2(v2[k]);
+                        pu[k] = __floats2bfloat162_rn(fq.x + fu.x, fq.y + fu.y);
+                        pv[k] = __floats2bfloat162_rn(fq.x + fv.x, fq.y + fv.y);
                     }
+                    const uint32_t off = (c8 >> 6) * 2048u + sw128(t, (c8 & 63) * 2);
+                    *reinterpret_cast<uint4 *>(st + g.st_q + off) = ou;
+                    *reinterpret_cast<uint4 *>(st + g.st_q + NCOL * 2048u + off) = ov;
                 }
             }
             // row table: window row j -> (box, row in box); the zero row outside
@@ -235,18 +268,18 @@ __global__ void __launch_bounds__(kThreads)
                 const int j = j0 + lane;
                 const int av = w - g.left + j;
                 const bool live = ok && j < W && av >= 0;
-                const int bi = live ? av / ps - nfirst : 0;
+                const int bi = live ? (av >> psh) - nfirst : 0;
                 const int sbox = __shfl_sync(0xffffffffu, start, bi & 31);
                 if (j < 16 * KS_P) {
                     in.rowoff[j] = live ? bi * NCOL * (int)g.box_bytes : -1;
-                    in.rowr[j] = live ? av % ps - sbox : 0;
+                    in.rowr[j] = live ? (av & (ps - 1)) - sbox : 0;
                 }
             }
             // streaming mask bits (encoder.py:167-227), one key per lane
             {
                 const int key_start = max(proc - clen, 0), off = g.left - clen;
                 const int left_chunks = g.left / chunk;
-                for (int kb = 0; kb < 4; ++kb) {
+                for (int kb = 0; kb < (W + 31) / 32; ++kb) {
                     const int j = kb * 32 + lane;
                     bool key_ok = j < W && j >= off;
                     int kc = 0;
@@ -255,28 +288,28 @@ __global__ void __launch_bounds__(kThreads)
                         key_ok = rr < clen || (rr - clen) < len;
                         kc = (key_start + rr) / chunk;
                     }
+                    int qc = (key_start + clen) / chunk, qrem = (key_start + clen) % chunk;
                     for (int i = 0; i < chunk; ++i) {
-                        const int dc = (key_start + clen + i) / chunk - kc;
+                        const int dc = qc - kc;
                         const unsigned bits = __ballot_sync(
                             0xffffffffu, key_ok && i < len && dc >= 0 && dc <= left_chunks);
                         if (lane == 0) in.mask[i][kb] = bits;
+                        if (++qrem == chunk) {
+                            qrem = 0;
+                            ++qc;
+                        }
                     }
                 }
             }
             if (lane == 0) {
                 in.ok = ok;
-                in.w = w;
-                in.proc = proc;
-                in.clen = clen;
-                in.len = len;
-                in.nb = nb;
                 in.lrel = lrel;
                 in.b = b;
                 in.h = h;
             }
             __syncwarp();
             if (lane == 0) {
-                mbar_arrive(&full_k[s]);  // release: the stage info above is visible
+                mbar_arrive(&full_k[s]);  // release: the tiles and info above are visible
                 mbar_arrive(&full_v[s]);
             }
             last_it[s] = it;
@@ -304,6 +337,7 @@ __global__ void __launch_bounds__(kThreads)
     consumer_sync();
     const uint32_t aZ = smem_u32(sZero), aPr = smem_u32(sPr);
     const float scale = rsqrtf((float)DH);
+    const int pad = 16 * KS_P - NT_S * 8;   // probability columns past the last key tile
 
     // Every consumer warp runs the same sequence of named barriers for every
     // item, whatever happens; a bounded wait that gives up sets s_abort, which
@@ -329,56 +363,36 @@ __global__ void __launch_bounds__(kThreads)
         const uint32_t aK = smem_u32(st + g.st_k), aV = smem_u32(st + g.st_v);
         const uint32_t aP = smem_u32(st + g.st_pos), aQ = smem_u32(st + g.st_q);
 
-        // A fragments of Qu = q + u and Qv = q + v (bf16 rounding as the reference's
-        // bf16 add, attention.py:108-109); rows >= chunk are zero
-        uint32_t fu[KSTEPS][4], fv[KSTEPS][4];
-#pragma unroll
-        for (int ks = 0; ks < KSTEPS; ++ks)
-#pragma unroll
-            for (int r = 0; r < 4; ++r) fu[ks][r] = fv[ks][r] = 0u;
         float sc[MAXT][4];
 #pragma unroll
         for (int t = 0; t < MAXT; ++t)
 #pragma unroll
             for (int e = 0; e < 4; ++e) sc[t][e] = 0.f;
         if (run) {
-            const T *bu = static_cast<const T *>(a.bias_u) + (int64_t)lrel * a.bias_ls + h * DH;
-            const T *bv = static_cast<const T *>(a.bias_v) + (int64_t)lrel * a.bias_ls + h * DH;
+            // A fragments of Qu (tile 0) and Qv (tile 1), rows 0..15
+            uint32_t fu[KSTEPS][4], fv[KSTEPS][4];
 #pragma unroll
             for (int ks = 0; ks < KSTEPS; ++ks) {
-#pragma unroll
-                for (int r = 0; r < 4; ++r) {
-                    const int row = gq + (r & 1) * 8;
-                    const int col = ks * 16 + (r >> 1) * 8 + 2 * tq;
-                    if (row < chunk) {
-                        const uint32_t qa = aQ + (col >> 6) * 2048u + sw128(row, (col & 63) * 2);
-                        uint32_t raw;
-                        asm volatile("ld.shared.b32 %0, [%1];" : "=r"(raw) : "r"(qa));
-                        const float2 q = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162 *>(&raw));
-                        const float2 u = __bfloat1622float2(__ldg(reinterpret_cast<const __nv_bfloat162 *>(bu + col)));
-                        const float2 v = __bfloat1622float2(__ldg(reinterpret_cast<const __nv_bfloat162 *>(bv + col)));
-                        __nv_bfloat162 pu = __floats2bfloat162_rn(q.x + u.x, q.y + u.y);
-                        __nv_bfloat162 pv = __floats2bfloat162_rn(q.x + v.x, q.y + v.y);
-                        fu[ks][r] = *reinterpret_cast<uint32_t *>(&pu);
-                        fv[ks][r] = *reinterpret_cast<uint32_t *>(&pv);
-                    }
-                }
+                const int col = ks * 16 + (lane / 16) * 8;
+                const uint32_t off = (col >> 6) * 2048u + sw128(lane % 16, (col & 63) * 2);
+                ldsm_x4(aQ + off, fu[ks]);
+                ldsm_x4(aQ + NCOL * 2048u + off, fv[ks]);
             }
             // BD = Qv . P^T (rel-pos tiles split over the consumer warps) -> sBD rows < chunk
             for (int nt = warp; nt < NT_P; nt += kCW) {
                 float c[4] = {0.f, 0.f, 0.f, 0.f};
+                const uint32_t prow = nt * 8 + (lane % 8);
 #pragma unroll
                 for (int kp = 0; kp < KSTEPS; kp += 2) {
                     const int col = kp * 16 + (lane / 8) * 8;
-                    const int p = nt * 8 + (lane % 8);
                     uint32_t bb[4];
-                    ldsm_x4(aP + (col >> 6) * g.pos_colbox_bytes + sw128(p, (col & 63) * 2), bb);
+                    ldsm_x4(aP + (col >> 6) * g.pos_colbox_bytes + sw128(prow, (col & 63) * 2), bb);
                     mma_bf16(c, fv[kp], bb[0], bb[1]);
                     mma_bf16(c, fv[kp + 1], bb[2], bb[3]);
                 }
                 const int p0 = nt * 8 + 2 * tq;
                 if (gq < chunk) *reinterpret_cast<float2 *>(sBD + gq * RPAD + p0) = make_float2(c[0], c[1]);
-                if (gq + 8 < chunk)
+                if (HI && gq + 8 < chunk)
                     *reinterpret_cast<float2 *>(sBD + (gq + 8) * RPAD + p0) = make_float2(c[2], c[3]);
             }
             // S = Qu . K^T (key tiles split over the consumer warps), in registers
@@ -386,12 +400,12 @@ __global__ void __launch_bounds__(kThreads)
             for (int t = 0; t < MAXT; ++t) {
                 const int nt = warp + t * kCW;
                 if (nt < NT_S) {
-                    const int j = nt * 8 + (lane % 8);
+                    const RowRef rk = row_ref(aK, aZ, in, nt * 8 + (lane % 8));
 #pragma unroll
                     for (int kp = 0; kp < KSTEPS; kp += 2) {
                         const int col = kp * 16 + (lane / 8) * 8;
                         uint32_t bb[4];
-                        ldsm_x4(win_addr(aK, aZ, in, g.box_bytes, j, col), bb);
+                        ldsm_x4(row_addr(rk, g.box_bytes, col >> 6, (col & 63) >> 3), bb);
                         mma_bf16(sc[t], fu[kp], bb[0], bb[1]);
                         mma_bf16(sc[t], fu[kp + 1], bb[2], bb[3]);
                     }
@@ -415,7 +429,7 @@ __global__ void __launch_bounds__(kThreads)
                 const int nt = warp + t * kCW;
                 if (nt >= NT_S) break;
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
+                for (int e = 0; e < NE; ++e) {
                     const int i = gq + (e >> 1) * 8, j = nt * 8 + 2 * tq + (e & 1);
                     float sv;
                     if (j >= W) {
@@ -433,17 +447,17 @@ __global__ void __launch_bounds__(kThreads)
             }
         }
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
+        for (int r = 0; r < (HI ? 2 : 1); ++r) {
             mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
             mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
         }
         if (tq == 0) {
             sRed[warp * 16 + gq] = mx[0];
-            sRed[warp * 16 + gq + 8] = mx[1];
+            if (HI) sRed[warp * 16 + gq + 8] = mx[1];
         }
         consumer_sync();  // barrier 2 of 3
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
+        for (int r = 0; r < (HI ? 2 : 1); ++r) {
             float m = -INFINITY;
 #pragma unroll
             for (int w2 = 0; w2 < kCW; ++w2) m = fmaxf(m, sRed[w2 * 16 + gq + r * 8]);
@@ -455,37 +469,35 @@ __global__ void __launch_bounds__(kThreads)
             for (int t = 0; t < MAXT; ++t) {
                 const int nt = warp + t * kCW;
                 if (nt >= NT_S) break;
+                float p[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float p = __expf(sc[t][e] - mx[e >> 1]);
-                    sc[t][e] = p;
-                    sum[e >> 1] += p;
+                for (int e = 0; e < NE; ++e) {
+                    p[e] = __expf(sc[t][e] - mx[e >> 1]);
+                    sum[e >> 1] += p[e];
                 }
                 const int j0 = nt * 8 + 2 * tq;
                 *reinterpret_cast<__nv_bfloat162 *>(sPr + gq * g.p_stride + j0 * 2) =
-                    __floats2bfloat162_rn(sc[t][0], sc[t][1]);
+                    __floats2bfloat162_rn(p[0], p[1]);
                 *reinterpret_cast<__nv_bfloat162 *>(sPr + (gq + 8) * g.p_stride + j0 * 2) =
-                    __floats2bfloat162_rn(sc[t][2], sc[t][3]);
+                    __floats2bfloat162_rn(p[2], p[3]);
             }
-            // zero the probability columns past the last key tile
-            const int pad = 16 * KS_P - NT_S * 8;
             for (int idx = tid; idx < 16 * pad; idx += kCW * 32) {
                 const int r = idx / pad, j = NT_S * 8 + idx % pad;
                 *reinterpret_cast<__nv_bfloat16 *>(sPr + r * g.p_stride + j * 2) = __float2bfloat16_rn(0.f);
             }
         }
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
+        for (int r = 0; r < (HI ? 2 : 1); ++r) {
             sum[r] += __shfl_xor_sync(0xffffffffu, sum[r], 1);
             sum[r] += __shfl_xor_sync(0xffffffffu, sum[r], 2);
         }
         if (tq == 0) {
             sRed[kCW * 16 + warp * 16 + gq] = sum[0];
-            sRed[kCW * 16 + warp * 16 + gq + 8] = sum[1];
+            if (HI) sRed[kCW * 16 + warp * 16 + gq + 8] = sum[1];
         }
         consumer_sync();  // probabilities and partial sums visible (barrier 3 of 3)
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
+        for (int r = 0; r < (HI ? 2 : 1); ++r) {
             float t2 = 0.f;
 #pragma unroll
             for (int w2 = 0; w2 < kCW; ++w2) t2 += sRed[kCW * 16 + w2 * 16 + gq + r * 8];
@@ -499,16 +511,16 @@ __global__ void __launch_bounds__(kThreads)
         }
         // O = P . V over this warp's pairs of 8-column output tiles
         if (run && got_v) {
-            const float inv0 = 1.f / sum[0], inv1 = 1.f / sum[1];
+            const float inv0 = 1.f / sum[0], inv1 = HI ? 1.f / sum[1] : 0.f;
             for (int np = warp; np < DH / 16; np += kCW) {
                 float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
+                const int col = np * 16 + (lane / 16) * 8;
                 for (int ks = 0; ks < KS_P; ++ks) {
                     uint32_t pa[4];
                     ldsm_x4(aPr + (lane % 16) * g.p_stride + (ks * 16 + (lane / 16) * 8) * 2, pa);
-                    const int j = ks * 16 + (lane % 8) + ((lane / 8) & 1) * 8;
-                    const int col = np * 16 + (lane / 16) * 8;
+                    const RowRef rv = row_ref(aV, aZ, in, ks * 16 + (lane % 8) + ((lane / 8) & 1) * 8);
                     uint32_t vb[4];
-                    ldsm_x4_t(win_addr(aV, aZ, in, g.box_bytes, j, col), vb);
+                    ldsm_x4_t(row_addr(rv, g.box_bytes, col >> 6, (col & 63) >> 3), vb);
                     mma_bf16(c0, pa, vb[0], vb[1]);
                     mma_bf16(c1, pa, vb[2], vb[3]);
                 }
@@ -518,7 +530,7 @@ __global__ void __launch_bounds__(kThreads)
                     *reinterpret_cast<__nv_bfloat162 *>(o + d0) = __floats2bfloat162_rn(c0[0] * inv0, c0[1] * inv0);
                     *reinterpret_cast<__nv_bfloat162 *>(o + d0 + 8) = __floats2bfloat162_rn(c1[0] * inv0, c1[1] * inv0);
                 }
-                if (gq + 8 < chunk) {
+                if (HI && gq + 8 < chunk) {
                     T *o = out_base + (int64_t)(gq + 8) * a.o_rs;
                     *reinterpret_cast<__nv_bfloat162 *>(o + d0) = __floats2bfloat162_rn(c0[2] * inv1, c0[3] * inv1);
                     *reinterpret_cast<__nv_bfloat162 *>(o + d0 + 8) = __floats2bfloat162_rn(c1[2] * inv1, c1[3] * inv1);
@@ -539,6 +551,9 @@ bool fill_pipe_geom(const pk_paged_kv *kv, const AttnArgs &a, int head_dim, int 
     g.left = d.left;
     g.chunk = d.chunk;
     g.page_size = d.page_size;
+    g.ps_shift = 0;
+    while ((1 << g.ps_shift) < d.page_size) ++g.ps_shift;
+    if ((1 << g.ps_shift) != d.page_size) return false;
     g.ring = d.ring;
     g.num_pages = d.num_pages;
     g.num_slots = d.num_slots;
@@ -547,7 +562,7 @@ bool fill_pipe_geom(const pk_paged_kv *kv, const AttnArgs &a, int head_dim, int 
     g.max_boxes = pk_pages_per_stream(d.left, d.chunk, d.page_size);
     g.batch = a.batch;
     g.items = a.nlayers * a.batch * d.num_heads;
-    if (g.max_boxes > kMaxBoxes || g.max_boxes > 32 || d.chunk > 16) return false;
+    if (g.max_boxes > kMaxBoxes || g.max_boxes > 31 || d.chunk > 16) return false;
     const int ks_p = (g.W + 15) / 16;
     if (16 * ks_p > kMaxKeys) return false;
     g.box_bytes = d.page_size * 128u;
@@ -557,7 +572,7 @@ bool fill_pipe_geom(const pk_paged_kv *kv, const AttnArgs &a, int head_dim, int 
     g.st_v = g.max_boxes * ncol * g.box_bytes;
     g.st_pos = 2 * g.st_v;
     g.st_q = g.st_pos + ncol * g.pos_colbox_bytes;
-    g.st_info = g.st_q + ncol * 2048u;
+    g.st_info = g.st_q + 2 * ncol * 2048u;
     g.stage_bytes = (g.st_info + (uint32_t)sizeof(StageInfo) + 1023u) & ~1023u;
     g.p_stride = ks_p * 32 + 16;
     g.off_p = ns * g.stage_bytes;
@@ -568,17 +583,18 @@ bool fill_pipe_geom(const pk_paged_kv *kv, const AttnArgs &a, int head_dim, int 
     return smem <= 227 * 1024;
 }
 
-template <int DH, int NS>
-int launch_pipe(const pk_paged_kv *kv, const CUtensorMap &pos_map, const CUtensorMap &q_map,
-                const AttnArgs &a, cudaStream_t s) {
+template <int DH, int NS, bool HI>
+int launch_pipe(const pk_paged_kv *kv, const CUtensorMap &pos_map, const AttnArgs &a,
+                cudaStream_t s) {
     PipeGeom g;
     size_t smem;
     if (!fill_pipe_geom(kv, a, DH, NS, g, smem)) return PK_ENOTSUP;
+    auto kernel = paged_attn_pipe_kernel<DH, NS, HI>;
     static size_t limit = 48 * 1024;
     static int sms = 0;
     if (smem > limit) {
-        cudaError_t e = cudaFuncSetAttribute(paged_attn_pipe_kernel<DH, NS>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem);
         if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(paged_attn_pipe)");
         limit = smem;
     }
@@ -589,26 +605,27 @@ int launch_pipe(const pk_paged_kv *kv, const CUtensorMap &pos_map, const CUtenso
         if (e != cudaSuccess) return cuda_status(e, "cudaDeviceGetAttribute");
     }
     int per_sm = 0;
-    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-        &per_sm, paged_attn_pipe_kernel<DH, NS>, kThreads, smem);
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, smem);
     if (e != cudaSuccess) return cuda_status(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
     if (per_sm < 1) return PK_ENOTSUP;
     const int grid = (int)std::min<long long>((long long)g.items, (long long)sms * per_sm);
-    paged_attn_pipe_kernel<DH, NS><<<grid, kThreads, smem, s>>>(kv->kv_map, pos_map, q_map, g,
-                                                               kv->d.page_table, kv->d.meta,
-                                                               kv->d.error, a);
+    kernel<<<grid, kThreads, smem, s>>>(kv->kv_map, pos_map, g, kv->d.page_table, kv->d.meta,
+                                        kv->d.error, a);
     return cuda_status(cudaGetLastError(), "paged_attn_pipe_kernel");
 }
 
 }  // namespace
 
-int launch_attention_bf16(const pk_paged_kv *kv, const CUtensorMap &pos_map,
-                          const CUtensorMap &q_map, const AttnArgs &a, cudaStream_t s) {
+int launch_attention_bf16(const pk_paged_kv *kv, const CUtensorMap &pos_map, const AttnArgs &a,
+                          cudaStream_t s) {
+    const bool hi = kv->d.chunk > 8;
     switch (kv->head_dim) {
         case 64:
-            return launch_pipe<64, 2>(kv, pos_map, q_map, a, s);
+            return hi ? launch_pipe<64, 2, true>(kv, pos_map, a, s)
+                      : launch_pipe<64, 2, false>(kv, pos_map, a, s);
         case 128:
-            return launch_pipe<128, 2>(kv, pos_map, q_map, a, s);
+            return hi ? launch_pipe<128, 2, true>(kv, pos_map, a, s)
+                      : launch_pipe<128, 2, false>(kv, pos_map, a, s);
         default:
             return PK_ENOTSUP;
     }

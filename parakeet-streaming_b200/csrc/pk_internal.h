@@ -52,11 +52,11 @@ struct AttnArgs {
     int64_t o_ls, o_bs, o_rs;
     int layer0, nlayers;
 };
-int launch_attention(const pk_paged_kv *kv, const CUtensorMap &pos_map, const CUtensorMap &q_map,
-                     const AttnArgs &a, cudaStream_t s);
+int launch_attention(const pk_paged_kv *kv, const CUtensorMap &pos_map, const AttnArgs &a,
+                     cudaStream_t s);
 // pk_attn_bf16.cu
-int launch_attention_bf16(const pk_paged_kv *kv, const CUtensorMap &pos_map,
-                          const CUtensorMap &q_map, const AttnArgs &a, cudaStream_t s);
+int launch_attention_bf16(const pk_paged_kv *kv, const CUtensorMap &pos_map, const AttnArgs &a,
+                          cudaStream_t s);
 
 // pk_conv.cu
 struct ConvArgs {
