@@ -242,7 +242,7 @@ def main():
     step_bytes = (nb["append"] + nb["attention"]) * units
 
     def step(buf, ev=None):
-        pool.begin_step(slots)
+        pool.begin_step(slots, lengths)
         pool.append(0, buf[..., D:2 * D], buf[..., 2 * D:], slots)
         if ev is not None:
             ev[0].record()
@@ -347,7 +347,7 @@ def main():
                               for l in range(L)], nb["conv"] * units, L),
         }
         hbm, _ = peaks()
-        pool.begin_step(slots)   # pages for this step's window; every op below re-runs it
+        pool.begin_step(slots, lengths)   # this step's pages and windows; every op re-runs it
         for name, (fn, nbytes, launches) in ops.items():
             t = timeit(fn)
             breakdown[name] = {"ms": round(t, 4), "GB/s": round(nbytes / t / 1e6, 1),

@@ -51,6 +51,25 @@ extern "C" {
 #define PK_META_CACHE_LEN 4  /* StreamingState.cache_lengths (<= left)     */
 #define PK_META_STRIDE 8
 
+/* per-batch-row window descriptor of the current step, int32
+ * [num_slots][PK_WIN_STRIDE], written by pk_pages_begin_step: the pages
+ * that hold the stream's window, the first row of each page's box, and the
+ * streaming mask as bit rows (bit j%32 of word [i*4 + j/32]: key j allowed
+ * for query i) */
+#define PK_WIN_OK 0
+#define PK_WIN_W 1
+#define PK_WIN_PROC 2
+#define PK_WIN_CLEN 3
+#define PK_WIN_LEN 4
+#define PK_WIN_NB 5
+#define PK_WIN_NFIRST 6
+#define PK_WIN_SLOT 7
+#define PK_WIN_PAGE 8
+#define PK_WIN_START 24
+#define PK_WIN_MASK 40
+#define PK_WIN_MAX_PAGES 16
+#define PK_WIN_STRIDE 128
+
 /*
  * Paged K/V window of every stream slot.  Replaces ModelCache.attn_k /
  * attn_v (parakeet/modules/cache.py:24-29) and the slot pool's state
@@ -63,6 +82,7 @@ typedef struct pk_paged_kv_desc {
     int64_t *ring_ctr;    /* [2] monotonic head (pop) and tail (push)        */
     int32_t *meta;        /* [num_slots][PK_META_STRIDE]                     */
     int32_t *error;       /* [1] device error word (PK_DEV_* bits)           */
+    int32_t *window;      /* [num_slots][PK_WIN_STRIDE] step window descriptors */
     int32_t num_pages;
     int32_t num_slots;
     int32_t num_layers;
@@ -96,11 +116,13 @@ int pk_pages_reset(pk_paged_kv *kv, const int32_t *init_order, void *stream);
  *  0. return every page of the `released` slots (finished streams,
  *     parakeet/engine/scheduler.py:101-104) and zero their counters;
  *  1. per batch row, in order: free pages wholly left of the window;
- *  2. per batch row, in order: allocate pages for rows [w, w + chunk).
+ *  2. per batch row, in order: allocate pages for rows [w, w + chunk);
+ *  3. write each batch row's window descriptor (`lengths` NULL = full
+ *     chunks), read by the attention kernels of every layer of the step.
  * Replaces the pool half of Scheduler.pack_states (scheduler.py:128-170):
  * nothing is gathered, the kernels read the pages in place. */
-int pk_pages_begin_step(pk_paged_kv *kv, const int32_t *slots, int32_t batch,
-                        const int32_t *released, int32_t num_released,
+int pk_pages_begin_step(pk_paged_kv *kv, const int32_t *slots, const int32_t *lengths,
+                        int32_t batch, const int32_t *released, int32_t num_released,
                         void *stream);
 
 /* End of the step: written += chunk, processed += length,
@@ -135,9 +157,10 @@ int pk_gather_window(pk_paged_kv *kv, int32_t layer, const int32_t *slots,
  *                        linear_pos(pos_emb) of that layer (attention.py:102-106)
  *   bias_u/v (l, h, d)   at l*bias_layer_stride + h*head_dim + d (pos_bias_u/v)
  *   out    (l, b, t, c)  at l*out_layer_stride + b*out_batch_stride + t*out_row_stride + c
- * The streaming mask is derived in-kernel from each slot's counters and
- * `lengths` (parakeet/modules/encoder.py:167-227).  Output is the heads
- * concatenated, before linear_out.
+ * The streaming mask (parakeet/modules/encoder.py:167-227) comes from the
+ * step's window descriptors, so pk_pages_begin_step must have run for the
+ * same `slots` and `lengths`.  Output is the heads concatenated, before
+ * linear_out.
  * Replaces ConformerAttention.forward lines 99-122
  * (parakeet/modules/attention.py), i.e. rel_shift + bias + SDPA. */
 int pk_paged_attention(pk_paged_kv *kv, int32_t layer0, int32_t num_layers,

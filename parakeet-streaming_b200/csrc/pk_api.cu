@@ -112,7 +112,7 @@ int32_t pk_ring_size(int32_t left, int32_t chunk, int32_t page_size) {
 int pk_paged_kv_create(const pk_paged_kv_desc *desc, pk_paged_kv **out) {
     PK_CHECK(desc && out, "null argument");
     const pk_paged_kv_desc &d = *desc;
-    PK_CHECK(d.kv && d.page_table && d.free_ring && d.ring_ctr && d.meta && d.error,
+    PK_CHECK(d.kv && d.page_table && d.free_ring && d.ring_ctr && d.meta && d.error && d.window,
              "null device buffer in descriptor");
     PK_CHECK(d.dtype == PK_DTYPE_F32 || d.dtype == PK_DTYPE_BF16, "bad dtype %d", d.dtype);
     PK_CHECK(d.num_pages > 0 && d.num_slots > 0 && d.num_layers > 0, "empty pool");
@@ -127,7 +127,10 @@ int pk_paged_kv_create(const pk_paged_kv_desc *desc, pk_paged_kv **out) {
     const int esize = d.dtype == PK_DTYPE_BF16 ? 2 : 4;
     PK_CHECK(((d.dim / d.num_heads) * esize) % 128 == 0,
              "head_dim * element size must be a multiple of 128 bytes");
-    PK_CHECK(d.left + 2 * d.chunk - 1 <= 256, "left + 2*chunk - 1 must be <= 256");
+    PK_CHECK(d.chunk <= 16 && d.left + d.chunk <= 128,
+             "chunk must be <= 16 frames and left + chunk <= 128");
+    PK_CHECK(pk_pages_per_stream(d.left, d.chunk, d.page_size) <= PK_WIN_MAX_PAGES,
+             "window spans more than PK_WIN_MAX_PAGES pages");
     pk_paged_kv *kv = static_cast<pk_paged_kv *>(calloc(1, sizeof(pk_paged_kv)));
     if (!kv) return PK_EINVAL;
     kv->d = d;
@@ -156,14 +159,18 @@ int pk_pages_reset(pk_paged_kv *kv, const int32_t *init_order, void *stream) {
     return launch_pages_reset(kv, init_order, static_cast<cudaStream_t>(stream));
 }
 
-int pk_pages_begin_step(pk_paged_kv *kv, const int32_t *slots, int32_t batch,
-                        const int32_t *released, int32_t num_released, void *stream) {
+int pk_pages_begin_step(pk_paged_kv *kv, const int32_t *slots, const int32_t *lengths,
+                        int32_t batch, const int32_t *released, int32_t num_released,
+                        void *stream) {
     PK_CHECK(kv, "null pool");
     PK_CHECK(batch >= 0 && num_released >= 0, "negative count");
+    PK_CHECK(batch <= kv->d.num_slots, "batch larger than the pool's slots");
     PK_CHECK(batch == 0 || slots, "null slots");
     PK_CHECK(num_released == 0 || released, "null released");
-    return launch_pages_begin(kv, slots, batch, released, num_released,
-                              static_cast<cudaStream_t>(stream));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    int st = launch_pages_begin(kv, slots, batch, released, num_released, s);
+    if (st != PK_OK) return st;
+    return launch_window_desc(kv, slots, lengths, batch, s);
 }
 
 int pk_pages_end_step(pk_paged_kv *kv, const int32_t *slots, const int32_t *lengths,

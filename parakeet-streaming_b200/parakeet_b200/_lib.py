@@ -19,6 +19,7 @@ PK_DTYPE_F32, PK_DTYPE_BF16 = 0, 1
 PK_DEV_POOL_EXHAUSTED, PK_DEV_BAD_PAGE, PK_DEV_TIMEOUT, PK_DEV_BAD_SLOT = 1, 2, 4, 8
 META_FIRST, META_NEXT, META_WRITTEN, META_PROCESSED, META_CACHE_LEN = 0, 1, 2, 3, 4
 META_STRIDE = 8
+WIN_STRIDE = 128
 
 
 class PKError(RuntimeError):
@@ -33,6 +34,7 @@ class PagedKVDesc(ctypes.Structure):
         ("ring_ctr", ctypes.c_void_p),
         ("meta", ctypes.c_void_p),
         ("error", ctypes.c_void_p),
+        ("window", ctypes.c_void_p),
         ("num_pages", ctypes.c_int32),
         ("num_slots", ctypes.c_int32),
         ("num_layers", ctypes.c_int32),
@@ -56,7 +58,7 @@ SIGNATURES = {
     "pk_pages_per_stream": [_I32, _I32, _I32],
     "pk_ring_size": [_I32, _I32, _I32],
     "pk_pages_reset": [_P, _P, _P],
-    "pk_pages_begin_step": [_P, _P, _I32, _P, _I32, _P],
+    "pk_pages_begin_step": [_P, _P, _P, _I32, _P, _I32, _P],
     "pk_pages_end_step": [_P, _P, _P, _I32, _P],
     "pk_append_kv": [_P, _I32, _I32, _P, _P, _I64, _I64, _I64, _P, _I32, _P],
     "pk_gather_window": [_P, _I32, _P, _I32, _P, _P, _P],

@@ -105,7 +105,7 @@ class ConformerEncoder(nn.Module):
         if length is None:
             length = torch.full((B,), T, dtype=torch.int32, device=pool.device)
         cache.lengths = torch.as_tensor(length).to(device=pool.device, dtype=torch.int32)
-        pool.begin_step(cache.slots)
+        pool.begin_step(cache.slots, cache.lengths)
         x, pos_emb = self.pos_enc(x, cache_len=self.att_context_size[0])
         for layer in self.layers:
             x = layer(x, pos_emb=pos_emb, pad_mask=None, attn_mask=None, cache=cache)

@@ -43,6 +43,7 @@ class PagedKVPool:
     ring_ctr    [2]                               int64 head / tail
     meta        [num_slots, 8]                    int32 counters (PK_META_*)
     error       [1]                               int32 PK_DEV_* bits
+    window      [num_slots, 128]                  int32 this step's window descriptors
     conv        [num_slots, L, D, kernel - 1]     model dtype (ModelCache.conv layout)
     """
 
@@ -75,11 +76,13 @@ class PagedKVPool:
         self.ring_ctr = torch.zeros(2, dtype=torch.int64, device=dev)
         self.meta = torch.zeros((num_slots, _lib.META_STRIDE), dtype=torch.int32, device=dev)
         self.error = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.window = torch.zeros((num_slots, _lib.WIN_STRIDE), dtype=torch.int32, device=dev)
         self.conv = torch.zeros((num_slots, num_layers, dim, conv_kernel - 1), dtype=dtype, device=dev)
         d = _lib.PagedKVDesc(
             kv=self.kv.data_ptr(), page_table=self.page_table.data_ptr(),
             free_ring=self.free_ring.data_ptr(), ring_ctr=self.ring_ctr.data_ptr(),
-            meta=self.meta.data_ptr(), error=self.error.data_ptr(), num_pages=self.num_pages,
+            meta=self.meta.data_ptr(), error=self.error.data_ptr(),
+            window=self.window.data_ptr(), num_pages=self.num_pages,
             num_slots=num_slots, num_layers=num_layers, dim=dim, num_heads=num_heads,
             left=self.left, chunk=self.chunk, page_size=page_size, ring=self.ring,
             dtype=DTYPES[dtype])
@@ -118,18 +121,21 @@ class PagedKVPool:
         with self._lock:
             self.pending_release.append(int(slot))
 
-    def begin_step(self, slots: torch.Tensor, released: torch.Tensor | None = None):
+    def begin_step(self, slots: torch.Tensor, lengths: torch.Tensor | None = None,
+                   released: torch.Tensor | None = None):
         """Page releases, frees and allocations for one step of ``slots``
-        (int32 [B], distinct).  ``released`` defaults to the queued releases."""
+        (int32 [B], distinct), then the step's window descriptors for chunks
+        of ``lengths`` (int32 [B]; None = full chunks).  ``released`` defaults
+        to the queued releases."""
         if released is None:
             with self._lock:
                 rel, self.pending_release = self.pending_release, []
             if rel:
                 released = torch.tensor(rel, dtype=torch.int32).to(self.device)
         n_rel = 0 if released is None else int(released.numel())
-        check(lib().pk_pages_begin_step(self._h, slots.data_ptr(), int(slots.numel()),
-                                        _ptr(released) if n_rel else None, n_rel,
-                                        _stream(self.device)), "pk_pages_begin_step")
+        check(lib().pk_pages_begin_step(self._h, slots.data_ptr(), _ptr(lengths),
+                                        int(slots.numel()), _ptr(released) if n_rel else None,
+                                        n_rel, _stream(self.device)), "pk_pages_begin_step")
 
     def end_step(self, slots: torch.Tensor, lengths: torch.Tensor):
         check(lib().pk_pages_end_step(self._h, slots.data_ptr(), lengths.data_ptr(),

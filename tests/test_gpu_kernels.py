@@ -69,7 +69,7 @@ def test_page_allocator_matches_cpu_model(att, cap):
         sl = torch.tensor(batch, dtype=torch.int32, device=DEV)
         ln = torch.tensor(lengths, dtype=torch.int32, device=DEV)
         assert model.begin_step(batch)
-        pool.begin_step(sl)
+        pool.begin_step(sl, ln)
         model.end_step(batch, lengths)
         pool.end_step(sl, ln)
         if step % 8 == 0 or step > 150:
@@ -115,7 +115,7 @@ def run_stream_steps(shape, dtype, steps, n_slots, seed, check_every=1, short_la
             lengths[-1] = max(1, T // 2)
         sl = torch.tensor(batch, dtype=torch.int32, device=DEV)
         ln = torch.tensor(lengths, dtype=torch.int32, device=DEV)
-        pool.begin_step(sl)
+        pool.begin_step(sl, ln)
         st, idx = dense.pack_states(batch)
         _, mask = streaming.streaming_masks(T, st.cache_lengths, st.processed_frames, lengths, att)
         for l in range(L):

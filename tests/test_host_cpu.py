@@ -39,7 +39,7 @@ def test_create_rejects_bad_descriptors_without_a_gpu():
     assert lib.pk_paged_kv_create(ctypes.byref(d), ctypes.byref(h)) == _lib.PK_EINVAL
     assert b"null" in lib.pk_last_error()
     fake = 1 << 20  # never dereferenced: validation fails first
-    for k in ("kv", "page_table", "free_ring", "ring_ctr", "meta", "error"):
+    for k in ("kv", "page_table", "free_ring", "ring_ctr", "meta", "error", "window"):
         setattr(d, k, fake)
     d.ring = 4   # smaller than pages_per_stream(70, 2, 16) = 6
     assert lib.pk_paged_kv_create(ctypes.byref(d), ctypes.byref(h)) == _lib.PK_EINVAL
@@ -47,7 +47,7 @@ def test_create_rejects_bad_descriptors_without_a_gpu():
     assert lib.pk_paged_kv_create(ctypes.byref(d), ctypes.byref(h)) == _lib.PK_EINVAL
     assert lib.pk_conv_step(None, 1, 1, 0, 512, 9, 2, 5, None, 0, 0, None, None, None, 1e-5,
                             None, None, 1, None, None, None) == _lib.PK_EINVAL
-    assert lib.pk_pages_begin_step(None, None, 1, None, 0, None) == _lib.PK_EINVAL
+    assert lib.pk_pages_begin_step(None, None, None, 1, None, 0, None) == _lib.PK_EINVAL
 
 
 def test_slot_allocator_matches_reference_sequence():
