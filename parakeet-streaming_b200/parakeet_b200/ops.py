@@ -43,7 +43,7 @@ class PagedKVPool:
     ring_ctr    [2]                               int64 head / tail
     meta        [num_slots, 8]                    int32 counters (PK_META_*)
     error       [1]                               int32 PK_DEV_* bits
-    window      [num_slots, 128]                  int32 this step's window descriptors
+    win_desc    [num_slots, 128]                  int32 this step's window descriptors
     conv        [num_slots, L, D, kernel - 1]     model dtype (ModelCache.conv layout)
     """
 
@@ -76,13 +76,13 @@ class PagedKVPool:
         self.ring_ctr = torch.zeros(2, dtype=torch.int64, device=dev)
         self.meta = torch.zeros((num_slots, _lib.META_STRIDE), dtype=torch.int32, device=dev)
         self.error = torch.zeros(1, dtype=torch.int32, device=dev)
-        self.window = torch.zeros((num_slots, _lib.WIN_STRIDE), dtype=torch.int32, device=dev)
+        self.win_desc = torch.zeros((num_slots, _lib.WIN_STRIDE), dtype=torch.int32, device=dev)
         self.conv = torch.zeros((num_slots, num_layers, dim, conv_kernel - 1), dtype=dtype, device=dev)
         d = _lib.PagedKVDesc(
             kv=self.kv.data_ptr(), page_table=self.page_table.data_ptr(),
             free_ring=self.free_ring.data_ptr(), ring_ctr=self.ring_ctr.data_ptr(),
             meta=self.meta.data_ptr(), error=self.error.data_ptr(),
-            window=self.window.data_ptr(), num_pages=self.num_pages,
+            window=self.win_desc.data_ptr(), num_pages=self.num_pages,
             num_slots=num_slots, num_layers=num_layers, dim=dim, num_heads=num_heads,
             left=self.left, chunk=self.chunk, page_size=page_size, ring=self.ring,
             dtype=DTYPES[dtype])
