@@ -25,8 +25,6 @@
 namespace pk {
 namespace {
 
-constexpr int kWarps = 4;
-constexpr int kThreads = kWarps * 32;
 
 struct Geom {
     int num_layers, num_heads, left, chunk, page_size, ps_shift, W, R, max_boxes;
@@ -80,14 +78,18 @@ __device__ __forceinline__ uint32_t row_addr(const RowRef &r, uint32_t box_bytes
     return r.zero ? r.base + ch * 16 : r.base + cb * box_bytes + sw128(r.row, ch * 16);
 }
 
-template <int DH, bool HI>
-__global__ void __launch_bounds__(kThreads)
+template <int DH, bool HI, int NW>
+__global__ void __launch_bounds__(NW * 32)
     paged_attn_bf16_kernel(const __grid_constant__ CUtensorMap kv_map,
                            const __grid_constant__ CUtensorMap pos_map, const Geom g,
                            const int32_t *__restrict__ window, int32_t *error, const AttnArgs a) {
     constexpr int NCOL = DH / 64;       // 128-byte column boxes per head
     constexpr int KSTEPS = DH / 16;
-    constexpr int MAXT = 4;             // key tiles of 8 per warp (W <= 128)
+    constexpr int kThreads = NW * 32;
+    constexpr int kWarps = NW;
+    constexpr int MAXT = (16 + NW - 1) / NW;   // key tiles of 8 per warp (W <= 128)
+    constexpr int MAXP = (18 + NW - 1) / NW;   // rel-pos tiles of 8 per warp (R <= 143)
+    constexpr int MAXKS = 8;                   // key steps of 16 for P.V (W <= 128)
     constexpr int NE = HI ? 4 : 2;      // fragment elements per tile that can be live rows
     using T = __nv_bfloat16;
     extern __shared__ char smem_raw[];
@@ -222,36 +224,56 @@ __global__ void __launch_bounds__(kThreads)
     }
 
     // BD = Qv . P^T over the rel-pos tiles of this warp -> sBD rows < chunk
-    for (int nt = warp; nt < NT_P; nt += kWarps) {
-        float c[4] = {0.f, 0.f, 0.f, 0.f};
-        const uint32_t prow = nt * 8 + (lane % 8);
+    {
+        float c[MAXP][4];
+#pragma unroll
+        for (int t = 0; t < MAXP; ++t)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) c[t][e] = 0.f;
 #pragma unroll
         for (int kp = 0; kp < KSTEPS; kp += 2) {
             const int col = kp * 16 + (lane / 8) * 8;
-            uint32_t bb[4];
-            ldsm_x4(aP + (col >> 6) * g.pos_colbox_bytes + sw128(prow, (col & 63) * 2), bb);
-            mma_bf16(c, fv[kp], bb[0], bb[1]);
-            mma_bf16(c, fv[kp + 1], bb[2], bb[3]);
+#pragma unroll
+            for (int t = 0; t < MAXP; ++t) {
+                const int nt = warp + t * kWarps;
+                if (nt < NT_P) {
+                    uint32_t bb[4];
+                    ldsm_x4(aP + (col >> 6) * g.pos_colbox_bytes +
+                                sw128(nt * 8 + (lane % 8), (col & 63) * 2), bb);
+                    mma_bf16(c[t], fv[kp], bb[0], bb[1]);
+                    mma_bf16(c[t], fv[kp + 1], bb[2], bb[3]);
+                }
+            }
         }
-        const int p0 = nt * 8 + 2 * tq;
-        if (gq < chunk) *reinterpret_cast<float2 *>(sBD + gq * RPAD + p0) = make_float2(c[0], c[1]);
-        if (HI && gq + 8 < chunk)
-            *reinterpret_cast<float2 *>(sBD + (gq + 8) * RPAD + p0) = make_float2(c[2], c[3]);
+#pragma unroll
+        for (int t = 0; t < MAXP; ++t) {
+            const int nt = warp + t * kWarps;
+            if (nt < NT_P) {
+                const int p0 = nt * 8 + 2 * tq;
+                if (gq < chunk)
+                    *reinterpret_cast<float2 *>(sBD + gq * RPAD + p0) = make_float2(c[t][0], c[t][1]);
+                if (HI && gq + 8 < chunk)
+                    *reinterpret_cast<float2 *>(sBD + (gq + 8) * RPAD + p0) = make_float2(c[t][2], c[t][3]);
+            }
+        }
     }
     // S = Qu . K^T over the key tiles of this warp, in registers
     float sc[MAXT][4];
+    RowRef rk[MAXT];
 #pragma unroll
     for (int t = 0; t < MAXT; ++t) {
-        const int nt = warp + t * kWarps;
 #pragma unroll
         for (int e = 0; e < 4; ++e) sc[t][e] = 0.f;
-        if (nt < NT_S) {
-            const RowRef rk = row_ref(aK, aZ, g, w, nfirst, s_start, NCOL, nt * 8 + (lane % 8));
+        rk[t] = row_ref(aK, aZ, g, w, nfirst, s_start, NCOL, (warp + t * kWarps) * 8 + (lane % 8));
+    }
 #pragma unroll
-            for (int kp = 0; kp < KSTEPS; kp += 2) {
-                const int col = kp * 16 + (lane / 8) * 8;
+    for (int kp = 0; kp < KSTEPS; kp += 2) {
+        const int col = kp * 16 + (lane / 8) * 8;
+#pragma unroll
+        for (int t = 0; t < MAXT; ++t) {
+            if (warp + t * kWarps < NT_S) {
                 uint32_t bb[4];
-                ldsm_x4(row_addr(rk, g.box_bytes, col >> 6, (col & 63) >> 3), bb);
+                ldsm_x4(row_addr(rk[t], g.box_bytes, col >> 6, (col & 63) >> 3), bb);
                 mma_bf16(sc[t], fu[kp], bb[0], bb[1]);
                 mma_bf16(sc[t], fu[kp + 1], bb[2], bb[3]);
             }
@@ -355,32 +377,46 @@ __global__ void __launch_bounds__(kThreads)
     const float inv0 = 1.f / sum[0], inv1 = HI ? 1.f / sum[1] : 0.f;
     for (int np = warp; np < DH / 16; np += kWarps) {
         float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
+        float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
         const int col = np * 16 + (lane / 16) * 8;
-        for (int ks = 0; ks < KS_P; ++ks) {
-            uint32_t pa[4];
-            ldsm_x4(aPr + (lane % 16) * g.p_stride + (ks * 16 + (lane / 16) * 8) * 2, pa);
-            const RowRef rv = row_ref(aV, aZ, g, w, nfirst, s_start, NCOL,
-                                      ks * 16 + (lane % 8) + ((lane / 8) & 1) * 8);
-            uint32_t vb[4];
-            ldsm_x4_t(row_addr(rv, g.box_bytes, col >> 6, (col & 63) >> 3), vb);
-            mma_bf16(c0, pa, vb[0], vb[1]);
-            mma_bf16(c1, pa, vb[2], vb[3]);
+#pragma unroll
+        for (int ks = 0; ks < MAXKS; ++ks) {
+            if (ks < KS_P) {
+                uint32_t pa[4];
+                ldsm_x4(aPr + (lane % 16) * g.p_stride + (ks * 16 + (lane / 16) * 8) * 2, pa);
+                const RowRef rv = row_ref(aV, aZ, g, w, nfirst, s_start, NCOL,
+                                          ks * 16 + (lane % 8) + ((lane / 8) & 1) * 8);
+                uint32_t vb[4];
+                ldsm_x4_t(row_addr(rv, g.box_bytes, col >> 6, (col & 63) >> 3), vb);
+                if (ks & 1) {
+                    mma_bf16(d0, pa, vb[0], vb[1]);
+                    mma_bf16(d1, pa, vb[2], vb[3]);
+                } else {
+                    mma_bf16(c0, pa, vb[0], vb[1]);
+                    mma_bf16(c1, pa, vb[2], vb[3]);
+                }
+            }
         }
-        const int d0 = np * 16 + 2 * tq;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            c0[e] += d0[e];
+            c1[e] += d1[e];
+        }
+        const int oc = np * 16 + 2 * tq;
         if (gq < chunk) {
             T *o = out_base + (int64_t)gq * a.o_rs;
-            *reinterpret_cast<__nv_bfloat162 *>(o + d0) = __floats2bfloat162_rn(c0[0] * inv0, c0[1] * inv0);
-            *reinterpret_cast<__nv_bfloat162 *>(o + d0 + 8) = __floats2bfloat162_rn(c1[0] * inv0, c1[1] * inv0);
+            *reinterpret_cast<__nv_bfloat162 *>(o + oc) = __floats2bfloat162_rn(c0[0] * inv0, c0[1] * inv0);
+            *reinterpret_cast<__nv_bfloat162 *>(o + oc + 8) = __floats2bfloat162_rn(c1[0] * inv0, c1[1] * inv0);
         }
         if (HI && gq + 8 < chunk) {
             T *o = out_base + (int64_t)(gq + 8) * a.o_rs;
-            *reinterpret_cast<__nv_bfloat162 *>(o + d0) = __floats2bfloat162_rn(c0[2] * inv1, c0[3] * inv1);
-            *reinterpret_cast<__nv_bfloat162 *>(o + d0 + 8) = __floats2bfloat162_rn(c1[2] * inv1, c1[3] * inv1);
+            *reinterpret_cast<__nv_bfloat162 *>(o + oc) = __floats2bfloat162_rn(c0[2] * inv1, c0[3] * inv1);
+            *reinterpret_cast<__nv_bfloat162 *>(o + oc + 8) = __floats2bfloat162_rn(c1[2] * inv1, c1[3] * inv1);
         }
     }
 }
 
-bool fill_geom(const pk_paged_kv *kv, int head_dim, Geom &g, size_t &smem) {
+bool fill_geom(const pk_paged_kv *kv, int head_dim, int nw, Geom &g, size_t &smem) {
     const pk_paged_kv_desc &d = kv->d;
     const int ncol = head_dim / 64;
     g.num_layers = d.num_layers;
@@ -406,7 +442,7 @@ bool fill_geom(const pk_paged_kv *kv, int head_dim, Geom &g, size_t &smem) {
     g.p_stride = ks_p * 32 + 16;
     g.off_bd = g.off_p + 16 * g.p_stride;
     g.off_red = g.off_bd + ((d.chunk * rpad * 4 + 15) & ~15);
-    g.off_zero = g.off_red + 2 * kWarps * 16 * 4;
+    g.off_zero = g.off_red + 2 * nw * 16 * 4;
     smem = g.off_zero + 128 + 1024;
     return smem <= 227 * 1024;
 }
@@ -414,10 +450,11 @@ bool fill_geom(const pk_paged_kv *kv, int head_dim, Geom &g, size_t &smem) {
 template <int DH, bool HI>
 int launch_typed(const pk_paged_kv *kv, const CUtensorMap &pos_map, const AttnArgs &a,
                  cudaStream_t s) {
+    constexpr int NW = DH == 128 ? 8 : 4;   // warps per CTA
     Geom g;
     size_t smem;
-    if (!fill_geom(kv, DH, g, smem)) return PK_ENOTSUP;
-    auto kernel = paged_attn_bf16_kernel<DH, HI>;
+    if (!fill_geom(kv, DH, NW, g, smem)) return PK_ENOTSUP;
+    auto kernel = paged_attn_bf16_kernel<DH, HI, NW>;
     static size_t limit = 48 * 1024;
     if (smem > limit) {
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -426,7 +463,7 @@ int launch_typed(const pk_paged_kv *kv, const CUtensorMap &pos_map, const AttnAr
         limit = smem;
     }
     dim3 grid(kv->d.num_heads, a.batch, a.nlayers);
-    kernel<<<grid, kThreads, smem, s>>>(kv->kv_map, pos_map, g, kv->d.window, kv->d.error, a);
+    kernel<<<grid, NW * 32, smem, s>>>(kv->kv_map, pos_map, g, kv->d.window, kv->d.error, a);
     return cuda_status(cudaGetLastError(), "paged_attn_bf16_kernel");
 }
 
