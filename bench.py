@@ -243,10 +243,11 @@ def main():
 
     def step(buf, ev=None):
         pool.begin_step(slots, lengths)
-        pool.append(0, buf[..., D:2 * D], buf[..., 2 * D:], slots)
         if ev is not None:
             ev[0].record()
-        pool.attention(0, buf[..., :D], pos, bu, bv, slots, lengths, out)
+        # append of the chunk's K/V rows fused into the attention call
+        pool.attention(0, buf[..., :D], pos, bu, bv, slots, lengths, out,
+                       key=buf[..., D:2 * D], value=buf[..., 2 * D:])
         if ev is not None:
             ev[1].record()
         pool.end_step(slots, lengths)
@@ -341,6 +342,10 @@ def main():
                        nb["append"] * units, 1),
             "attention": (lambda: pool.attention(0, qkv[0][..., :D], pos, bu, bv, slots, lengths, out),
                           nb["attention"] * units, 1),
+            "attention+append": (lambda: pool.attention(0, qkv[0][..., :D], pos, bu, bv, slots,
+                                                        lengths, out, key=qkv[0][..., D:2 * D],
+                                                        value=qkv[0][..., 2 * D:]),
+                                 (nb["attention"] + nb["append"]) * units, 1),
             "gather": (lambda: [pool.gather(l, slots, *kv_out) for l in range(L)],
                        nb["gather"] * units, L),
             "conv": (lambda: [pool.conv_step(l, x2, wconv, slots, lengths, lnw, lnb, 1e-5, yconv)
@@ -352,7 +357,7 @@ def main():
             t = timeit(fn)
             breakdown[name] = {"ms": round(t, 4), "GB/s": round(nbytes / t / 1e6, 1),
                                "frac": round(nbytes / t / 1e6 / hbm, 3), "launches": launches,
-                               "bytes_per_stream_layer": nb[name]}
+                               "bytes_per_stream_layer": nbytes // units}
 
     if world > 1:
         t = torch.tensor([ms, e2e_ms, attn_ms], device=dev)
@@ -361,7 +366,9 @@ def main():
 
     if rank == 0:
         hbm, kind = peaks()
-        attn_bytes = nb["attention"] * units
+        kernel_name = ("paged_attn_stacked_kernel" if H * T <= 16 and dh == 64
+                       else "paged_attn_bf16_kernel (+append_kernel)")
+        attn_bytes = step_bytes    # the fused kernel moves the append's bytes too
         achieved = attn_bytes / (attn_ms * 1e-3) / 1e9
         traffic = None
         tp = os.path.join(REPO, "profiles", "attention_traffic.json")
@@ -388,7 +395,7 @@ def main():
                        "l2": f"inputs > L2: {pool.kv.numel() * 2 / 1e6:.0f} MB page pool, "
                              f"{step_bytes / 1e6:.0f} MB read+written per step",
                        "parallelism": f"{world} independent replicas (stream sharding)"},
-            "roofline": {"bound": "hbm", "kernel": "paged_attn_kernel",
+            "roofline": {"bound": "hbm", "kernel": kernel_name,
                          "achieved": round(achieved, 1), "peak": hbm, "peak_kind": kind,
                          "unit": "GB/s", "frac": round(achieved / hbm, 3), "traffic": traffic,
                          "alg_bytes_per_launch": attn_bytes, "avg_launch_ms": round(attn_ms, 4)},
@@ -396,7 +403,7 @@ def main():
             "e2e": {"value": round(e2e, 1), "unit": "GB/s",
                     "h2d_bytes_per_step": qkv[0].numel() * 2, "d2h_bytes_per_step": out.numel() * 2,
                     "ms_per_step": round(e2e_ms, 4)},
-            "gpu_launches": 4 * K,
+            "gpu_launches": 4 * K,   # allocator, window descriptors, attention+append, counters
             "clocks": clk,
             "device_error_word": err,
             "ops": breakdown,

@@ -151,8 +151,13 @@ int pk_gather_window(pk_paged_kv *kv, int32_t layer, const int32_t *slots,
                      int32_t batch, void *k_out, void *v_out, void *stream);
 
 /* Chunked rel-pos multi-head self-attention over the paged window, for
- * layers [layer0, layer0 + num_layers), after pk_append_kv of the step.
+ * layers [layer0, layer0 + num_layers).
  *   query  (l, b, t, c)  at l*q_layer_stride + b*q_batch_stride + t*q_row_stride + c
+ *   key/value            NULL, or this step's new K/V rows with the query's
+ *                        strides (e.g. the K and V thirds of the fused qkv GEMM
+ *                        output): they are appended to the pages as part of
+ *                        the call, so pk_append_kv is not needed.  With NULL,
+ *                        pk_append_kv must have run for this step.
  *   pos_proj (l, p, c)   at l*pos_layer_stride + p*dim + c, p < 2*(left+chunk)-1:
  *                        linear_pos(pos_emb) of that layer (attention.py:102-106)
  *   bias_u/v (l, h, d)   at l*bias_layer_stride + h*head_dim + d (pos_bias_u/v)
@@ -161,11 +166,13 @@ int pk_gather_window(pk_paged_kv *kv, int32_t layer, const int32_t *slots,
  * step's window descriptors, so pk_pages_begin_step must have run for the
  * same `slots` and `lengths`.  Output is the heads concatenated, before
  * linear_out.
- * Replaces ConformerAttention.forward lines 99-122
+ * Replaces ModelCache.update_attn_cache (cache.py:36-45, when key/value are
+ * given) and ConformerAttention.forward lines 99-122
  * (parakeet/modules/attention.py), i.e. rel_shift + bias + SDPA. */
 int pk_paged_attention(pk_paged_kv *kv, int32_t layer0, int32_t num_layers,
                        const void *query, int64_t q_layer_stride,
                        int64_t q_batch_stride, int64_t q_row_stride,
+                       const void *key, const void *value,
                        const void *pos_proj, int64_t pos_layer_stride,
                        const void *bias_u, const void *bias_v,
                        int64_t bias_layer_stride, const int32_t *slots,

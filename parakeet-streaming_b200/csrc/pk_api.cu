@@ -213,42 +213,42 @@ int pk_gather_window(pk_paged_kv *kv, int32_t layer, const int32_t *slots, int32
 
 int pk_paged_attention(pk_paged_kv *kv, int32_t layer0, int32_t num_layers, const void *query,
                        int64_t q_layer_stride, int64_t q_batch_stride, int64_t q_row_stride,
-                       const void *pos_proj, int64_t pos_layer_stride, const void *bias_u,
-                       const void *bias_v, int64_t bias_layer_stride, const int32_t *slots,
-                       const int32_t *lengths, int32_t batch, void *out,
-                       int64_t out_layer_stride, int64_t out_batch_stride,
-                       int64_t out_row_stride, void *stream) {
+                       const void *key, const void *value, const void *pos_proj,
+                       int64_t pos_layer_stride, const void *bias_u, const void *bias_v,
+                       int64_t bias_layer_stride, const int32_t *slots, const int32_t *lengths,
+                       int32_t batch, void *out, int64_t out_layer_stride,
+                       int64_t out_batch_stride, int64_t out_row_stride, void *stream) {
     PK_CHECK(kv, "null pool");
     PK_CHECK(batch >= 0 && num_layers >= 0 && layer0 >= 0 &&
                  layer0 + num_layers <= kv->d.num_layers,
              "layer range outside the pool");
     if (batch == 0 || num_layers == 0) return PK_OK;
     PK_CHECK(query && pos_proj && bias_u && bias_v && slots && lengths && out, "null pointer");
+    PK_CHECK((key == nullptr) == (value == nullptr), "key and value go together");
     PK_CHECK(aligned16(pos_proj), "pos_proj not 16-byte aligned");
     PK_CHECK(kv->head_dim == 64 || kv->head_dim == 128, "head_dim %d not handled", kv->head_dim);
     PK_CHECK(out_row_stride % 2 == 0 && out_batch_stride % 2 == 0 && out_layer_stride % 2 == 0 &&
                  (reinterpret_cast<uintptr_t>(out) % (2 * kv->esize)) == 0,
              "out must allow 2-element stores");
     const int es = kv->esize;
+    PK_CHECK(aligned16(query) && (q_row_stride * es) % 16 == 0 &&
+                 (q_batch_stride * es) % 16 == 0 && (q_layer_stride * es) % 16 == 0,
+             "query must be 16-byte aligned with 16-byte strides");
+    PK_CHECK(!key || (aligned16(key) && aligned16(value)), "key/value not 16-byte aligned");
     const int P = 2 * (kv->d.left + kv->d.chunk) - 1;
     const int R = kv->d.left + 2 * kv->d.chunk - 1;
     const uint64_t row = (uint64_t)kv->d.dim * es;
     uint64_t lstride = (uint64_t)pos_layer_stride * es;
     if (num_layers == 1) lstride = row * P;
     PK_CHECK(lstride % 16 == 0 && lstride >= row * P, "bad pos_layer_stride");
-    CUtensorMap pos_map;
-    int st = encode_tmap_3d(&pos_map, kv->d.dtype, pos_proj, kv->d.dim, P, num_layers, row,
-                            lstride, 128 / es, R, 1);
-    if (st != PK_OK) return st;
-    if (kv->d.dtype == PK_DTYPE_BF16)
-        PK_CHECK(aligned16(query) && (q_row_stride * es) % 16 == 0 &&
-                     (q_batch_stride * es) % 16 == 0 && (q_layer_stride * es) % 16 == 0,
-                 "query must be 16-byte aligned with 16-byte strides");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
     AttnArgs a;
     a.q = query;
     a.q_ls = q_layer_stride;
     a.q_bs = q_batch_stride;
     a.q_rs = q_row_stride;
+    a.k_new = key;
+    a.v_new = value;
     a.bias_u = bias_u;
     a.bias_v = bias_v;
     a.bias_ls = bias_layer_stride;
@@ -261,7 +261,27 @@ int pk_paged_attention(pk_paged_kv *kv, int32_t layer0, int32_t num_layers, cons
     a.o_rs = out_row_stride;
     a.layer0 = layer0;
     a.nlayers = num_layers;
-    st = launch_attention(kv, pos_map, a, static_cast<cudaStream_t>(stream));
+    int st;
+    if (kv->d.dtype == PK_DTYPE_BF16) {
+        // all heads of a (stream, layer) per CTA when they fill one m16 tile
+        CUtensorMap pos16;
+        st = encode_tmap_3d(&pos16, kv->d.dtype, pos_proj, kv->d.dim, P, num_layers, row, lstride,
+                            128 / es, 16, 1);
+        if (st != PK_OK) return st;
+        st = launch_attention_stacked(kv, pos16, a, s);
+        if (st != PK_ENOTSUP) return st;
+    }
+    if (key) {   // the other kernels read the new rows from the pages: append first
+        st = launch_append(kv, layer0, num_layers, key, value, q_layer_stride, q_batch_stride,
+                           q_row_stride, slots, batch, s);
+        if (st != PK_OK) return st;
+        a.k_new = a.v_new = nullptr;
+    }
+    CUtensorMap pos_map;
+    st = encode_tmap_3d(&pos_map, kv->d.dtype, pos_proj, kv->d.dim, P, num_layers, row, lstride,
+                        128 / es, R, 1);
+    if (st != PK_OK) return st;
+    st = launch_attention(kv, pos_map, a, s);
     if (st == PK_ENOTSUP) pk::set_error("attention configuration not handled (smem or boxes)");
     return st;
 }

@@ -1,0 +1,402 @@
+// Paged chunked rel-pos attention, bf16, for chunks where heads x chunk <= 16
+// (the small streaming model: 8 heads x 2 frames): one CTA per (stream,
+// layer) with every head in it.
+//
+// Same computation as pk_attn.cu / pk_attn_bf16.cu (ConformerAttention.
+// forward lines 99-122, parakeet/modules/attention.py; streaming mask of
+// parakeet/modules/encoder.py:167-227).  With only T = 2 query rows per
+// head, a per-head CTA spends most of its instructions on setup and on the
+// 14 padding rows of every m16 tile.  Here:
+//
+// * a producer warp streams 16 KB blocks through an NS-stage ring with
+//   128B-swizzled TMA tile loads (cp.async.bulk.tensor, one box per head):
+//   the rel-pos rows in blocks of 16, then the stream's K pages, then its V
+//   pages - each page box shifted so that rows outside the window are
+//   zero-filled without being read;
+// * consumer warp h owns head h: BD = (q+v) P^T and S = (q+u) K^T on tensor
+//   cores (mma.sync m16n8k16, bf16 in, fp32 accumulate), written to shared
+//   memory in the stacked [head * T + query] row order;
+// * one dense softmax over all heads' rows (16 threads per row) with the
+//   reference's -1e5 masked fill, probabilities kept as bf16 per page box;
+// * O_h = P V_h on tensor cores, normalised by the row sums;
+// * optionally the step's new K/V rows are appended here as well: each
+//   warp writes its head's rows to the page in global memory and over the
+//   freshly loaded box in shared memory, so no separate append launch and
+//   no second read of the new rows are needed;
+// * every mbarrier wait is bounded (1 s) and records PK_DEV_TIMEOUT.
+#include <math.h>
+
+#include "pk_common.cuh"
+#include "pk_internal.h"
+
+namespace pk {
+namespace {
+
+constexpr int kH = 8;                    // heads = consumer warps
+constexpr int kThreads = (kH + 1) * 32;  // + producer warp
+constexpr int kBox = 2048;               // one head's 16 rows x 128 bytes
+constexpr int kMaxBoxes = 8;             // pages per window handled
+constexpr int kMaxPosBlocks = 8;         // rel-pos blocks of 16 rows (R <= 128)
+constexpr int kPStride = 48;             // bytes per row of a 16x16 bf16 probability tile
+
+struct SGeom {
+    int num_layers, left, chunk, W, R, npb, max_boxes;
+    uint32_t off_s, off_bd, off_p, stage_bytes;
+    int bd_stride;  // floats per stacked row of sBD
+};
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void mma_bf16(float (&c)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, "
+        "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void consumer_sync() {
+    asm volatile("bar.sync 1, %0;" ::"n"(kH * 32) : "memory");
+}
+
+template <int NS>
+__global__ void __launch_bounds__(kThreads, 2)
+    paged_attn_stacked_kernel(const __grid_constant__ CUtensorMap kv_map,
+                              const __grid_constant__ CUtensorMap pos_map, const SGeom g,
+                              const pk_paged_kv_desc d, const AttnArgs a) {
+    using T = __nv_bfloat16;
+    extern __shared__ char smem_raw[];
+    char *smem = reinterpret_cast<char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                          ~uintptr_t(1023));
+    __shared__ uint64_t full[NS], empty[NS];
+    __shared__ int s_ok, s_w, s_nfirst, s_nb;
+    __shared__ volatile int s_abort;
+    __shared__ int s_page[kMaxBoxes], s_start[kMaxBoxes];
+    __shared__ uint32_t s_mask[16 * 4];
+    __shared__ float s_rowsum[16];
+
+    const int b = blockIdx.x, lrel = blockIdx.y;
+    const int layer = a.layer0 + lrel;
+    const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+    const int chunk = g.chunk, W = g.W, npb = g.npb;
+    float *sS = reinterpret_cast<float *>(smem + g.off_s);    // [box][16 rows][16]
+    float *sBD = reinterpret_cast<float *>(smem + g.off_bd);  // [16 rows][bd_stride]
+    char *sP = smem + g.off_p;                                // [box][16 rows][kPStride B]
+
+    if (warp == kH) {
+        // window descriptor of this stream (written by pk_pages_begin_step)
+        const int32_t *wd = d.window + (int64_t)b * PK_WIN_STRIDE;
+        if (lane < kMaxBoxes) {
+            s_page[lane] = wd[PK_WIN_PAGE + lane];
+            s_start[lane] = wd[PK_WIN_START + lane];
+        }
+        s_mask[lane] = (uint32_t)wd[PK_WIN_MASK + lane];
+        s_mask[32 + lane] = (uint32_t)wd[PK_WIN_MASK + 32 + lane];
+        if (lane == 0) {
+            const int nb = wd[PK_WIN_NB];
+            s_ok = wd[PK_WIN_OK] && nb <= g.max_boxes && nb <= kMaxBoxes;
+            s_w = wd[PK_WIN_W];
+            s_nfirst = wd[PK_WIN_NFIRST];
+            s_nb = nb;
+            s_abort = 0;
+            for (int s = 0; s < NS; ++s) {
+                mbar_init(&full[s], 1);
+                mbar_init(&empty[s], kH);
+            }
+            fence_mbar_init();
+        }
+    }
+    __syncthreads();
+    const int nb = s_nb, w = s_w, nfirst = s_nfirst;
+    const int nblocks = npb + 2 * nb;
+    T *out_base = static_cast<T *>(a.out) + (int64_t)lrel * a.o_ls + (int64_t)b * a.o_bs;
+    if (!s_ok) {
+        for (int idx = tid; idx < chunk * kH * 64; idx += kThreads)
+            out_base[(int64_t)(idx / (kH * 64)) * a.o_rs + idx % (kH * 64)] = __float2bfloat16_rn(0.f);
+        return;
+    }
+
+    if (warp == kH) {
+        // ================= producer: rel-pos blocks, K pages, V pages =================
+        int last_n[NS];
+#pragma unroll
+        for (int s = 0; s < NS; ++s) last_n[s] = -1;
+        for (int n = 0; n < nblocks; ++n) {
+            const int s = n % NS, u = n / NS;
+            int got = 1;
+            if (u >= 1 && lane == 0) got = mbar_wait_bounded(&empty[s], (u - 1) & 1, kWaitLimitNs);
+            got = __shfl_sync(0xffffffffu, got, 0);
+            if (!got) {
+                if (lane == 0) {
+                    raise(d.error, PK_DEV_TIMEOUT);
+                    s_abort = 1;
+                }
+                break;
+            }
+            if (lane == 0) mbar_arrive_expect_tx(&full[s], kH * kBox);
+            __syncwarp();
+            if (lane < kH) {
+                char *dst = smem + s * g.stage_bytes + lane * kBox;
+                if (n < npb) {
+                    tma_load_3d(dst, &pos_map, &full[s], lane * 64, n * 16, lrel);
+                } else {
+                    const int i = (n - npb) % nb, kvi = (n - npb) / nb;
+                    const int plane = ((s_page[i] * d.num_layers + layer) * 2 + kvi) * kH + lane;
+                    tma_load_3d(dst, &kv_map, &full[s], 0, s_start[i], plane);
+                }
+            }
+            last_n[s] = n;
+        }
+        if (lane == 0) {   // leave none of our loads in flight
+#pragma unroll
+            for (int s = 0; s < NS; ++s)
+                if (last_n[s] >= 0) mbar_wait_bounded(&full[s], (last_n[s] / NS) & 1, kWaitLimitNs);
+        }
+        return;
+    }
+
+    // ============================ consumer warp h = head h ============================
+    const int h = warp;
+    const int gq = lane / 4, tq = lane % 4;
+    const float scale = 0.125f;  // 1 / sqrt(64)
+    const int bds = g.bd_stride;
+
+    // A fragments: rows 0..chunk-1 of the m16 tile are this head's queries
+    uint32_t fu[4][4], fv[4][4];
+    {
+        const T *qb = static_cast<const T *>(a.q) + (int64_t)lrel * a.q_ls + (int64_t)b * a.q_bs + h * 64;
+        const T *bu = static_cast<const T *>(a.bias_u) + (int64_t)lrel * a.bias_ls + h * 64;
+        const T *bv = static_cast<const T *>(a.bias_v) + (int64_t)lrel * a.bias_ls + h * 64;
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                const int row = gq + (r & 1) * 8, col = ks * 16 + (r >> 1) * 8 + 2 * tq;
+                uint32_t pu = 0u, pv = 0u;
+                if (row < chunk) {
+                    const float2 q = __bfloat1622float2(
+                        *reinterpret_cast<const __nv_bfloat162 *>(qb + (int64_t)row * a.q_rs + col));
+                    const float2 u = __bfloat1622float2(__ldg(reinterpret_cast<const __nv_bfloat162 *>(bu + col)));
+                    const float2 v = __bfloat1622float2(__ldg(reinterpret_cast<const __nv_bfloat162 *>(bv + col)));
+                    __nv_bfloat162 xu = __floats2bfloat162_rn(q.x + u.x, q.y + u.y);
+                    __nv_bfloat162 xv = __floats2bfloat162_rn(q.x + v.x, q.y + v.y);
+                    pu = *reinterpret_cast<uint32_t *>(&xu);
+                    pv = *reinterpret_cast<uint32_t *>(&xv);
+                }
+                fu[ks][r] = pu;
+                fv[ks][r] = pv;
+            }
+    }
+
+    // overwrite (and store to its page) this step's rows of box i, K or V, head h
+    auto append_rows = [&](const T *src, int kvi, int i, char *box) {
+        for (int idx = lane; idx < chunk * 8; idx += 32) {
+            const int t = idx / 8, c = idx % 8;
+            const int av = w + t;
+            if ((av >> 4) - nfirst != i) continue;
+            const int pr = av & 15, r = pr - s_start[i];
+            const uint4 val = *reinterpret_cast<const uint4 *>(
+                src + (int64_t)lrel * a.q_ls + (int64_t)b * a.q_bs + (int64_t)t * a.q_rs + h * 64 + c * 8);
+            *reinterpret_cast<uint4 *>(box + sw128(r, c * 16)) = val;
+            T *pool = static_cast<T *>(d.kv);
+            const int64_t plane = ((int64_t)(s_page[i] * d.num_layers + layer) * 2 + kvi) * kH + h;
+            *reinterpret_cast<uint4 *>(pool + (plane * 16 + pr) * 64 + c * 8) = val;
+        }
+        __syncwarp();
+    };
+
+    // ---- pass 1: rel-pos blocks -> BD rows, K pages -> S rows
+    for (int n = 0; n < npb + nb; ++n) {
+        const int s = n % NS;
+        if (s_abort) break;
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(&full[s], (n / NS) & 1, kWaitLimitNs))) {
+            if (lane == 0) {
+                raise(d.error, PK_DEV_TIMEOUT);
+                s_abort = 1;
+            }
+            break;
+        }
+        char *box = smem + s * g.stage_bytes + h * kBox;
+        const uint32_t abox = smem_u32(box);
+        if (n < npb) {
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+                float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int kp = 0; kp < 4; kp += 2) {
+                    uint32_t bb[4];
+                    ldsm_x4(abox + sw128(nt * 8 + (lane % 8), (kp * 16 + (lane / 8) * 8) * 2), bb);
+                    mma_bf16(c, fv[kp], bb[0], bb[1]);
+                    mma_bf16(c, fv[kp + 1], bb[2], bb[3]);
+                }
+                if (gq < chunk)
+                    *reinterpret_cast<float2 *>(sBD + (h * chunk + gq) * bds + n * 16 + nt * 8 + 2 * tq) =
+                        make_float2(c[0], c[1]);
+            }
+        } else {
+            const int i = n - npb;
+            if (a.k_new) append_rows(static_cast<const T *>(a.k_new), 0, i, box);
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+                float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int kp = 0; kp < 4; kp += 2) {
+                    uint32_t bb[4];
+                    ldsm_x4(abox + sw128(nt * 8 + (lane % 8), (kp * 16 + (lane / 8) * 8) * 2), bb);
+                    mma_bf16(c, fu[kp], bb[0], bb[1]);
+                    mma_bf16(c, fu[kp + 1], bb[2], bb[3]);
+                }
+                if (gq < chunk)
+                    *reinterpret_cast<float2 *>(sS + (i * 16 + h * chunk + gq) * 16 + nt * 8 + 2 * tq) =
+                        make_float2(c[0], c[1]);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    consumer_sync();   // S and BD of every head complete
+    if (s_abort) return;
+
+    // ---- dense softmax over the stacked rows: 16 threads per row
+    {
+        const int row = tid / 16, sub = tid % 16;
+        const int rows = kH * chunk;
+        const int iq = row % chunk;
+        float sv[kMaxBoxes];
+        float mx = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < kMaxBoxes; ++i) {
+            sv[i] = -INFINITY;
+            if (i < nb && row < rows) {
+                const int pr = s_start[i] + sub;
+                const int av = ((nfirst + i) << 4) + pr;
+                const int j = av - (w - g.left);
+                if (pr >= 0 && pr < 16 && av >= 0 && j >= 0 && j < W) {
+                    const float c = sS[(i * 16 + row) * 16 + sub] * scale;
+                    const bool allowed = (s_mask[iq * 4 + (j >> 5)] >> (j & 31)) & 1u;
+                    sv[i] = allowed ? c + sBD[row * bds + chunk - 1 - iq + j] * scale
+                                    : c - 1e5f;   // masked_fill(-1e5), attention.py:115
+                }
+            }
+            mx = fmaxf(mx, sv[i]);
+        }
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        float sum = 0.f;
+#pragma unroll
+        for (int i = 0; i < kMaxBoxes; ++i) {
+            if (i < nb) {
+                const float p = sv[i] == -INFINITY ? 0.f : __expf(sv[i] - mx);
+                sum += p;
+                *reinterpret_cast<__nv_bfloat16 *>(sP + (i * 16 + row) * kPStride + sub * 2) =
+                    __float2bfloat16_rn(p);
+            }
+        }
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if (sub == 0) s_rowsum[row] = sum;
+    }
+    consumer_sync();   // probabilities visible
+
+    // ---- pass 2: O_h = P V_h over the V pages
+    float o[4][2][4];
+#pragma unroll
+    for (int np = 0; np < 4; ++np)
+#pragma unroll
+        for (int k = 0; k < 2; ++k)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) o[np][k][e] = 0.f;
+    for (int n = npb + nb; n < nblocks; ++n) {
+        const int s = n % NS, i = n - npb - nb;
+        if (s_abort) break;
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(&full[s], (n / NS) & 1, kWaitLimitNs))) {
+            if (lane == 0) {
+                raise(d.error, PK_DEV_TIMEOUT);
+                s_abort = 1;
+            }
+            break;
+        }
+        char *box = smem + s * g.stage_bytes + h * kBox;
+        const uint32_t abox = smem_u32(box);
+        if (a.v_new) append_rows(static_cast<const T *>(a.v_new), 1, i, box);
+        uint32_t pa[4];
+        ldsm_x4(smem_u32(sP) + (i * 16 + lane % 16) * kPStride + (lane / 16) * 16, pa);
+        const int key = (lane % 8) + ((lane / 8) & 1) * 8;
+#pragma unroll
+        for (int np = 0; np < 4; ++np) {
+            uint32_t vb[4];
+            ldsm_x4_t(abox + sw128(key, (np * 16 + (lane / 16) * 8) * 2), vb);
+            mma_bf16(o[np][0], pa, vb[0], vb[1]);
+            mma_bf16(o[np][1], pa, vb[2], vb[3]);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    if (s_abort) return;
+
+    // ---- this head's rows h*chunk + t of the stacked tile -> out
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+        const int srow = gq + half * 8;                 // stacked row held in c[2*half..]
+        const int t = srow - h * chunk;
+        if (t < 0 || t >= chunk) continue;
+        const float inv = 1.f / s_rowsum[srow];
+        T *orow = out_base + (int64_t)t * a.o_rs + h * 64;
+#pragma unroll
+        for (int np = 0; np < 4; ++np)
+#pragma unroll
+            for (int k = 0; k < 2; ++k)
+                *reinterpret_cast<__nv_bfloat162 *>(orow + np * 16 + k * 8 + 2 * tq) =
+                    __floats2bfloat162_rn(o[np][k][2 * half] * inv, o[np][k][2 * half + 1] * inv);
+    }
+}
+
+}  // namespace
+
+int launch_attention_stacked(const pk_paged_kv *kv, const CUtensorMap &pos_map16,
+                             const AttnArgs &a, cudaStream_t s) {
+    const pk_paged_kv_desc &d = kv->d;
+    if (d.dtype != PK_DTYPE_BF16 || kv->head_dim != 64 || d.num_heads != kH ||
+        d.num_heads * d.chunk > 16 || d.page_size != 16)
+        return PK_ENOTSUP;
+    constexpr int NS = 4;
+    SGeom g;
+    g.num_layers = d.num_layers;
+    g.left = d.left;
+    g.chunk = d.chunk;
+    g.W = d.left + d.chunk;
+    g.R = g.W + d.chunk - 1;
+    g.npb = (g.R + 15) / 16;
+    g.max_boxes = pk_pages_per_stream(d.left, d.chunk, d.page_size);
+    if (g.max_boxes > kMaxBoxes || g.npb > kMaxPosBlocks) return PK_ENOTSUP;
+    g.stage_bytes = kH * kBox;
+    g.off_s = NS * g.stage_bytes;
+    g.off_bd = g.off_s + kMaxBoxes * 16 * 16 * 4;
+    g.bd_stride = g.npb * 16;
+    g.off_p = g.off_bd + 16 * g.bd_stride * 4;
+    const size_t smem = g.off_p + kMaxBoxes * 16 * kPStride + 1024;
+    static size_t limit = 48 * 1024;
+    if (smem > limit) {
+        cudaError_t e = cudaFuncSetAttribute(paged_attn_stacked_kernel<NS>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(paged_attn_stacked)");
+        limit = smem;
+    }
+    dim3 grid(a.batch, a.nlayers);
+    paged_attn_stacked_kernel<NS><<<grid, kThreads, smem, s>>>(kv->kv_map, pos_map16, g, d, a);
+    return cuda_status(cudaGetLastError(), "paged_attn_stacked_kernel");
+}
+
+}  // namespace pk

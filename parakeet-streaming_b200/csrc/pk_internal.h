@@ -47,6 +47,7 @@ int launch_gather(const pk_paged_kv *kv, int layer, const int32_t *slots, int ba
 struct AttnArgs {
     const void *q;
     int64_t q_ls, q_bs, q_rs;
+    const void *k_new, *v_new;   // optional: this step's K/V rows (q's strides) to append
     const void *bias_u, *bias_v;
     int64_t bias_ls;
     const int32_t *slots, *lengths;
@@ -60,6 +61,10 @@ int launch_attention(const pk_paged_kv *kv, const CUtensorMap &pos_map, const At
 // pk_attn_bf16.cu
 int launch_attention_bf16(const pk_paged_kv *kv, const CUtensorMap &pos_map, const AttnArgs &a,
                           cudaStream_t s);
+// pk_attn_stacked.cu: all heads of a (stream, layer) per CTA, when heads * chunk <= 16;
+// returns PK_ENOTSUP for other shapes.  pos_map16 has 16-row boxes.
+int launch_attention_stacked(const pk_paged_kv *kv, const CUtensorMap &pos_map16,
+                             const AttnArgs &a, cudaStream_t s);
 
 // pk_conv.cu
 struct ConvArgs {

@@ -8,9 +8,9 @@ parameter names (``qkv``, ``linear_pos``, ``linear_out``, ``pos_bias_u``,
 
 The forward keeps the two projections on cuBLAS (``qkv`` and ``linear_out``)
 and replaces everything between them - cache append, ``linear_pos``,
-``rel_shift``, the -1e5 mask fill and SDPA - with two libpk kernels: the
-paged append and the paged attention, which builds the streaming mask
-itself from the slot counters.  ``linear_pos(pos_emb)`` depends only on the
+``rel_shift``, the -1e5 mask fill and SDPA - with one libpk call that
+appends the chunk's K/V rows to the pages and runs the paged attention with
+the streaming mask of the step's window descriptors.  ``linear_pos(pos_emb)`` depends only on the
 fixed left context, so it is computed once per layer and reused.
 """
 from __future__ import annotations
@@ -84,10 +84,10 @@ class ConformerAttention(nn.Module):
         D = x.shape[-1]
         qkv = self.qkv(x)                                             # attention.py:94
         query, key, value = qkv[..., :D], qkv[..., D:2 * D], qkv[..., 2 * D:]
-        pool = cache.pool
-        pool.append(self.layer_idx, key, value, cache.slots)          # attention.py:98
-        out = pool.attention(self.layer_idx, query, self.pos_projection(pos_emb),
-                             self.pos_bias_u, self.pos_bias_v, cache.slots, cache.lengths)
+        # cache append (attention.py:98) fused into the paged attention call
+        out = cache.pool.attention(self.layer_idx, query, self.pos_projection(pos_emb),
+                                   self.pos_bias_u, self.pos_bias_v, cache.slots, cache.lengths,
+                                   key=key, value=value)
         return self.linear_out(out)                                   # attention.py:123
 
 

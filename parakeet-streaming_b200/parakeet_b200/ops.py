@@ -182,10 +182,12 @@ class PagedKVPool:
 
     def attention(self, layer: int, query: torch.Tensor, pos_proj: torch.Tensor,
                   bias_u: torch.Tensor, bias_v: torch.Tensor, slots: torch.Tensor,
-                  lengths: torch.Tensor, out: torch.Tensor | None = None):
+                  lengths: torch.Tensor, out: torch.Tensor | None = None,
+                  key: torch.Tensor | None = None, value: torch.Tensor | None = None):
         """query [B, T, D] or [nl, B, T, D]; pos_proj [P, D] or [nl, P, D];
-        bias_u/v [H, dh] or [nl, H, dh]; lengths int32 [B].  Returns out with
-        the query's leading shape (contiguous)."""
+        bias_u/v [H, dh] or [nl, H, dh]; lengths int32 [B].  With key/value
+        (this step's new rows, the query's shape and strides) the append is
+        part of the call.  Returns out with the query's leading shape."""
         squeeze = query.dim() == 3
         if squeeze:
             query, pos_proj = query.unsqueeze(0), pos_proj.unsqueeze(0)
@@ -207,9 +209,18 @@ class PagedKVPool:
             out = torch.empty((nl, B, T, D), dtype=self.dtype, device=self.device)
         elif out.dim() == 3:
             out = out.unsqueeze(0)
+        kp = vp = None
+        if key is not None:
+            if key.dim() == 3:
+                key, value = key.unsqueeze(0), value.unsqueeze(0)
+            self._check_rows(key, "key")
+            self._check_rows(value, "value")
+            if key.shape != query.shape or key.stride() != query.stride() or value.stride() != query.stride():
+                raise ValueError("key/value must have the query's shape and strides")
+            kp, vp = key.data_ptr(), value.data_ptr()
         check(lib().pk_paged_attention(
             self._h, layer, nl, query.data_ptr(), query.stride(0), query.stride(1),
-            query.stride(2), pos_proj.data_ptr(), pos_proj.stride(0), bias_u.data_ptr(),
+            query.stride(2), kp, vp, pos_proj.data_ptr(), pos_proj.stride(0), bias_u.data_ptr(),
             bias_v.data_ptr(), bias_u.stride(0), slots.data_ptr(), lengths.data_ptr(), B,
             out.data_ptr(), out.stride(0), out.stride(1), out.stride(2), _stream(self.device)),
             "pk_paged_attention")

@@ -88,7 +88,8 @@ def test_pool_exhaustion_sets_error_bit_and_allocates_nothing():
     assert pool.ring_ctr.tolist() == [0, 2]
 
 
-def run_stream_steps(shape, dtype, steps, n_slots, seed, check_every=1, short_last=True):
+def run_stream_steps(shape, dtype, steps, n_slots, seed, check_every=1, short_last=True,
+                     fused=False):
     """Staggered streams through append + gather + attention, against the
     oracle's dense slot pool (pack -> update_attn_cache -> unpack) and masks."""
     cfg = SHAPES[shape]
@@ -121,9 +122,12 @@ def run_stream_steps(shape, dtype, steps, n_slots, seed, check_every=1, short_la
         for l in range(L):
             qkv = to(rng.standard_normal((len(batch), T, 3 * D)) / 8)
             q, k, v = qkv[..., :D], qkv[..., D:2 * D], qkv[..., 2 * D:]
-            pool.append(l, k, v, sl)
             kw_ref, vw_ref = st.cache.update_attn_cache(l, rd(k), rd(v))
-            out = pool.attention(l, q, pos_t[l], bu_t[l], bv_t[l], sl, ln)
+            if fused:   # the append happens inside the attention call
+                out = pool.attention(l, q, pos_t[l], bu_t[l], bv_t[l], sl, ln, key=k, value=v)
+            else:
+                pool.append(l, k, v, sl)
+                out = pool.attention(l, q, pos_t[l], bu_t[l], bv_t[l], sl, ln)
             if step % check_every == 0 or step == steps - 1:
                 kw, vw = pool.gather(l, sl)
                 assert np.array_equal(rd(kw), kw_ref), (step, l)
@@ -143,14 +147,16 @@ def run_stream_steps(shape, dtype, steps, n_slots, seed, check_every=1, short_la
     return worst
 
 
+@pytest.mark.parametrize("fused", [False, True])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_append_gather_attention_small(dtype):
-    run_stream_steps("small", dtype, steps=44, n_slots=5, seed=3, check_every=5)
+def test_append_gather_attention_small(dtype, fused):
+    run_stream_steps("small", dtype, steps=44, n_slots=5, seed=3, check_every=5, fused=fused)
 
 
+@pytest.mark.parametrize("fused", [False, True])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_append_gather_attention_large(dtype):
-    run_stream_steps("large", dtype, steps=9, n_slots=3, seed=4)
+def test_append_gather_attention_large(dtype, fused):
+    run_stream_steps("large", dtype, steps=9, n_slots=3, seed=4, fused=fused)
 
 
 def conv_oracle(x2d, cache, w, lengths, g, b, eps=1e-5):
