@@ -1,35 +1,30 @@
 // Paged chunked rel-pos attention, bf16, for chunks where heads x chunk <= 16
-// (the small streaming model: 8 heads x 2 frames): persistent CTAs, each item
-// one (stream, layer) with all of its heads.
+// (the small streaming model: 8 heads x 2 frames): one CTA per (stream,
+// layer) with every head in it.
 //
 // Same computation as pk_attn.cu / pk_attn_bf16.cu (ConformerAttention.
 // forward lines 99-122, parakeet/modules/attention.py; streaming mask of
 // parakeet/modules/encoder.py:167-227).  With only T = 2 query rows per
 // head, a per-head CTA spends most of its instructions on setup and on the
-// padding rows of every m16 tile, and a per-(stream, layer) CTA that starts
-// cold leaves DRAM idle while it resolves its window.  Here:
+// 14 padding rows of every m16 tile.  Here:
 //
-// * a producer warp walks the CTA's items and, per item, copies the window
-//   descriptor into a double-buffered item slot and starts bulk async copies
-//   (cp.async.bulk) of the item's query rows, new K/V rows and pos_bias_u/v
-//   into it; then it streams 16 KB blocks through an NS-stage ring with
+// * a producer warp streams 16 KB blocks through an NS-stage ring with
 //   128B-swizzled TMA tile loads (cp.async.bulk.tensor, one box per head):
-//   the K pages, the rel-pos rows in blocks of 16, the V pages - each page
-//   box shifted so that rows outside the window are zero-filled without
-//   being read.  The ring never drains between items;
-// * consumer warp h owns head h: S = (q+u) K^T and BD = (q+v) P^T on tensor
-//   cores (mma.sync m16n8k16, bf16 in, fp32 accumulate), stored in the
-//   stacked [head * T + query] row order;
+//   the stream's K pages first (DRAM), then the rel-pos rows in blocks of 16
+//   (L2-resident), then its V pages - each page box shifted so that rows
+//   outside the window are zero-filled without being read;
+// * consumer warp h owns head h: BD = (q+v) P^T and S = (q+u) K^T on tensor
+//   cores (mma.sync m16n8k16, bf16 in, fp32 accumulate), written to shared
+//   memory in the stacked [head * T + query] row order;
 // * one dense softmax over all heads' rows (16 threads per row) with the
 //   reference's -1e5 masked fill, probabilities kept as bf16 per page box;
 // * O_h = P V_h on tensor cores, normalised by the row sums;
-// * with new K/V rows given, each warp writes its head's rows into its page
-//   in global memory and over the freshly landed box in shared memory: the
-//   append costs no launch and no second read;
+// * optionally the step's new K/V rows are appended here as well: each
+//   warp writes its head's rows to the page in global memory and over the
+//   freshly loaded box in shared memory, so no separate append launch and
+//   no second read of the new rows are needed;
 // * every mbarrier wait is bounded (1 s) and records PK_DEV_TIMEOUT.
 #include <math.h>
-
-#include <algorithm>
 
 #include "pk_common.cuh"
 #include "pk_internal.h"
@@ -38,33 +33,15 @@ namespace pk {
 namespace {
 
 constexpr int kH = 8;                    // heads = consumer warps
-constexpr int kD = kH * 64;              // model width
-constexpr int kTMax = 2;                 // chunk frames (kH * kTMax = 16 rows)
 constexpr int kThreads = (kH + 1) * 32;  // + producer warp
 constexpr int kBox = 2048;               // one head's 16 rows x 128 bytes
-constexpr int kStage = kH * kBox;        // one block: every head's box
 constexpr int kMaxBoxes = 8;             // pages per window handled
 constexpr int kMaxPosBlocks = 8;         // rel-pos blocks of 16 rows (R <= 128)
 constexpr int kPStride = 48;             // bytes per row of a 16x16 bf16 probability tile
 
-// Per-item slot written by the producer (header by stores, rows by bulk copies)
-struct ItemHdr {
-    int ok, nb, w, nfirst, b, lrel, pad0, pad1;
-    int start[kMaxBoxes];
-    int page[kMaxBoxes];
-    uint32_t mask[64];
-};
-constexpr uint32_t kSlotQ = 512;                     // [kTMax][kD] bf16
-constexpr uint32_t kSlotK = kSlotQ + kTMax * kD * 2; // [kTMax][kD] bf16
-constexpr uint32_t kSlotV = kSlotK + kTMax * kD * 2;
-constexpr uint32_t kSlotU = kSlotV + kTMax * kD * 2; // [kD] bf16
-constexpr uint32_t kSlotVB = kSlotU + kD * 2;
-constexpr uint32_t kSlotBytes = ((kSlotVB + kD * 2) + 1023) / 1024 * 1024;
-static_assert(sizeof(ItemHdr) <= kSlotQ, "item header too large");
-
 struct SGeom {
-    int num_layers, left, chunk, W, R, npb, max_boxes, items, batch;
-    uint32_t off_slots, off_s, off_bd, off_p;
+    int num_layers, left, chunk, W, R, npb, max_boxes;
+    uint32_t off_s, off_bd, off_p, stage_bytes;
     int bd_stride;  // floats per stacked row of sBD
 };
 
@@ -93,12 +70,9 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
 __device__ __forceinline__ void consumer_sync() {
     asm volatile("bar.sync 1, %0;" ::"n"(kH * 32) : "memory");
 }
-__device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity) {
-    return __all_sync(0xffffffffu, mbar_wait_bounded(bar, parity, kWaitLimitNs));
-}
 
 template <int NS>
-__global__ void __launch_bounds__(kThreads, NS <= 4 ? 2 : 1)
+__global__ void __launch_bounds__(kThreads, 2)
     paged_attn_stacked_kernel(const __grid_constant__ CUtensorMap kv_map,
                               const __grid_constant__ CUtensorMap pos_map, const SGeom g,
                               const pk_paged_kv_desc d, const AttnArgs a) {
@@ -106,160 +80,89 @@ __global__ void __launch_bounds__(kThreads, NS <= 4 ? 2 : 1)
     extern __shared__ char smem_raw[];
     char *smem = reinterpret_cast<char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                           ~uintptr_t(1023));
-    __shared__ uint64_t full[NS], empty[NS], info_full[2], info_empty[2];
+    __shared__ uint64_t full[NS], empty[NS];
+    __shared__ int s_ok, s_w, s_nfirst, s_nb;
     __shared__ volatile int s_abort;
+    __shared__ int s_page[kMaxBoxes], s_start[kMaxBoxes];
+    __shared__ uint32_t s_mask[16 * 4];
     __shared__ float s_rowsum[16];
 
+    const int b = blockIdx.x, lrel = blockIdx.y;
+    const int layer = a.layer0 + lrel;
     const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
     const int chunk = g.chunk, W = g.W, npb = g.npb;
-    const bool has_kv = a.k_new != nullptr;
-    char *slots = smem + g.off_slots;                           // [2][kSlotBytes]
-    float *sS = reinterpret_cast<float *>(smem + g.off_s);      // [box][16 rows][16]
-    float *sBD = reinterpret_cast<float *>(smem + g.off_bd);    // [16 rows][bd_stride]
-    char *sP = smem + g.off_p;                                  // [box][16 rows][kPStride B]
-
-    if (tid == 0) {
-        for (int s = 0; s < NS; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kH);
-        }
-        for (int s = 0; s < 2; ++s) {
-            mbar_init(&info_full[s], 1);
-            mbar_init(&info_empty[s], kH);
-        }
-        s_abort = 0;
-        fence_mbar_init();
-    }
-    __syncthreads();
+    float *sS = reinterpret_cast<float *>(smem + g.off_s);    // [box][16 rows][16]
+    float *sBD = reinterpret_cast<float *>(smem + g.off_bd);  // [16 rows][bd_stride]
+    char *sP = smem + g.off_p;                                // [box][16 rows][kPStride B]
 
     if (warp == kH) {
-        // ============================ producer warp ============================
-        if (lane == 0) {
-            prefetch_tmap(&kv_map);
-            prefetch_tmap(&pos_map);
+        // window descriptor of this stream (written by pk_pages_begin_step)
+        const int32_t *wd = d.window + (int64_t)b * PK_WIN_STRIDE;
+        if (lane < kMaxBoxes) {
+            s_page[lane] = wd[PK_WIN_PAGE + lane];
+            s_start[lane] = wd[PK_WIN_START + lane];
         }
-        int n = 0, k = 0;
+        s_mask[lane] = (uint32_t)wd[PK_WIN_MASK + lane];
+        s_mask[32 + lane] = (uint32_t)wd[PK_WIN_MASK + 32 + lane];
+        if (lane == 0) {
+            const int nb = wd[PK_WIN_NB];
+            s_ok = wd[PK_WIN_OK] && nb <= g.max_boxes && nb <= kMaxBoxes;
+            s_w = wd[PK_WIN_W];
+            s_nfirst = wd[PK_WIN_NFIRST];
+            s_nb = nb;
+            s_abort = 0;
+            for (int s = 0; s < NS; ++s) {
+                mbar_init(&full[s], 1);
+                mbar_init(&empty[s], kH);
+            }
+            fence_mbar_init();
+        }
+    }
+    __syncthreads();
+    const int nb = s_nb, w = s_w, nfirst = s_nfirst;
+    const int nblocks = npb + 2 * nb;
+    T *out_base = static_cast<T *>(a.out) + (int64_t)lrel * a.o_ls + (int64_t)b * a.o_bs;
+    if (!s_ok) {
+        for (int idx = tid; idx < chunk * kH * 64; idx += kThreads)
+            out_base[(int64_t)(idx / (kH * 64)) * a.o_rs + idx % (kH * 64)] = __float2bfloat16_rn(0.f);
+        return;
+    }
+
+    if (warp == kH) {
+        // ================= producer: K pages, rel-pos blocks, V pages =================
         int last_n[NS];
 #pragma unroll
         for (int s = 0; s < NS; ++s) last_n[s] = -1;
-        int last_k[2] = {-1, -1};
-        for (int item = blockIdx.x; item < g.items; item += gridDim.x, ++k) {
-            const int slot = k & 1;
-            if (k >= 2) {
-                int got = 1;
-                if (lane == 0) got = mbar_wait_bounded(&info_empty[slot], ((k >> 1) - 1) & 1, kWaitLimitNs);
-                if (!__shfl_sync(0xffffffffu, got, 0)) {
-                    if (lane == 0) {
-                        raise(d.error, PK_DEV_TIMEOUT);
-                        s_abort = 1;
-                    }
-                    break;
+        for (int n = 0; n < nblocks; ++n) {
+            const int s = n % NS, u = n / NS;
+            int got = 1;
+            if (u >= 1 && lane == 0) got = mbar_wait_bounded(&empty[s], (u - 1) & 1, kWaitLimitNs);
+            got = __shfl_sync(0xffffffffu, got, 0);
+            if (!got) {
+                if (lane == 0) {
+                    raise(d.error, PK_DEV_TIMEOUT);
+                    s_abort = 1;
                 }
+                break;
             }
-            const int b = item % g.batch, lrel = item / g.batch;
-            const int layer = a.layer0 + lrel;
-            char *sl = slots + slot * kSlotBytes;
-            ItemHdr &hd = *reinterpret_cast<ItemHdr *>(sl);
-            // window descriptor of this stream (written by pk_pages_begin_step)
-            const int32_t *wd = d.window + (int64_t)b * PK_WIN_STRIDE;
-            const int nb = wd[PK_WIN_NB];
-            const int ok = wd[PK_WIN_OK] && nb <= g.max_boxes && nb <= kMaxBoxes;
-            const int page = lane < kMaxBoxes ? wd[PK_WIN_PAGE + lane] : 0;
-            const int start = lane < kMaxBoxes ? wd[PK_WIN_START + lane] : 0;
-            hd.mask[lane] = (uint32_t)wd[PK_WIN_MASK + lane];
-            hd.mask[32 + lane] = (uint32_t)wd[PK_WIN_MASK + 32 + lane];
-            if (lane < kMaxBoxes) {
-                hd.start[lane] = start;
-                hd.page[lane] = page;
-            }
-            if (lane == 0) {
-                hd.ok = ok;
-                hd.nb = nb;
-                hd.w = wd[PK_WIN_W];
-                hd.nfirst = wd[PK_WIN_NFIRST];
-                hd.b = b;
-                hd.lrel = lrel;
-            }
+            if (lane == 0) mbar_arrive_expect_tx(&full[s], kH * kBox);
             __syncwarp();
-            // rows of this item: query (+ new K, V) rows and the two position biases
-            const uint32_t row_bytes = kD * 2;
-            if (lane == 0) {
-                const uint32_t bytes = ok ? (uint32_t)chunk * row_bytes * (has_kv ? 3 : 1) + 2 * row_bytes : 0;
-                mbar_arrive_expect_tx(&info_full[slot], bytes);   // release: the header above
-            }
-            __syncwarp();
-            if (ok) {
-                const int64_t base = (int64_t)lrel * a.q_ls + (int64_t)b * a.q_bs;
-                if (lane < chunk)
-                    bulk_load(sl + kSlotQ + lane * row_bytes,
-                              static_cast<const T *>(a.q) + base + (int64_t)lane * a.q_rs, row_bytes,
-                              &info_full[slot]);
-                if (has_kv && lane >= 8 && lane < 8 + chunk)
-                    bulk_load(sl + kSlotK + (lane - 8) * row_bytes,
-                              static_cast<const T *>(a.k_new) + base + (int64_t)(lane - 8) * a.q_rs,
-                              row_bytes, &info_full[slot]);
-                if (has_kv && lane >= 16 && lane < 16 + chunk)
-                    bulk_load(sl + kSlotV + (lane - 16) * row_bytes,
-                              static_cast<const T *>(a.v_new) + base + (int64_t)(lane - 16) * a.q_rs,
-                              row_bytes, &info_full[slot]);
-                if (lane == 30)
-                    bulk_load(sl + kSlotU, static_cast<const T *>(a.bias_u) + (int64_t)lrel * a.bias_ls,
-                              row_bytes, &info_full[slot]);
-                if (lane == 31)
-                    bulk_load(sl + kSlotVB, static_cast<const T *>(a.bias_v) + (int64_t)lrel * a.bias_ls,
-                              row_bytes, &info_full[slot]);
-            }
-            last_k[slot] = k;
-            if (!ok) continue;
-            // blocks: K pages, rel-pos rows, V pages
-            const int nblocks = 2 * nb + npb;
-            bool stop = false;
-            for (int q = 0; q < nblocks; ++q, ++n) {
-                const int s = n % NS, u = n / NS;
-                int got = 1;
-                if (u >= 1 && lane == 0) got = mbar_wait_bounded(&empty[s], (u - 1) & 1, kWaitLimitNs);
-                if (!__shfl_sync(0xffffffffu, got, 0)) {
-                    if (lane == 0) {
-                        raise(d.error, PK_DEV_TIMEOUT);
-                        s_abort = 1;
-                    }
-                    stop = true;
-                    break;
-                }
-                if (lane == 0) mbar_arrive_expect_tx(&full[s], kStage);
-                __syncwarp();
-                int kind, i;   // 0 = K page, 1 = rel-pos block, 2 = V page
-                if (q < nb) {
-                    kind = 0;
-                    i = q;
-                } else if (q < nb + npb) {
-                    kind = 1;
-                    i = q - nb;
+            if (lane < kH) {
+                char *dst = smem + s * g.stage_bytes + lane * kBox;
+                if (n >= nb && n < nb + npb) {
+                    tma_load_3d(dst, &pos_map, &full[s], lane * 64, (n - nb) * 16, lrel);
                 } else {
-                    kind = 2;
-                    i = q - nb - npb;
+                    const int i = n < nb ? n : n - nb - npb, kvi = n < nb ? 0 : 1;
+                    const int plane = ((s_page[i] * d.num_layers + layer) * 2 + kvi) * kH + lane;
+                    tma_load_3d(dst, &kv_map, &full[s], 0, s_start[i], plane);
                 }
-                const int pg = __shfl_sync(0xffffffffu, page, i & 31);
-                const int st = __shfl_sync(0xffffffffu, start, i & 31);
-                if (lane < kH) {
-                    char *dst = smem + s * kStage + lane * kBox;
-                    if (kind == 1) {
-                        tma_load_3d(dst, &pos_map, &full[s], lane * 64, i * 16, lrel);
-                    } else {
-                        const int plane = ((pg * d.num_layers + layer) * 2 + (kind == 2)) * kH + lane;
-                        tma_load_3d(dst, &kv_map, &full[s], 0, st, plane);
-                    }
-                }
-                last_n[s] = n;
             }
-            if (stop) break;
+            last_n[s] = n;
         }
-        if (lane == 0) {   // leave none of our copies in flight
+        if (lane == 0) {   // leave none of our loads in flight
 #pragma unroll
             for (int s = 0; s < NS; ++s)
                 if (last_n[s] >= 0) mbar_wait_bounded(&full[s], (last_n[s] / NS) & 1, kWaitLimitNs);
-            for (int s = 0; s < 2; ++s)
-                if (last_k[s] >= 0) mbar_wait_bounded(&info_full[s], (last_k[s] >> 1) & 1, kWaitLimitNs);
         }
         return;
     }
@@ -269,87 +172,76 @@ __global__ void __launch_bounds__(kThreads, NS <= 4 ? 2 : 1)
     const int gq = lane / 4, tq = lane % 4;
     const float scale = 0.125f;  // 1 / sqrt(64)
     const int bds = g.bd_stride;
-    int n = 0, k = 0;
-    for (int item = blockIdx.x; item < g.items; item += gridDim.x, ++k) {
-        const int slot = k & 1;
+
+    // A fragments: rows 0..chunk-1 of the m16 tile are this head's queries
+    uint32_t fu[4][4], fv[4][4];
+    {
+        const T *qb = static_cast<const T *>(a.q) + (int64_t)lrel * a.q_ls + (int64_t)b * a.q_bs + h * 64;
+        const T *bu = static_cast<const T *>(a.bias_u) + (int64_t)lrel * a.bias_ls + h * 64;
+        const T *bv = static_cast<const T *>(a.bias_v) + (int64_t)lrel * a.bias_ls + h * 64;
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                const int row = gq + (r & 1) * 8, col = ks * 16 + (r >> 1) * 8 + 2 * tq;
+                uint32_t pu = 0u, pv = 0u;
+                if (row < chunk) {
+                    const float2 q = __bfloat1622float2(
+                        *reinterpret_cast<const __nv_bfloat162 *>(qb + (int64_t)row * a.q_rs + col));
+                    const float2 u = __bfloat1622float2(__ldg(reinterpret_cast<const __nv_bfloat162 *>(bu + col)));
+                    const float2 v = __bfloat1622float2(__ldg(reinterpret_cast<const __nv_bfloat162 *>(bv + col)));
+                    __nv_bfloat162 xu = __floats2bfloat162_rn(q.x + u.x, q.y + u.y);
+                    __nv_bfloat162 xv = __floats2bfloat162_rn(q.x + v.x, q.y + v.y);
+                    pu = *reinterpret_cast<uint32_t *>(&xu);
+                    pv = *reinterpret_cast<uint32_t *>(&xv);
+                }
+                fu[ks][r] = pu;
+                fv[ks][r] = pv;
+            }
+    }
+
+    // this step's new K/V rows of head h, 16 bytes per lane (chunk * 8 <= 16 lanes),
+    // fetched now so that the append below does not wait on memory
+    uint4 knew = make_uint4(0, 0, 0, 0), vnew = knew;
+    const bool app_lane = a.k_new != nullptr && lane < chunk * 8;
+    if (app_lane) {
+        const int64_t off = (int64_t)lrel * a.q_ls + (int64_t)b * a.q_bs +
+                            (int64_t)(lane / 8) * a.q_rs + h * 64 + (lane % 8) * 8;
+        knew = *reinterpret_cast<const uint4 *>(static_cast<const T *>(a.k_new) + off);
+        vnew = *reinterpret_cast<const uint4 *>(static_cast<const T *>(a.v_new) + off);
+    }
+    // write those rows into box i (K or V) and into their page in global memory
+    auto append_rows = [&](const uint4 &val, int kvi, int i, char *box) {
+        if (app_lane) {
+            const int t = lane / 8, c = lane % 8;
+            const int av = w + t;
+            if ((av >> 4) - nfirst == i) {
+                const int pr = av & 15, r = pr - s_start[i];
+                *reinterpret_cast<uint4 *>(box + sw128(r, c * 16)) = val;
+                T *pool = static_cast<T *>(d.kv);
+                const int64_t plane = ((int64_t)(s_page[i] * d.num_layers + layer) * 2 + kvi) * kH + h;
+                *reinterpret_cast<uint4 *>(pool + (plane * 16 + pr) * 64 + c * 8) = val;
+            }
+        }
+        __syncwarp();
+    };
+
+    // ---- pass 1: rel-pos blocks -> BD rows, K pages -> S rows
+    for (int n = 0; n < npb + nb; ++n) {
+        const int s = n % NS;
         if (s_abort) break;
-        if (!warp_wait(&info_full[slot], (k >> 1) & 1)) {
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(&full[s], (n / NS) & 1, kWaitLimitNs))) {
             if (lane == 0) {
                 raise(d.error, PK_DEV_TIMEOUT);
                 s_abort = 1;
             }
             break;
         }
-        const char *sl = slots + slot * kSlotBytes;
-        const ItemHdr &hd = *reinterpret_cast<const ItemHdr *>(sl);
-        const int b = hd.b, lrel = hd.lrel, nb = hd.nb, w = hd.w, nfirst = hd.nfirst;
-        const int layer = a.layer0 + lrel;
-        T *out_base = static_cast<T *>(a.out) + (int64_t)lrel * a.o_ls + (int64_t)b * a.o_bs + h * 64;
-        if (!hd.ok) {
-            for (int idx = lane; idx < chunk * 64; idx += 32)
-                out_base[(int64_t)(idx / 64) * a.o_rs + idx % 64] = __float2bfloat16_rn(0.f);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&info_empty[slot]);
-            continue;
-        }
-
-        // A fragments: rows 0..chunk-1 of the m16 tile are this head's queries,
-        // (q + u) and (q + v) rounded to bf16 as the reference's bf16 add is
-        uint32_t fu[4][4], fv[4][4];
-        {
-            const T *qs = reinterpret_cast<const T *>(sl + kSlotQ) + h * 64;
-            const T *us = reinterpret_cast<const T *>(sl + kSlotU) + h * 64;
-            const T *vs = reinterpret_cast<const T *>(sl + kSlotVB) + h * 64;
-#pragma unroll
-            for (int ks = 0; ks < 4; ++ks)
-#pragma unroll
-                for (int r = 0; r < 4; ++r) {
-                    const int row = gq + (r & 1) * 8, col = ks * 16 + (r >> 1) * 8 + 2 * tq;
-                    uint32_t pu = 0u, pv = 0u;
-                    if (row < chunk) {
-                        const float2 q = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(qs + row * kD + col));
-                        const float2 u = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(us + col));
-                        const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(vs + col));
-                        __nv_bfloat162 xu = __floats2bfloat162_rn(q.x + u.x, q.y + u.y);
-                        __nv_bfloat162 xv = __floats2bfloat162_rn(q.x + v.x, q.y + v.y);
-                        pu = *reinterpret_cast<uint32_t *>(&xu);
-                        pv = *reinterpret_cast<uint32_t *>(&xv);
-                    }
-                    fu[ks][r] = pu;
-                    fv[ks][r] = pv;
-                }
-        }
-        // write this step's rows of box i (K or V, head h) to the page and over the box
-        auto append_rows = [&](uint32_t src_off, int kvi, int i, char *box) {
-            for (int idx = lane; idx < chunk * 8; idx += 32) {
-                const int t = idx / 8, c = idx % 8;
-                const int av = w + t;
-                if ((av >> 4) - nfirst != i) continue;
-                const int pr = av & 15, r = pr - hd.start[i];
-                const uint4 val = *reinterpret_cast<const uint4 *>(sl + src_off + (t * kD + h * 64 + c * 8) * 2);
-                *reinterpret_cast<uint4 *>(box + sw128(r, c * 16)) = val;
-                const int64_t plane = ((int64_t)(hd.page[i] * d.num_layers + layer) * 2 + kvi) * kH + h;
-                *reinterpret_cast<uint4 *>(static_cast<T *>(d.kv) + (plane * 16 + pr) * 64 + c * 8) = val;
-            }
-            __syncwarp();
-        };
-
-        // ---- pass 1: K pages -> S rows, rel-pos blocks -> BD rows
-        bool failed = false;
-        for (int q = 0; q < nb + npb; ++q, ++n) {
-            const int s = n % NS;
-            if (!warp_wait(&full[s], (n / NS) & 1)) {
-                if (lane == 0) {
-                    raise(d.error, PK_DEV_TIMEOUT);
-                    s_abort = 1;
-                }
-                failed = true;
-                break;
-            }
-            char *box = smem + s * kStage + h * kBox;
-            const uint32_t abox = smem_u32(box);
-            const bool is_k = q < nb;
-            if (is_k && has_kv) append_rows(kSlotK, 0, q, box);
+        char *box = smem + s * g.stage_bytes + h * kBox;
+        const uint32_t abox = smem_u32(box);
+        const bool is_pos = n >= nb;
+        const int pblk = n - nb, kbox = n;
+        if (is_pos) {
 #pragma unroll
             for (int nt = 0; nt < 2; ++nt) {
                 float c[4] = {0.f, 0.f, 0.f, 0.f};
@@ -357,120 +249,128 @@ __global__ void __launch_bounds__(kThreads, NS <= 4 ? 2 : 1)
                 for (int kp = 0; kp < 4; kp += 2) {
                     uint32_t bb[4];
                     ldsm_x4(abox + sw128(nt * 8 + (lane % 8), (kp * 16 + (lane / 8) * 8) * 2), bb);
-                    if (is_k) {
-                        mma_bf16(c, fu[kp], bb[0], bb[1]);
-                        mma_bf16(c, fu[kp + 1], bb[2], bb[3]);
-                    } else {
-                        mma_bf16(c, fv[kp], bb[0], bb[1]);
-                        mma_bf16(c, fv[kp + 1], bb[2], bb[3]);
-                    }
+                    mma_bf16(c, fv[kp], bb[0], bb[1]);
+                    mma_bf16(c, fv[kp + 1], bb[2], bb[3]);
                 }
-                if (gq < chunk) {
-                    float *dst = is_k ? sS + (q * 16 + h * chunk + gq) * 16 + nt * 8 + 2 * tq
-                                      : sBD + (h * chunk + gq) * bds + (q - nb) * 16 + nt * 8 + 2 * tq;
-                    *reinterpret_cast<float2 *>(dst) = make_float2(c[0], c[1]);
-                }
+                if (gq < chunk)
+                    *reinterpret_cast<float2 *>(sBD + (h * chunk + gq) * bds + pblk * 16 + nt * 8 + 2 * tq) =
+                        make_float2(c[0], c[1]);
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[s]);
+        } else {
+            const int i = kbox;
+            if (a.k_new) append_rows(knew, 0, i, box);
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+                float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int kp = 0; kp < 4; kp += 2) {
+                    uint32_t bb[4];
+                    ldsm_x4(abox + sw128(nt * 8 + (lane % 8), (kp * 16 + (lane / 8) * 8) * 2), bb);
+                    mma_bf16(c, fu[kp], bb[0], bb[1]);
+                    mma_bf16(c, fu[kp + 1], bb[2], bb[3]);
+                }
+                if (gq < chunk)
+                    *reinterpret_cast<float2 *>(sS + (i * 16 + h * chunk + gq) * 16 + nt * 8 + 2 * tq) =
+                        make_float2(c[0], c[1]);
+            }
         }
-        consumer_sync();   // S and BD of every head complete (all warps reach this)
-        if (s_abort || failed) break;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    consumer_sync();   // S and BD of every head complete
+    if (s_abort) return;
 
-        // ---- dense softmax over the stacked rows: 16 threads per row
-        {
-            const int row = tid / 16, sub = tid % 16;
-            const int rows = kH * chunk;
-            const int iq = row % chunk;
-            float sv[kMaxBoxes];
-            float mx = -INFINITY;
+    // ---- dense softmax over the stacked rows: 16 threads per row
+    {
+        const int row = tid / 16, sub = tid % 16;
+        const int rows = kH * chunk;
+        const int iq = row % chunk;
+        float sv[kMaxBoxes];
+        float mx = -INFINITY;
 #pragma unroll
-            for (int i = 0; i < kMaxBoxes; ++i) {
-                sv[i] = -INFINITY;
-                if (i < nb && row < rows) {
-                    const int pr = hd.start[i] + sub;
-                    const int av = ((nfirst + i) << 4) + pr;
-                    const int j = av - (w - g.left);
-                    if (pr >= 0 && pr < 16 && av >= 0 && j >= 0 && j < W) {
-                        const float c = sS[(i * 16 + row) * 16 + sub] * scale;
-                        const bool allowed = (hd.mask[iq * 4 + (j >> 5)] >> (j & 31)) & 1u;
-                        sv[i] = allowed ? c + sBD[row * bds + chunk - 1 - iq + j] * scale
-                                        : c - 1e5f;   // masked_fill(-1e5), attention.py:115
-                    }
-                }
-                mx = fmaxf(mx, sv[i]);
-            }
-#pragma unroll
-            for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-            float sum = 0.f;
-#pragma unroll
-            for (int i = 0; i < kMaxBoxes; ++i) {
-                if (i < nb) {
-                    const float p = sv[i] == -INFINITY ? 0.f : __expf(sv[i] - mx);
-                    sum += p;
-                    *reinterpret_cast<__nv_bfloat16 *>(sP + (i * 16 + row) * kPStride + sub * 2) =
-                        __float2bfloat16_rn(p);
+        for (int i = 0; i < kMaxBoxes; ++i) {
+            sv[i] = -INFINITY;
+            if (i < nb && row < rows) {
+                const int pr = s_start[i] + sub;
+                const int av = ((nfirst + i) << 4) + pr;
+                const int j = av - (w - g.left);
+                if (pr >= 0 && pr < 16 && av >= 0 && j >= 0 && j < W) {
+                    const float c = sS[(i * 16 + row) * 16 + sub] * scale;
+                    const bool allowed = (s_mask[iq * 4 + (j >> 5)] >> (j & 31)) & 1u;
+                    sv[i] = allowed ? c + sBD[row * bds + chunk - 1 - iq + j] * scale
+                                    : c - 1e5f;   // masked_fill(-1e5), attention.py:115
                 }
             }
-#pragma unroll
-            for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-            if (sub == 0) s_rowsum[row] = sum;
+            mx = fmaxf(mx, sv[i]);
         }
-        consumer_sync();   // probabilities visible
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        float sum = 0.f;
+#pragma unroll
+        for (int i = 0; i < kMaxBoxes; ++i) {
+            if (i < nb) {
+                const float p = sv[i] == -INFINITY ? 0.f : __expf(sv[i] - mx);
+                sum += p;
+                *reinterpret_cast<__nv_bfloat16 *>(sP + (i * 16 + row) * kPStride + sub * 2) =
+                    __float2bfloat16_rn(p);
+            }
+        }
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if (sub == 0) s_rowsum[row] = sum;
+    }
+    consumer_sync();   // probabilities visible
 
-        // ---- pass 2: O_h = P V_h over the V pages
-        float o[4][2][4];
+    // ---- pass 2: O_h = P V_h over the V pages
+    float o[4][2][4];
+#pragma unroll
+    for (int np = 0; np < 4; ++np)
+#pragma unroll
+        for (int k = 0; k < 2; ++k)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) o[np][k][e] = 0.f;
+    for (int n = npb + nb; n < nblocks; ++n) {
+        const int s = n % NS, i = n - npb - nb;
+        if (s_abort) break;
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(&full[s], (n / NS) & 1, kWaitLimitNs))) {
+            if (lane == 0) {
+                raise(d.error, PK_DEV_TIMEOUT);
+                s_abort = 1;
+            }
+            break;
+        }
+        char *box = smem + s * g.stage_bytes + h * kBox;
+        const uint32_t abox = smem_u32(box);
+        if (a.v_new) append_rows(vnew, 1, i, box);
+        uint32_t pa[4];
+        ldsm_x4(smem_u32(sP) + (i * 16 + lane % 16) * kPStride + (lane / 16) * 16, pa);
+        const int key = (lane % 8) + ((lane / 8) & 1) * 8;
+#pragma unroll
+        for (int np = 0; np < 4; ++np) {
+            uint32_t vb[4];
+            ldsm_x4_t(abox + sw128(key, (np * 16 + (lane / 16) * 8) * 2), vb);
+            mma_bf16(o[np][0], pa, vb[0], vb[1]);
+            mma_bf16(o[np][1], pa, vb[2], vb[3]);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    if (s_abort) return;
+
+    // ---- this head's rows h*chunk + t of the stacked tile -> out
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+        const int srow = gq + half * 8;                 // stacked row held in c[2*half..]
+        const int t = srow - h * chunk;
+        if (t < 0 || t >= chunk) continue;
+        const float inv = 1.f / s_rowsum[srow];
+        T *orow = out_base + (int64_t)t * a.o_rs + h * 64;
 #pragma unroll
         for (int np = 0; np < 4; ++np)
 #pragma unroll
-            for (int kk = 0; kk < 2; ++kk)
-#pragma unroll
-                for (int e = 0; e < 4; ++e) o[np][kk][e] = 0.f;
-        for (int i = 0; i < nb; ++i, ++n) {
-            const int s = n % NS;
-            if (!warp_wait(&full[s], (n / NS) & 1)) {
-                if (lane == 0) {
-                    raise(d.error, PK_DEV_TIMEOUT);
-                    s_abort = 1;
-                }
-                failed = true;
-                break;
-            }
-            char *box = smem + s * kStage + h * kBox;
-            const uint32_t abox = smem_u32(box);
-            if (has_kv) append_rows(kSlotV, 1, i, box);
-            uint32_t pa[4];
-            ldsm_x4(smem_u32(sP) + (i * 16 + lane % 16) * kPStride + (lane / 16) * 16, pa);
-            const int key = (lane % 8) + ((lane / 8) & 1) * 8;
-#pragma unroll
-            for (int np = 0; np < 4; ++np) {
-                uint32_t vb[4];
-                ldsm_x4_t(abox + sw128(key, (np * 16 + (lane / 16) * 8) * 2), vb);
-                mma_bf16(o[np][0], pa, vb[0], vb[1]);
-                mma_bf16(o[np][1], pa, vb[2], vb[3]);
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[s]);
-        }
-        if (failed) break;
-
-        // ---- this head's rows h*chunk + t of the stacked tile -> out
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-            const int srow = gq + half * 8;
-            const int t = srow - h * chunk;
-            if (t < 0 || t >= chunk) continue;
-            const float inv = 1.f / s_rowsum[srow];
-            T *orow = out_base + (int64_t)t * a.o_rs;
-#pragma unroll
-            for (int np = 0; np < 4; ++np)
-#pragma unroll
-                for (int kk = 0; kk < 2; ++kk)
-                    *reinterpret_cast<__nv_bfloat162 *>(orow + np * 16 + kk * 8 + 2 * tq) =
-                        __floats2bfloat162_rn(o[np][kk][2 * half] * inv, o[np][kk][2 * half + 1] * inv);
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&info_empty[slot]);   // this warp is done with the slot
+            for (int k = 0; k < 2; ++k)
+                *reinterpret_cast<__nv_bfloat162 *>(orow + np * 16 + k * 8 + 2 * tq) =
+                    __floats2bfloat162_rn(o[np][k][2 * half] * inv, o[np][k][2 * half + 1] * inv);
     }
 }
 
@@ -480,11 +380,7 @@ int launch_attention_stacked(const pk_paged_kv *kv, const CUtensorMap &pos_map16
                              const AttnArgs &a, cudaStream_t s) {
     const pk_paged_kv_desc &d = kv->d;
     if (d.dtype != PK_DTYPE_BF16 || kv->head_dim != 64 || d.num_heads != kH ||
-        d.chunk > kTMax || d.page_size != 16)
-        return PK_ENOTSUP;
-    // the slot's bulk copies need 16-byte aligned, 16-byte strided rows
-    if ((reinterpret_cast<uintptr_t>(a.bias_u) | reinterpret_cast<uintptr_t>(a.bias_v)) & 15 ||
-        (a.bias_ls * 2) % 16)
+        d.num_heads * d.chunk > 16 || d.page_size != 16)
         return PK_ENOTSUP;
     constexpr int NS = 4;
     SGeom g;
@@ -495,36 +391,22 @@ int launch_attention_stacked(const pk_paged_kv *kv, const CUtensorMap &pos_map16
     g.R = g.W + d.chunk - 1;
     g.npb = (g.R + 15) / 16;
     g.max_boxes = pk_pages_per_stream(d.left, d.chunk, d.page_size);
-    g.items = a.batch * a.nlayers;
-    g.batch = a.batch;
     if (g.max_boxes > kMaxBoxes || g.npb > kMaxPosBlocks) return PK_ENOTSUP;
-    g.off_slots = NS * kStage;
-    g.off_s = g.off_slots + 2 * kSlotBytes;
+    g.stage_bytes = kH * kBox;
+    g.off_s = NS * g.stage_bytes;
     g.off_bd = g.off_s + kMaxBoxes * 16 * 16 * 4;
     g.bd_stride = g.npb * 16;
     g.off_p = g.off_bd + 16 * g.bd_stride * 4;
     const size_t smem = g.off_p + kMaxBoxes * 16 * kPStride + 1024;
-    auto kernel = paged_attn_stacked_kernel<NS>;
     static size_t limit = 48 * 1024;
-    static int sms = 0;
     if (smem > limit) {
-        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)smem);
+        cudaError_t e = cudaFuncSetAttribute(paged_attn_stacked_kernel<NS>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(paged_attn_stacked)");
         limit = smem;
     }
-    if (sms == 0) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaError_t e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        if (e != cudaSuccess) return cuda_status(e, "cudaDeviceGetAttribute");
-    }
-    int per_sm = 0;
-    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, smem);
-    if (e != cudaSuccess) return cuda_status(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
-    if (per_sm < 1) return PK_ENOTSUP;
-    const int grid = (int)std::min<long long>(g.items, (long long)sms * per_sm);
-    kernel<<<grid, kThreads, smem, s>>>(kv->kv_map, pos_map16, g, d, a);
+    dim3 grid(a.batch, a.nlayers);
+    paged_attn_stacked_kernel<NS><<<grid, kThreads, smem, s>>>(kv->kv_map, pos_map16, g, d, a);
     return cuda_status(cudaGetLastError(), "paged_attn_stacked_kernel");
 }
 
