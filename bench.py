@@ -63,6 +63,7 @@ def parse():
     ap.add_argument("--streams", type=int, default=80)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-breakdown", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="time eager launches only")
     ap.add_argument("--profile", action="store_true",
                     help="prefill + warmup + --steps steps only (for ncu), no report")
     return ap.parse_args()
@@ -275,6 +276,7 @@ def main():
         torch.cuda.synchronize()
 
     K = args.steps
+    # (a) eager steps with CUDA events around the attention kernel: roofline timing
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(K)]
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -288,8 +290,32 @@ def main():
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    ms = e0.elapsed_time(e1) / K
+    eager_ms = e0.elapsed_time(e1) / K
     attn_ms = sum(a.elapsed_time(b) for a, b in evs) / K
+
+    # (b) the same steps replayed as CUDA graphs (one graph per input buffer): `value`
+    ms = eager_ms
+    graphs = []
+    if not args.no_graph:
+        for i in range(NBUF):
+            gph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gph):
+                step(qkv[i])
+            graphs.append(gph)
+        for i in range(max(3, args.warmup)):
+            graphs[i % NBUF].replay()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record()
+        for i in range(K):
+            graphs[i % NBUF].replay()
+        g1.record()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        ms = g0.elapsed_time(g1) / K
     clk = clocks.stop()
     err = pool.read_error()
 
@@ -306,12 +332,24 @@ def main():
     for i in range(max(3, args.warmup)):
         e2e_step(i)
     torch.cuda.synchronize()
+    e2e_run = e2e_step
+    if graphs:   # copies in, the step, copy out: one graph per input buffer
+        e2e_graphs = []
+        for i in range(NBUF):
+            gph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gph):
+                e2e_step(i)
+            e2e_graphs.append(gph)
+        e2e_run = lambda i: e2e_graphs[i % NBUF].replay()  # noqa: E731
+        for i in range(max(3, args.warmup)):
+            e2e_run(i)
+        torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     f0.record()
     for i in range(K):
-        e2e_step(i)
+        e2e_run(i)
     f1.record()
     torch.cuda.synchronize()
     e2e_ms = f0.elapsed_time(f1) / K
@@ -360,9 +398,9 @@ def main():
                                "bytes_per_stream_layer": nbytes // units}
 
     if world > 1:
-        t = torch.tensor([ms, e2e_ms, attn_ms], device=dev)
+        t = torch.tensor([ms, e2e_ms, attn_ms, eager_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, e2e_ms, attn_ms = t.tolist()
+        ms, e2e_ms, attn_ms, eager_ms = t.tolist()
 
     if rank == 0:
         hbm, kind = peaks()
@@ -386,7 +424,8 @@ def main():
         line = {
             "metric": "paged-attn HBM GB/s (append + attention, algorithmic bytes)",
             "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": K,
-            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "ms_per_step_eager": round(eager_ms, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": f"configs[1] isolated paged-attention step, {args.model} model",
                        "streams_per_gpu": B, "layers": L, "heads": H, "head_dim": dh,
@@ -394,7 +433,8 @@ def main():
                        "page_order": "randperm seed 1",
                        "l2": f"inputs > L2: {pool.kv.numel() * 2 / 1e6:.0f} MB page pool, "
                              f"{step_bytes / 1e6:.0f} MB read+written per step",
-                       "parallelism": f"{world} independent replicas (stream sharding)"},
+                       "parallelism": f"{world} independent replicas (stream sharding)",
+                       "launch": "CUDA graph per step" if graphs else "eager"},
             "roofline": {"bound": "hbm", "kernel": kernel_name,
                          "achieved": round(achieved, 1), "peak": hbm, "peak_kind": kind,
                          "unit": "GB/s", "frac": round(achieved / hbm, 3), "traffic": traffic,
@@ -403,7 +443,7 @@ def main():
             "e2e": {"value": round(e2e, 1), "unit": "GB/s",
                     "h2d_bytes_per_step": qkv[0].numel() * 2, "d2h_bytes_per_step": out.numel() * 2,
                     "ms_per_step": round(e2e_ms, 4)},
-            "gpu_launches": 4 * K,   # allocator, window descriptors, attention+append, counters
+            "gpu_launches": 3 * K,   # per step: allocator+windows, attention+append, counters
             "clocks": clk,
             "device_error_word": err,
             "ops": breakdown,

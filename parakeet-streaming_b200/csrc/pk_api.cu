@@ -167,10 +167,9 @@ int pk_pages_begin_step(pk_paged_kv *kv, const int32_t *slots, const int32_t *le
     PK_CHECK(batch <= kv->d.num_slots, "batch larger than the pool's slots");
     PK_CHECK(batch == 0 || slots, "null slots");
     PK_CHECK(num_released == 0 || released, "null released");
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    int st = launch_pages_begin(kv, slots, batch, released, num_released, s);
-    if (st != PK_OK) return st;
-    return launch_window_desc(kv, slots, lengths, batch, s);
+    PK_CHECK(batch <= 4096, "batch above 4096 rows");
+    return launch_pages_begin(kv, slots, lengths, batch, released, num_released,
+                              static_cast<cudaStream_t>(stream));
 }
 
 int pk_pages_end_step(pk_paged_kv *kv, const int32_t *slots, const int32_t *lengths,

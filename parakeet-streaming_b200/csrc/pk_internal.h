@@ -28,13 +28,11 @@ int encode_tmap_3d(CUtensorMap *map, int dtype, const void *base, uint64_t d0, u
 
 // pk_pages.cu
 int launch_pages_reset(const pk_paged_kv *kv, const int32_t *init_order, cudaStream_t s);
-int launch_pages_begin(const pk_paged_kv *kv, const int32_t *slots, int batch,
-                       const int32_t *released, int num_released, cudaStream_t s);
+int launch_pages_begin(const pk_paged_kv *kv, const int32_t *slots, const int32_t *lengths,
+                       int batch, const int32_t *released, int num_released, cudaStream_t s);
 int launch_pages_end(const pk_paged_kv *kv, const int32_t *slots, const int32_t *lengths,
                      int batch, cudaStream_t s);
-// pk_window.cu
-int launch_window_desc(const pk_paged_kv *kv, const int32_t *slots, const int32_t *lengths,
-                       int batch, cudaStream_t s);
+
 
 // pk_kv.cu
 int launch_append(const pk_paged_kv *kv, int layer0, int nlayers, const void *key,
