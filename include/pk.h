@@ -82,7 +82,8 @@ typedef struct pk_paged_kv_desc {
     int64_t *ring_ctr;    /* [2] monotonic head (pop) and tail (push)        */
     int32_t *meta;        /* [num_slots][PK_META_STRIDE]                     */
     int32_t *error;       /* [1] device error word (PK_DEV_* bits)           */
-    int32_t *window;      /* [num_slots][PK_WIN_STRIDE] step window descriptors */
+    int32_t *window;      /* [num_slots][PK_WIN_STRIDE] step window descriptors,
+                             16-byte aligned */
     int32_t num_pages;
     int32_t num_slots;
     int32_t num_layers;
@@ -91,7 +92,8 @@ typedef struct pk_paged_kv_desc {
     int32_t left;         /* left attention context (70)                     */
     int32_t chunk;        /* frames per step T = right context + 1           */
     int32_t page_size;    /* frames per page (16)                            */
-    int32_t ring;         /* page-table entries per slot (power of two)      */
+    int32_t ring;         /* page-table entries per slot (power of two,
+                             pk_pages_per_stream() <= ring <= PK_WIN_MAX_PAGES) */
     int32_t dtype;        /* PK_DTYPE_*                                       */
 } pk_paged_kv_desc;
 
@@ -112,7 +114,7 @@ int32_t pk_ring_size(int32_t left, int32_t chunk, int32_t page_size);
  * like deque(range(pool)) in scheduler.py:84. */
 int pk_pages_reset(pk_paged_kv *kv, const int32_t *init_order, void *stream);
 
-/* Start of one batched step (one CTA, deterministic order):
+/* Start of one batched step (one CTA, deterministic order; batch <= 2048):
  *  0. return every page of the `released` slots (finished streams,
  *     parakeet/engine/scheduler.py:101-104) and zero their counters;
  *  1. per batch row, in order: free pages wholly left of the window;

@@ -121,8 +121,9 @@ int pk_paged_kv_create(const pk_paged_kv_desc *desc, pk_paged_kv **out) {
     PK_CHECK(d.page_size >= 8 && d.page_size <= 256 && (d.page_size & (d.page_size - 1)) == 0,
              "page_size must be a power of two in [8, 256]");
     PK_CHECK(d.ring >= pk_pages_per_stream(d.left, d.chunk, d.page_size) &&
-                 (d.ring & (d.ring - 1)) == 0,
-             "ring must be a power of two >= pk_pages_per_stream()");
+                 d.ring <= PK_WIN_MAX_PAGES && (d.ring & (d.ring - 1)) == 0,
+             "ring must be a power of two in [pk_pages_per_stream(), PK_WIN_MAX_PAGES]");
+    PK_CHECK(aligned16(d.window), "window descriptors not 16-byte aligned");
     PK_CHECK(aligned16(d.kv), "kv pool not 16-byte aligned");
     const int esize = d.dtype == PK_DTYPE_BF16 ? 2 : 4;
     PK_CHECK(((d.dim / d.num_heads) * esize) % 128 == 0,
@@ -167,7 +168,7 @@ int pk_pages_begin_step(pk_paged_kv *kv, const int32_t *slots, const int32_t *le
     PK_CHECK(batch <= kv->d.num_slots, "batch larger than the pool's slots");
     PK_CHECK(batch == 0 || slots, "null slots");
     PK_CHECK(num_released == 0 || released, "null released");
-    PK_CHECK(batch <= 4096, "batch above 4096 rows");
+    PK_CHECK(batch <= 2048, "batch above 2048 rows");
     return launch_pages_begin(kv, slots, lengths, batch, released, num_released,
                               static_cast<cudaStream_t>(stream));
 }

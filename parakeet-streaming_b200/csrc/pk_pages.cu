@@ -19,7 +19,7 @@ namespace pk {
 namespace {
 
 constexpr int kAllocThreads = 1024;
-constexpr int kRowsPerThread = 4;   // batch <= 4096
+constexpr int kMaxBatch = 2 * kAllocThreads;
 using Scan = cub::BlockScan<int, kAllocThreads>;
 
 __global__ void pages_reset_kernel(pk_paged_kv_desc d, const int32_t *init_order) {
@@ -35,94 +35,100 @@ __global__ void pages_reset_kernel(pk_paged_kv_desc d, const int32_t *init_order
     }
 }
 
-__device__ __forceinline__ int64_t ring_idx(int64_t ctr, int n) { return ctr % n; }
+// Per-row state of one step, in shared memory: the row's slot and counters,
+// and a copy of its page-table ring (ring <= PK_WIN_MAX_PAGES entries).
+struct RowState {
+    int slot, len, first, next, w, proc, clen, valid;
+};
 
-// Window descriptor of batch row b (one warp): pages of rows [w - left, w + chunk),
-// each page's box start row, and the mask bit rows.
-__device__ void build_window(const pk_paged_kv_desc &d, const int32_t *slots,
-                             const int32_t *lengths, int b, int lane) {
-    const int chunk = d.chunk, W = d.left + d.chunk, ps = d.page_size;
-    int32_t *out = d.window + (int64_t)b * PK_WIN_STRIDE;
-    int ok = 1, w = 0, proc = 0, clen = 0, len = chunk;
-    const int slot = slots[b];
-    if (slot < 0 || slot >= d.num_slots) {
-        ok = 0;
-    } else {
-        const int32_t *m = d.meta + (int64_t)slot * PK_META_STRIDE;
-        w = m[PK_META_WRITTEN];
-        proc = m[PK_META_PROCESSED];
-        clen = m[PK_META_CACHE_LEN];
-        if (lengths) len = lengths[b];
-    }
-    const int a_lo = max(w - d.left, 0), a_hi = w + chunk;
+__device__ __forceinline__ unsigned range_bits(int lo, int hi, int base) {
+    const int a = max(lo, base), b = min(hi, base + 32);
+    if (a >= b) return 0u;
+    const unsigned n = (unsigned)(b - a);
+    return (n == 32u ? 0xffffffffu : ((1u << n) - 1u)) << (a - base);
+}
+
+// Window descriptor of one batch row, written by the thread that owns the row:
+// pages of rows [w - left, w + chunk), each page's box start row, and the mask
+// bit rows.  Key j of query row i is visible when ConformerEncoder's mask allows
+// it (parakeet/modules/encoder.py:167-227): the key holds a real frame,
+// j - off < clen + len, and its chunk index is 0..left/chunk chunks behind the
+// query's.  Both conditions are intervals in j, so each bit row is one range.
+__device__ void write_window(const pk_paged_kv_desc &d, const RowState &r, const int *ring,
+                             int b) {
+    const int chunk = d.chunk, W = d.left + chunk, ps = d.page_size, rmask = d.ring - 1;
+    int4 *out = reinterpret_cast<int4 *>(d.window + (int64_t)b * PK_WIN_STRIDE);
+    int ok = r.valid;
+    const int a_lo = max(r.w - d.left, 0), a_hi = r.w + chunk;
     const int nfirst = a_lo / ps;
     const int nb = (a_hi - 1) / ps - nfirst + 1;
     if (nb > PK_WIN_MAX_PAGES) ok = 0;
-    int page = -1, start = 0;
-    if (ok && lane < nb) {
-        const int n = nfirst + lane;
-        page = d.page_table[(int64_t)slot * d.ring + (n & (d.ring - 1))];
-        const int lo = max(a_lo - n * ps, 0), hi = min(a_hi - n * ps, ps);
-        start = lo > 0 ? lo : (hi < ps ? hi - ps : 0);
-    }
-    if (__any_sync(0xffffffffu, ok && lane < nb && (page < 0 || page >= d.num_pages))) {
-        if (lane == 0) raise(d.error, PK_DEV_BAD_PAGE);
-        ok = 0;
-    }
-    if (lane < PK_WIN_MAX_PAGES) {
-        out[PK_WIN_PAGE + lane] = lane < nb ? page : -1;
-        out[PK_WIN_START + lane] = start;
-    }
-    // mask rows < chunk; rows >= chunk stay zero
-    const int key_start = max(proc - clen, 0), off = d.left - clen;
-    const int left_chunks = d.left / chunk;
-    for (int kb = 0; kb < 4; ++kb) {
-        const int j = kb * 32 + lane;
-        bool key_ok = ok && j < W && j >= off;
-        int kc = 0;
-        if (key_ok) {
-            const int rr = j - off;
-            key_ok = rr < clen || (rr - clen) < len;
-            kc = (key_start + rr) / chunk;
-        }
-        int qc = (key_start + clen) / chunk, qrem = (key_start + clen) % chunk;
-        for (int i = 0; i < chunk; ++i) {
-            const int dc = qc - kc;
-            const unsigned bits =
-                __ballot_sync(0xffffffffu, key_ok && i < len && dc >= 0 && dc <= left_chunks);
-            if (lane == 0) out[PK_WIN_MASK + i * 4 + kb] = (int32_t)bits;
-            if (++qrem == chunk) {
-                qrem = 0;
-                ++qc;
+    bool bad = false;
+#pragma unroll
+    for (int g = 0; g < PK_WIN_MAX_PAGES / 4; ++g) {
+        int pv[4], sv[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int l = g * 4 + e;
+            pv[e] = -1;
+            sv[e] = 0;
+            if (ok && l < nb) {
+                const int n = nfirst + l;
+                pv[e] = ring[n & rmask];
+                bad |= pv[e] < 0 || pv[e] >= d.num_pages;
+                const int lo = max(a_lo - n * ps, 0), hi = min(a_hi - n * ps, ps);
+                sv[e] = lo > 0 ? lo : (hi < ps ? hi - ps : 0);
             }
         }
+        out[PK_WIN_PAGE / 4 + g] = make_int4(pv[0], pv[1], pv[2], pv[3]);
+        out[PK_WIN_START / 4 + g] = make_int4(sv[0], sv[1], sv[2], sv[3]);
     }
-    for (int idx = chunk * 4 + lane; idx < 64; idx += 32) out[PK_WIN_MASK + idx] = 0;
-    if (lane == 0) {
-        out[PK_WIN_OK] = ok;
-        out[PK_WIN_W] = w;
-        out[PK_WIN_PROC] = proc;
-        out[PK_WIN_CLEN] = clen;
-        out[PK_WIN_LEN] = len;
-        out[PK_WIN_NB] = nb;
-        out[PK_WIN_NFIRST] = nfirst;
-        out[PK_WIN_SLOT] = slot;
+    if (bad) {
+        raise(d.error, PK_DEV_BAD_PAGE);
+        ok = 0;
     }
+    const int key_start = max(r.proc - r.clen, 0), off = d.left - r.clen;
+    const int lc = d.left / chunk;
+    for (int i = 0; i < 16; ++i) {
+        int4 m = make_int4(0, 0, 0, 0);
+        if (ok && i < chunk && i < r.len) {
+            const int qc = (key_start + r.clen + i) / chunk;
+            const int lo = off + max(0, (qc - lc) * chunk - key_start);
+            const int hi = min(W, off + min(r.clen + r.len, (qc + 1) * chunk - key_start));
+            m = make_int4((int)range_bits(lo, hi, 0), (int)range_bits(lo, hi, 32),
+                          (int)range_bits(lo, hi, 64), (int)range_bits(lo, hi, 96));
+        }
+        out[PK_WIN_MASK / 4 + i] = m;
+    }
+    out[0] = make_int4(ok, r.w, r.proc, r.clen);
+    out[1] = make_int4(r.len, nb, nfirst, r.slot);
 }
 
+// One CTA, one thread per batch row (two for batch > 1024).  Every row keeps
+// its owner thread through all phases, so only the scans cross threads.
 __global__ void __launch_bounds__(kAllocThreads)
     pages_begin_kernel(pk_paged_kv_desc d, const int32_t *slots, const int32_t *lengths,
                        int batch, const int32_t *released, int num_released) {
+    extern __shared__ __align__(16) int s_dyn[];
     __shared__ typename Scan::TempStorage scan_tmp;
-    __shared__ int64_t s_head, s_tail;
-    __shared__ int s_fail;
+    __shared__ int64_t s_ctr[2];
+    RowState *rows = reinterpret_cast<RowState *>(s_dyn);
+    int *rings = s_dyn + batch * (int)(sizeof(RowState) / sizeof(int));
     const int tid = threadIdx.x;
-    const int N = d.num_pages;
+    const int N = d.num_pages, rmask = d.ring - 1;
+    const int nk = (batch + kAllocThreads - 1) / kAllocThreads;
 
+    // inputs first: they do not depend on the releases below
+    for (int k = 0; k < nk; ++k) {
+        const int b = tid + k * kAllocThreads;
+        if (b < batch) {
+            rows[b].slot = slots[b];
+            rows[b].len = lengths ? lengths[b] : d.chunk;
+        }
+    }
     if (tid == 0) {
-        s_head = d.ring_ctr[0];
-        s_tail = d.ring_ctr[1];
-        s_fail = 0;
+        int64_t tail = d.ring_ctr[1];
+        s_ctr[0] = d.ring_ctr[0];
         // 0. releases, in release order (serial: a handful of pages each)
         for (int r = 0; r < num_released; ++r) {
             const int s = released[r];
@@ -132,105 +138,114 @@ __global__ void __launch_bounds__(kAllocThreads)
             }
             int32_t *m = d.meta + (int64_t)s * PK_META_STRIDE;
             for (int pg = m[PK_META_FIRST]; pg < m[PK_META_NEXT]; ++pg) {
-                int32_t *e = d.page_table + (int64_t)s * d.ring + (pg & (d.ring - 1));
-                d.free_ring[ring_idx(s_tail++, N)] = *e;
+                int32_t *e = d.page_table + (int64_t)s * d.ring + (pg & rmask);
+                d.free_ring[tail++ % N] = *e;
                 *e = -1;
             }
             for (int f = 0; f < PK_META_STRIDE; ++f) m[f] = 0;
         }
+        s_ctr[1] = tail;
     }
     __syncthreads();
 
-    // this thread's batch rows b = tid + k * 1024 and their counters, read once
-    int slot[kRowsPerThread], first[kRowsPerThread], next[kRowsPerThread], wr[kRowsPerThread];
-#pragma unroll
-    for (int k = 0; k < kRowsPerThread; ++k) {
+    // counters and page-table ring of each row (after the releases reset theirs)
+    for (int k = 0; k < nk; ++k) {
         const int b = tid + k * kAllocThreads;
-        slot[k] = -1;
-        first[k] = next[k] = wr[k] = 0;
-        if (b < batch) {
-            const int s = slots[b];
-            if (s >= 0 && s < d.num_slots) {
-                const int32_t *m = d.meta + (int64_t)s * PK_META_STRIDE;
-                slot[k] = s;
-                first[k] = m[PK_META_FIRST];
-                next[k] = m[PK_META_NEXT];
-                wr[k] = m[PK_META_WRITTEN];
-            } else {
-                raise(d.error, PK_DEV_BAD_SLOT);
-            }
+        if (b >= batch) continue;
+        RowState &r = rows[b];
+        const int s = r.slot;
+        r.valid = s >= 0 && s < d.num_slots;
+        r.first = r.next = r.w = r.proc = r.clen = 0;
+        if (r.valid) {
+            const int32_t *m = d.meta + (int64_t)s * PK_META_STRIDE;
+            const int32_t *pt = d.page_table + (int64_t)s * d.ring;
+            r.first = m[PK_META_FIRST];
+            r.next = m[PK_META_NEXT];
+            r.w = m[PK_META_WRITTEN];
+            r.proc = m[PK_META_PROCESSED];
+            r.clen = m[PK_META_CACHE_LEN];
+#pragma unroll
+            for (int p = 0; p < PK_WIN_MAX_PAGES; ++p)
+                if (p <= rmask) rings[b * PK_WIN_MAX_PAGES + p] = pt[p];
+        } else {
+            r.len = d.chunk;
+            raise(d.error, PK_DEV_BAD_SLOT);
         }
     }
+    int64_t head = s_ctr[0], tail = s_ctr[1];
 
-    // 1. frees: pages n with (n + 1) * page_size <= written - left, batch order
-#pragma unroll
-    for (int k = 0; k < kRowsPerThread; ++k) {
-        if (k * kAllocThreads >= batch) break;
+    // 1. frees: pages n < (written - left) / page_size still held, batch order
+    for (int k = 0; k < nk; ++k) {
+        const int b = tid + k * kAllocThreads;
         int nfree = 0;
-        if (slot[k] >= 0) {
-            const int lim = wr[k] - d.left;
-            while (first[k] + nfree < next[k] && (first[k] + nfree + 1) * d.page_size <= lim) ++nfree;
+        if (b < batch && rows[b].valid) {
+            const int lim = rows[b].w - d.left;   // C division: <= 0 pages for lim < page_size
+            nfree = max(0, min(rows[b].next, lim / d.page_size) - rows[b].first);
         }
         int off, total;
         Scan(scan_tmp).ExclusiveSum(nfree, off, total);
         if (nfree > 0) {
-            int32_t *row = d.page_table + (int64_t)slot[k] * d.ring;
+            RowState &r = rows[b];
+            int32_t *pt = d.page_table + (int64_t)r.slot * d.ring;
             for (int j = 0; j < nfree; ++j) {
-                int32_t *e = row + ((first[k] + j) & (d.ring - 1));
-                d.free_ring[ring_idx(s_tail + off + j, N)] = *e;
-                *e = -1;
+                const int pos = (r.first + j) & rmask;
+                d.free_ring[(tail + off + j) % N] = rings[b * PK_WIN_MAX_PAGES + pos];
+                rings[b * PK_WIN_MAX_PAGES + pos] = -1;
+                pt[pos] = -1;
             }
-            first[k] += nfree;
-            d.meta[(int64_t)slot[k] * PK_META_STRIDE + PK_META_FIRST] = first[k];
+            r.first += nfree;
+            d.meta[(int64_t)r.slot * PK_META_STRIDE + PK_META_FIRST] = r.first;
         }
-        __syncthreads();
-        if (tid == 0) s_tail += total;
-        __syncthreads();
+        tail += total;
+        __syncthreads();   // scan storage reuse; pushed entries visible to the pops
     }
 
     // 2. allocations from the head, batch order; all-or-nothing like the CPU model
-    int need[kRowsPerThread];
     int demand = 0;
-#pragma unroll
-    for (int k = 0; k < kRowsPerThread; ++k) {
-        need[k] = 0;
-        if (slot[k] >= 0) need[k] = max(0, (wr[k] + d.chunk - 1) / d.page_size - next[k] + 1);
-        demand += need[k];
+    for (int k = 0; k < nk; ++k) {
+        const int b = tid + k * kAllocThreads;
+        if (b < batch && rows[b].valid)
+            demand += max(0, (rows[b].w + d.chunk - 1) / d.page_size - rows[b].next + 1);
     }
     int demand_off, total_demand;
     Scan(scan_tmp).ExclusiveSum(demand, demand_off, total_demand);
     __syncthreads();
-    if (tid == 0 && (int64_t)total_demand > s_tail - s_head) {
-        s_fail = 1;
-        raise(d.error, PK_DEV_POOL_EXHAUSTED);
-    }
-    __syncthreads();
-    if (!s_fail) {
-#pragma unroll
-        for (int k = 0; k < kRowsPerThread; ++k) {
-            if (k * kAllocThreads >= batch) break;
+    if ((int64_t)total_demand > tail - head) {   // block-uniform
+        if (tid == 0) raise(d.error, PK_DEV_POOL_EXHAUSTED);
+    } else {
+        for (int k = 0; k < nk; ++k) {
+            const int b = tid + k * kAllocThreads;
+            int need = 0;
+            if (b < batch && rows[b].valid)
+                need = max(0, (rows[b].w + d.chunk - 1) / d.page_size - rows[b].next + 1);
             int off, total;
-            Scan(scan_tmp).ExclusiveSum(need[k], off, total);
-            if (need[k] > 0) {
-                int32_t *row = d.page_table + (int64_t)slot[k] * d.ring;
-                for (int j = 0; j < need[k]; ++j)
-                    row[(next[k] + j) & (d.ring - 1)] = d.free_ring[ring_idx(s_head + off + j, N)];
-                d.meta[(int64_t)slot[k] * PK_META_STRIDE + PK_META_NEXT] = next[k] + need[k];
+            Scan(scan_tmp).ExclusiveSum(need, off, total);
+            if (need > 0) {
+                RowState &r = rows[b];
+                int32_t *pt = d.page_table + (int64_t)r.slot * d.ring;
+                for (int j = 0; j < need; ++j) {
+                    const int pos = (r.next + j) & rmask;
+                    const int page = d.free_ring[(head + off + j) % N];
+                    rings[b * PK_WIN_MAX_PAGES + pos] = page;
+                    pt[pos] = page;
+                }
+                r.next += need;
+                d.meta[(int64_t)r.slot * PK_META_STRIDE + PK_META_NEXT] = r.next;
             }
-            __syncthreads();
-            if (tid == 0) s_head += total;
+            head += total;
             __syncthreads();
         }
     }
     if (tid == 0) {
-        d.ring_ctr[0] = s_head;
-        d.ring_ctr[1] = s_tail;
+        d.ring_ctr[0] = head;
+        d.ring_ctr[1] = tail;
     }
-    __syncthreads();   // page table of this step visible to every warp of the block
 
-    // 3. window descriptors, one warp per batch row
-    const int warp = tid / 32, lane = tid % 32;
-    for (int b = warp; b < batch; b += kAllocThreads / 32) build_window(d, slots, lengths, b, lane);
+    // 3. window descriptors: each thread its own rows
+    for (int k = 0; k < nk; ++k) {
+        const int b = tid + k * kAllocThreads;
+        if (b < batch) write_window(d, rows[b], rings + b * PK_WIN_MAX_PAGES, b);
+    }
 }
 
 __global__ void pages_end_kernel(pk_paged_kv_desc d, const int32_t *slots, const int32_t *lengths,
@@ -258,9 +273,19 @@ int launch_pages_reset(const pk_paged_kv *kv, const int32_t *init_order, cudaStr
 
 int launch_pages_begin(const pk_paged_kv *kv, const int32_t *slots, const int32_t *lengths,
                        int batch, const int32_t *released, int num_released, cudaStream_t s) {
-    if (batch > kAllocThreads * kRowsPerThread) return PK_ENOTSUP;
-    pages_begin_kernel<<<1, kAllocThreads, 0, s>>>(kv->d, slots, lengths, batch, released,
-                                                   num_released);
+    if (batch > kMaxBatch || kv->d.ring > PK_WIN_MAX_PAGES) return PK_ENOTSUP;
+    const size_t smem = (size_t)batch * (sizeof(RowState) + PK_WIN_MAX_PAGES * sizeof(int));
+    static size_t limit = 48 * 1024;
+    if (smem > limit) {
+        cudaError_t e = cudaFuncSetAttribute(pages_begin_kernel,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)(kMaxBatch * (sizeof(RowState) +
+                                                                PK_WIN_MAX_PAGES * sizeof(int))));
+        if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(pages_begin)");
+        limit = kMaxBatch * (sizeof(RowState) + PK_WIN_MAX_PAGES * sizeof(int));
+    }
+    pages_begin_kernel<<<1, kAllocThreads, smem, s>>>(kv->d, slots, lengths, batch, released,
+                                                      num_released);
     return cuda_status(cudaGetLastError(), "pages_begin_kernel");
 }
 
