@@ -95,6 +95,15 @@ __global__ void __launch_bounds__(kThreads, 2)
     float *sBD = reinterpret_cast<float *>(smem + g.off_bd);  // [16 rows][bd_stride]
     char *sP = smem + g.off_p;                                // [box][16 rows][kPStride B]
 
+    if (warp == kH && lane == 0) {
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kH);
+        }
+        fence_mbar_init();
+        s_abort = 0;
+    }
+    grid_dep_wait();   // descriptors, pages and q may come from the previous kernel
     if (warp == kH) {
         // window descriptor of this stream (written by pk_pages_begin_step)
         const int32_t *wd = d.window + (int64_t)b * PK_WIN_STRIDE;
@@ -110,12 +119,6 @@ __global__ void __launch_bounds__(kThreads, 2)
             s_w = wd[PK_WIN_W];
             s_nfirst = wd[PK_WIN_NFIRST];
             s_nb = nb;
-            s_abort = 0;
-            for (int s = 0; s < NS; ++s) {
-                mbar_init(&full[s], 1);
-                mbar_init(&empty[s], kH);
-            }
-            fence_mbar_init();
         }
     }
     __syncthreads();
@@ -320,6 +323,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (sub == 0) s_rowsum[row] = sum;
     }
     consumer_sync();   // probabilities visible
+    grid_dep_launch();   // the step's next kernel may be scheduled (it waits for us)
 
     // ---- pass 2: O_h = P V_h over the V pages
     float o[4][2][4];
@@ -406,8 +410,9 @@ int launch_attention_stacked(const pk_paged_kv *kv, const CUtensorMap &pos_map16
         limit = smem;
     }
     dim3 grid(a.batch, a.nlayers);
-    paged_attn_stacked_kernel<NS><<<grid, kThreads, smem, s>>>(kv->kv_map, pos_map16, g, d, a);
-    return cuda_status(cudaGetLastError(), "paged_attn_stacked_kernel");
+    return cuda_status(launch_pdl(paged_attn_stacked_kernel<NS>, grid, dim3(kThreads), smem, s,
+                                  kv->kv_map, pos_map16, g, d, a),
+                       "paged_attn_stacked_kernel");
 }
 
 }  // namespace pk

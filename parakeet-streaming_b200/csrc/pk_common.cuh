@@ -47,6 +47,19 @@ __device__ __forceinline__ void raise(int32_t *error, int bits) {
     if (error) atomicOr(error, bits);
 }
 
+// ------------------------------------------------- programmatic dependent launch
+// A kernel launched with programmatic stream serialization may start while the
+// kernel before it in the stream still runs.  grid_dep_wait() blocks until that
+// kernel has completed and its writes are visible (a no-op for a plain launch);
+// nothing the previous kernel may have written is read before it.
+// grid_dep_launch() lets the next such kernel start being scheduled.
+__device__ __forceinline__ void grid_dep_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dep_launch() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- smem / PTX
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));

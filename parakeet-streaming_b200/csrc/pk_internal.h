@@ -26,6 +26,25 @@ int encode_tmap_3d(CUtensorMap *map, int dtype, const void *base, uint64_t d0, u
                    uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box0,
                    uint32_t box1, uint32_t box2);
 
+// Launch with programmatic stream serialization: the kernel may be scheduled
+// while the previous kernel of the stream finishes, and must call
+// grid_dep_wait() before it reads anything that kernel could have written.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t s, Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args &&>(args)...);
+}
+
 // pk_pages.cu
 int launch_pages_reset(const pk_paged_kv *kv, const int32_t *init_order, cudaStream_t s);
 int launch_pages_begin(const pk_paged_kv *kv, const int32_t *slots, const int32_t *lengths,

@@ -117,6 +117,8 @@ __global__ void __launch_bounds__(kAllocThreads)
     const int tid = threadIdx.x;
     const int N = d.num_pages, rmask = d.ring - 1;
     const int nk = (batch + kAllocThreads - 1) / kAllocThreads;
+    grid_dep_wait();     // the previous step's counters and this step's inputs
+    grid_dep_launch();   // the step's attention may be scheduled (it waits for us)
 
     // inputs first: they do not depend on the releases below
     for (int k = 0; k < nk; ++k) {
@@ -251,6 +253,8 @@ __global__ void __launch_bounds__(kAllocThreads)
 __global__ void pages_end_kernel(pk_paged_kv_desc d, const int32_t *slots, const int32_t *lengths,
                                  int batch) {
     const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    grid_dep_wait();
+    grid_dep_launch();
     if (b >= batch) return;
     const int s = slots[b];
     if (s < 0 || s >= d.num_slots) {
@@ -284,16 +288,17 @@ int launch_pages_begin(const pk_paged_kv *kv, const int32_t *slots, const int32_
         if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(pages_begin)");
         limit = kMaxBatch * (sizeof(RowState) + PK_WIN_MAX_PAGES * sizeof(int));
     }
-    pages_begin_kernel<<<1, kAllocThreads, smem, s>>>(kv->d, slots, lengths, batch, released,
-                                                      num_released);
-    return cuda_status(cudaGetLastError(), "pages_begin_kernel");
+    return cuda_status(launch_pdl(pages_begin_kernel, dim3(1), dim3(kAllocThreads), smem, s,
+                                  kv->d, slots, lengths, batch, released, num_released),
+                       "pages_begin_kernel");
 }
 
 int launch_pages_end(const pk_paged_kv *kv, const int32_t *slots, const int32_t *lengths,
                      int batch, cudaStream_t s) {
     if (batch == 0) return PK_OK;
-    pages_end_kernel<<<(batch + 255) / 256, 256, 0, s>>>(kv->d, slots, lengths, batch);
-    return cuda_status(cudaGetLastError(), "pages_end_kernel");
+    return cuda_status(launch_pdl(pages_end_kernel, dim3((batch + 255) / 256), dim3(256), 0, s,
+                                  kv->d, slots, lengths, batch),
+                       "pages_end_kernel");
 }
 
 }  // namespace pk
