@@ -38,6 +38,11 @@ constexpr int kBox = 2048;               // one head's 16 rows x 128 bytes
 constexpr int kMaxBoxes = 8;             // pages per window handled
 constexpr int kMaxPosBlocks = 8;         // rel-pos blocks of 16 rows (R <= 128)
 constexpr int kPStride = 48;             // bytes per row of a 16x16 bf16 probability tile
+// Three CTAs per SM with a 3-stage ring (68 KB of shared memory each) beat two with
+// 4 or 5 stages: the kernel is bound by how many page reads are in flight per SM,
+// and a third CTA adds more of them than deeper rings do.
+constexpr int kStages = 3;
+constexpr int kCtasPerSm = 3;
 
 struct SGeom {
     int num_layers, left, chunk, W, R, npb, max_boxes;
@@ -72,7 +77,7 @@ __device__ __forceinline__ void consumer_sync() {
 }
 
 template <int NS>
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads, kCtasPerSm)
     paged_attn_stacked_kernel(const __grid_constant__ CUtensorMap kv_map,
                               const __grid_constant__ CUtensorMap pos_map, const SGeom g,
                               const pk_paged_kv_desc d, const AttnArgs a) {
@@ -386,7 +391,7 @@ int launch_attention_stacked(const pk_paged_kv *kv, const CUtensorMap &pos_map16
     if (d.dtype != PK_DTYPE_BF16 || kv->head_dim != 64 || d.num_heads != kH ||
         d.num_heads * d.chunk > 16 || d.page_size != 16)
         return PK_ENOTSUP;
-    constexpr int NS = 4;
+    constexpr int NS = kStages;
     SGeom g;
     g.num_layers = d.num_layers;
     g.left = d.left;
