@@ -4,23 +4,49 @@
 // The reference keeps one dense window per slot (parakeet/modules/cache.py:24-29)
 // and hands out slots from a FIFO deque (parakeet/engine/scheduler.py:84,93-104).
 // Here every slot owns a ring of page-table entries and pages come from one
-// FIFO free ring.  One CTA runs each step's releases, frees and allocations in
-// batch order with block-wide scans, so the page-id sequence is deterministic
-// and equals the CPU model op for op; the same CTA then writes, one warp per
-// batch row, the row's window descriptor: its pages, the first row of each
-// page's TMA box, and the streaming mask of ConformerEncoder.
+// FIFO free ring.  One CTA, one thread per batch row, runs each step's
+// releases, frees and allocations in batch order with block-wide scans, so the
+// page-id sequence is deterministic and equals the CPU model op for op; each
+// row's thread then writes the row's window descriptor: its pages, the first
+// row of each page's TMA box, and the streaming mask of ConformerEncoder.
 // _create_streaming_masks (parakeet/modules/encoder.py:167-227) as bit rows.
-#include <cub/block/block_scan.cuh>
-
 #include "pk_common.cuh"
 #include "pk_internal.h"
 
 namespace pk {
 namespace {
 
-constexpr int kAllocThreads = 1024;
+constexpr int kAllocThreads = 1024;            // most threads of the step-start CTA
 constexpr int kMaxBatch = 2 * kAllocThreads;
-using Scan = cub::BlockScan<int, kAllocThreads>;
+
+// Exclusive prefix sum of v over the CTA (blockDim.x a multiple of 32), in batch
+// order of the threads; `total` gets the CTA's sum.  s_warp: 33 ints of scratch.
+__device__ int block_exclusive_sum(int v, int &total, int *s_warp) {
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) s_warp[wid] = x;
+    __syncthreads();
+    if (wid == 0) {
+        int t = lane < nw ? s_warp[lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, t, o);
+            if (lane >= o) t += y;
+        }
+        if (lane < nw) s_warp[lane] = t;   // inclusive over warps
+        if (lane == 31) s_warp[32] = t;
+    }
+    __syncthreads();
+    total = s_warp[32];
+    const int res = (wid > 0 ? s_warp[wid - 1] : 0) + x - v;
+    __syncthreads();   // scratch free for the next scan
+    return res;
+}
 
 __global__ void pages_reset_kernel(pk_paged_kv_desc d, const int32_t *init_order) {
     const int tid = blockIdx.x * blockDim.x + threadIdx.x;
@@ -110,19 +136,20 @@ __global__ void __launch_bounds__(kAllocThreads)
     pages_begin_kernel(pk_paged_kv_desc d, const int32_t *slots, const int32_t *lengths,
                        int batch, const int32_t *released, int num_released) {
     extern __shared__ __align__(16) int s_dyn[];
-    __shared__ typename Scan::TempStorage scan_tmp;
+    __shared__ int scan_tmp[33];
     __shared__ int64_t s_ctr[2];
     RowState *rows = reinterpret_cast<RowState *>(s_dyn);
     int *rings = s_dyn + batch * (int)(sizeof(RowState) / sizeof(int));
     const int tid = threadIdx.x;
     const int N = d.num_pages, rmask = d.ring - 1;
-    const int nk = (batch + kAllocThreads - 1) / kAllocThreads;
+    const int nthreads = blockDim.x;
+    const int nk = (batch + nthreads - 1) / nthreads;
     grid_dep_wait();     // the previous step's counters and this step's inputs
     grid_dep_launch();   // the step's attention may be scheduled (it waits for us)
 
     // inputs first: they do not depend on the releases below
     for (int k = 0; k < nk; ++k) {
-        const int b = tid + k * kAllocThreads;
+        const int b = tid + k * nthreads;
         if (b < batch) {
             rows[b].slot = slots[b];
             rows[b].len = lengths ? lengths[b] : d.chunk;
@@ -152,7 +179,7 @@ __global__ void __launch_bounds__(kAllocThreads)
 
     // counters and page-table ring of each row (after the releases reset theirs)
     for (int k = 0; k < nk; ++k) {
-        const int b = tid + k * kAllocThreads;
+        const int b = tid + k * nthreads;
         if (b >= batch) continue;
         RowState &r = rows[b];
         const int s = r.slot;
@@ -178,14 +205,14 @@ __global__ void __launch_bounds__(kAllocThreads)
 
     // 1. frees: pages n < (written - left) / page_size still held, batch order
     for (int k = 0; k < nk; ++k) {
-        const int b = tid + k * kAllocThreads;
+        const int b = tid + k * nthreads;
         int nfree = 0;
         if (b < batch && rows[b].valid) {
             const int lim = rows[b].w - d.left;   // C division: <= 0 pages for lim < page_size
             nfree = max(0, min(rows[b].next, lim / d.page_size) - rows[b].first);
         }
-        int off, total;
-        Scan(scan_tmp).ExclusiveSum(nfree, off, total);
+        int total;
+        const int off = block_exclusive_sum(nfree, total, scan_tmp);
         if (nfree > 0) {
             RowState &r = rows[b];
             int32_t *pt = d.page_table + (int64_t)r.slot * d.ring;
@@ -205,23 +232,22 @@ __global__ void __launch_bounds__(kAllocThreads)
     // 2. allocations from the head, batch order; all-or-nothing like the CPU model
     int demand = 0;
     for (int k = 0; k < nk; ++k) {
-        const int b = tid + k * kAllocThreads;
+        const int b = tid + k * nthreads;
         if (b < batch && rows[b].valid)
             demand += max(0, (rows[b].w + d.chunk - 1) / d.page_size - rows[b].next + 1);
     }
-    int demand_off, total_demand;
-    Scan(scan_tmp).ExclusiveSum(demand, demand_off, total_demand);
-    __syncthreads();
+    int total_demand;
+    block_exclusive_sum(demand, total_demand, scan_tmp);
     if ((int64_t)total_demand > tail - head) {   // block-uniform
         if (tid == 0) raise(d.error, PK_DEV_POOL_EXHAUSTED);
     } else {
         for (int k = 0; k < nk; ++k) {
-            const int b = tid + k * kAllocThreads;
+            const int b = tid + k * nthreads;
             int need = 0;
             if (b < batch && rows[b].valid)
                 need = max(0, (rows[b].w + d.chunk - 1) / d.page_size - rows[b].next + 1);
-            int off, total;
-            Scan(scan_tmp).ExclusiveSum(need, off, total);
+            int total;
+            const int off = block_exclusive_sum(need, total, scan_tmp);
             if (need > 0) {
                 RowState &r = rows[b];
                 int32_t *pt = d.page_table + (int64_t)r.slot * d.ring;
@@ -245,7 +271,7 @@ __global__ void __launch_bounds__(kAllocThreads)
 
     // 3. window descriptors: each thread its own rows
     for (int k = 0; k < nk; ++k) {
-        const int b = tid + k * kAllocThreads;
+        const int b = tid + k * nthreads;
         if (b < batch) write_window(d, rows[b], rings + b * PK_WIN_MAX_PAGES, b);
     }
 }
@@ -288,8 +314,11 @@ int launch_pages_begin(const pk_paged_kv *kv, const int32_t *slots, const int32_
         if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(pages_begin)");
         limit = kMaxBatch * (sizeof(RowState) + PK_WIN_MAX_PAGES * sizeof(int));
     }
-    return cuda_status(launch_pdl(pages_begin_kernel, dim3(1), dim3(kAllocThreads), smem, s,
-                                  kv->d, slots, lengths, batch, released, num_released),
+    // one thread per row up to 1024 rows: small batches scan over a few warps only
+    int threads = batch >= kAllocThreads ? kAllocThreads : (batch + 31) / 32 * 32;
+    if (threads == 0) threads = 32;
+    return cuda_status(launch_pdl(pages_begin_kernel, dim3(1), dim3(threads), smem, s, kv->d,
+                                  slots, lengths, batch, released, num_released),
                        "pages_begin_kernel");
 }
 

@@ -41,10 +41,14 @@ def assert_pool_equals_model(pool, model):
     assert free == list(model.free)
 
 
-@pytest.mark.parametrize("att,cap", [((70, 1), 0.6), ((70, 13), 0.6), ((70, 1), 1.0)])
-def test_page_allocator_matches_cpu_model(att, cap):
+@pytest.mark.parametrize("att,cap,n_slots,arrivals", [((70, 1), 0.6, 24, 4), ((70, 13), 0.6, 24, 4),
+                                                      ((70, 1), 1.0, 24, 4),
+                                                      ((70, 1), 0.8, 1100, 120)])
+def test_page_allocator_matches_cpu_model(att, cap, n_slots, arrivals):
+    """Device allocator vs the CPU model, op for op; the 1100-slot case runs
+    batches above 1024 rows (two rows per thread of the step-start CTA)."""
     rng = np.random.default_rng(7)
-    left, T, ps, n_slots = att[0], att[1] + 1, 16, 24
+    left, T, ps = att[0], att[1] + 1, 16
     per = pages.pages_per_stream(left, T, ps)
     n_pages = int(cap * n_slots * per)
     order = np.random.default_rng(1).permutation(n_pages)
@@ -60,7 +64,7 @@ def test_page_allocator_matches_cpu_model(att, cap):
                 alloc.release(s)
                 pool.release_slot(s)
                 model.release_slot(s)
-        for _ in range(int(rng.integers(0, 4))):
+        for _ in range(int(rng.integers(0, arrivals))):
             s = alloc.acquire()
             if s is not None:
                 live.append(s)
