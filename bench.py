@@ -5,10 +5,12 @@ Workload: one isolated paged-attention step of the
 small model, bf16 - 80 streams x 17 layers, 8 heads of 64, chunk of 2 frames
 over 70 cached left-context frames (window 72), 16-frame pages, the free
 list a random permutation of the pool (seed 1), Q/K/V and the rel-pos
-projection N(0,1)/8.  A step is: page allocator (begin) -> paged append of
-the chunk's K/V for all 17 layers -> paged rel-pos attention for all 17
-layers -> counter update (end).  Streams are independent, so N GPUs run N
-replicas with no collective on the data path (weak scaling).
+projection N(0,1)/8.  A step is three launches: step start (page allocator
+and window descriptors) -> paged rel-pos attention for all 17 layers with the
+chunk's K/V append fused in -> counter update (end).  Streams are
+independent, so N GPUs run N replicas with no collective on the data path
+(weak scaling): each rank owns its own pool and streams, and the only
+collectives are the timing barriers and one max-reduce of the timings.
 
 Metric: paged-attn HBM GB/s = algorithmic bytes of the step / step time.
 Algorithmic bytes per stream-layer (bf16): append 8,192 (read new K,V,
@@ -196,6 +198,23 @@ def run_reference_arm(args):
                 "d2h_bytes_per_step": 0},
         "bytes_per_stream_layer": {"append": b["append"], "attention": b["attention"]},
     }), flush=True)
+
+
+def max_over_ranks(vals, device):
+    """Element-wise max of per-rank timings over the process group (the step
+    time of a weak-scaling run is its slowest rank's); identity on one rank."""
+    import torch
+    import torch.distributed as dist
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return list(vals)
+    t = torch.tensor(list(vals), dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
+def job_throughput(bytes_per_rank_step, world, ms):
+    """Whole-job GB/s: every rank moved bytes_per_rank_step per step, in ms (max over ranks)."""
+    return bytes_per_rank_step * world / (ms * 1e-3) / 1e9
 
 
 # ---------------------------------------------------------------- B200 arm
@@ -397,10 +416,7 @@ def main():
                                "frac": round(nbytes / t / 1e6 / hbm, 3), "launches": launches,
                                "bytes_per_stream_layer": nbytes // units}
 
-    if world > 1:
-        t = torch.tensor([ms, e2e_ms, attn_ms, eager_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, e2e_ms, attn_ms, eager_ms = t.tolist()
+    ms, e2e_ms, attn_ms, eager_ms = max_over_ranks([ms, e2e_ms, attn_ms, eager_ms], dev)
 
     if rank == 0:
         hbm, kind = peaks()
@@ -419,8 +435,8 @@ def main():
             gbs, done, el, threads, sample = cpu_reference(args, args.cpu_seconds)
             cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port",
                    "sample": sample}
-        value = step_bytes * world / (ms * 1e-3) / 1e9
-        e2e = step_bytes * world / (e2e_ms * 1e-3) / 1e9
+        value = job_throughput(step_bytes, world, ms)
+        e2e = job_throughput(step_bytes, world, e2e_ms)
         line = {
             "metric": "paged-attn HBM GB/s (append + attention, algorithmic bytes)",
             "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": K,

@@ -112,7 +112,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
     return true;
 }
 
-// 3-D tiled TMA load global -> shared, completion on `bar` (no multicast).
+// 3-D tiled TMA load global -> this CTA's shared memory, completion on `bar`.
 __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, uint64_t *bar,
                                             int32_t c0, int32_t c1, int32_t c2) {
     asm volatile(
@@ -123,7 +123,7 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, u
 }
 
 // Untiled bulk copy global -> shared (16-byte aligned, size a multiple of 16),
-// completion on `bar` (no multicast).
+// into this CTA's shared memory, completion on `bar`.
 __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes,
                                           uint64_t *bar) {
     asm volatile(
