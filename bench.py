@@ -378,18 +378,33 @@ def main():
     # ---- per-op breakdown (separate loops, same pool)
     breakdown = {}
     if not args.no_breakdown and rank == 0:
+        flush_w = torch.empty(256 << 20, dtype=torch.uint8, device=dev)   # 2x L2
+        flush_r = torch.ones(64 << 20, dtype=torch.int32, device=dev)     # 2x L2
+
         def timeit(fn, n=20):
+            """Device time of fn's launches: captured once as a CUDA graph (no host
+            launch cost), each replay timed with events after an L2 flush (a
+            256 MB write, then a 256 MB read that writes its dirty lines back)."""
             for _ in range(3):
                 fn()
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             torch.cuda.synchronize()
-            a.record()
-            for _ in range(n):
+            gph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gph):
                 fn()
-            b.record()
-            torch.cuda.synchronize()
-            return a.elapsed_time(b) / n
+            gph.replay()
+            total = 0.0
+            for _ in range(n):
+                flush_w.zero_()
+                flush_r.sum()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                gph.replay()
+                b.record()
+                b.synchronize()
+                total += a.elapsed_time(b)
+            return total / n
         kv_out = [torch.empty(B, W, D, dtype=dt, device=dev) for _ in range(2)]
+        kv_all = [torch.empty(L, B, W, D, dtype=dt, device=dev) for _ in range(2)]
         x2 = rnd(B, T, 2 * D)
         wconv = rnd(D, 1, 9)
         lnw, lnb = rnd(D) + 1, rnd(D)
@@ -405,6 +420,8 @@ def main():
                                  (nb["attention"] + nb["append"]) * units, 1),
             "gather": (lambda: [pool.gather(l, slots, *kv_out) for l in range(L)],
                        nb["gather"] * units, L),
+            "gather_all_layers": (lambda: pool.gather_layers(0, L, slots, *kv_all),
+                                  nb["gather"] * units, 1),
             "conv": (lambda: [pool.conv_step(l, x2, wconv, slots, lengths, lnw, lnb, 1e-5, yconv)
                               for l in range(L)], nb["conv"] * units, L),
         }

@@ -152,6 +152,14 @@ int pk_append_kv(pk_paged_kv *kv, int32_t layer0, int32_t num_layers,
 int pk_gather_window(pk_paged_kv *kv, int32_t layer, const int32_t *slots,
                      int32_t batch, void *k_out, void *v_out, void *stream);
 
+/* pk_gather_window for layers [layer0, layer0 + num_layers) in one launch:
+ * layer l's windows at k_out / v_out + (l - layer0) * out_layer_stride
+ * elements (>= batch * (left + chunk) * dim, 16-byte multiple).  Same
+ * replaced calls, for callers that materialise every layer of a step. */
+int pk_gather_windows(pk_paged_kv *kv, int32_t layer0, int32_t num_layers,
+                      const int32_t *slots, int32_t batch, void *k_out, void *v_out,
+                      int64_t out_layer_stride, void *stream);
+
 /* Chunked rel-pos multi-head self-attention over the paged window, for
  * layers [layer0, layer0 + num_layers).
  *   query  (l, b, t, c)  at l*q_layer_stride + b*q_batch_stride + t*q_row_stride + c

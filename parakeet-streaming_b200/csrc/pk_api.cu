@@ -208,7 +208,27 @@ int pk_gather_window(pk_paged_kv *kv, int32_t layer, const int32_t *slots, int32
     if (batch == 0) return PK_OK;
     PK_CHECK(slots && k_out && v_out, "null pointer");
     PK_CHECK(aligned16(k_out) && aligned16(v_out), "outputs not 16-byte aligned");
-    return launch_gather(kv, layer, slots, batch, k_out, v_out, static_cast<cudaStream_t>(stream));
+    return launch_gather(kv, layer, 1, slots, batch, k_out, v_out, 0,
+                         static_cast<cudaStream_t>(stream));
+}
+
+int pk_gather_windows(pk_paged_kv *kv, int32_t layer0, int32_t num_layers, const int32_t *slots,
+                      int32_t batch, void *k_out, void *v_out, int64_t out_layer_stride,
+                      void *stream) {
+    PK_CHECK(kv, "null pool");
+    PK_CHECK(batch >= 0 && num_layers >= 0 && layer0 >= 0 &&
+                 layer0 + num_layers <= kv->d.num_layers,
+             "layer range [%d, %d) outside [0, %d)", layer0, layer0 + num_layers,
+             kv->d.num_layers);
+    if (batch == 0 || num_layers == 0) return PK_OK;
+    PK_CHECK(slots && k_out && v_out, "null pointer");
+    PK_CHECK(aligned16(k_out) && aligned16(v_out), "outputs not 16-byte aligned");
+    const int64_t W = kv->d.left + kv->d.chunk;
+    PK_CHECK(num_layers == 1 || out_layer_stride >= (int64_t)batch * W * kv->d.dim,
+             "out_layer_stride below batch * window * dim");
+    PK_CHECK((out_layer_stride * kv->esize) % 16 == 0, "out_layer_stride not 16-byte aligned");
+    return launch_gather(kv, layer0, num_layers, slots, batch, k_out, v_out, out_layer_stride,
+                         static_cast<cudaStream_t>(stream));
 }
 
 int pk_paged_attention(pk_paged_kv *kv, int32_t layer0, int32_t num_layers, const void *query,

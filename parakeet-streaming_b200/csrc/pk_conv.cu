@@ -1,5 +1,8 @@
 // Depthwise causal conv with its time cache, fused with GLU, the pad mask,
-// LayerNorm and SiLU.  One CTA per stream, four channels per thread.
+// LayerNorm and SiLU.  One CTA per stream, two channels per thread.  A layer's
+// call moves about 1.8 MB for 80 streams, so the kernel is latency-bound: the
+// loads that do not depend on the slot go out before the slot's cache, and the
+// LayerNorm needs one block reduction.
 //
 // Restates ConformerConvolution.forward (parakeet/modules/convolution.py:
 // 150-162) from the GLU to the SiLU, with CausalConv1d.update_cache/forward
@@ -18,168 +21,205 @@ namespace {
 
 constexpr int kTMax = 16;  // frames per chunk handled by one thread's registers
 
-template <typename T>
-__device__ __forceinline__ void load4(const T *p, float *f) {
-    if constexpr (sizeof(T) == 2) {
-        const uint2 u = *reinterpret_cast<const uint2 *>(p);
-        const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&u.x));
-        const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&u.y));
-        f[0] = a.x, f[1] = a.y, f[2] = b.x, f[3] = b.y;
-    } else {
-        const float4 u = *reinterpret_cast<const float4 *>(p);
-        f[0] = u.x, f[1] = u.y, f[2] = u.z, f[3] = u.w;
-    }
-}
-
-template <typename T>
-__device__ __forceinline__ void store4(T *p, const float *f) {
-    if constexpr (sizeof(T) == 2) {
-        __nv_bfloat162 a = __floats2bfloat162_rn(f[0], f[1]);
-        __nv_bfloat162 b = __floats2bfloat162_rn(f[2], f[3]);
-        uint2 u;
-        u.x = *reinterpret_cast<uint32_t *>(&a);
-        u.y = *reinterpret_cast<uint32_t *>(&b);
-        *reinterpret_cast<uint2 *>(p) = u;
-    } else {
-        *reinterpret_cast<float4 *>(p) = make_float4(f[0], f[1], f[2], f[3]);
-    }
-}
-
 __device__ __forceinline__ float round_to(float v, const __nv_bfloat16 *) {
     return __bfloat162float(__float2bfloat16_rn(v));
 }
 __device__ __forceinline__ float round_to(float v, const float *) { return v; }
 
-// Sum of v over the CTA for every frame t < chunk; all threads get the sums.
-__device__ __forceinline__ void block_sum(float (&v)[kTMax], int chunk, float (*red)[8]) {
-    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, nw = blockDim.x / 32;
-#pragma unroll
-    for (int t = 0; t < kTMax; ++t) {
-        if (t >= chunk) break;
-        float x = v[t];
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
-        if (lane == 0) red[t][warp] = x;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int t = 0; t < kTMax; ++t) {
-        if (t >= chunk) break;
-        float x = 0.f;
-        for (int k = 0; k < nw; ++k) x += red[t][k];
-        v[t] = x;
-    }
-    __syncthreads();
+// (count, mean, M2) of a set of values; two sets combine exactly (Chan et al.'s
+// pairwise update), so one reduction gives the LayerNorm mean and variance
+// with the accuracy of the two-pass formula.
+struct Moments {
+    float n, mean, m2;
+};
+__device__ __forceinline__ Moments combine(const Moments &a, const Moments &b) {
+    const float n = a.n + b.n;
+    if (n == 0.f) return a;
+    const float delta = b.mean - a.mean, fb = __fdividef(b.n, n);
+    return {n, a.mean + delta * fb, a.m2 + b.m2 + delta * delta * a.n * fb};
 }
 
-template <typename T, int K>
-__global__ void __launch_bounds__(256) conv_step_kernel(const ConvArgs a) {
-    constexpr int KC = K - 1;
-    __shared__ float red[kTMax][8];
-    const int b = blockIdx.x;
-    const int s = a.slots[b];
-    if (s < 0 || s >= a.num_slots) {
-        if (threadIdx.x == 0) raise(a.error, PK_DEV_BAD_SLOT);
-        return;
+template <typename T>
+__device__ __forceinline__ void load2(const T *p, float *f) {
+    if constexpr (sizeof(T) == 2) {
+        const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(p));
+        f[0] = a.x, f[1] = a.y;
+    } else {
+        const float2 u = *reinterpret_cast<const float2 *>(p);
+        f[0] = u.x, f[1] = u.y;
     }
-    const int D = a.dim, chunk = a.chunk;
-    const int n = a.lengths[b];
-    const int c0 = threadIdx.x * 4;
-    const bool active = c0 < D;
+}
+template <typename T>
+__device__ __forceinline__ void store2(T *p, const float *f) {
+    if constexpr (sizeof(T) == 2)
+        *reinterpret_cast<__nv_bfloat162 *>(p) = __floats2bfloat162_rn(f[0], f[1]);
+    else
+        *reinterpret_cast<float2 *>(p) = make_float2(f[0], f[1]);
+}
+// a channel's K-1 = 8 cached frames: 16 bytes in bf16
+template <typename T, int KC>
+__device__ __forceinline__ void load_cache(const T *p, float *h) {
+    if constexpr (sizeof(T) == 2 && KC == 8) {
+        const uint4 u = *reinterpret_cast<const uint4 *>(p);
+        unpack16(u, h, static_cast<const __nv_bfloat16 *>(nullptr));
+    } else {
+#pragma unroll
+        for (int k = 0; k < KC; ++k) h[k] = Elem<T>::to_f(p[k]);
+    }
+}
+template <typename T, int KC>
+__device__ __forceinline__ void store_cache(T *p, const float *h) {
+    if constexpr (sizeof(T) == 2 && KC == 8) {
+        uint4 u;
+        uint32_t *w = reinterpret_cast<uint32_t *>(&u);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            __nv_bfloat162 v = __floats2bfloat162_rn(h[2 * i], h[2 * i + 1]);
+            w[i] = *reinterpret_cast<uint32_t *>(&v);
+        }
+        *reinterpret_cast<uint4 *>(p) = u;
+    } else {
+#pragma unroll
+        for (int k = 0; k < KC; ++k) p[k] = Elem<T>::from_f(h[k]);
+    }
+}
+__device__ __forceinline__ float sigmoid(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
 
-    float hist[4][KC + kTMax];
-    float y[4][kTMax];
-    T *cache = static_cast<T *>(a.state) + (((int64_t)s * a.num_layers + a.layer) * D + c0) * KC;
+constexpr int kCpt = 2;   // channels per thread
+
+// One CTA per stream, kCpt channels per thread; TM >= chunk frames in registers.
+// Every load that does not depend on the slot id goes out first, the cache
+// follows the slot, and LayerNorm takes one block reduction per frame.
+template <typename T, int K, int TM>
+__global__ void __launch_bounds__(512) conv_step_kernel(const ConvArgs a) {
+    constexpr int KC = K - 1;
+    __shared__ Moments red[TM][16];
+    const int b = blockIdx.x;
+    const int D = a.dim, chunk = a.chunk;
+    const int c0 = threadIdx.x * kCpt;
+    const bool active = c0 < D;
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, nw = blockDim.x / 32;
+
+    // inputs that do not depend on the slot: the GLU input rows, taps, LN affine
+    float va[TM][kCpt], vg[TM][kCpt], wk[kCpt][K], g[kCpt] = {0.f, 0.f}, be[kCpt] = {0.f, 0.f};
+    const int s = a.slots[b];
+    const int n = a.lengths[b];
     if (active) {
-#pragma unroll
-        for (int ch = 0; ch < 4; ++ch)
-#pragma unroll
-            for (int k = 0; k < KC; ++k) hist[ch][k] = Elem<T>::to_f(cache[ch * KC + k]);
         const T *xb = static_cast<const T *>(a.x) + (int64_t)b * a.x_bs;
 #pragma unroll
-        for (int t = 0; t < kTMax; ++t) {
+        for (int t = 0; t < TM; ++t) {
             if (t >= chunk) break;
-            float va[4], vg[4];
-            load4<T>(xb + (int64_t)t * a.x_rs + c0, va);
-            load4<T>(xb + (int64_t)t * a.x_rs + D + c0, vg);
-#pragma unroll
-            for (int ch = 0; ch < 4; ++ch) {
-                // F.glu then masked_fill(pad_mask, 0) (convolution.py:153-155)
-                const float v = round_to(va[ch] / (1.f + expf(-vg[ch])), static_cast<const T *>(nullptr));
-                hist[ch][KC + t] = t < n ? v : 0.f;
-            }
+            load2<T>(xb + (int64_t)t * a.x_rs + c0, va[t]);
+            load2<T>(xb + (int64_t)t * a.x_rs + D + c0, vg[t]);
         }
         const T *wt = static_cast<const T *>(a.w) + (int64_t)c0 * K;
 #pragma unroll
-        for (int ch = 0; ch < 4; ++ch) {
-            float wk[K];
+        for (int ch = 0; ch < kCpt; ++ch)
 #pragma unroll
-            for (int k = 0; k < K; ++k) wk[k] = Elem<T>::to_f(wt[ch * K + k]);
+            for (int k = 0; k < K; ++k) wk[ch][k] = Elem<T>::to_f(wt[ch * K + k]);
+        if (a.ln_w) {
+            load2<T>(static_cast<const T *>(a.ln_w) + c0, g);
+            load2<T>(static_cast<const T *>(a.ln_b) + c0, be);
+        }
+    }
+    const bool slot_ok = s >= 0 && s < a.num_slots;   // block-uniform
+    if (!slot_ok) {
+        if (threadIdx.x == 0) raise(a.error, PK_DEV_BAD_SLOT);
+        return;
+    }
+
+    float y[kCpt][TM];
+    if (active) {
+        T *cache = static_cast<T *>(a.state) + (((int64_t)s * a.num_layers + a.layer) * D + c0) * KC;
 #pragma unroll
-            for (int t = 0; t < kTMax; ++t) {
+        for (int ch = 0; ch < kCpt; ++ch) {
+            float hist[KC + TM];
+            load_cache<T, KC>(cache + ch * KC, hist);
+#pragma unroll
+            for (int t = 0; t < TM; ++t) {
+                if (t >= chunk) break;
+                // F.glu then masked_fill(pad_mask, 0) (convolution.py:153-155)
+                const float v = round_to(va[t][ch] * sigmoid(vg[t][ch]), static_cast<const T *>(nullptr));
+                hist[KC + t] = t < n ? v : 0.f;
+            }
+#pragma unroll
+            for (int t = 0; t < TM; ++t) {
                 if (t >= chunk) break;
                 float acc = 0.f;
 #pragma unroll
-                for (int k = 0; k < K; ++k) acc = fmaf(wk[k], hist[ch][t + k], acc);
+                for (int k = 0; k < K; ++k) acc = fmaf(wk[ch][k], hist[t + k], acc);
                 y[ch][t] = acc;
             }
             // next cache: the last K-1 entries of cat(cache, x)
+            float nc[KC];
 #pragma unroll
             for (int k = 0; k < KC; ++k) {
                 float v = 0.f;
 #pragma unroll
-                for (int t = 0; t <= kTMax; ++t)
-                    if (t == chunk) v = hist[ch][t + k];
-                cache[ch * KC + k] = Elem<T>::from_f(v);
+                for (int t = 0; t <= TM; ++t)
+                    if (t == chunk) v = hist[t + k];
+                nc[k] = v;
             }
+            store_cache<T, KC>(cache + ch * KC, nc);
         }
     } else {
 #pragma unroll
-        for (int ch = 0; ch < 4; ++ch)
+        for (int ch = 0; ch < kCpt; ++ch)
 #pragma unroll
-            for (int t = 0; t < kTMax; ++t) y[ch][t] = 0.f;
+            for (int t = 0; t < TM; ++t) y[ch][t] = 0.f;
     }
 
     T *yb = static_cast<T *>(a.y) + (int64_t)b * chunk * D;
     if (a.ln_w) {
         // LayerNorm over channels (the module's "batch_norm", convolution.py:138,157), then SiLU
-        float m[kTMax], v[kTMax];
 #pragma unroll
-        for (int t = 0; t < kTMax; ++t) m[t] = active ? y[0][t] + y[1][t] + y[2][t] + y[3][t] : 0.f;
-        block_sum(m, chunk, red);
+        for (int t = 0; t < TM; ++t) {
+            if (t >= chunk) break;
+            Moments m = {0.f, 0.f, 0.f};
+            if (active) {
+                const float mean = 0.5f * (y[0][t] + y[1][t]);
+                const float d0 = y[0][t] - mean, d1 = y[1][t] - mean;
+                m = {2.f, mean, d0 * d0 + d1 * d1};
+            }
 #pragma unroll
-        for (int t = 0; t < kTMax; ++t) {
-            m[t] *= 1.f / D;
-            float q = 0.f;
-            if (active)
-#pragma unroll
-                for (int ch = 0; ch < 4; ++ch) q += (y[ch][t] - m[t]) * (y[ch][t] - m[t]);
-            v[t] = q;
+            for (int o = 1; o < 32; o <<= 1) {
+                const Moments other = {__shfl_xor_sync(0xffffffffu, m.n, o),
+                                       __shfl_xor_sync(0xffffffffu, m.mean, o),
+                                       __shfl_xor_sync(0xffffffffu, m.m2, o)};
+                m = (lane & o) ? combine(other, m) : combine(m, other);
+            }
+            if (lane == 0) red[t][warp] = m;
         }
-        block_sum(v, chunk, red);
-        if (active) {
-            float g[4], be[4];
-            load4<T>(static_cast<const T *>(a.ln_w) + c0, g);
-            load4<T>(static_cast<const T *>(a.ln_b) + c0, be);
+        __syncthreads();
+        {   // every lane of every warp takes part in the shuffles below
 #pragma unroll
-            for (int t = 0; t < kTMax; ++t) {
+            for (int t = 0; t < TM; ++t) {
                 if (t >= chunk) break;
-                const float inv = rsqrtf(v[t] * (1.f / D) + a.eps);
-                float o[4];
+                // the warps' partials (lanes >= nw empty), combined over all 32 lanes
+                Moments m = lane < nw ? red[t][lane] : Moments{0.f, 0.f, 0.f};
 #pragma unroll
-                for (int ch = 0; ch < 4; ++ch) {
-                    const float z = (y[ch][t] - m[t]) * inv * g[ch] + be[ch];
-                    o[ch] = z / (1.f + expf(-z));
+                for (int o = 1; o < 32; o <<= 1) {
+                    const Moments other = {__shfl_xor_sync(0xffffffffu, m.n, o),
+                                           __shfl_xor_sync(0xffffffffu, m.mean, o),
+                                           __shfl_xor_sync(0xffffffffu, m.m2, o)};
+                    m = (lane & o) ? combine(other, m) : combine(m, other);
                 }
-                store4<T>(yb + (int64_t)t * D + c0, o);
+                const float inv = rsqrtf(__fdividef(m.m2, m.n) + a.eps);
+                float o[kCpt];
+#pragma unroll
+                for (int ch = 0; ch < kCpt; ++ch) {
+                    const float z = (y[ch][t] - m.mean) * inv * g[ch] + be[ch];
+                    o[ch] = z * sigmoid(z);
+                }
+                if (active) store2<T>(yb + (int64_t)t * D + c0, o);
             }
         }
     } else if (active) {
 #pragma unroll
-        for (int t = 0; t < kTMax; ++t) {
+        for (int t = 0; t < TM; ++t) {
             if (t >= chunk) break;
-            float o[4] = {y[0][t], y[1][t], y[2][t], y[3][t]};
-            store4<T>(yb + (int64_t)t * D + c0, o);
+            float o[kCpt] = {y[0][t], y[1][t]};
+            store2<T>(yb + (int64_t)t * D + c0, o);
         }
     }
 }
@@ -188,12 +228,23 @@ __global__ void __launch_bounds__(256) conv_step_kernel(const ConvArgs a) {
 
 int launch_conv(const ConvArgs &a, cudaStream_t s) {
     if (a.batch == 0) return PK_OK;
-    if (a.kernel != 9 || a.chunk > kTMax || a.dim % 4 != 0 || a.dim > 1024) return PK_ENOTSUP;
-    const int threads = ((a.dim / 4 + 31) / 32) * 32;
+    if (a.kernel != 9 || a.chunk > kTMax || a.dim % kCpt != 0 || a.dim > 512 * kCpt)
+        return PK_ENOTSUP;
+    const int threads = ((a.dim / kCpt + 31) / 32) * 32;
+    const int tm = a.chunk <= 2 ? 2 : a.chunk <= 4 ? 4 : a.chunk <= 8 ? 8 : 16;
+    auto pick = [&](auto tag) {
+        using T = decltype(tag);
+        switch (tm) {
+            case 2: conv_step_kernel<T, 9, 2><<<a.batch, threads, 0, s>>>(a); break;
+            case 4: conv_step_kernel<T, 9, 4><<<a.batch, threads, 0, s>>>(a); break;
+            case 8: conv_step_kernel<T, 9, 8><<<a.batch, threads, 0, s>>>(a); break;
+            default: conv_step_kernel<T, 9, 16><<<a.batch, threads, 0, s>>>(a); break;
+        }
+    };
     if (a.dtype == PK_DTYPE_BF16)
-        conv_step_kernel<__nv_bfloat16, 9><<<a.batch, threads, 0, s>>>(a);
+        pick(__nv_bfloat16());
     else
-        conv_step_kernel<float, 9><<<a.batch, threads, 0, s>>>(a);
+        pick(float());
     return cuda_status(cudaGetLastError(), "conv_step_kernel");
 }
 

@@ -57,8 +57,8 @@ int launch_pages_end(const pk_paged_kv *kv, const int32_t *slots, const int32_t 
 int launch_append(const pk_paged_kv *kv, int layer0, int nlayers, const void *key,
                   const void *value, int64_t ls, int64_t bs, int64_t rs, const int32_t *slots,
                   int batch, cudaStream_t s);
-int launch_gather(const pk_paged_kv *kv, int layer, const int32_t *slots, int batch,
-                  void *k_out, void *v_out, cudaStream_t s);
+int launch_gather(const pk_paged_kv *kv, int layer0, int nlayers, const int32_t *slots, int batch,
+                  void *k_out, void *v_out, int64_t out_layer_stride, cudaStream_t s);
 
 // pk_attn.cu
 struct AttnArgs {

@@ -62,6 +62,7 @@ SIGNATURES = {
     "pk_pages_end_step": [_P, _P, _P, _I32, _P],
     "pk_append_kv": [_P, _I32, _I32, _P, _P, _I64, _I64, _I64, _P, _I32, _P],
     "pk_gather_window": [_P, _I32, _P, _I32, _P, _P, _P],
+    "pk_gather_windows": [_P, _I32, _I32, _P, _I32, _P, _P, _I64, _P],
     "pk_paged_attention": [_P, _I32, _I32, _P, _I64, _I64, _I64, _P, _P, _P, _I64, _P, _P,
                            _I64, _P, _P, _I32, _P, _I64, _I64, _I64, _P],
     "pk_conv_step": [_P, _I32, _I32, _I32, _I32, _I32, _I32, _I32, _P, _I64, _I64, _P, _P, _P,

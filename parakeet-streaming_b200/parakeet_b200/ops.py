@@ -180,6 +180,21 @@ class PagedKVPool:
                                      v.data_ptr(), _stream(self.device)), "pk_gather_window")
         return k, v
 
+    def gather_layers(self, layer0: int, num_layers: int, slots: torch.Tensor, out_k=None,
+                      out_v=None):
+        """gather() of layers layer0 .. layer0 + num_layers - 1 in one launch:
+        contiguous [num_layers, B, W, D] outputs."""
+        B = int(slots.numel())
+        shape = (num_layers, B, self.window, self.dim)
+        k = out_k if out_k is not None else torch.empty(shape, dtype=self.dtype, device=self.device)
+        v = out_v if out_v is not None else torch.empty(shape, dtype=self.dtype, device=self.device)
+        if not (k.is_contiguous() and v.is_contiguous() and tuple(k.shape) == shape):
+            raise ValueError("gather_layers outputs must be contiguous [L, B, W, D]")
+        check(lib().pk_gather_windows(self._h, layer0, num_layers, slots.data_ptr(), B,
+                                      k.data_ptr(), v.data_ptr(), k.stride(0),
+                                      _stream(self.device)), "pk_gather_windows")
+        return k, v
+
     def attention(self, layer: int, query: torch.Tensor, pos_proj: torch.Tensor,
                   bias_u: torch.Tensor, bias_v: torch.Tensor, slots: torch.Tensor,
                   lengths: torch.Tensor, out: torch.Tensor | None = None,

@@ -143,6 +143,12 @@ def run_stream_steps(shape, dtype, steps, n_slots, seed, check_every=1, short_la
                 e = rel_l2(np.stack([got[b, t] for b, t in rows]), np.stack([ref[b, t] for b, t in rows]))
                 worst = max(worst, e)
                 assert e <= TOL[dtype], (step, l, e)
+        if step % check_every == 0 or step == steps - 1:
+            # every layer in one launch == the per-layer gathers, bit for bit
+            kl, vl = pool.gather_layers(0, L, sl)
+            for l in range(L):
+                kw, vw = pool.gather(l, sl)
+                assert torch.equal(kl[l], kw) and torch.equal(vl[l], vw), (step, l)
         st.processed_frames += np.asarray(lengths)
         st.cache_lengths = np.minimum(st.cache_lengths + np.asarray(lengths), left)
         dense.unpack_states(st, idx)
