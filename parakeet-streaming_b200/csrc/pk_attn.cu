@@ -206,6 +206,7 @@ __global__ void __launch_bounds__(kF32Threads)
     float *S = reinterpret_cast<float *>(smem + g.off_s);
     int *rowoff = reinterpret_cast<int *>(smem + g.off_rows);
     int *rowr = rowoff + W;
+    grid_dep_wait();   // pages, counters and q may come from the previous kernel
 
     if (tid == 0)
         issue_window_loads<T, DH>(&kv_map, &pos_map, g, page_table, meta, error, a, h, b, lrel,
@@ -366,10 +367,11 @@ int launch_f32(const pk_paged_kv *kv, const CUtensorMap &pos_map, const AttnArgs
     int st = set_smem(paged_attn_f32_kernel<DH>, smem, limit);
     if (st != PK_OK) return st;
     dim3 grid(kv->d.num_heads, a.batch, a.nlayers);
-    paged_attn_f32_kernel<DH><<<grid, kF32Threads, smem, s>>>(kv->kv_map, pos_map, g,
-                                                              kv->d.page_table, kv->d.meta,
-                                                              kv->d.error, a);
-    return cuda_status(cudaGetLastError(), "paged_attn_f32_kernel");
+    return cuda_status(launch_pdl(paged_attn_f32_kernel<DH>, grid, dim3(kF32Threads), smem, s,
+                                  kv->kv_map, pos_map, g,
+                                  static_cast<const int32_t *>(kv->d.page_table),
+                                  static_cast<const int32_t *>(kv->d.meta), kv->d.error, a),
+                       "paged_attn_f32_kernel");
 }
 
 }  // namespace

@@ -113,6 +113,7 @@ __global__ void __launch_bounds__(NW * 32)
     float *sBD = reinterpret_cast<float *>(smem + g.off_bd);
     float *sRed = reinterpret_cast<float *>(smem + g.off_red);
     char *sZero = smem + g.off_zero;
+    grid_dep_wait();   // descriptors, pages and q may come from the previous kernel
 
     if (warp == 0) {
         // window descriptor -> TMA loads, one page per lane
@@ -463,8 +464,9 @@ int launch_typed(const pk_paged_kv *kv, const CUtensorMap &pos_map, const AttnAr
         limit = smem;
     }
     dim3 grid(kv->d.num_heads, a.batch, a.nlayers);
-    kernel<<<grid, NW * 32, smem, s>>>(kv->kv_map, pos_map, g, kv->d.window, kv->d.error, a);
-    return cuda_status(cudaGetLastError(), "paged_attn_bf16_kernel");
+    return cuda_status(launch_pdl(kernel, grid, dim3(NW * 32), smem, s, kv->kv_map, pos_map, g,
+                                  kv->d.window, kv->d.error, a),
+                       "paged_attn_bf16_kernel");
 }
 
 }  // namespace

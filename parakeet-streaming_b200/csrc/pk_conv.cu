@@ -102,6 +102,8 @@ __global__ void __launch_bounds__(512) conv_step_kernel(const ConvArgs a) {
 
     // inputs that do not depend on the slot: the GLU input rows, taps, LN affine
     float va[TM][kCpt], vg[TM][kCpt], wk[kCpt][K], g[kCpt] = {0.f, 0.f}, be[kCpt] = {0.f, 0.f};
+    grid_dep_wait();     // x and the cache may come from the previous kernel
+    grid_dep_launch();   // one wave: the next kernel may be scheduled (it waits for us)
     const int s = a.slots[b];
     const int n = a.lengths[b];
     if (active) {
@@ -234,18 +236,12 @@ int launch_conv(const ConvArgs &a, cudaStream_t s) {
     const int tm = a.chunk <= 2 ? 2 : a.chunk <= 4 ? 4 : a.chunk <= 8 ? 8 : 16;
     auto pick = [&](auto tag) {
         using T = decltype(tag);
-        switch (tm) {
-            case 2: conv_step_kernel<T, 9, 2><<<a.batch, threads, 0, s>>>(a); break;
-            case 4: conv_step_kernel<T, 9, 4><<<a.batch, threads, 0, s>>>(a); break;
-            case 8: conv_step_kernel<T, 9, 8><<<a.batch, threads, 0, s>>>(a); break;
-            default: conv_step_kernel<T, 9, 16><<<a.batch, threads, 0, s>>>(a); break;
-        }
+        auto kernel = tm == 2 ? conv_step_kernel<T, 9, 2> : tm == 4 ? conv_step_kernel<T, 9, 4>
+                    : tm == 8 ? conv_step_kernel<T, 9, 8> : conv_step_kernel<T, 9, 16>;
+        return launch_pdl(kernel, dim3(a.batch), dim3(threads), 0, s, a);
     };
-    if (a.dtype == PK_DTYPE_BF16)
-        pick(__nv_bfloat16());
-    else
-        pick(float());
-    return cuda_status(cudaGetLastError(), "conv_step_kernel");
+    const cudaError_t e = a.dtype == PK_DTYPE_BF16 ? pick(__nv_bfloat16()) : pick(float());
+    return cuda_status(e, "conv_step_kernel");
 }
 
 }  // namespace pk

@@ -62,6 +62,8 @@ __global__ void __launch_bounds__(512)
     const uint4 *src = reinterpret_cast<const uint4 *>((kvi ? value : key) +
                                                        ((int64_t)lrel * ls + (int64_t)b * bs) * esize) + v;
     const int64_t rs16 = rs * esize / 16;
+    grid_dep_wait();     // the new rows may come from the previous kernel
+    grid_dep_launch();   // one wave: the next kernel may be scheduled (it waits for us)
     uint4 val[TM];
 #pragma unroll
     for (int t = 0; t < TM; ++t)
@@ -100,6 +102,8 @@ __global__ void __launch_bounds__(kGatherThreads)
     const int W = d.left + d.chunk;
     const int j0 = blockIdx.z * rows;
     const int nrows = min(rows, W - j0);
+    grid_dep_wait();     // pages and counters may come from the previous kernel
+    grid_dep_launch();   // one wave: the next kernel may be scheduled (it waits for us)
     if (nrows <= 0) return;
     load_slot_ctx(d, slots, b, ctx);
     const int vpr = d.dim * esize / 16, vph = vpr / d.num_heads, dh_bytes = vph * 16;
@@ -146,15 +150,11 @@ int launch_append(const pk_paged_kv *kv, int layer0, int nlayers, const void *ke
     dim3 grid(batch, nlayers);
     const char *k = static_cast<const char *>(key), *v = static_cast<const char *>(value);
     const int c = kv->d.chunk;
-    if (c <= 2)
-        append_kernel<2><<<grid, threads, 0, s>>>(kv->d, kv->esize, layer0, k, v, ls, bs, rs, slots);
-    else if (c <= 4)
-        append_kernel<4><<<grid, threads, 0, s>>>(kv->d, kv->esize, layer0, k, v, ls, bs, rs, slots);
-    else if (c <= 8)
-        append_kernel<8><<<grid, threads, 0, s>>>(kv->d, kv->esize, layer0, k, v, ls, bs, rs, slots);
-    else
-        append_kernel<16><<<grid, threads, 0, s>>>(kv->d, kv->esize, layer0, k, v, ls, bs, rs, slots);
-    return cuda_status(cudaGetLastError(), "append_kernel");
+    auto kernel = c <= 2 ? append_kernel<2> : c <= 4 ? append_kernel<4>
+                : c <= 8 ? append_kernel<8> : append_kernel<16>;
+    return cuda_status(launch_pdl(kernel, grid, dim3(threads), 0, s, kv->d, kv->esize, layer0, k,
+                                  v, ls, bs, rs, slots),
+                       "append_kernel");
 }
 
 int launch_gather(const pk_paged_kv *kv, int layer0, int nlayers, const int32_t *slots, int batch,
@@ -168,10 +168,10 @@ int launch_gather(const pk_paged_kv *kv, int layer0, int nlayers, const int32_t 
     if (rows < 1) rows = 1;
     if (rows > W) rows = W;
     dim3 grid(batch, 2 * nlayers, (W + rows - 1) / rows);
-    gather_kernel<<<grid, kGatherThreads, 0, s>>>(kv->d, kv->esize, layer0, slots,
-                                                  static_cast<char *>(k_out),
-                                                  static_cast<char *>(v_out), out_ls, rows);
-    return cuda_status(cudaGetLastError(), "gather_kernel");
+    return cuda_status(launch_pdl(gather_kernel, grid, dim3(kGatherThreads), 0, s, kv->d,
+                                  kv->esize, layer0, slots, static_cast<char *>(k_out),
+                                  static_cast<char *>(v_out), out_ls, rows),
+                       "gather_kernel");
 }
 
 }  // namespace pk
