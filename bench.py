@@ -461,7 +461,8 @@ def main():
 
     if rank == 0:
         hbm, kind = peaks()
-        kernel_name = ("paged_attn_stacked_kernel" if H * T <= 16 and dh == 64
+        kernel_name = ("paged_attn_stacked_kernel (append fused)" if H * T <= 16 and dh == 64
+                       else "paged_attn_heads_kernel (+append_kernel)" if dh == 128 and 8 <= T <= 16
                        else "paged_attn_bf16_kernel (+append_kernel)")
         attn_bytes = step_bytes    # the fused kernel moves the append's bytes too
         achieved = attn_bytes / (attn_ms * 1e-3) / 1e9

@@ -282,9 +282,9 @@ int pk_paged_attention(pk_paged_kv *kv, int32_t layer0, int32_t num_layers, cons
     a.layer0 = layer0;
     a.nlayers = num_layers;
     int st;
+    CUtensorMap pos16;
     if (kv->d.dtype == PK_DTYPE_BF16) {
         // all heads of a (stream, layer) per CTA when they fill one m16 tile
-        CUtensorMap pos16;
         st = encode_tmap_3d(&pos16, kv->d.dtype, pos_proj, kv->d.dim, P, num_layers, row, lstride,
                             128 / es, 16, 1);
         if (st != PK_OK) return st;
@@ -296,6 +296,11 @@ int pk_paged_attention(pk_paged_kv *kv, int32_t layer0, int32_t num_layers, cons
                            q_row_stride, slots, batch, s);
         if (st != PK_OK) return st;
         a.k_new = a.v_new = nullptr;
+    }
+    if (kv->d.dtype == PK_DTYPE_BF16) {
+        // a group of heads per CTA when each head's chunk fills an m16 tile
+        st = launch_attention_heads(kv, pos16, a, s);
+        if (st != PK_ENOTSUP) return st;
     }
     CUtensorMap pos_map;
     st = encode_tmap_3d(&pos_map, kv->d.dtype, pos_proj, kv->d.dim, P, num_layers, row, lstride,

@@ -82,6 +82,10 @@ int launch_attention_bf16(const pk_paged_kv *kv, const CUtensorMap &pos_map, con
 // returns PK_ENOTSUP for other shapes.  pos_map16 has 16-row boxes.
 int launch_attention_stacked(const pk_paged_kv *kv, const CUtensorMap &pos_map16,
                              const AttnArgs &a, cudaStream_t s);
+// pk_attn_heads.cu: head_dim 128, chunks of 8..16 frames, K/V appended before;
+// returns PK_ENOTSUP for other shapes.  pos_map16 has 16-row boxes of 64 columns.
+int launch_attention_heads(const pk_paged_kv *kv, const CUtensorMap &pos_map16,
+                           const AttnArgs &a, cudaStream_t s);
 
 // pk_conv.cu
 struct ConvArgs {
