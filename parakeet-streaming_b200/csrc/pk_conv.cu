@@ -1,8 +1,8 @@
 // Depthwise causal conv with its time cache, fused with GLU, the pad mask,
-// LayerNorm and SiLU.  One CTA per stream, two channels per thread.  A layer's
-// call moves about 1.8 MB for 80 streams, so the kernel is latency-bound: the
-// loads that do not depend on the slot go out before the slot's cache, and the
-// LayerNorm needs one block reduction.
+// LayerNorm and SiLU.  One CTA per stream.  A layer's call moves about 1.8 MB
+// for 80 streams, so the kernel is latency-bound: the loads that do not depend
+// on the slot go out before the slot's cache, and the LayerNorm runs one warp
+// per frame over the conv outputs kept in shared memory.
 //
 // Restates ConformerConvolution.forward (parakeet/modules/convolution.py:
 // 150-162) from the GLU to the SiLU, with CausalConv1d.update_cache/forward
@@ -25,19 +25,6 @@ __device__ __forceinline__ float round_to(float v, const __nv_bfloat16 *) {
     return __bfloat162float(__float2bfloat16_rn(v));
 }
 __device__ __forceinline__ float round_to(float v, const float *) { return v; }
-
-// (count, mean, M2) of a set of values; two sets combine exactly (Chan et al.'s
-// pairwise update), so one reduction gives the LayerNorm mean and variance
-// with the accuracy of the two-pass formula.
-struct Moments {
-    float n, mean, m2;
-};
-__device__ __forceinline__ Moments combine(const Moments &a, const Moments &b) {
-    const float n = a.n + b.n;
-    if (n == 0.f) return a;
-    const float delta = b.mean - a.mean, fb = __fdividef(b.n, n);
-    return {n, a.mean + delta * fb, a.m2 + b.m2 + delta * delta * a.n * fb};
-}
 
 template <typename T>
 __device__ __forceinline__ void load2(const T *p, float *f) {
@@ -85,23 +72,25 @@ __device__ __forceinline__ void store_cache(T *p, const float *h) {
 }
 __device__ __forceinline__ float sigmoid(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
 
-constexpr int kCpt = 2;   // channels per thread
+constexpr int kCpt = 2;   // channels per thread in the conv phase
 
-// One CTA per stream, kCpt channels per thread; TM >= chunk frames in registers.
-// Every load that does not depend on the slot id goes out first, the cache
-// follows the slot, and LayerNorm takes one block reduction per frame.
+// One CTA per stream.  Conv phase: kCpt channels per thread, TM >= chunk frames in
+// registers; every load that does not depend on the slot id goes out first and
+// the cache follows the slot.  LayerNorm phase: the conv outputs [chunk][D] sit
+// in shared memory and one warp per frame takes the exact two-pass mean and
+// variance, then writes the frame's normalised SiLU output with coalesced stores.
 template <typename T, int K, int TM>
 __global__ void __launch_bounds__(512) conv_step_kernel(const ConvArgs a) {
     constexpr int KC = K - 1;
-    __shared__ Moments red[TM][16];
+    extern __shared__ float ys[];   // [chunk][D] conv outputs (LayerNorm only)
     const int b = blockIdx.x;
     const int D = a.dim, chunk = a.chunk;
     const int c0 = threadIdx.x * kCpt;
     const bool active = c0 < D;
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, nw = blockDim.x / 32;
 
-    // inputs that do not depend on the slot: the GLU input rows, taps, LN affine
-    float va[TM][kCpt], vg[TM][kCpt], wk[kCpt][K], g[kCpt] = {0.f, 0.f}, be[kCpt] = {0.f, 0.f};
+    // inputs that do not depend on the slot: the GLU input rows and the taps
+    float va[TM][kCpt], vg[TM][kCpt], wk[kCpt][K];
     grid_dep_wait();     // x and the cache may come from the previous kernel
     grid_dep_launch();   // one wave: the next kernel may be scheduled (it waits for us)
     const int s = a.slots[b];
@@ -119,10 +108,6 @@ __global__ void __launch_bounds__(512) conv_step_kernel(const ConvArgs a) {
         for (int ch = 0; ch < kCpt; ++ch)
 #pragma unroll
             for (int k = 0; k < K; ++k) wk[ch][k] = Elem<T>::to_f(wt[ch * K + k]);
-        if (a.ln_w) {
-            load2<T>(static_cast<const T *>(a.ln_w) + c0, g);
-            load2<T>(static_cast<const T *>(a.ln_b) + c0, be);
-        }
     }
     const bool slot_ok = s >= 0 && s < a.num_slots;   // block-uniform
     if (!slot_ok) {
@@ -130,9 +115,10 @@ __global__ void __launch_bounds__(512) conv_step_kernel(const ConvArgs a) {
         return;
     }
 
-    float y[kCpt][TM];
+    T *yb = static_cast<T *>(a.y) + (int64_t)b * chunk * D;
     if (active) {
         T *cache = static_cast<T *>(a.state) + (((int64_t)s * a.num_layers + a.layer) * D + c0) * KC;
+        float y[kCpt][TM];
 #pragma unroll
         for (int ch = 0; ch < kCpt; ++ch) {
             float hist[KC + TM];
@@ -164,64 +150,49 @@ __global__ void __launch_bounds__(512) conv_step_kernel(const ConvArgs a) {
             }
             store_cache<T, KC>(cache + ch * KC, nc);
         }
-    } else {
 #pragma unroll
-        for (int ch = 0; ch < kCpt; ++ch)
-#pragma unroll
-            for (int t = 0; t < TM; ++t) y[ch][t] = 0.f;
+        for (int t = 0; t < TM; ++t) {
+            if (t >= chunk) break;
+            if (a.ln_w) {
+                *reinterpret_cast<float2 *>(ys + t * D + c0) = make_float2(y[0][t], y[1][t]);
+            } else {
+                const float o[kCpt] = {y[0][t], y[1][t]};
+                store2<T>(yb + (int64_t)t * D + c0, o);
+            }
+        }
     }
+    if (!a.ln_w) return;
+    __syncthreads();
 
-    T *yb = static_cast<T *>(a.y) + (int64_t)b * chunk * D;
-    if (a.ln_w) {
-        // LayerNorm over channels (the module's "batch_norm", convolution.py:138,157), then SiLU
-#pragma unroll
-        for (int t = 0; t < TM; ++t) {
-            if (t >= chunk) break;
-            Moments m = {0.f, 0.f, 0.f};
-            if (active) {
-                const float mean = 0.5f * (y[0][t] + y[1][t]);
-                const float d0 = y[0][t] - mean, d1 = y[1][t] - mean;
-                m = {2.f, mean, d0 * d0 + d1 * d1};
-            }
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const Moments other = {__shfl_xor_sync(0xffffffffu, m.n, o),
-                                       __shfl_xor_sync(0xffffffffu, m.mean, o),
-                                       __shfl_xor_sync(0xffffffffu, m.m2, o)};
-                m = (lane & o) ? combine(other, m) : combine(m, other);
-            }
-            if (lane == 0) red[t][warp] = m;
+    // LayerNorm over channels (the module's "batch_norm", convolution.py:138,157), then SiLU
+    const T *lw = static_cast<const T *>(a.ln_w), *lb = static_cast<const T *>(a.ln_b);
+    for (int t = warp; t < chunk; t += nw) {
+        const float *row = ys + t * D;
+        float sum = 0.f;
+        for (int c = 2 * lane; c < D; c += 64) {
+            const float2 v = *reinterpret_cast<const float2 *>(row + c);
+            sum += v.x + v.y;
         }
-        __syncthreads();
-        {   // every lane of every warp takes part in the shuffles below
 #pragma unroll
-            for (int t = 0; t < TM; ++t) {
-                if (t >= chunk) break;
-                // the warps' partials (lanes >= nw empty), combined over all 32 lanes
-                Moments m = lane < nw ? red[t][lane] : Moments{0.f, 0.f, 0.f};
-#pragma unroll
-                for (int o = 1; o < 32; o <<= 1) {
-                    const Moments other = {__shfl_xor_sync(0xffffffffu, m.n, o),
-                                           __shfl_xor_sync(0xffffffffu, m.mean, o),
-                                           __shfl_xor_sync(0xffffffffu, m.m2, o)};
-                    m = (lane & o) ? combine(other, m) : combine(m, other);
-                }
-                const float inv = rsqrtf(__fdividef(m.m2, m.n) + a.eps);
-                float o[kCpt];
-#pragma unroll
-                for (int ch = 0; ch < kCpt; ++ch) {
-                    const float z = (y[ch][t] - m.mean) * inv * g[ch] + be[ch];
-                    o[ch] = z * sigmoid(z);
-                }
-                if (active) store2<T>(yb + (int64_t)t * D + c0, o);
-            }
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        const float mean = sum / D;
+        float sq = 0.f;
+        for (int c = 2 * lane; c < D; c += 64) {
+            const float2 v = *reinterpret_cast<const float2 *>(row + c);
+            sq += (v.x - mean) * (v.x - mean) + (v.y - mean) * (v.y - mean);
         }
-    } else if (active) {
 #pragma unroll
-        for (int t = 0; t < TM; ++t) {
-            if (t >= chunk) break;
-            float o[kCpt] = {y[0][t], y[1][t]};
-            store2<T>(yb + (int64_t)t * D + c0, o);
+        for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+        const float inv = rsqrtf(sq / D + a.eps);
+        for (int c = 2 * lane; c < D; c += 64) {
+            const float2 v = *reinterpret_cast<const float2 *>(row + c);
+            float gw[2], gb[2];
+            load2<T>(lw + c, gw);
+            load2<T>(lb + c, gb);
+            const float z0 = (v.x - mean) * inv * gw[0] + gb[0];
+            const float z1 = (v.y - mean) * inv * gw[1] + gb[1];
+            const float o[2] = {z0 * sigmoid(z0), z1 * sigmoid(z1)};
+            store2<T>(yb + (int64_t)t * D + c, o);
         }
     }
 }
@@ -238,7 +209,13 @@ int launch_conv(const ConvArgs &a, cudaStream_t s) {
         using T = decltype(tag);
         auto kernel = tm == 2 ? conv_step_kernel<T, 9, 2> : tm == 4 ? conv_step_kernel<T, 9, 4>
                     : tm == 8 ? conv_step_kernel<T, 9, 8> : conv_step_kernel<T, 9, 16>;
-        return launch_pdl(kernel, dim3(a.batch), dim3(threads), 0, s, a);
+        const size_t smem = a.ln_w ? (size_t)a.chunk * a.dim * sizeof(float) : 0;
+        if (smem > 48 * 1024) {   // at most 64 KB: chunk <= 16, dim <= 1024
+            const cudaError_t e = cudaFuncSetAttribute(
+                kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return e;
+        }
+        return launch_pdl(kernel, dim3(a.batch), dim3(threads), smem, s, a);
     };
     const cudaError_t e = a.dtype == PK_DTYPE_BF16 ? pick(__nv_bfloat16()) : pick(float());
     return cuda_status(e, "conv_step_kernel");
