@@ -68,6 +68,10 @@ def parse():
     ap.add_argument("--no-graph", action="store_true", help="time eager launches only")
     ap.add_argument("--profile", action="store_true",
                     help="prefill + warmup + --steps steps only (for ncu), no report")
+    ap.add_argument("--profile-op", default=None,
+                    choices=["append", "attention", "attention+append", "gather",
+                             "gather_all_layers", "conv"],
+                    help="prefill + warmup, then --steps runs of one breakdown op (for ncu)")
     return ap.parse_args()
 
 
@@ -272,18 +276,50 @@ def main():
             ev[1].record()
         pool.end_step(slots, lengths)
 
+    def make_ops():
+        """The per-op breakdown: name -> (launch fn, algorithmic bytes, launches)."""
+        kv_out = [torch.empty(B, W, D, dtype=dt, device=dev) for _ in range(2)]
+        kv_all = [torch.empty(L, B, W, D, dtype=dt, device=dev) for _ in range(2)]
+        x2 = rnd(B, T, 2 * D)
+        wconv = rnd(D, 1, 9)
+        lnw, lnb = rnd(D) + 1, rnd(D)
+        yconv = torch.empty(B, T, D, dtype=dt, device=dev)
+        ops = {
+            "append": (lambda: pool.append(0, qkv[0][..., D:2 * D], qkv[0][..., 2 * D:], slots),
+                       nb["append"] * units, 1),
+            "attention": (lambda: pool.attention(0, qkv[0][..., :D], pos, bu, bv, slots, lengths, out),
+                          nb["attention"] * units, 1),
+            "attention+append": (lambda: pool.attention(0, qkv[0][..., :D], pos, bu, bv, slots,
+                                                        lengths, out, key=qkv[0][..., D:2 * D],
+                                                        value=qkv[0][..., 2 * D:]),
+                                 (nb["attention"] + nb["append"]) * units, 1),
+            "gather": (lambda: [pool.gather(l, slots, *kv_out) for l in range(L)],
+                       nb["gather"] * units, L),
+            "gather_all_layers": (lambda: pool.gather_layers(0, L, slots, *kv_all),
+                                  nb["gather"] * units, 1),
+            "conv": (lambda: [pool.conv_step(l, x2, wconv, slots, lengths, lnw, lnb, 1e-5, yconv)
+                              for l in range(L)], nb["conv"] * units, L),
+        }
+        return ops
+
     # fill the 70-frame left context, then warm up
     for i in range(-(-left // T)):
         step(qkv[i % NBUF])
     for i in range(args.warmup):
         step(qkv[i % NBUF])
     torch.cuda.synchronize()
-    if args.profile:   # a short, fixed launch sequence for ncu; reports nothing
-        for i in range(args.steps):
-            step(qkv[i % NBUF])
+    if args.profile or args.profile_op:   # a short, fixed launch sequence for ncu; no report
+        if args.profile_op:
+            fn = make_ops()[args.profile_op][0]
+            pool.begin_step(slots, lengths)
+            for i in range(args.steps):
+                fn()
+        else:
+            for i in range(args.steps):
+                step(qkv[i % NBUF])
         torch.cuda.synchronize()
-        print(json.dumps({"profile_run": args.model, "steps": args.steps,
-                          "device_error_word": pool.read_error()}))
+        print(json.dumps({"profile_run": args.model, "op": args.profile_op or "step",
+                          "steps": args.steps, "device_error_word": pool.read_error()}))
         return
 
     clocks = ClockSampler(local)
@@ -427,28 +463,7 @@ def main():
                 b.synchronize()
                 total += a.elapsed_time(b)
             return total / n
-        kv_out = [torch.empty(B, W, D, dtype=dt, device=dev) for _ in range(2)]
-        kv_all = [torch.empty(L, B, W, D, dtype=dt, device=dev) for _ in range(2)]
-        x2 = rnd(B, T, 2 * D)
-        wconv = rnd(D, 1, 9)
-        lnw, lnb = rnd(D) + 1, rnd(D)
-        yconv = torch.empty(B, T, D, dtype=dt, device=dev)
-        ops = {
-            "append": (lambda: pool.append(0, qkv[0][..., D:2 * D], qkv[0][..., 2 * D:], slots),
-                       nb["append"] * units, 1),
-            "attention": (lambda: pool.attention(0, qkv[0][..., :D], pos, bu, bv, slots, lengths, out),
-                          nb["attention"] * units, 1),
-            "attention+append": (lambda: pool.attention(0, qkv[0][..., :D], pos, bu, bv, slots,
-                                                        lengths, out, key=qkv[0][..., D:2 * D],
-                                                        value=qkv[0][..., 2 * D:]),
-                                 (nb["attention"] + nb["append"]) * units, 1),
-            "gather": (lambda: [pool.gather(l, slots, *kv_out) for l in range(L)],
-                       nb["gather"] * units, L),
-            "gather_all_layers": (lambda: pool.gather_layers(0, L, slots, *kv_all),
-                                  nb["gather"] * units, 1),
-            "conv": (lambda: [pool.conv_step(l, x2, wconv, slots, lengths, lnw, lnb, 1e-5, yconv)
-                              for l in range(L)], nb["conv"] * units, L),
-        }
+        ops = make_ops()
         hbm, _ = peaks()
         pool.begin_step(slots, lengths)   # this step's pages and windows; every op re-runs it
         for name, (fn, nbytes, launches) in ops.items():
@@ -469,9 +484,9 @@ def main():
         traffic = None
         tp = os.path.join(REPO, "profiles", "attention_traffic.json")
         if os.path.exists(tp):
-            tj = json.load(open(tp))
-            if tj.get("model") == args.model and tj.get("streams") == B:
-                traffic = tj.get("dram_bytes_per_launch")
+            for tj in json.load(open(tp)):
+                if tj.get("model") == args.model and tj.get("streams") == B:
+                    traffic = tj.get("dram_bytes_per_launch")
         cpu = None
         if world == 1:
             gbs, done, el, threads, sample = cpu_reference(args, args.cpu_seconds)
