@@ -204,6 +204,65 @@ def run_reference_arm(args):
     }), flush=True)
 
 
+def encoder_step(model, streams, steps, dev):
+    """The drop-in ConformerEncoder (random bf16 weights) stepping `streams`
+    slots of one pool: begin step -> 17 layers (cuBLAS GEMMs + this package's
+    attention and conv kernels) -> end step, eager and as one CUDA graph."""
+    import torch
+
+    from parakeet_b200.modules import ConformerEncoder
+    from parakeet_b200.weights import random_encoder_layers
+    c = SHAPES[model]
+    L, D, H, att = c["layers"], c["dim"], c["heads"], c["att"]
+    T = att[1] + 1
+    enc = ConformerEncoder(feat_in=128, hidden_size=D, ff_expansion_factor=4, num_layers=L,
+                           num_heads=H, subsampling_factor=8, pos_emb_max_len=5000,
+                           conv_kernel_size=9, att_context_size=att,
+                           subsampling_conv_channels=256, use_bias=False)
+    sd = random_encoder_layers(0, L, D, H)
+    enc.load_state_dict({k: torch.from_numpy(v) for k, v in sd.items()}, strict=True)
+    enc = enc.to(device=dev, dtype=torch.bfloat16).eval()
+    state = enc.init_streaming_state(streams, dev, torch.bfloat16)
+    g = torch.Generator(device=dev).manual_seed(7)
+    x = torch.randn(streams, T, D, generator=g, device=dev).to(torch.bfloat16)
+    length = torch.full((streams,), T, dtype=torch.int32, device=dev)
+    out = {}
+    with torch.inference_mode():
+        for _ in range(-(-att[0] // T) + 3):   # fill the left context
+            y, state = enc(x, state, length=length)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(steps):
+            y, state = enc(x, state, length=length)
+        b.record()
+        torch.cuda.synchronize()
+        out["ms_per_step_eager"] = round(a.elapsed_time(b) / steps, 4)
+        try:
+            gph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gph):
+                y, state = enc(x, state, length=length)
+            gph.replay()
+            torch.cuda.synchronize()
+            a.record()
+            for _ in range(steps):
+                gph.replay()
+            b.record()
+            torch.cuda.synchronize()
+            out["ms_per_step_graph"] = round(a.elapsed_time(b) / steps, 4)
+            del gph
+        except Exception as e:   # the measurement is informative; keep the run going
+            out["graph_error"] = str(e)[:200]
+        out["finite"] = bool(torch.isfinite(y).all().item())
+    best = min(v for k, v in out.items() if k.startswith("ms_per_step"))
+    audio_ms = T * 80.0   # 8x subsampling of 10 ms frames
+    out.update({"model": model, "streams": streams, "layers": L, "chunk_frames": T,
+                "audio_ms_per_step": audio_ms,
+                "encoder_realtime_factor": round(audio_ms / best, 1),
+                "device_error_word": state.cache.pool.read_error()})
+    return out
+
+
 def max_over_ranks(vals, device):
     """Element-wise max of per-rank timings over the process group (the step
     time of a weak-scaling run is its slowest rank's); identity on one rank."""
@@ -372,6 +431,9 @@ def main():
             dist.barrier()
         ms = g0.elapsed_time(g1) / K
     clk = clocks.stop()
+    enc_line = None
+    if rank == 0 and not args.no_breakdown:
+        enc_line = encoder_step(args.model, 160 if args.model == "small" else 480, 20, dev)
     err = pool.read_error()
 
     # ---- end to end through the public API, as a serving loop runs it: every step
@@ -521,6 +583,7 @@ def main():
             "clocks": clk,
             "device_error_word": err,
             "ops": breakdown,
+            "encoder_step": enc_line,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
