@@ -141,14 +141,15 @@ __global__ void __launch_bounds__(NW * 32)
             if (lane < nb) {
                 const int kplane = ((page * g.num_layers + layer) * 2) * g.num_heads + h;
                 const int vplane = kplane + g.num_heads;
+                const uint64_t stream_once = l2_evict_first();
 #pragma unroll
                 for (int cb = 0; cb < NCOL; ++cb)
-                    tma_load_3d(sK + (lane * NCOL + cb) * g.box_bytes, &kv_map, &bar_k, cb * 64,
-                                start, kplane);
+                    tma_load_3d_hint(sK + (lane * NCOL + cb) * g.box_bytes, &kv_map, &bar_k,
+                                     cb * 64, start, kplane, stream_once);
 #pragma unroll
                 for (int cb = 0; cb < NCOL; ++cb)
-                    tma_load_3d(sV + (lane * NCOL + cb) * g.box_bytes, &kv_map, &bar_v, cb * 64,
-                                start, vplane);
+                    tma_load_3d_hint(sV + (lane * NCOL + cb) * g.box_bytes, &kv_map, &bar_v,
+                                     cb * 64, start, vplane, stream_once);
             }
             if (lane == 31) {
 #pragma unroll

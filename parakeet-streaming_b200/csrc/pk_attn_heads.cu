@@ -163,10 +163,11 @@ __global__ void __launch_bounds__(kThreads, 3)
             if (lane < 2 * kHG) {
                 char *dst = smem + s * kBlock + hb * kHeadBox + cb * 2048;
                 if (is_pos) {
-                    tma_load_3d(dst, &pos_map, &full[s], (hg0 + hb) * kDH + cb * 64, n * 16, lrel);
+                    tma_load_3d_hint(dst, &pos_map, &full[s], (hg0 + hb) * kDH + cb * 64, n * 16,
+                                     lrel, l2_evict_last());
                 } else {
                     const int plane = ((pg * d.num_layers + layer) * 2 + kvi) * d.num_heads + hg0 + hb;
-                    tma_load_3d(dst, &kv_map, &full[s], cb * 64, st, plane);
+                    tma_load_3d_hint(dst, &kv_map, &full[s], cb * 64, st, plane, l2_evict_first());
                 }
             }
             last_n[s] = n;

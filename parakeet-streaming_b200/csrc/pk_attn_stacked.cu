@@ -158,11 +158,12 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
             if (lane < kH) {
                 char *dst = smem + s * g.stage_bytes + lane * kBox;
                 if (n >= nb && n < nb + npb) {
-                    tma_load_3d(dst, &pos_map, &full[s], lane * 64, (n - nb) * 16, lrel);
+                    tma_load_3d_hint(dst, &pos_map, &full[s], lane * 64, (n - nb) * 16, lrel,
+                                     l2_evict_last());
                 } else {
                     const int i = n < nb ? n : n - nb - npb, kvi = n < nb ? 0 : 1;
                     const int plane = ((s_page[i] * d.num_layers + layer) * 2 + kvi) * kH + lane;
-                    tma_load_3d(dst, &kv_map, &full[s], 0, s_start[i], plane);
+                    tma_load_3d_hint(dst, &kv_map, &full[s], 0, s_start[i], plane, l2_evict_first());
                 }
             }
             last_n[s] = n;

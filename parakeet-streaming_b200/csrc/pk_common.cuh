@@ -122,6 +122,34 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, u
         : "memory");
 }
 
+// L2 cache policies for TMA loads: pages stream through once (evict first, so
+// they do not push out lines that are reused); the rel-pos rows are read by every
+// stream of a layer (evict last).
+__device__ __forceinline__ uint64_t l2_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.L2::evict_unchanged.b64 %0, 1.0;"
+                 : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ uint64_t l2_evict_last() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.L2::evict_unchanged.b64 %0, 1.0;"
+                 : "=l"(p));
+    return p;
+}
+
+// tma_load_3d with an L2 cache policy
+__device__ __forceinline__ void tma_load_3d_hint(void *dst, const CUtensorMap *map, uint64_t *bar,
+                                                 int32_t c0, int32_t c1, int32_t c2,
+                                                 uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        ".L2::cache_hint [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar)),
+        "l"(policy)
+        : "memory");
+}
+
 // Untiled bulk copy global -> shared (16-byte aligned, size a multiple of 16),
 // into this CTA's shared memory, completion on `bar`.
 __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes,
