@@ -67,7 +67,7 @@ __global__ void __launch_bounds__(512)
     uint4 val[TM];
 #pragma unroll
     for (int t = 0; t < TM; ++t)
-        if (t < d.chunk) val[t] = __ldg(src + t * rs16);
+        if (t < d.chunk) val[t] = __ldcs(src + t * rs16);   // read once: evict first
     load_slot_ctx(d, slots, b, ctx);
     if (!ctx.ok) return;
     const int ps_shift = __ffs(d.page_size) - 1;
@@ -127,7 +127,7 @@ __global__ void __launch_bounds__(kGatherThreads)
             }
             const int h = v / vph;
             const int64_t plane = (((int64_t)page * d.num_layers + l) * 2 + kvi) * d.num_heads + h;
-            val[k] = __ldg(reinterpret_cast<const uint4 *>(
+            val[k] = __ldcs(reinterpret_cast<const uint4 *>(   // read once: evict first
                 pool + (plane * d.page_size + a % d.page_size) * dh_bytes + (v % vph) * 16));
         }
 #pragma unroll
