@@ -208,6 +208,36 @@ int pk_conv_step(void *conv_state, int32_t num_slots, int32_t num_layers,
                  const int32_t *slots, const int32_t *lengths, int32_t batch,
                  void *y, int32_t *error, void *stream);
 
+/* ---------------- batched greedy RNNT decode (device-side bookkeeping) ----
+ * A chunk's decode runs, for every frame f < frames and symbol s <
+ * max_symbols, joint -> pk_rnnt_pick -> prediction step -> pk_lstm_cell, all
+ * on one stream with no host round trip.  Replaces the per-symbol host work of
+ * ModelRunner._decode_frame_batch (parakeet/engine/model_runner.py:415-447):
+ * logits.argmax, the blank mask, `bool(blank_mask.all())`, `ids.tolist()` and
+ * the torch.where state selects. */
+
+/* Argmax (first maximum) of each row's `num_classes` logits (row stride
+ * `logits_ld` elements, `dtype` PK_DTYPE_*).  Row b emits when it has not
+ * stopped in this frame (done[b], reset when symbol == 0), frame < lengths[b]
+ * and the argmax is not `blank`: emit[b] = 1, ids[b] = token, tokens[b][frame]
+ * [symbol] = token, counts[b][frame] += 1; otherwise emit[b] = 0, ids[b] =
+ * blank, tokens[...] = -1 and the row stops for the frame.  tokens is int32
+ * [batch][frames][max_symbols], counts int32 [batch][frames]. */
+int pk_rnnt_pick(const void *logits, int64_t logits_ld, int32_t dtype, int32_t batch,
+                 int32_t num_classes, int32_t blank, const int32_t *lengths, int32_t frame,
+                 int32_t symbol, int32_t max_symbols, int32_t frames, int32_t *done,
+                 int32_t *emit, int64_t *ids, int32_t *tokens, int32_t *counts, void *stream);
+
+/* One LSTM cell step from precomputed gates [batch][4 * hidden] (x W_ih^T +
+ * h W_hh^T + biases, PyTorch order i, f, g, o; row stride `gates_ld`) into the
+ * state rows h, c (row stride `state_ld`), only for rows with emit[b] != 0;
+ * other rows keep their state.  Replaces the nn.LSTM step of
+ * Predictor.forward (parakeet/modules/decoder.py:44-50) and the torch.where of
+ * model_runner.py:433-445. */
+int pk_lstm_cell(const void *gates, int64_t gates_ld, void *h, void *c, int64_t state_ld,
+                 const int32_t *emit, int32_t batch, int32_t hidden, int32_t dtype,
+                 void *stream);
+
 /* Text of the last PK_ECUDA / PK_EINVAL cause seen by this thread. */
 const char *pk_last_error(void);
 

@@ -354,4 +354,35 @@ int pk_conv_step(void *conv_state, int32_t num_slots, int32_t num_layers, int32_
     return st;
 }
 
+
+int pk_rnnt_pick(const void *logits, int64_t logits_ld, int32_t dtype, int32_t batch,
+                 int32_t num_classes, int32_t blank, const int32_t *lengths, int32_t frame,
+                 int32_t symbol, int32_t max_symbols, int32_t frames, int32_t *done,
+                 int32_t *emit, int64_t *ids, int32_t *tokens, int32_t *counts, void *stream) {
+    PK_CHECK(dtype == PK_DTYPE_F32 || dtype == PK_DTYPE_BF16, "bad dtype %d", dtype);
+    PK_CHECK(batch >= 0, "negative batch");
+    if (batch == 0) return PK_OK;
+    PK_CHECK(logits && lengths && done && emit && ids && tokens && counts, "null pointer");
+    PK_CHECK(num_classes > 0 && logits_ld >= num_classes, "bad logits shape");
+    PK_CHECK(blank >= 0 && blank < num_classes, "blank outside the classes");
+    PK_CHECK(frames > 0 && frame >= 0 && frame < frames, "frame outside [0, frames)");
+    PK_CHECK(max_symbols > 0 && symbol >= 0 && symbol < max_symbols,
+             "symbol outside [0, max_symbols)");
+    return launch_rnnt_pick(logits, logits_ld, dtype, batch, num_classes, blank, lengths, frame,
+                            symbol, max_symbols, frames, done, emit, ids, tokens, counts,
+                            static_cast<cudaStream_t>(stream));
+}
+
+int pk_lstm_cell(const void *gates, int64_t gates_ld, void *h, void *c, int64_t state_ld,
+                 const int32_t *emit, int32_t batch, int32_t hidden, int32_t dtype,
+                 void *stream) {
+    PK_CHECK(dtype == PK_DTYPE_F32 || dtype == PK_DTYPE_BF16, "bad dtype %d", dtype);
+    PK_CHECK(batch >= 0 && hidden >= 0, "negative shape");
+    if (batch == 0 || hidden == 0) return PK_OK;
+    PK_CHECK(gates && h && c && emit, "null pointer");
+    PK_CHECK(gates_ld >= 4 * (int64_t)hidden && state_ld >= hidden, "bad strides");
+    return launch_lstm_cell(gates, gates_ld, h, c, state_ld, emit, batch, hidden, dtype,
+                            static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

@@ -102,4 +102,12 @@ struct ConvArgs {
 };
 int launch_conv(const ConvArgs &a, cudaStream_t s);
 
+// pk_rnnt.cu
+int launch_rnnt_pick(const void *logits, int64_t ld, int dtype, int batch, int nclass, int blank,
+                     const int32_t *lengths, int frame, int symbol, int max_symbols, int frames,
+                     int32_t *done, int32_t *emit, int64_t *ids, int32_t *tokens, int32_t *counts,
+                     cudaStream_t s);
+int launch_lstm_cell(const void *gates, int64_t gld, void *h, void *c, int64_t sld,
+                     const int32_t *emit, int batch, int hidden, int dtype, cudaStream_t s);
+
 }  // namespace pk

@@ -60,3 +60,35 @@ def random_encoder_layers(seed, num_layers, dim, heads, ff_mult=4, conv_kernel=9
 def seeded_normal(seed, shape, scale=1.0, dtype=np.float32):
     """Synthetic activations: N(0, 1) * scale from a PCG64 stream."""
     return (np.random.default_rng(seed).standard_normal(shape) * scale).astype(dtype)
+
+
+def random_decoder_state_dict(seed, enc_dim, pred_dim=640, joint_dim=640, vocab_size=1026,
+                              pred_layers=1, blank_bias=0.0):
+    """Prediction network + joint network parameters with the keys of the
+    reference's ``Predictor`` and ``Joiner`` state_dicts
+    (parakeet/modules/decoder.py:5-86): an embedding of vocab_size + 1 rows
+    (the blank row, the padding index, is zero), a ``pred_layers``-layer LSTM,
+    and the joint's enc / pred projections and output layer over vocab_size + 1
+    classes.  ``blank_bias`` is added to the blank class's output bias; random
+    weights otherwise almost never emit blank."""
+    rng = np.random.default_rng(seed)
+    sd = {}
+    emb = rng.standard_normal((vocab_size + 1, pred_dim)).astype(np.float32)
+    emb[vocab_size] = 0.0
+    sd["predictor.prediction.embed.weight"] = emb
+    for k in range(pred_layers):
+        sd[f"predictor.prediction.dec_rnn.weight_ih_l{k}"] = _lin(rng, 4 * pred_dim, pred_dim)
+        sd[f"predictor.prediction.dec_rnn.weight_hh_l{k}"] = _lin(rng, 4 * pred_dim, pred_dim)
+        sd[f"predictor.prediction.dec_rnn.bias_ih_l{k}"] = (
+            0.1 * rng.standard_normal(4 * pred_dim)).astype(np.float32)
+        sd[f"predictor.prediction.dec_rnn.bias_hh_l{k}"] = (
+            0.1 * rng.standard_normal(4 * pred_dim)).astype(np.float32)
+    sd["joiner.pred.weight"] = _lin(rng, joint_dim, pred_dim)
+    sd["joiner.pred.bias"] = (0.1 * rng.standard_normal(joint_dim)).astype(np.float32)
+    sd["joiner.enc.weight"] = _lin(rng, joint_dim, enc_dim)
+    sd["joiner.enc.bias"] = (0.1 * rng.standard_normal(joint_dim)).astype(np.float32)
+    sd["joiner.joint_net.2.weight"] = _lin(rng, vocab_size + 1, joint_dim)
+    out_b = (0.1 * rng.standard_normal(vocab_size + 1)).astype(np.float32)
+    out_b[vocab_size] += np.float32(blank_bias)
+    sd["joiner.joint_net.2.bias"] = out_b
+    return sd
