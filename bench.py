@@ -263,6 +263,79 @@ def encoder_step(model, streams, steps, dev):
     return out
 
 
+DECODE_CFG = {"small": dict(enc_dim=512, pred_layers=1, vocab=1026, streams=160),
+              "large": dict(enc_dim=1024, pred_layers=2, vocab=1024, streams=480)}
+
+
+def rnnt_decode_step(model, steps, dev, cpu_sample=2):
+    """Batched greedy RNNT decode of one chunk for every stream (random bf16
+    prediction / joint weights, blank bias set so that about 2.5 tokens are
+    emitted per frame): eager and as one CUDA graph; beside it the float64
+    restatement of the reference's decode loop (oracle/decode.py) on
+    `cpu_sample` streams of the same chunk, scaled to the full batch."""
+    import numpy as np
+    import torch
+
+    from parakeet_b200.engine.decoding import BatchedGreedyDecoder
+    from parakeet_b200.modules import Joiner, Predictor
+    from parakeet_b200.weights import random_decoder_state_dict
+    c, d = SHAPES[model], DECODE_CFG[model]
+    T = c["att"][1] + 1
+    B, D, V = d["streams"], d["enc_dim"], d["vocab"]
+    sd = random_decoder_state_dict(5, D, 640, 640, V, d["pred_layers"], blank_bias=2.3)
+    pred, join = Predictor(640, 640, d["pred_layers"], V), Joiner(D, 640, 640, num_classes=V)
+    pred.load_state_dict({k[10:]: torch.from_numpy(v) for k, v in sd.items()
+                          if k.startswith("predictor.")})
+    join.load_state_dict({k[7:]: torch.from_numpy(v) for k, v in sd.items()
+                          if k.startswith("joiner.")})
+    pred, join = pred.to(dev, torch.bfloat16).eval(), join.to(dev, torch.bfloat16).eval()
+    dec = BatchedGreedyDecoder(pred, join, V, num_slots=B, max_symbols=5)
+    slots = torch.arange(B, dtype=torch.int64, device=dev)
+    dec.reset_slots(slots)
+    g = torch.Generator(device=dev).manual_seed(9)
+    enc = torch.randn(B, T, D, generator=g, device=dev).to(torch.bfloat16)
+    lengths = torch.full((B,), T, dtype=torch.int32, device=dev)
+    out = {"model": model, "streams": B, "frames_per_chunk": T, "max_symbols": 5}
+    with torch.inference_mode():
+        for _ in range(3):
+            tokens, counts = dec.decode(enc, lengths, slots)
+        torch.cuda.synchronize()
+        out["tokens_per_frame"] = round(float(counts.float().mean()), 2)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(steps):
+            dec.decode(enc, lengths, slots)
+        b.record()
+        torch.cuda.synchronize()
+        out["ms_per_chunk_eager"] = round(a.elapsed_time(b) / steps, 4)
+        try:
+            gph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gph):
+                dec.decode(enc, lengths, slots)
+            gph.replay()
+            torch.cuda.synchronize()
+            a.record()
+            for _ in range(steps):
+                gph.replay()
+            b.record()
+            torch.cuda.synchronize()
+            out["ms_per_chunk_graph"] = round(a.elapsed_time(b) / steps, 4)
+            del gph
+        except Exception as e:   # informative; keep the run going
+            out["graph_error"] = str(e)[:200]
+    from oracle.decode import GreedyDecoderModel
+    m = GreedyDecoderModel(sd, d["pred_layers"], V, 5)
+    x = enc.float().cpu().numpy().astype(np.float64)
+    t0 = time.perf_counter()
+    for i in range(cpu_sample):
+        m.decode_chunk(x[i].T, *m.new_stream())
+    cpu_s = (time.perf_counter() - t0) / cpu_sample * B
+    out["cpu_reference_ms_per_chunk"] = round(cpu_s * 1e3, 1)
+    out["cpu_reference"] = (f"oracle/decode.py float64 numpy, {cpu_sample} streams timed, "
+                            f"scaled to {B}")
+    return out
+
+
 def max_over_ranks(vals, device):
     """Element-wise max of per-rank timings over the process group (the step
     time of a weak-scaling run is its slowest rank's); identity on one rank."""
@@ -431,9 +504,10 @@ def main():
             dist.barrier()
         ms = g0.elapsed_time(g1) / K
     clk = clocks.stop()
-    enc_line = None
+    enc_line = dec_line = None
     if rank == 0 and not args.no_breakdown:
         enc_line = encoder_step(args.model, 160 if args.model == "small" else 480, 20, dev)
+        dec_line = rnnt_decode_step(args.model, 10, dev)
     err = pool.read_error()
 
     # ---- end to end through the public API, as a serving loop runs it: every step
@@ -584,6 +658,7 @@ def main():
             "device_error_word": err,
             "ops": breakdown,
             "encoder_step": enc_line,
+            "rnnt_decode": dec_line,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
