@@ -336,6 +336,74 @@ def rnnt_decode_step(model, steps, dev, cpu_sample=2):
     return out
 
 
+def pre_encode_step(model, steps, dev, cpu_sample=4):
+    """Batched streaming pre-encode of one chunk per stream (cache-prefixed
+    feature frames -> ConvSubsampling -> drop 2), bf16, eager and as one CUDA
+    graph; beside it the reference's per-stream loop (one subsampling call per
+    stream, model_runner.py:181-233) run with the drop-in module on the host in
+    fp32 on `cpu_sample` streams, scaled to the batch."""
+    import torch
+
+    from parakeet_b200.engine.pre_encode import BatchedPreEncoder
+    from parakeet_b200.modules import ConvSubsampling
+    from parakeet_b200.weights import random_pre_encode_state_dict
+    c = SHAPES[model]
+    la = c["att"][1]
+    B = 160 if model == "small" else 480
+    F = 8 + 8 * la
+    sd = random_pre_encode_state_dict(6, 128, 256, c["dim"])
+    m = ConvSubsampling(c["dim"], 256, 128, 8)
+    m.load_state_dict({k: torch.from_numpy(v) for k, v in sd.items()})
+    pe = BatchedPreEncoder(m.to(dev, torch.bfloat16).eval(), num_slots=B)
+    g = torch.Generator(device=dev).manual_seed(3)
+    feats = torch.randn(B, 128, F, generator=g, device=dev).to(torch.bfloat16)
+    slots = torch.arange(B, dtype=torch.int32, device=dev)
+    out = {"model": model, "streams": B, "feature_frames": F}
+    with torch.inference_mode():
+        for _ in range(3):
+            y = pe.pre_encode(feats, slots, first=False)
+        torch.cuda.synchronize()
+        out["out_frames"] = int(y.shape[1])
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(steps):
+            pe.pre_encode(feats, slots, first=False)
+        b.record()
+        torch.cuda.synchronize()
+        out["ms_per_chunk_eager"] = round(a.elapsed_time(b) / steps, 4)
+        try:
+            gph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gph):
+                pe.pre_encode(feats, slots, first=False)
+            gph.replay()
+            torch.cuda.synchronize()
+            a.record()
+            for _ in range(steps):
+                gph.replay()
+            b.record()
+            torch.cuda.synchronize()
+            out["ms_per_chunk_graph"] = round(a.elapsed_time(b) / steps, 4)
+            del gph
+        except Exception as e:   # informative; keep the run going
+            out["graph_error"] = str(e)[:200]
+    cpu = ConvSubsampling(c["dim"], 256, 128, 8)
+    cpu.load_state_dict({k: torch.from_numpy(v) for k, v in sd.items()})
+    cpu.eval()
+    x = feats[:cpu_sample].float().cpu()
+    cache = torch.zeros(128, 9)
+    with torch.inference_mode():
+        t0 = time.perf_counter()
+        for i in range(cpu_sample):
+            xi = torch.cat([cache, x[i]], -1)[None]
+            cpu(xi.transpose(1, 2), torch.full((1,), xi.size(-1)))
+        el = time.perf_counter() - t0
+    out["cpu_reference_ms_per_chunk"] = round(el / cpu_sample * B * 1e3, 1)
+    out["cpu_reference"] = (f"per-stream subsampling (model_runner.py:181-233) with the drop-in "
+                            f"module, fp32 torch on {torch.get_num_threads()} host threads, "
+                            f"{cpu_sample} streams timed, scaled to {B}")
+    return out
+
+
 def max_over_ranks(vals, device):
     """Element-wise max of per-rank timings over the process group (the step
     time of a weak-scaling run is its slowest rank's); identity on one rank."""
@@ -504,10 +572,11 @@ def main():
             dist.barrier()
         ms = g0.elapsed_time(g1) / K
     clk = clocks.stop()
-    enc_line = dec_line = None
+    enc_line = dec_line = pre_line = None
     if rank == 0 and not args.no_breakdown:
         enc_line = encoder_step(args.model, 160 if args.model == "small" else 480, 20, dev)
         dec_line = rnnt_decode_step(args.model, 10, dev)
+        pre_line = pre_encode_step(args.model, 10, dev)
     err = pool.read_error()
 
     # ---- end to end through the public API, as a serving loop runs it: every step
@@ -659,6 +728,7 @@ def main():
             "ops": breakdown,
             "encoder_step": enc_line,
             "rnnt_decode": dec_line,
+            "pre_encode": pre_line,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

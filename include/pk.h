@@ -208,6 +208,18 @@ int pk_conv_step(void *conv_state, int32_t num_slots, int32_t num_layers,
                  const int32_t *slots, const int32_t *lengths, int32_t batch,
                  void *y, int32_t *error, void *stream);
 
+/* Streaming pre-encoder input of a batch: out[b] = cat(cache[slots[b]],
+ * feats[b]) along time ([batch][feat_in][csize + frames]; just feats[b] when
+ * use_cache == 0, a stream's first chunk), then cache[slots[b]] = the last
+ * csize frames (frames >= csize).  cache [num_slots][feat_in][csize], feats
+ * [batch][feat_in][frames], `dtype` PK_DTYPE_*; bad slot ids set
+ * PK_DEV_BAD_SLOT in *error.  Replaces the per-stream cache copies of
+ * ModelRunner._run_pre_encode (parakeet/engine/model_runner.py:197-233). */
+int pk_pre_encode_window(void *cache, int32_t num_slots, const void *feats,
+                         const int32_t *slots, int32_t batch, int32_t feat_in, int32_t frames,
+                         int32_t csize, int32_t use_cache, void *out, int32_t dtype,
+                         int32_t *error, void *stream);
+
 /* ---------------- batched greedy RNNT decode (device-side bookkeeping) ----
  * A chunk's decode runs, for every frame f < frames and symbol s <
  * max_symbols, joint -> pk_rnnt_pick -> prediction step -> pk_lstm_cell, all

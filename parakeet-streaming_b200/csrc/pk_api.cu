@@ -355,6 +355,21 @@ int pk_conv_step(void *conv_state, int32_t num_slots, int32_t num_layers, int32_
 }
 
 
+int pk_pre_encode_window(void *cache, int32_t num_slots, const void *feats,
+                         const int32_t *slots, int32_t batch, int32_t feat_in, int32_t frames,
+                         int32_t csize, int32_t use_cache, void *out, int32_t dtype,
+                         int32_t *error, void *stream) {
+    PK_CHECK(dtype == PK_DTYPE_F32 || dtype == PK_DTYPE_BF16, "bad dtype %d", dtype);
+    PK_CHECK(batch >= 0, "negative batch");
+    if (batch == 0) return PK_OK;
+    PK_CHECK(cache && feats && slots && out && num_slots > 0, "null pointer or empty pool");
+    PK_CHECK(feat_in > 0 && csize > 0 && csize <= 32, "cache of 1..32 frames");
+    PK_CHECK(frames >= csize, "a chunk shorter than the cache is not handled");
+    return launch_pre_encode_window(cache, feats, slots, batch, feat_in, frames, csize,
+                                    use_cache != 0, out, dtype, error, num_slots,
+                                    static_cast<cudaStream_t>(stream));
+}
+
 int pk_rnnt_pick(const void *logits, int64_t logits_ld, int32_t dtype, int32_t batch,
                  int32_t num_classes, int32_t blank, const int32_t *lengths, int32_t frame,
                  int32_t symbol, int32_t max_symbols, int32_t frames, int32_t *done,

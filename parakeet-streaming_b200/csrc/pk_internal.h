@@ -102,6 +102,11 @@ struct ConvArgs {
 };
 int launch_conv(const ConvArgs &a, cudaStream_t s);
 
+// pk_pre_encode.cu
+int launch_pre_encode_window(void *cache, const void *feats, const int32_t *slots, int batch,
+                             int feat_in, int frames, int csize, int use_cache, void *out,
+                             int dtype, int32_t *error, int num_slots, cudaStream_t s);
+
 // pk_rnnt.cu
 int launch_rnnt_pick(const void *logits, int64_t ld, int dtype, int batch, int nclass, int blank,
                      const int32_t *lengths, int frame, int symbol, int max_symbols, int frames,

@@ -66,6 +66,7 @@ SIGNATURES = {
     "pk_rnnt_pick": [_P, _I64, _I32, _I32, _I32, _I32, _P, _I32, _I32, _I32, _I32, _P, _P, _P, _P,
                      _P, _P],
     "pk_lstm_cell": [_P, _I64, _P, _P, _I64, _P, _I32, _I32, _I32, _P],
+    "pk_pre_encode_window": [_P, _I32, _P, _P, _I32, _I32, _I32, _I32, _I32, _P, _I32, _P, _P],
     "pk_paged_attention": [_P, _I32, _I32, _P, _I64, _I64, _I64, _P, _P, _P, _I64, _P, _P,
                            _I64, _P, _P, _I32, _P, _I64, _I64, _I64, _P],
     "pk_conv_step": [_P, _I32, _I32, _I32, _I32, _I32, _I32, _I32, _P, _I64, _I64, _P, _P, _P,

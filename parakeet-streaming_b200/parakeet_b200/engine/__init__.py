@@ -1,6 +1,7 @@
 from .decoding import BatchedGreedyDecoder
+from .pre_encode import BatchedPreEncoder
 from .scheduler import Scheduler, SlotAllocator, StreamResult
 from .sequence import Sequence, SequenceStatus
 
-__all__ = ["BatchedGreedyDecoder", "Scheduler", "SlotAllocator", "StreamResult", "Sequence",
+__all__ = ["BatchedGreedyDecoder", "BatchedPreEncoder", "Scheduler", "SlotAllocator", "StreamResult", "Sequence",
            "SequenceStatus"]

@@ -92,3 +92,25 @@ def random_decoder_state_dict(seed, enc_dim, pred_dim=640, joint_dim=640, vocab_
     out_b[vocab_size] += np.float32(blank_bias)
     sd["joiner.joint_net.2.bias"] = out_b
     return sd
+
+
+def random_pre_encode_state_dict(seed, feat_in=128, channels=256, hidden=512, factor=8):
+    """``ConvSubsampling`` parameters (parakeet/modules/subsample.py:61-150) with
+    the reference's keys: conv.0 (1 -> channels, 3x3 stride 2), then per further
+    factor of 2 a depthwise 3x3 stride-2 conv (conv.2, conv.5, ...) and a
+    pointwise 1x1 conv (conv.3, conv.6, ...), and the output projection ``out``
+    from channels x final frequency bins to ``hidden``."""
+    rng = np.random.default_rng(seed)
+    sd = {"conv.0.weight": (rng.standard_normal((channels, 1, 3, 3)) / 3.0).astype(np.float32),
+          "conv.0.bias": (0.1 * rng.standard_normal(channels)).astype(np.float32)}
+    idx, freq = 2, (feat_in + 2 + 1 - 3) // 2 + 1
+    for _ in range(int(round(np.log2(factor))) - 1):
+        sd[f"conv.{idx}.weight"] = (rng.standard_normal((channels, 1, 3, 3)) / 3.0).astype(np.float32)
+        sd[f"conv.{idx}.bias"] = (0.1 * rng.standard_normal(channels)).astype(np.float32)
+        sd[f"conv.{idx + 1}.weight"] = _lin(rng, channels, channels)[:, :, None, None]
+        sd[f"conv.{idx + 1}.bias"] = (0.1 * rng.standard_normal(channels)).astype(np.float32)
+        idx += 3
+        freq = (freq + 2 + 1 - 3) // 2 + 1
+    sd["out.weight"] = _lin(rng, hidden, channels * freq)
+    sd["out.bias"] = (0.1 * rng.standard_normal(hidden)).astype(np.float32)
+    return sd
