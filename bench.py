@@ -392,6 +392,8 @@ def pre_encode_step(model, steps, dev, cpu_sample=4):
     x = feats[:cpu_sample].float().cpu()
     cache = torch.zeros(128, 9)
     with torch.inference_mode():
+        xi = torch.cat([cache, x[0]], -1)[None]
+        cpu(xi.transpose(1, 2), torch.full((1,), xi.size(-1)))   # warm (threads, allocations)
         t0 = time.perf_counter()
         for i in range(cpu_sample):
             xi = torch.cat([cache, x[i]], -1)[None]

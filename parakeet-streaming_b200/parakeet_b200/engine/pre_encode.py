@@ -47,8 +47,7 @@ class BatchedPreEncoder:
                                          sl.data_ptr(), B, M, F, self.cache_size, int(not first),
                                          x.data_ptr(), DTYPES[self.dtype], self.error.data_ptr(),
                                          _stream(self.device)), "pk_pre_encode_window")
-        lengths = torch.full((B,), pre + F, dtype=torch.int64, device=self.device)
-        y, _ = self.module(x.transpose(1, 2), lengths)
+        y = self.module.forward_full(x.transpose(1, 2))   # every row spans all frames
         if not first and self.drop_extra > 0:
             y = y[:, self.drop_extra:]
         return y

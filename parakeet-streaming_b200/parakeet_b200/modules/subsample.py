@@ -63,5 +63,23 @@ class ConvSubsampling(nn.Module):
         b, c, t, f = x.shape
         return self.out(x.transpose(1, 2).reshape(b, t, c * f)), lengths
 
+    def forward_full(self, x: Tensor) -> Tensor:
+        """``forward`` for a batch whose rows all span every frame (the
+        streaming pre-encode: no masks to apply).  Channels-last activations;
+        the causal padding is the conv's own symmetric padding of kernel-1 with
+        the trailing output frame dropped when the causal length is shorter,
+        which selects the same input windows as padding kernel-1 before and
+        stride-1 after."""
+        x = x.unsqueeze(1).contiguous(memory_format=torch.channels_last)
+        for layer in self.conv:
+            if isinstance(layer, nn.Conv2d) and layer.kernel_size[0] > 1:
+                t, f = self._out_len(x.shape[2]), self._out_len(x.shape[3])
+                x = F.conv2d(x, layer.weight, layer.bias, layer.stride, self._left_padding,
+                             1, layer.groups)[:, :, :t, :f]
+            else:
+                x = layer(x)
+        b, c, t, f = x.shape
+        return self.out(x.permute(0, 2, 1, 3).reshape(b, t, c * f))
+
 
 __all__ = ["ConvSubsampling"]

@@ -55,3 +55,12 @@ def test_subsampling_masks_frames_beyond_length():
     y, lens = m(torch.stack([x[0], x2[1]])[:, :25], torch.tensor([25, 17]))
     assert lens.tolist() == [4, l_full.item()]
     assert torch.allclose(y[1, : l_full.item()], y_full[0], rtol=1e-4, atol=1e-5)
+
+
+def test_full_length_path_equals_masked_forward():
+    m = build(PRE_SMALL)
+    x = torch.randn(3, 25, 128)
+    with torch.inference_mode():
+        y, _ = m(x, torch.full((3,), 25))
+        y2 = m.forward_full(x)
+    assert torch.allclose(y, y2, rtol=1e-5, atol=1e-5)
