@@ -406,6 +406,77 @@ def pre_encode_step(model, steps, dev, cpu_sample=4):
     return out
 
 
+def streaming_step(model, steps, dev):
+    """Features -> tokens for every stream of configs[2] (small, 160 streams)
+    or configs[3] on one GPU (large, 480 streams): batched pre-encode -> paged
+    encoder -> batched greedy decode (engine.pipeline.StreamingPipeline), random
+    bf16 weights, as one CUDA graph per steady-state step.  Streams that one
+    GPU sustains in real time at this batch = batch x audio per step / step time."""
+    import torch
+
+    from parakeet_b200.engine import StreamingPipeline
+    from parakeet_b200.modules import ConformerEncoder, ConvSubsampling, Joiner, Predictor
+    from parakeet_b200.weights import (random_decoder_state_dict, random_encoder_layers,
+                                       random_pre_encode_state_dict)
+    c, d = SHAPES[model], DECODE_CFG[model]
+    L, D, H, att = c["layers"], c["dim"], c["heads"], c["att"]
+    la, B, V = att[1], d["streams"], d["vocab"]
+    enc = ConformerEncoder(feat_in=128, hidden_size=D, ff_expansion_factor=4, num_layers=L,
+                           num_heads=H, subsampling_factor=8, pos_emb_max_len=5000,
+                           conv_kernel_size=9, att_context_size=att, subsampling_conv_channels=256,
+                           use_bias=False)
+    enc.load_state_dict({k: torch.from_numpy(v) for k, v in random_encoder_layers(0, L, D, H).items()})
+    pre = ConvSubsampling(D, 256, 128, 8)
+    pre.load_state_dict({k: torch.from_numpy(v)
+                         for k, v in random_pre_encode_state_dict(6, 128, 256, D).items()})
+    sd = random_decoder_state_dict(5, D, 640, 640, V, d["pred_layers"], blank_bias=2.3)
+    pred, join = Predictor(640, 640, d["pred_layers"], V), Joiner(D, 640, 640, num_classes=V)
+    pred.load_state_dict({k[10:]: torch.from_numpy(v) for k, v in sd.items()
+                          if k.startswith("predictor.")})
+    join.load_state_dict({k[7:]: torch.from_numpy(v) for k, v in sd.items()
+                          if k.startswith("joiner.")})
+    mods = [m.to(dev, torch.bfloat16).eval() for m in (enc, pre, pred, join)]
+    pipe = StreamingPipeline(*mods, blank_id=V, num_slots=B)
+    slots = torch.arange(B, dtype=torch.int32, device=dev)
+    pipe.start_streams(slots)
+    g = torch.Generator(device=dev).manual_seed(11)
+    first = torch.randn(B, 128, 1 + 8 * la, generator=g, device=dev).to(torch.bfloat16)
+    nxt = torch.randn(B, 128, 8 + 8 * la, generator=g, device=dev).to(torch.bfloat16)
+    out = {"model": model, "streams": B, "audio_ms_per_step": (la + 1) * 80.0}
+    with torch.inference_mode():
+        pipe.step(first, slots, first=True)
+        for _ in range(-(-att[0] // (la + 1)) + 2):   # fill the left context
+            tok, cnt = pipe.step(nxt, slots, first=False)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(steps):
+            pipe.step(nxt, slots, first=False)
+        b.record()
+        torch.cuda.synchronize()
+        out["ms_per_step_eager"] = round(a.elapsed_time(b) / steps, 4)
+        try:
+            gph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gph):
+                tok, cnt = pipe.step(nxt, slots, first=False)
+            gph.replay()
+            torch.cuda.synchronize()
+            a.record()
+            for _ in range(steps):
+                gph.replay()
+            b.record()
+            torch.cuda.synchronize()
+            out["ms_per_step_graph"] = round(a.elapsed_time(b) / steps, 4)
+            del gph
+        except Exception as e:   # informative; keep the run going
+            out["graph_error"] = str(e)[:200]
+        out["tokens_per_frame"] = round(float(cnt.float().mean()), 2)
+    best = min(v for k, v in out.items() if k.startswith("ms_per_step"))
+    out["realtime_streams_at_this_batch"] = int(B * out["audio_ms_per_step"] / best)
+    out["device_error_word"] = pipe.pool.read_error()
+    return out
+
+
 def max_over_ranks(vals, device):
     """Element-wise max of per-rank timings over the process group (the step
     time of a weak-scaling run is its slowest rank's); identity on one rank."""
@@ -574,11 +645,12 @@ def main():
             dist.barrier()
         ms = g0.elapsed_time(g1) / K
     clk = clocks.stop()
-    enc_line = dec_line = pre_line = None
+    enc_line = dec_line = pre_line = pipe_line = None
     if rank == 0 and not args.no_breakdown:
         enc_line = encoder_step(args.model, 160 if args.model == "small" else 480, 20, dev)
         dec_line = rnnt_decode_step(args.model, 10, dev)
         pre_line = pre_encode_step(args.model, 10, dev)
+        pipe_line = streaming_step(args.model, 10, dev)
     err = pool.read_error()
 
     # ---- end to end through the public API, as a serving loop runs it: every step
@@ -731,6 +803,7 @@ def main():
             "encoder_step": enc_line,
             "rnnt_decode": dec_line,
             "pre_encode": pre_line,
+            "streaming_step": pipe_line,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

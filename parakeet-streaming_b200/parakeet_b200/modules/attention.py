@@ -72,7 +72,11 @@ class ConformerAttention(nn.Module):
         """linear_pos(pos_emb) as [P, D], cached while pos_emb and the weight
         are unchanged (attention.py:102-106 recomputes it every call)."""
         w = self.linear_pos.weight
-        key = (pos_emb.data_ptr(), tuple(pos_emb.shape), pos_emb.dtype, w.data_ptr(), w._version)
+        try:
+            version = w._version
+        except RuntimeError:   # an inference-mode tensor has no version counter
+            version = None
+        key = (pos_emb.data_ptr(), tuple(pos_emb.shape), pos_emb.dtype, w.data_ptr(), version)
         if self._pos_key != key:
             self._pos_proj = self.linear_pos(pos_emb.to(w.dtype)).reshape(-1, w.shape[0]).contiguous()
             self._pos_key = key
