@@ -70,7 +70,7 @@ def parse():
                     help="prefill + warmup + --steps steps only (for ncu), no report")
     ap.add_argument("--profile-op", default=None,
                     choices=["append", "attention", "attention+append", "gather",
-                             "gather_all_layers", "conv"],
+                             "gather_all_layers", "conv", "features"],
                     help="prefill + warmup, then --steps runs of one breakdown op (for ncu)")
     return ap.parse_args()
 
@@ -406,12 +406,166 @@ def pre_encode_step(model, steps, dev, cpu_sample=4):
     return out
 
 
+def synth_audio_batch(streams, n, seed):
+    """float32 [streams, n] of configs[2]'s synthetic audio: per stream three
+    tones in 100-4000 Hz with random phases plus white noise at 20 dB SNR,
+    quantised to pcm16, scaled to [-1, 1)."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    t = np.arange(n) / 16000.0
+    out = np.empty((streams, n), np.float32)
+    for i in range(streams):
+        f, ph = rng.uniform(100.0, 4000.0, 3), rng.uniform(0.0, 2 * np.pi, 3)
+        tone = sum(np.sin(2 * np.pi * fk * t + p) for fk, p in zip(f, ph)) / 3.0
+        x = 0.5 * (tone + rng.standard_normal(n) * np.sqrt(np.mean(tone ** 2)) / 10.0)
+        out[i] = np.clip(np.round(x * 32767.0), -32768, 32767) / 32768.0
+    return out
+
+
+def feature_step(model, steps, dev, cpu_sample=8):
+    """Batched streaming log-mel extraction of one steady-state chunk per
+    stream (pk_features_push: pre-emphasis, window, 512-point FFT, slaney mel,
+    log; the reference's defaults, dither included), bf16 output as the
+    pre-encoder takes it, eager and as a CUDA graph.  Beside it the reference's
+    per-stream push (recompute over the retained buffer, feature_extractor.py:
+    97-151) restated in oracle/features.py, timed on `cpu_sample` streams and
+    scaled to the batch."""
+    import torch
+
+    from parakeet_b200.modules import FeatureExtractor
+    la = SHAPES[model]["att"][1]
+    B = 160 if model == "small" else 480
+    hop = 160
+    n0, n = (1 + 8 * la) * hop, (8 + 8 * la) * hop
+    F = n // hop
+    fe = FeatureExtractor(num_slots=B, device=dev, out_dtype=torch.bfloat16)
+    audio = synth_audio_batch(B, n0 + n, seed=21)
+    fe.push_batch(audio[:, :n0], list(range(B)), first=True)
+    x = torch.from_numpy(audio[:, n0:]).to(dev).contiguous()
+    ns = torch.full((B,), n, dtype=torch.int32, device=dev)
+    flags = torch.zeros(B, dtype=torch.int32, device=dev)
+    slots = torch.arange(B, dtype=torch.int32, device=dev)
+    out = torch.empty(B, 128, F, dtype=torch.bfloat16, device=dev)
+    nf = torch.empty(B, dtype=torch.int32, device=dev)
+    res = {"model": model, "streams": B, "samples_per_push": n, "frames_per_push": F}
+    for _ in range(3):
+        fe.launch(x, ns, flags, slots, out, F, nf)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        fe.launch(x, ns, flags, slots, out, F, nf)
+    b.record()
+    torch.cuda.synchronize()
+    res["ms_per_push_eager"] = round(a.elapsed_time(b) / steps, 4)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    gph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s), torch.cuda.graph(gph, stream=s):
+        for _ in range(10):
+            fe.launch(x, ns, flags, slots, out, F, nf)
+    torch.cuda.current_stream().wait_stream(s)
+    gph.replay()
+    torch.cuda.synchronize()
+    reps = max(1, steps // 10)
+    a.record()
+    for _ in range(reps):
+        gph.replay()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / (reps * 10)
+    del gph
+    res["ms_per_push_graph"] = round(ms, 4)
+    res["device_error_word"] = fe.error_bits()
+    alg = B * n * 4 + B * 512 * 4 * 2 + B * 128 * F * 2
+    res["alg_bytes_per_push"] = alg
+    res["GB/s"] = round(alg / (ms * 1e-3) / 1e9, 1)
+    res["frames_per_s"] = int(B * F / (ms * 1e-3))
+    res["l2"] = "inputs L2-resident (back-to-back pushes of one chunk)"
+    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+    from oracle.features import FeatureStream, LogMel
+    mel = LogMel()
+    k = min(cpu_sample, B)
+    streams = [FeatureStream(mel) for _ in range(k)]
+    for i in range(k):
+        streams[i].push(audio[i, :n0])
+    t0 = time.perf_counter()
+    for i in range(k):
+        streams[i].push(audio[i, n0:])
+    el = time.perf_counter() - t0
+    res["cpu_reference_ms_per_push"] = round(el / k * B * 1e3, 2)
+    res["cpu_reference"] = (f"oracle/features.py FeatureStream.push (the reference's recompute "
+                            f"over the retained buffer, numpy float64, 1 thread), {k} streams "
+                            f"timed, scaled to {B}")
+    return res
+
+
+def profile_features(model, steps, dev):
+    """First push, then `steps` steady pushes of the log-mel kernel (the
+    configuration of feature_step), nothing else: a short launch list for ncu."""
+    import torch
+
+    from parakeet_b200.modules import FeatureExtractor
+    la = SHAPES[model]["att"][1]
+    B = 160 if model == "small" else 480
+    n0, n = (1 + 8 * la) * 160, (8 + 8 * la) * 160
+    fe = FeatureExtractor(num_slots=B, device=dev, out_dtype=torch.bfloat16)
+    audio = synth_audio_batch(B, n0 + n * steps, seed=21)
+    fe.push_batch(audio[:, :n0], list(range(B)), first=True)
+    for k in range(steps):
+        fe.push_batch(audio[:, n0 + k * n:n0 + (k + 1) * n], list(range(B)))
+    torch.cuda.synchronize()
+    return {"profile_run": model, "op": "features", "steps": steps,
+            "device_error_word": fe.error_bits()}
+
+
+def stage_times(pipe, samples, slots, reps):
+    """Device time of each stage of one steady step_audio, each stage captured
+    as its own CUDA graph and replayed `reps` times (the stages run in order,
+    so every replay sees the state its predecessor left)."""
+    import torch
+
+    from parakeet_b200.modules.cache import PagedModelCache, StreamingState
+    B, n = samples.shape
+    F = pipe.frames_per_push(n, False)
+    ns, flags, feats, nframes = pipe._fe_bufs[(B, n, False)]
+    graphs, res = [], {}
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def timed(name, fn):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            r = fn()
+        graphs.append(g)
+        g.replay()
+        torch.cuda.synchronize()
+        a.record()
+        for _ in range(reps):
+            g.replay()
+        b.record()
+        torch.cuda.synchronize()
+        res[name] = round(a.elapsed_time(b) / reps, 4)
+        return r
+
+    timed("features", lambda: pipe.fe.launch(samples, ns, flags, slots, feats, F, nframes))
+    x = timed("pre_encode", lambda: pipe.pre.pre_encode(feats, slots, False))
+    y = timed("encoder", lambda: pipe.encoder(x, StreamingState(PagedModelCache(pipe.pool, slots)),
+                                              bypass_pre_encode=True)[0])
+    T = x.shape[1]
+    lengths = torch.full((B,), T, dtype=torch.int32, device=samples.device)
+    timed("decode", lambda: pipe.dec.decode(y.transpose(1, 2), lengths, slots))
+    del graphs
+    return res
+
+
 def streaming_step(model, steps, dev):
-    """Features -> tokens for every stream of configs[2] (small, 160 streams)
-    or configs[3] on one GPU (large, 480 streams): batched pre-encode -> paged
-    encoder -> batched greedy decode (engine.pipeline.StreamingPipeline), random
-    bf16 weights, as one CUDA graph per steady-state step.  Streams that one
-    GPU sustains in real time at this batch = batch x audio per step / step time."""
+    """Audio -> tokens for every stream of configs[2] (small, 160 streams) or
+    configs[3] on one GPU (large, 480 streams): batched log-mel features ->
+    batched pre-encode -> paged encoder -> batched greedy decode
+    (engine.pipeline.StreamingPipeline.step_audio), random bf16 weights,
+    synthetic audio of configs[2], as one CUDA graph per steady-state step.
+    Streams that one GPU sustains in real time at this batch = batch x audio
+    per step / step time."""
     import torch
 
     from parakeet_b200.engine import StreamingPipeline
@@ -439,26 +593,27 @@ def streaming_step(model, steps, dev):
     pipe = StreamingPipeline(*mods, blank_id=V, num_slots=B)
     slots = torch.arange(B, dtype=torch.int32, device=dev)
     pipe.start_streams(slots)
-    g = torch.Generator(device=dev).manual_seed(11)
-    first = torch.randn(B, 128, 1 + 8 * la, generator=g, device=dev).to(torch.bfloat16)
-    nxt = torch.randn(B, 128, 8 + 8 * la, generator=g, device=dev).to(torch.bfloat16)
-    out = {"model": model, "streams": B, "audio_ms_per_step": (la + 1) * 80.0}
+    n0, n = (1 + 8 * la) * 160, (8 + 8 * la) * 160
+    audio = torch.from_numpy(synth_audio_batch(B, n0 + n, seed=11)).to(dev)
+    first, nxt = audio[:, :n0].contiguous(), audio[:, n0:].contiguous()
+    out = {"model": model, "streams": B, "audio_ms_per_step": (la + 1) * 80.0,
+           "input": "16 kHz float samples, one chunk per stream per step"}
     with torch.inference_mode():
-        pipe.step(first, slots, first=True)
-        for _ in range(-(-att[0] // (la + 1)) + 2):   # fill the left context
-            tok, cnt = pipe.step(nxt, slots, first=False)
+        pipe.step_audio(first, slots, 0)
+        for k in range(-(-att[0] // (la + 1)) + 2):   # fill the left context
+            tok, cnt = pipe.step_audio(nxt, slots, 1 + k)
         torch.cuda.synchronize()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         for _ in range(steps):
-            pipe.step(nxt, slots, first=False)
+            pipe.step_audio(nxt, slots, 2)
         b.record()
         torch.cuda.synchronize()
         out["ms_per_step_eager"] = round(a.elapsed_time(b) / steps, 4)
         try:
             gph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(gph):
-                tok, cnt = pipe.step(nxt, slots, first=False)
+                tok, cnt = pipe.step_audio(nxt, slots, 2)
             gph.replay()
             torch.cuda.synchronize()
             a.record()
@@ -471,9 +626,13 @@ def streaming_step(model, steps, dev):
         except Exception as e:   # informative; keep the run going
             out["graph_error"] = str(e)[:200]
         out["tokens_per_frame"] = round(float(cnt.float().mean()), 2)
+        try:
+            out["stage_ms_graph"] = stage_times(pipe, nxt, slots, steps)
+        except Exception as e:   # informative; keep the run going
+            out["stage_error"] = str(e)[:200]
     best = min(v for k, v in out.items() if k.startswith("ms_per_step"))
     out["realtime_streams_at_this_batch"] = int(B * out["audio_ms_per_step"] / best)
-    out["device_error_word"] = pipe.pool.read_error()
+    out["device_error_word"] = pipe.pool.read_error() | pipe.fe.error_bits()
     return out
 
 
@@ -513,6 +672,9 @@ def main():
         dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    if args.profile_op == "features":   # the log-mel kernel alone, for ncu
+        print(json.dumps(profile_features(args.model, args.steps, dev)))
+        return
     c = SHAPES[args.model]
     L, D, H, att = c["layers"], c["dim"], c["heads"], c["att"]
     left, T = att[0], att[1] + 1
@@ -645,11 +807,12 @@ def main():
             dist.barrier()
         ms = g0.elapsed_time(g1) / K
     clk = clocks.stop()
-    enc_line = dec_line = pre_line = pipe_line = None
+    enc_line = dec_line = pre_line = fe_line = pipe_line = None
     if rank == 0 and not args.no_breakdown:
         enc_line = encoder_step(args.model, 160 if args.model == "small" else 480, 20, dev)
         dec_line = rnnt_decode_step(args.model, 10, dev)
         pre_line = pre_encode_step(args.model, 10, dev)
+        fe_line = feature_step(args.model, 50, dev)
         pipe_line = streaming_step(args.model, 10, dev)
     err = pool.read_error()
 
@@ -803,6 +966,7 @@ def main():
             "encoder_step": enc_line,
             "rnnt_decode": dec_line,
             "pre_encode": pre_line,
+            "features": fe_line,
             "streaming_step": pipe_line,
         }
         print(json.dumps(line), flush=True)

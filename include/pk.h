@@ -208,16 +208,18 @@ int pk_conv_step(void *conv_state, int32_t num_slots, int32_t num_layers,
                  const int32_t *slots, const int32_t *lengths, int32_t batch,
                  void *y, int32_t *error, void *stream);
 
-/* Streaming pre-encoder input of a batch: out[b] = cat(cache[slots[b]],
- * feats[b]) along time ([batch][feat_in][csize + frames]; just feats[b] when
- * use_cache == 0, a stream's first chunk), then cache[slots[b]] = the last
- * csize frames (frames >= csize).  cache [num_slots][feat_in][csize], feats
- * [batch][feat_in][frames], `dtype` PK_DTYPE_*; bad slot ids set
- * PK_DEV_BAD_SLOT in *error.  Replaces the per-stream cache copies of
+/* Streaming pre-encoder input of a batch: out[b] = cat(the last prefix_frames
+ * cached frames of slot slots[b], feats[b]) along time ([batch][feat_in]
+ * [prefix_frames + frames]; prefix_frames = 0 for a stream's first chunk),
+ * then cache[slots[b]] = the last min(csize, prefix_frames + frames) frames of
+ * out[b], right-aligned.  cache [num_slots][feat_in][csize], feats [batch]
+ * [feat_in][frames], `dtype` PK_DTYPE_*; prefix_frames must not exceed the
+ * frames the slot's cache holds (csize, or a shorter first window); bad slot
+ * ids set PK_DEV_BAD_SLOT in *error.  Replaces the per-stream cache copies of
  * ModelRunner._run_pre_encode (parakeet/engine/model_runner.py:197-233). */
 int pk_pre_encode_window(void *cache, int32_t num_slots, const void *feats,
                          const int32_t *slots, int32_t batch, int32_t feat_in, int32_t frames,
-                         int32_t csize, int32_t use_cache, void *out, int32_t dtype,
+                         int32_t csize, int32_t prefix_frames, void *out, int32_t dtype,
                          int32_t *error, void *stream);
 
 /* ---------------- batched greedy RNNT decode (device-side bookkeeping) ----
@@ -249,6 +251,68 @@ int pk_rnnt_pick(const void *logits, int64_t logits_ld, int32_t dtype, int32_t b
 int pk_lstm_cell(const void *gates, int64_t gates_ld, void *h, void *c, int64_t state_ld,
                  const int32_t *emit, int32_t batch, int32_t hidden, int32_t dtype,
                  void *stream);
+
+/* ---------------- streaming log-mel features ------------------------------
+ * The feature extractor of every stream in one launch per push.  Replaces
+ * FeatureExtractor.push / _compute_features / _trim_samples
+ * (parakeet/modules/feature_extractor.py:63-151), which recompute an STFT
+ * over each stream's retained samples on the host at every push: here each
+ * slot keeps its last PK_FE_HIST samples and two counters on the device, and
+ * a push computes only the frames it emits.  Frame f of a stream covers
+ * samples [f*hop - n_fft/2, f*hop + n_fft/2) after pre-emphasis (y[0] = x[0]),
+ * zero outside [0, samples seen); a push emits the frames the reference's
+ * push emits (every frame whose window ends inside the samples seen, or up to
+ * samples_seen / hop on a final push; none on an empty push). */
+#define PK_FE_HIST 512        /* samples of history kept per slot             */
+#define PK_FE_META_STRIDE 4   /* int64 per slot: samples seen, frames emitted,
+                                 stream epoch, CTA ticket (zero when idle)     */
+#define PK_FE_FIRST 1         /* push flag: a fresh stream (counters restart)  */
+#define PK_FE_FINAL 2         /* push flag: the stream's last samples (frames
+                                 up to samples_seen / hop, zero-padded)        */
+#define PK_DEV_BAD_COUNT 16   /* device error bit: a row's sample count outside
+                                 [0, samples_ld] or more frames than max_frames */
+
+typedef struct pk_features_desc {
+    const void *tables;   /* device copy of pk_features_tables' output        */
+    float *history;       /* [num_slots][PK_FE_HIST] last samples of each slot */
+    int64_t *meta;        /* [num_slots][PK_FE_META_STRIDE], zeroed once       */
+    int32_t *error;       /* [1] device error word (PK_DEV_* bits)            */
+    int32_t num_slots;
+    int32_t n_fft;        /* 512 (the only size this build handles)           */
+    int32_t hop;          /* window_stride * sample_rate (160), <= n_fft      */
+    int32_t n_mels;       /* <= 256                                           */
+    int32_t mel_nnz;      /* nonzero filter weights, from pk_features_tables  */
+    float preemph;        /* 0.97                                             */
+    float dither;         /* std of the Gaussian dither added to the samples  */
+    float mag_power;      /* spectrum = |X| ** mag_power (2.0)                */
+    float log_guard;      /* log(mel + log_guard) (2 ** -24)                  */
+    float pad_value;      /* output columns past a row's frame count          */
+    uint64_t seed;        /* dither: Philox-4x32-10 key                       */
+} pk_features_desc;
+
+/* Constant tables of an extractor configuration, written to the host buffer
+ * `host_out` (NULL: only report the size): the n_fft-point twiddles, the
+ * symmetric Hann window of win_length samples centred in n_fft
+ * (torch.hann_window(periodic=False), as torch.stft pads it), and the mel
+ * filters of librosa.filters.mel(sr, n_fft, n_mels, fmin, fmax, norm) with
+ * norm 1 = "slaney", 0 = none, stored by their nonzero runs.  *bytes is the
+ * size, *mel_nnz the nonzero weights (the desc's mel_nnz).  Replaces the
+ * constructor's tables (feature_extractor.py:46-57). */
+int pk_features_tables(int32_t sample_rate, int32_t n_fft, int32_t win_length, int32_t n_mels,
+                       double fmin, double fmax, int32_t mel_norm, void *host_out,
+                       int64_t *bytes, int32_t *mel_nnz);
+
+/* One push for `batch` streams: row b appends num_samples[b] float samples
+ * (samples + b * samples_ld) to slot slots[b] (flags[b]: PK_FE_FIRST,
+ * PK_FE_FINAL) and writes the log-mel frames it emits to out[b] ([n_mels]
+ * [max_frames], `out_dtype` PK_DTYPE_*, columns past the row's count =
+ * pad_value) and their count to num_frames[b].  A row with more frames than
+ * max_frames keeps the first max_frames and sets PK_DEV_BAD_COUNT.  Each slot
+ * appears at most once per call. */
+int pk_features_push(const pk_features_desc *fe, const float *samples, int64_t samples_ld,
+                     const int32_t *num_samples, const int32_t *flags, const int32_t *slots,
+                     int32_t batch, void *out, int32_t out_dtype, int32_t max_frames,
+                     int32_t *num_frames, void *stream);
 
 /* Text of the last PK_ECUDA / PK_EINVAL cause seen by this thread. */
 const char *pk_last_error(void);

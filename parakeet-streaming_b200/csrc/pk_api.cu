@@ -357,16 +357,18 @@ int pk_conv_step(void *conv_state, int32_t num_slots, int32_t num_layers, int32_
 
 int pk_pre_encode_window(void *cache, int32_t num_slots, const void *feats,
                          const int32_t *slots, int32_t batch, int32_t feat_in, int32_t frames,
-                         int32_t csize, int32_t use_cache, void *out, int32_t dtype,
+                         int32_t csize, int32_t prefix_frames, void *out, int32_t dtype,
                          int32_t *error, void *stream) {
     PK_CHECK(dtype == PK_DTYPE_F32 || dtype == PK_DTYPE_BF16, "bad dtype %d", dtype);
     PK_CHECK(batch >= 0, "negative batch");
     if (batch == 0) return PK_OK;
     PK_CHECK(cache && feats && slots && out && num_slots > 0, "null pointer or empty pool");
     PK_CHECK(feat_in > 0 && csize > 0 && csize <= 32, "cache of 1..32 frames");
-    PK_CHECK(frames >= csize, "a chunk shorter than the cache is not handled");
+    PK_CHECK(frames > 0, "empty chunk");
+    PK_CHECK(prefix_frames >= 0 && prefix_frames <= csize, "prefix_frames %d outside [0, %d]",
+             prefix_frames, csize);
     return launch_pre_encode_window(cache, feats, slots, batch, feat_in, frames, csize,
-                                    use_cache != 0, out, dtype, error, num_slots,
+                                    prefix_frames, out, dtype, error, num_slots,
                                     static_cast<cudaStream_t>(stream));
 }
 
@@ -398,6 +400,80 @@ int pk_lstm_cell(const void *gates, int64_t gates_ld, void *h, void *c, int64_t 
     PK_CHECK(gates_ld >= 4 * (int64_t)hidden && state_ld >= hidden, "bad strides");
     return launch_lstm_cell(gates, gates_ld, h, c, state_ld, emit, batch, hidden, dtype,
                             static_cast<cudaStream_t>(stream));
+}
+
+int pk_features_tables(int32_t sample_rate, int32_t n_fft, int32_t win_length, int32_t n_mels,
+                       double fmin, double fmax, int32_t mel_norm, void *host_out,
+                       int64_t *bytes, int32_t *mel_nnz) {
+    PK_CHECK(bytes && mel_nnz, "null pointer");
+    PK_CHECK(sample_rate > 0, "sample rate %d", sample_rate);
+    PK_CHECK(n_fft >= 2 && (n_fft & (n_fft - 1)) == 0 && n_fft <= 65536,
+             "n_fft %d is not a power of two", n_fft);
+    PK_CHECK(win_length >= 1 && win_length <= n_fft, "win_length %d outside [1, n_fft]",
+             win_length);
+    PK_CHECK(n_mels >= 1 && n_mels <= 256, "n_mels %d outside [1, 256]", n_mels);
+    PK_CHECK(fmin >= 0.0 && fmax > fmin && fmax <= sample_rate / 2.0,
+             "mel range [%g, %g] outside [0, sample_rate / 2]", fmin, fmax);
+    PK_CHECK(mel_norm == 0 || mel_norm == 1, "mel_norm %d (0 none, 1 slaney)", mel_norm);
+    int64_t words = 0;
+    build_feature_tables(sample_rate, n_fft, win_length, n_mels, fmin, fmax, mel_norm, nullptr,
+                         &words, mel_nnz);
+    *bytes = words * (int64_t)sizeof(int32_t);
+    if (!host_out) return PK_OK;
+    return build_feature_tables(sample_rate, n_fft, win_length, n_mels, fmin, fmax, mel_norm,
+                                static_cast<int32_t *>(host_out), &words, mel_nnz);
+}
+
+int pk_features_push(const pk_features_desc *fe, const float *samples, int64_t samples_ld,
+                     const int32_t *num_samples, const int32_t *flags, const int32_t *slots,
+                     int32_t batch, void *out, int32_t out_dtype, int32_t max_frames,
+                     int32_t *num_frames, void *stream) {
+    PK_CHECK(fe, "null descriptor");
+    PK_CHECK(out_dtype == PK_DTYPE_F32 || out_dtype == PK_DTYPE_BF16, "bad dtype %d", out_dtype);
+    PK_CHECK(batch >= 0 && batch <= 65535, "batch %d outside [0, 65535]", batch);
+    if (batch == 0) return PK_OK;
+    PK_CHECK(fe->tables && fe->history && fe->meta && fe->error && fe->num_slots > 0,
+             "descriptor has a null buffer or no slots");
+    if (fe->n_fft != 512) {
+        set_error("n_fft %d: this build computes 512-point frames", fe->n_fft);
+        return PK_ENOTSUP;
+    }
+    PK_CHECK(fe->hop >= 1 && fe->hop <= fe->n_fft, "hop %d outside [1, n_fft]", fe->hop);
+    PK_CHECK(fe->n_mels >= 1 && fe->n_mels <= 256, "n_mels %d outside [1, 256]", fe->n_mels);
+    PK_CHECK(fe->mel_nnz >= 0 && fe->mel_nnz <= fe->n_mels * (fe->n_fft / 2 + 1),
+             "mel_nnz %d", fe->mel_nnz);
+    PK_CHECK(num_samples && flags && slots && num_frames, "null pointer");
+    PK_CHECK(samples || samples_ld == 0, "null samples with samples_ld > 0");
+    PK_CHECK(samples_ld >= 0, "negative samples_ld");
+    PK_CHECK(max_frames >= 0, "negative max_frames");
+    PK_CHECK(max_frames == 0 || out, "null output");
+    FeArgs a;
+    a.tables = static_cast<const int32_t *>(fe->tables);
+    a.hist = fe->history;
+    a.meta = fe->meta;
+    a.error = fe->error;
+    a.num_slots = fe->num_slots;
+    a.hop = fe->hop;
+    a.n_mels = fe->n_mels;
+    a.nnz = fe->mel_nnz;
+    a.preemph = fe->preemph;
+    a.dither = fe->dither;
+    a.mag_power = fe->mag_power;
+    a.guard = fe->log_guard;
+    a.pad = fe->pad_value;
+    a.seed_lo = (uint32_t)fe->seed;
+    a.seed_hi = (uint32_t)(fe->seed >> 32);
+    a.samples = samples;
+    a.ld = samples_ld;
+    a.nsamp = num_samples;
+    a.flags = flags;
+    a.slots = slots;
+    a.batch = batch;
+    a.out = out;
+    a.out_dtype = out_dtype;
+    a.max_frames = max_frames;
+    a.nframes = num_frames;
+    return launch_features(a, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

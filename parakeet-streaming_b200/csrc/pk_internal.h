@@ -104,7 +104,7 @@ int launch_conv(const ConvArgs &a, cudaStream_t s);
 
 // pk_pre_encode.cu
 int launch_pre_encode_window(void *cache, const void *feats, const int32_t *slots, int batch,
-                             int feat_in, int frames, int csize, int use_cache, void *out,
+                             int feat_in, int frames, int csize, int prefix, void *out,
                              int dtype, int32_t *error, int num_slots, cudaStream_t s);
 
 // pk_rnnt.cu
@@ -114,5 +114,32 @@ int launch_rnnt_pick(const void *logits, int64_t ld, int dtype, int batch, int n
                      cudaStream_t s);
 int launch_lstm_cell(const void *gates, int64_t gld, void *h, void *c, int64_t sld,
                      const int32_t *emit, int batch, int hidden, int dtype, cudaStream_t s);
+
+// pk_features.cu.  Table block: int32 header[kFeHeader], then float2
+// twiddle[n_fft] (exp(-2 pi i u / n_fft)), float window[n_fft], int32 lo[n_mels],
+// cnt[n_mels], off[n_mels] (first bin, length and offset of each filter's
+// nonzero run), float weight[nnz].
+constexpr int kFeHeader = 16;
+enum FeHeaderField { kFeMagic = 0, kFeNfft, kFeNmels, kFeNnz, kFeWin, kFeRate };
+constexpr int32_t kFeMagicValue = 0x45464b50;  // "PKFE"
+int build_feature_tables(int sample_rate, int n_fft, int win_length, int n_mels, double fmin,
+                         double fmax, int norm, int32_t *words, int64_t *nwords, int32_t *nnz);
+struct FeArgs {
+    const int32_t *tables;
+    float *hist;
+    int64_t *meta;
+    int32_t *error;
+    int num_slots, hop, n_mels, nnz;
+    float preemph, dither, mag_power, guard, pad;
+    uint32_t seed_lo, seed_hi;
+    const float *samples;
+    int64_t ld;
+    const int32_t *nsamp, *flags, *slots;
+    int batch;
+    void *out;
+    int out_dtype, max_frames;
+    int32_t *nframes;
+};
+int launch_features(const FeArgs &a, cudaStream_t s);
 
 }  // namespace pk

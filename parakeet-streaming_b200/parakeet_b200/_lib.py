@@ -17,6 +17,8 @@ HEADER = os.path.join(os.path.dirname(os.path.dirname(_HERE)), "include", "pk.h"
 PK_OK, PK_EINVAL, PK_ECUDA, PK_ENOTSUP = 0, 1, 2, 3
 PK_DTYPE_F32, PK_DTYPE_BF16 = 0, 1
 PK_DEV_POOL_EXHAUSTED, PK_DEV_BAD_PAGE, PK_DEV_TIMEOUT, PK_DEV_BAD_SLOT = 1, 2, 4, 8
+PK_DEV_BAD_COUNT = 16
+PK_FE_HIST, PK_FE_META_STRIDE, PK_FE_FIRST, PK_FE_FINAL = 512, 4, 1, 2
 META_FIRST, META_NEXT, META_WRITTEN, META_PROCESSED, META_CACHE_LEN = 0, 1, 2, 3, 4
 META_STRIDE = 8
 WIN_STRIDE = 128
@@ -48,6 +50,26 @@ class PagedKVDesc(ctypes.Structure):
     ]
 
 
+class FeaturesDesc(ctypes.Structure):
+    _fields_ = [
+        ("tables", ctypes.c_void_p),
+        ("history", ctypes.c_void_p),
+        ("meta", ctypes.c_void_p),
+        ("error", ctypes.c_void_p),
+        ("num_slots", ctypes.c_int32),
+        ("n_fft", ctypes.c_int32),
+        ("hop", ctypes.c_int32),
+        ("n_mels", ctypes.c_int32),
+        ("mel_nnz", ctypes.c_int32),
+        ("preemph", ctypes.c_float),
+        ("dither", ctypes.c_float),
+        ("mag_power", ctypes.c_float),
+        ("log_guard", ctypes.c_float),
+        ("pad_value", ctypes.c_float),
+        ("seed", ctypes.c_uint64),
+    ]
+
+
 _P = ctypes.c_void_p
 _I32 = ctypes.c_int32
 _I64 = ctypes.c_int64
@@ -71,6 +93,10 @@ SIGNATURES = {
                            _I64, _P, _P, _I32, _P, _I64, _I64, _I64, _P],
     "pk_conv_step": [_P, _I32, _I32, _I32, _I32, _I32, _I32, _I32, _P, _I64, _I64, _P, _P, _P,
                      ctypes.c_float, _P, _P, _I32, _P, _P, _P],
+    "pk_features_tables": [_I32, _I32, _I32, _I32, ctypes.c_double, ctypes.c_double, _I32, _P,
+                           ctypes.POINTER(_I64), ctypes.POINTER(_I32)],
+    "pk_features_push": [ctypes.POINTER(FeaturesDesc), _P, _I64, _P, _P, _P, _I32, _P, _I32, _I32,
+                         _P, _P],
     "pk_last_error": [],
 }
 RESTYPES = {"pk_last_error": ctypes.c_char_p}

@@ -32,19 +32,25 @@ class BatchedPreEncoder:
                                  device=self.device)
         self.error = torch.zeros(1, dtype=torch.int32, device=self.device)
 
-    def pre_encode(self, feats: torch.Tensor, slots: torch.Tensor, first: bool) -> torch.Tensor:
+    def pre_encode(self, feats: torch.Tensor, slots: torch.Tensor, first: bool,
+                   prefix: int | None = None) -> torch.Tensor:
         """feats [B, feat_in, frames] (the feature extractor's layout), slots
-        [B]; ``first``: the streams' first chunks (no cache).  Returns the
-        pre-encoded frames [B, frames', hidden] and advances the caches."""
+        [B]; ``first``: the streams' first chunks (no cache); ``prefix``: the
+        cached frames to prepend (default: the cache size; fewer after a first
+        chunk shorter than the cache, which the cache then holds whole,
+        model_runner.py:225-230).  Returns the pre-encoded frames [B, frames',
+        hidden] and advances the caches."""
         B, M, F = feats.shape
         if M != self.feat_in:
             raise ValueError(f"{M} feature bins, the subsampling takes {self.feat_in}")
+        pre = 0 if first else (self.cache_size if prefix is None else int(prefix))
+        if not 0 <= pre <= self.cache_size:
+            raise ValueError(f"prefix {pre} outside [0, {self.cache_size}]")
         feats = feats.to(device=self.device, dtype=self.dtype).contiguous()
         sl = slots.to(device=self.device, dtype=torch.int32).contiguous()
-        pre = 0 if first else self.cache_size
         x = torch.empty(B, M, pre + F, dtype=self.dtype, device=self.device)
         check(lib().pk_pre_encode_window(self.cache.data_ptr(), self.num_slots, feats.data_ptr(),
-                                         sl.data_ptr(), B, M, F, self.cache_size, int(not first),
+                                         sl.data_ptr(), B, M, F, self.cache_size, pre,
                                          x.data_ptr(), DTYPES[self.dtype], self.error.data_ptr(),
                                          _stream(self.device)), "pk_pre_encode_window")
         y = self.module.forward_full(x.transpose(1, 2))   # every row spans all frames

@@ -10,7 +10,10 @@ extractor): feats_in = cat(cache, feats) when a cache exists, subsample, drop
 the first ``drop_extra_pre_encoded`` output frames when a cache was used,
 cache = last ``pre_encode_cache_size`` frames of feats_in.  First chunks have
 1 + 8 * lookahead feature frames, later ones 8 + 8 * lookahead
-(model_runner.py:53-56).  Saves ``pre_encode_small.npz`` / ``_large.npz``.
+(model_runner.py:53-56); ``PRE_SMALL_AUDIO`` has the 8-frame first chunks that
+the feature extractor emits from a first chunk of samples, shorter than the
+cache, which then holds the whole first window.  Saves
+``pre_encode_small.npz`` / ``_large.npz`` / ``_small_audio.npz``.
 
 Usage:  python tests/golden/make_golden_pre_encode.py --reference <path to reference>
 """
@@ -34,10 +37,15 @@ PRE_SMALL = dict(feat_in=128, channels=256, hidden=512, lookahead=1, cache=9, dr
                  steps=4, streams=[("a", 0), ("b", 0), ("c", 2)])
 PRE_LARGE = dict(feat_in=128, channels=256, hidden=1024, lookahead=13, cache=9, drop=2, seed=42,
                  steps=3, streams=[("a", 0), ("b", 1)])
+# first chunks as the feature extractor emits them from 1 + 8 * lookahead hops of
+# samples: 8 * lookahead frames, fewer than the cache for lookahead 1
+PRE_SMALL_AUDIO = dict(PRE_SMALL, seed=43, first_frames=8)
 
 
 def chunk_frames(cfg, first):
-    return 1 + 8 * cfg["lookahead"] if first else 8 + 8 * cfg["lookahead"]
+    if first:
+        return cfg.get("first_frames", 1 + 8 * cfg["lookahead"])
+    return 8 + 8 * cfg["lookahead"]
 
 
 def feature_chunk(cfg, step, i, frames):
@@ -81,6 +89,7 @@ def main():
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     np.savez_compressed(os.path.join(HERE, "pre_encode_small.npz"), **run(PRE_SMALL))
     np.savez_compressed(os.path.join(HERE, "pre_encode_large.npz"), **run(PRE_LARGE))
+    np.savez_compressed(os.path.join(HERE, "pre_encode_small_audio.npz"), **run(PRE_SMALL_AUDIO))
     print("golden vectors written to", HERE)
 
 

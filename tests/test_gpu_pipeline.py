@@ -3,7 +3,9 @@ GPU: a batch of streams stepped together gives each stream the same tokens as
 stepping it alone (slot isolation of the three per-slot states: mel cache,
 K/V pages + conv cache, prediction state), in fp32, over a first chunk and
 later chunks; and one steady-state step replays as a CUDA graph with the same
-result."""
+result.  The same for the audio -> tokens step (sample history as a fourth
+per-slot state)."""
+import numpy as np
 import pytest
 import torch
 
@@ -16,7 +18,7 @@ pytestmark = pytest.mark.gpu
 D, LAYERS, HEADS, V = 512, 2, 8, 1026
 
 
-def make(num_slots):
+def make(num_slots, **kw):
     torch.backends.cuda.matmul.allow_tf32 = False
     torch.backends.cudnn.allow_tf32 = False
     enc = ConformerEncoder(feat_in=128, hidden_size=D, ff_expansion_factor=4, num_layers=LAYERS,
@@ -35,7 +37,7 @@ def make(num_slots):
     join.load_state_dict({k[7:]: torch.from_numpy(v) for k, v in sd.items()
                           if k.startswith("joiner.")})
     mods = [m.to("cuda", torch.float32).eval() for m in (enc, pre, pred, join)]
-    return StreamingPipeline(*mods, blank_id=V, num_slots=num_slots)
+    return StreamingPipeline(*mods, blank_id=V, num_slots=num_slots, **kw)
 
 
 def feats(step, i):
@@ -87,6 +89,89 @@ def test_steady_step_replays_as_cuda_graph():
         with torch.cuda.graph(g):
             tok, cnt = pipe.step(static_f, slots, first=False)
     # the capture ran no kernels: replaying it now performs this step
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(tok, want[0]) and torch.equal(cnt, want[1])
+
+
+SMALL_FIRST, SMALL_NEXT = 9 * 160, 16 * 160     # samples per chunk, lookahead 1
+
+
+def audio(step, i):
+    rng = np.random.default_rng(7000 + 100 * i + step)
+    n = SMALL_FIRST if step == 0 else SMALL_NEXT
+    t = np.arange(n) / 16000.0
+    f = rng.uniform(100, 4000, 3)
+    x = sum(np.sin(2 * np.pi * fk * t + rng.uniform(0, 6.3)) for fk in f) / 3
+    x = x + 0.1 * rng.standard_normal(n)
+    return torch.from_numpy((0.4 * x).astype(np.float32))[None]
+
+
+def run_audio(streams, steps, pipe, slot_of):
+    out = {}
+    with torch.inference_mode():
+        for step in range(steps):
+            x = torch.cat([audio(step, i) for i in streams]).cuda()
+            slots = torch.tensor([slot_of[i] for i in streams], dtype=torch.int32, device="cuda")
+            tok, cnt = pipe.step_audio(x, slots, push=step)
+            tok, cnt = tok.cpu(), cnt.cpu()
+            for r, i in enumerate(streams):
+                out[(step, i)] = [int(x) for t in range(tok.shape[1])
+                                  for x in tok[r, t, : int(cnt[r, t])]]
+    return out
+
+
+def test_audio_step_is_features_then_step():
+    """step_audio = the extractor's push_batch followed by step."""
+    a, b = make(3), make(3)
+    slots = [2, 0]
+    a.start_streams(slots)
+    b.start_streams(slots)
+    sl = torch.tensor(slots, dtype=torch.int32, device="cuda")
+    with torch.inference_mode():
+        for step in range(4):
+            x = torch.cat([audio(step, i) for i in range(2)]).cuda()
+            ta, ca = a.step_audio(x, sl, push=step)
+            f, counts = b.fe.push_batch(x, slots, first=step == 0)
+            assert list(counts) == [8 if step == 0 else 16] * 2
+            # the second window takes the 8 frames the first one left in the cache
+            tb, cb = b.step(f, sl, first=step == 0, prefix=8 if step == 1 else None)
+            assert torch.equal(ta, tb) and torch.equal(ca, cb), step
+    assert a.fe.error_bits() == 0
+
+
+def test_audio_batched_step_equals_streams_alone():
+    streams, steps = [0, 1, 2], 5
+    kw = dict(feature_kw=dict(dither=0.0))
+    pipe = make(4, **kw)
+    pipe.start_streams([3, 1, 0])
+    together = run_audio(streams, steps, pipe, {0: 3, 1: 1, 2: 0})
+    for i in streams:
+        alone_pipe = make(1, **kw)
+        alone_pipe.start_streams([0])
+        alone = run_audio([i], steps, alone_pipe, {i: 0})
+        for step in range(steps):
+            assert together[(step, i)] == alone[(step, i)], (step, i)
+    assert sum(len(v) for v in together.values()) > 0
+
+
+def test_audio_steady_step_replays_as_cuda_graph():
+    pipe, ref_pipe = make(2), make(2)
+    pipe.start_streams([0, 1])
+    ref_pipe.start_streams([0, 1])
+    slots = torch.tensor([0, 1], dtype=torch.int32, device="cuda")
+    with torch.inference_mode():
+        for push in range(2):
+            x = torch.cat([audio(push, 0), audio(push, 1)]).cuda()
+            pipe.step_audio(x, slots, push)
+            ref_pipe.step_audio(x, slots, push)
+        x2 = torch.cat([audio(2, 0), audio(2, 1)]).cuda()
+        want = ref_pipe.step_audio(x2, slots, 2)
+        static_x = x2.clone()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            tok, cnt = pipe.step_audio(static_x, slots, 2)
+    # the capture ran no kernels: replaying it now performs push 2
     g.replay()
     torch.cuda.synchronize()
     assert torch.equal(tok, want[0]) and torch.equal(cnt, want[1])

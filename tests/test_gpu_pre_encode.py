@@ -1,7 +1,9 @@
 """Batched streaming pre-encode on the GPU (parakeet_b200.engine.pre_encode:
 the pk_pre_encode_window cache kernel through the C ABI + the ConvSubsampling
 drop-in) against the reference's own outputs (tests/golden/
-make_golden_pre_encode.py): rel-L2 <= 1e-5 in fp32 (TF32 off)."""
+make_golden_pre_encode.py): rel-L2 <= 1e-5 in fp32 (TF32 off), including
+first chunks shorter than the cache (the 8-frame first windows of the small
+model's engine), whose streams' second windows take an 8-frame prefix."""
 import os
 import sys
 
@@ -11,7 +13,8 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(HERE, "golden"))
-from make_golden_pre_encode import PRE_LARGE, PRE_SMALL, chunk_frames, feature_chunk  # noqa: E402
+from make_golden_pre_encode import (PRE_LARGE, PRE_SMALL, PRE_SMALL_AUDIO,  # noqa: E402
+                                    chunk_frames, feature_chunk)
 from parakeet_b200.engine.pre_encode import BatchedPreEncoder  # noqa: E402
 from parakeet_b200.modules import ConvSubsampling  # noqa: E402
 from parakeet_b200.weights import random_pre_encode_state_dict  # noqa: E402
@@ -24,7 +27,8 @@ def rel_l2(a, b):
 
 
 @pytest.mark.parametrize("cfg,name", [(PRE_SMALL, "pre_encode_small.npz"),
-                                      (PRE_LARGE, "pre_encode_large.npz")])
+                                      (PRE_LARGE, "pre_encode_large.npz"),
+                                      (PRE_SMALL_AUDIO, "pre_encode_small_audio.npz")])
 def test_batched_pre_encode_matches_reference(cfg, name):
     torch.backends.cuda.matmul.allow_tf32 = False
     torch.backends.cudnn.allow_tf32 = False
@@ -35,16 +39,20 @@ def test_batched_pre_encode_matches_reference(cfg, name):
     pe = BatchedPreEncoder(m.to("cuda").eval(), num_slots=len(cfg["streams"]),
                            cache_size=cfg["cache"], drop_extra=cfg["drop"])
     index = g["index"]
+    held = {}                    # frames each stream's cache holds
     with torch.inference_mode():
         for step in sorted(set(int(s) for s in index[:, 0])):
             rows = [(int(i), bool(f)) for s, i, f in index if s == step]
-            for first in (True, False):      # first chunks and later chunks batch apart
-                group = [i for i, f in rows if f == first]
-                if not group:
-                    continue
+            groups = {}          # rows batch together when their windows have one length
+            for i, f in rows:
+                groups.setdefault((f, 0 if f else held[i]), []).append(i)
+            for (first, pre), group in sorted(groups.items()):
+                F = chunk_frames(cfg, first)
                 feats = torch.from_numpy(np.concatenate(
-                    [feature_chunk(cfg, step, i, chunk_frames(cfg, first)) for i in group]))
-                y = pe.pre_encode(feats, torch.tensor(group), first).float().cpu().numpy()
+                    [feature_chunk(cfg, step, i, F) for i in group]))
+                y = pe.pre_encode(feats, torch.tensor(group), first,
+                                  prefix=None if first else pre).float().cpu().numpy()
                 for r, i in enumerate(group):
                     assert rel_l2(y[r], g[f"y_{step}_{i}"]) <= 1e-5, (step, i, first)
+                    held[i] = min(cfg["cache"], pre + F)
     assert int(pe.error.item()) == 0

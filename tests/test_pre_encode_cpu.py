@@ -10,7 +10,8 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(HERE, "golden"))
-from make_golden_pre_encode import PRE_LARGE, PRE_SMALL, chunk_frames, feature_chunk  # noqa: E402
+from make_golden_pre_encode import (PRE_LARGE, PRE_SMALL, PRE_SMALL_AUDIO,  # noqa: E402
+                                    chunk_frames, feature_chunk)
 from parakeet_b200.modules import ConvSubsampling  # noqa: E402
 from parakeet_b200.weights import random_pre_encode_state_dict  # noqa: E402
 
@@ -27,7 +28,8 @@ def rel_l2(a, b):
 
 
 @pytest.mark.parametrize("cfg,name", [(PRE_SMALL, "pre_encode_small.npz"),
-                                      (PRE_LARGE, "pre_encode_large.npz")])
+                                      (PRE_LARGE, "pre_encode_large.npz"),
+                                      (PRE_SMALL_AUDIO, "pre_encode_small_audio.npz")])
 def test_subsampling_drop_in_matches_reference(cfg, name):
     g = np.load(os.path.join(HERE, "golden", name))
     m = build(cfg)
