@@ -70,7 +70,7 @@ def parse():
                     help="prefill + warmup + --steps steps only (for ncu), no report")
     ap.add_argument("--profile-op", default=None,
                     choices=["append", "attention", "attention+append", "gather",
-                             "gather_all_layers", "conv", "features"],
+                             "gather_all_layers", "conv", "features", "streaming"],
                     help="prefill + warmup, then --steps runs of one breakdown op (for ncu)")
     return ap.parse_args()
 
@@ -558,7 +558,7 @@ def stage_times(pipe, samples, slots, reps):
     return res
 
 
-def streaming_step(model, steps, dev):
+def streaming_step(model, steps, dev, profile=False):
     """Audio -> tokens for every stream of configs[2] (small, 160 streams) or
     configs[3] on one GPU (large, 480 streams): batched log-mel features ->
     batched pre-encode -> paged encoder -> batched greedy decode
@@ -603,6 +603,14 @@ def streaming_step(model, steps, dev):
         for k in range(-(-att[0] // (la + 1)) + 2):   # fill the left context
             tok, cnt = pipe.step_audio(nxt, slots, 1 + k)
         torch.cuda.synchronize()
+        if profile:   # eager steps only, bracketed for `ncu --profile-from-start off`
+            torch.cuda.cudart().cudaProfilerStart()
+            for _ in range(steps):
+                pipe.step_audio(nxt, slots, 2)
+            torch.cuda.synchronize()
+            torch.cuda.cudart().cudaProfilerStop()
+            return {"profile_run": model, "op": "streaming", "steps": steps,
+                    "device_error_word": pipe.pool.read_error() | pipe.fe.error_bits()}
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         for _ in range(steps):
@@ -674,6 +682,9 @@ def main():
     dev = torch.device("cuda", local)
     if args.profile_op == "features":   # the log-mel kernel alone, for ncu
         print(json.dumps(profile_features(args.model, args.steps, dev)))
+        return
+    if args.profile_op == "streaming":  # --steps audio -> tokens steps inside a profiler range
+        print(json.dumps(streaming_step(args.model, args.steps, dev, profile=True)))
         return
     c = SHAPES[args.model]
     L, D, H, att = c["layers"], c["dim"], c["heads"], c["att"]

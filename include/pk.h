@@ -252,6 +252,19 @@ int pk_lstm_cell(const void *gates, int64_t gates_ld, void *h, void *c, int64_t 
                  const int32_t *emit, int32_t batch, int32_t hidden, int32_t dtype,
                  void *stream);
 
+/* LayerNorm over the last dimension of `rows` rows (row strides x_ld, y_ld
+ * elements): y = (x - mean) / sqrt(var + eps) * gamma + beta, fp32 statistics
+ * (exact two-pass).  With gamma2 != NULL the same launch also writes
+ * y2 = LayerNorm(y as stored; gamma2, beta2, eps2): a ConformerLayer's
+ * norm_out followed by the next layer's norm_feed_forward1.  dim = 1, 2, 4
+ * or 8 x 256 (bf16) / x 128 (f32); buffers 16-byte aligned.  Replaces the
+ * nn.LayerNorm calls of ConformerLayer.forward (parakeet/modules/encoder.py:
+ * 60-81). */
+int pk_layer_norm(const void *x, int64_t x_ld, int32_t rows, int32_t dim, const void *gamma,
+                  const void *beta, float eps, void *y, int64_t y_ld, const void *gamma2,
+                  const void *beta2, float eps2, void *y2, int64_t y2_ld, int32_t dtype,
+                  void *stream);
+
 /* ---------------- streaming log-mel features ------------------------------
  * The feature extractor of every stream in one launch per push.  Replaces
  * FeatureExtractor.push / _compute_features / _trim_samples

@@ -402,6 +402,46 @@ int pk_lstm_cell(const void *gates, int64_t gates_ld, void *h, void *c, int64_t 
                             static_cast<cudaStream_t>(stream));
 }
 
+int pk_layer_norm(const void *x, int64_t x_ld, int32_t rows, int32_t dim, const void *gamma,
+                  const void *beta, float eps, void *y, int64_t y_ld, const void *gamma2,
+                  const void *beta2, float eps2, void *y2, int64_t y2_ld, int32_t dtype,
+                  void *stream) {
+    PK_CHECK(dtype == PK_DTYPE_F32 || dtype == PK_DTYPE_BF16, "bad dtype %d", dtype);
+    PK_CHECK(rows >= 0, "negative rows");
+    if (rows == 0) return PK_OK;
+    const int vec = dtype == PK_DTYPE_BF16 ? 8 : 4;
+    const int nv = dim / (32 * vec);
+    PK_CHECK(dim > 0 && dim % (32 * vec) == 0 && (nv == 1 || nv == 2 || nv == 4 || nv == 8),
+             "dim %d: 1, 2, 4 or 8 x %d", dim, 32 * vec);
+    PK_CHECK(x && gamma && beta && y, "null pointer");
+    PK_CHECK(x_ld >= dim && y_ld >= dim && x_ld % vec == 0 && y_ld % vec == 0,
+             "row strides must be >= dim and multiples of 16 bytes");
+    PK_CHECK(aligned16(x) && aligned16(y) && aligned16(gamma) && aligned16(beta),
+             "buffers must be 16-byte aligned");
+    if (gamma2) {
+        PK_CHECK(beta2 && y2 && aligned16(gamma2) && aligned16(beta2) && aligned16(y2),
+                 "second LayerNorm: null or unaligned buffer");
+        PK_CHECK(y2_ld >= dim && y2_ld % vec == 0, "bad y2 row stride");
+    }
+    LnArgs a;
+    a.x = x;
+    a.x_ld = x_ld;
+    a.rows = rows;
+    a.dim = dim;
+    a.dtype = dtype;
+    a.g1 = gamma;
+    a.b1 = beta;
+    a.eps1 = eps;
+    a.y1 = y;
+    a.y1_ld = y_ld;
+    a.g2 = gamma2;
+    a.b2 = beta2;
+    a.eps2 = eps2;
+    a.y2 = y2;
+    a.y2_ld = y2_ld;
+    return launch_layer_norm(a, static_cast<cudaStream_t>(stream));
+}
+
 int pk_features_tables(int32_t sample_rate, int32_t n_fft, int32_t win_length, int32_t n_mels,
                        double fmin, double fmax, int32_t mel_norm, void *host_out,
                        int64_t *bytes, int32_t *mel_nnz) {

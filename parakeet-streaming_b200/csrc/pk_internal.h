@@ -115,6 +115,22 @@ int launch_rnnt_pick(const void *logits, int64_t ld, int dtype, int batch, int n
 int launch_lstm_cell(const void *gates, int64_t gld, void *h, void *c, int64_t sld,
                      const int32_t *emit, int batch, int hidden, int dtype, cudaStream_t s);
 
+// pk_norm.cu
+struct LnArgs {
+    const void *x;
+    int64_t x_ld;
+    int rows, dim, dtype;
+    const void *g1, *b1;
+    float eps1;
+    void *y1;
+    int64_t y1_ld;
+    const void *g2, *b2;   // optional second LayerNorm of y1 (g2 == nullptr: none)
+    float eps2;
+    void *y2;
+    int64_t y2_ld;
+};
+int launch_layer_norm(const LnArgs &a, cudaStream_t s);
+
 // pk_features.cu.  Table block: int32 header[kFeHeader], then float2
 // twiddle[n_fft] (exp(-2 pi i u / n_fft)), float window[n_fft], int32 lo[n_mels],
 // cnt[n_mels], off[n_mels] (first bin, length and offset of each filter's

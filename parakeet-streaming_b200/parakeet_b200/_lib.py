@@ -93,6 +93,8 @@ SIGNATURES = {
                            _I64, _P, _P, _I32, _P, _I64, _I64, _I64, _P],
     "pk_conv_step": [_P, _I32, _I32, _I32, _I32, _I32, _I32, _I32, _P, _I64, _I64, _P, _P, _P,
                      ctypes.c_float, _P, _P, _I32, _P, _P, _P],
+    "pk_layer_norm": [_P, _I64, _I32, _I32, _P, _P, ctypes.c_float, _P, _I64, _P, _P,
+                      ctypes.c_float, _P, _I64, _I32, _P],
     "pk_features_tables": [_I32, _I32, _I32, _I32, ctypes.c_double, ctypes.c_double, _I32, _P,
                            ctypes.POINTER(_I64), ctypes.POINTER(_I32)],
     "pk_features_push": [ctypes.POINTER(FeaturesDesc), _P, _I64, _P, _P, _P, _I32, _P, _I32, _I32,

@@ -21,6 +21,7 @@ import torch
 from torch import Tensor, nn
 
 from .cache import PagedModelCache
+from .feedforward import residual_linear
 
 
 class PositionalEncoding(nn.Module):
@@ -82,17 +83,25 @@ class ConformerAttention(nn.Module):
             self._pos_key = key
         return self._pos_proj
 
-    def forward(self, x: Tensor, pos_emb: Tensor, attn_mask=None, cache: PagedModelCache = None):
+    def _context(self, x: Tensor, pos_emb: Tensor, cache: PagedModelCache) -> Tensor:
         if not isinstance(cache, PagedModelCache):
             raise TypeError("ConformerAttention needs the paged streaming cache")
         D = x.shape[-1]
         qkv = self.qkv(x)                                             # attention.py:94
         query, key, value = qkv[..., :D], qkv[..., D:2 * D], qkv[..., 2 * D:]
         # cache append (attention.py:98) fused into the paged attention call
-        out = cache.pool.attention(self.layer_idx, query, self.pos_projection(pos_emb),
-                                   self.pos_bias_u, self.pos_bias_v, cache.slots, cache.lengths,
-                                   key=key, value=value)
-        return self.linear_out(out)                                   # attention.py:123
+        return cache.pool.attention(self.layer_idx, query, self.pos_projection(pos_emb),
+                                    self.pos_bias_u, self.pos_bias_v, cache.slots, cache.lengths,
+                                    key=key, value=value)
+
+    def forward(self, x: Tensor, pos_emb: Tensor, attn_mask=None, cache: PagedModelCache = None):
+        return self.linear_out(self._context(x, pos_emb, cache))      # attention.py:123
+
+    def forward_residual(self, res: Tensor, x: Tensor, pos_emb: Tensor,
+                         cache: PagedModelCache = None) -> Tensor:
+        """res + forward(x) with the residual add in the output projection's
+        GEMM (encoder.py:66)."""
+        return residual_linear(res, self._context(x, pos_emb, cache), self.linear_out)
 
 
 __all__ = ["ConformerAttention", "PositionalEncoding"]

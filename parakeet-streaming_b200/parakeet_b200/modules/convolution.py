@@ -10,6 +10,7 @@ in place by slot.
 """
 from __future__ import annotations
 
+import torch
 import torch.nn.functional as F
 from torch import Tensor, nn
 
@@ -38,6 +39,20 @@ class ConformerConvolution(nn.Module):
         y = c.pool.conv_step(cache.layer_idx, h, self.depthwise_conv.weight, c.slots, c.lengths,
                              self.batch_norm.weight, self.batch_norm.bias, self.batch_norm.eps)
         return F.linear(y, self.pointwise_conv2.weight[:, :, 0]), cache
+
+    def forward_residual(self, res: Tensor, x: Tensor, cache: ConvCacheRef = None) -> Tensor:
+        """res + forward(x)[0] with the residual add in pointwise_conv2's GEMM
+        (encoder.py:71-74)."""
+        if not isinstance(cache, ConvCacheRef):
+            raise TypeError("ConformerConvolution needs the paged cache's conv handle")
+        c = cache.cache
+        h = F.linear(x, self.pointwise_conv1.weight[:, :, 0])            # [B, T, 2D]
+        y = c.pool.conv_step(cache.layer_idx, h, self.depthwise_conv.weight, c.slots, c.lengths,
+                             self.batch_norm.weight, self.batch_norm.bias, self.batch_norm.eps)
+        w2 = self.pointwise_conv2.weight[:, :, 0]
+        shape = res.shape
+        return torch.addmm(res.reshape(-1, shape[-1]), y.reshape(-1, y.shape[-1]), w2.t(),
+                           beta=1, alpha=1).reshape(shape)
 
 
 __all__ = ["ConformerConvolution"]

@@ -17,7 +17,7 @@ from __future__ import annotations
 import torch
 from torch import Tensor, nn
 
-from ..ops import PagedKVPool
+from ..ops import PagedKVPool, layer_norm
 from .attention import ConformerAttention, PositionalEncoding
 from .cache import PagedModelCache, StreamingState
 from .convolution import ConformerConvolution
@@ -42,14 +42,22 @@ class ConformerLayer(nn.Module):
         self.norm_out = nn.LayerNorm(hidden_size)
 
     def forward(self, x: Tensor, pos_emb: Tensor, pad_mask, attn_mask, cache: PagedModelCache):
-        res = x + 0.5 * self.feed_forward1(self.norm_feed_forward1(x))
-        res = res + self.self_attn(self.norm_self_att(res), pos_emb, attn_mask, cache)
-        conv_cache = cache.get_conv_cache(self.layer_idx)
-        y, conv_cache = self.conv(self.norm_conv(res), pad_mask, conv_cache)
-        cache.update_conv_cache(self.layer_idx, conv_cache)
-        res = res + y
-        res = res + 0.5 * self.feed_forward2(self.norm_feed_forward2(res))
-        return self.norm_out(res)
+        return self.forward_fused(x, layer_norm(x, self.norm_feed_forward1), pos_emb, cache)
+
+    def forward_fused(self, x: Tensor, h: Tensor, pos_emb: Tensor, cache: PagedModelCache,
+                      next_norm: nn.LayerNorm | None = None):
+        """``forward`` given h = norm_feed_forward1(x).  The residual adds and
+        the FF halves ride in the epilogue of each module's last GEMM
+        (res + alpha * acc); the LayerNorms are libpk launches, and with
+        ``next_norm`` (the next layer's norm_feed_forward1) the last one also
+        returns that layer's h: (out, h_next)."""
+        res = self.feed_forward1.forward_residual(x, h, 0.5)
+        res = self.self_attn.forward_residual(res, layer_norm(res, self.norm_self_att), pos_emb,
+                                              cache)
+        conv_cache = cache.get_conv_cache(self.layer_idx)          # updated in place
+        res = self.conv.forward_residual(res, layer_norm(res, self.norm_conv), conv_cache)
+        res = self.feed_forward2.forward_residual(res, layer_norm(res, self.norm_feed_forward2), 0.5)
+        return layer_norm(res, self.norm_out, next_norm)
 
 
 class ConformerEncoder(nn.Module):
@@ -107,8 +115,11 @@ class ConformerEncoder(nn.Module):
         cache.lengths = torch.as_tensor(length).to(device=pool.device, dtype=torch.int32)
         pool.begin_step(cache.slots, cache.lengths)
         x, pos_emb = self.pos_enc(x, cache_len=self.att_context_size[0])
-        for layer in self.layers:
-            x = layer(x, pos_emb=pos_emb, pad_mask=None, attn_mask=None, cache=cache)
+        h = layer_norm(x, self.layers[0].norm_feed_forward1)
+        for i, layer in enumerate(self.layers):
+            nxt = self.layers[i + 1].norm_feed_forward1 if i + 1 < len(self.layers) else None
+            out = layer.forward_fused(x, h, pos_emb, cache, nxt)
+            x, h = out if nxt is not None else (out, None)
         pool.end_step(cache.slots, cache.lengths)             # encoder.py:257-260
         return x.transpose(1, 2), state
 

@@ -1,5 +1,8 @@
 """``ConformerFeedForward`` (parakeet/modules/feedforward.py): Linear, SiLU,
-Linear; plain cuBLAS GEMMs, kept for state_dict compatibility."""
+Linear; plain cuBLAS GEMMs, kept for state_dict compatibility.
+``forward_residual`` gives the layer's ``x + scale * FF(h)`` with the scale
+and the residual add folded into the second GEMM (alpha/beta of one addmm)."""
+import torch
 from torch import nn
 
 
@@ -15,5 +18,21 @@ class ConformerFeedForward(nn.Module):
     def forward(self, x):
         return self.linear2(self.dropout(self.activation(self.linear1(x))))
 
+    def forward_residual(self, res, x, scale: float):
+        """res + scale * forward(x) (encoder.py:63,76) in two GEMM launches
+        and the activation."""
+        a = self.dropout(self.activation(self.linear1(x)))
+        return residual_linear(res, a, self.linear2, scale)
 
-__all__ = ["ConformerFeedForward"]
+
+def residual_linear(res, a, linear: nn.Linear, scale: float = 1.0):
+    """res + scale * linear(a) as one GEMM with the epilogue res + alpha * acc."""
+    shape = res.shape
+    r = res.reshape(-1, shape[-1])
+    if linear.bias is not None:
+        r = r + scale * linear.bias
+    return torch.addmm(r, a.reshape(-1, a.shape[-1]), linear.weight.t(),
+                       beta=1, alpha=scale).reshape(shape)
+
+
+__all__ = ["ConformerFeedForward", "residual_linear"]

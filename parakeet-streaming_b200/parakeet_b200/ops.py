@@ -26,6 +26,37 @@ def _stream(device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
+def layer_norm(x: torch.Tensor, ln, ln2=None):
+    """nn.LayerNorm ``ln`` over the last dim of ``x`` (one libpk launch); with
+    ``ln2`` also ``ln2(ln(x))`` from the same launch, returned as a pair.
+    Widths the kernel does not take, or non-CUDA tensors, go through
+    torch.nn.functional.layer_norm."""
+    D = x.shape[-1]
+    vec = 8 if x.dtype == torch.bfloat16 else 4
+    ok = (x.is_cuda and x.dtype in DTYPES and D % (32 * vec) == 0
+          and D // (32 * vec) in (1, 2, 4, 8) and ln.weight.dtype == x.dtype
+          and (ln2 is None or ln2.weight.dtype == x.dtype))
+    if not ok:
+        y = torch.nn.functional.layer_norm(x, (D,), ln.weight, ln.bias, ln.eps)
+        if ln2 is None:
+            return y
+        return y, torch.nn.functional.layer_norm(y, (D,), ln2.weight, ln2.bias, ln2.eps)
+    x2 = x.reshape(-1, D)
+    if x2.stride(-1) != 1 or x2.stride(0) % vec or x2.data_ptr() % 16:
+        x2 = x2.contiguous()
+    rows = x2.shape[0]
+    y = torch.empty((rows, D), dtype=x.dtype, device=x.device)
+    y2 = torch.empty_like(y) if ln2 is not None else None
+    check(lib().pk_layer_norm(
+        x2.data_ptr(), x2.stride(0), rows, D, ln.weight.data_ptr(), ln.bias.data_ptr(),
+        float(ln.eps), y.data_ptr(), D,
+        _ptr(ln2.weight) if ln2 is not None else None, _ptr(ln2.bias) if ln2 is not None else None,
+        float(ln2.eps) if ln2 is not None else 0.0, _ptr(y2), D, DTYPES[x.dtype],
+        _stream(x.device)), "pk_layer_norm")
+    y = y.reshape(x.shape)
+    return y if ln2 is None else (y, y2.reshape(x.shape))
+
+
 def pages_per_stream(left: int, chunk: int, page_size: int) -> int:
     return int(lib().pk_pages_per_stream(left, chunk, page_size))
 
