@@ -70,7 +70,7 @@ def parse():
                     help="prefill + warmup + --steps steps only (for ncu), no report")
     ap.add_argument("--profile-op", default=None,
                     choices=["append", "attention", "attention+append", "gather",
-                             "gather_all_layers", "conv", "features", "streaming"],
+                             "gather_all_layers", "conv", "features", "streaming", "gemm"],
                     help="prefill + warmup, then --steps runs of one breakdown op (for ncu)")
     return ap.parse_args()
 
@@ -81,6 +81,14 @@ def peaks():
         d = json.load(open(p))
         return float(d["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
+
+
+def tensor_peak():
+    """Measured dense bf16 TFLOP/s (burst: the GEMMs are timed alone)."""
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        return float(json.load(open(p))["bf16_tflops"]), "measured"
+    return 1590.0, "fallback"
 
 
 # ---------------------------------------------------------------- clocks
@@ -500,6 +508,89 @@ def feature_step(model, steps, dev, cpu_sample=8):
     return res
 
 
+GEMM_SHAPES = {   # (name, M, N, K, epilogue): the FF GEMMs of one encoder step's layer
+    "small": [("ff_linear1+silu", 320, 2048, 512, "silu"),
+              ("ff_linear2+residual", 320, 512, 2048, "residual"),
+              ("qkv", 320, 1536, 512, "store")],
+    "large": [("ff_linear1+silu", 6720, 4096, 1024, "silu"),
+              ("ff_linear2+residual", 6720, 1024, 4096, "residual"),
+              ("qkv", 6720, 3072, 1024, "store")],
+}
+
+
+def gemm_step(model, steps, dev):
+    """The encoder's projection GEMMs at the streaming batch (160 small / 480
+    large streams): pk_gemm_bf16 (tcgen05, epilogue fused) against cuBLAS
+    (torch.matmul, epilogue as separate elementwise launches), each replayed
+    as a CUDA graph of `steps` launches after an L2 flush."""
+    import torch
+
+    from parakeet_b200.ops import gemm
+    peak, kind = tensor_peak()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    res = {"peak_tflops": peak, "peak_kind": kind, "shapes": []}
+    g = torch.Generator(device=dev).manual_seed(5)
+    for name, M, N, K, epi in GEMM_SHAPES[model]:
+        a = torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16)
+        w = (torch.randn(N, K, generator=g, device=dev) / K ** 0.5).to(torch.bfloat16)
+        r = torch.randn(M, N, generator=g, device=dev).to(torch.bfloat16)
+
+        def ours():
+            return gemm(a, w, epi, residual=r if epi == "residual" else None, alpha=0.5)
+
+        def cublas():
+            y = a @ w.t()
+            if epi == "silu":
+                return torch.nn.functional.silu(y)
+            if epi == "residual":
+                return r + 0.5 * y
+            return y
+
+        row = {"name": name, "M": M, "N": N, "K": K}
+        for label, fn in (("tcgen05", ours), ("cublas", cublas)):
+            for _ in range(3):
+                fn()
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            gph = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(s), torch.cuda.graph(gph, stream=s):
+                for _ in range(steps):
+                    fn()
+            torch.cuda.current_stream().wait_stream(s)
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            gph.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / steps
+            del gph
+            tf = 2.0 * M * N * K / (ms * 1e-3) / 1e12
+            row[label] = {"us": round(ms * 1e3, 2), "tflops": round(tf, 1),
+                          "frac": round(tf / peak, 3)}
+        res["shapes"].append(row)
+    res["note"] = ("launches back to back in one graph (weights L2-resident after the "
+                   "first; the 256 MB flush precedes the replay)")
+    return res
+
+
+def profile_gemm(model, steps, dev):
+    """`steps` launches of each GEMM of GEMM_SHAPES[model], nothing else (for ncu)."""
+    import torch
+
+    from parakeet_b200.ops import gemm, gemm_error_word
+    g = torch.Generator(device=dev).manual_seed(5)
+    for name, M, N, K, epi in GEMM_SHAPES[model]:
+        a = torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16)
+        w = (torch.randn(N, K, generator=g, device=dev) / K ** 0.5).to(torch.bfloat16)
+        r = torch.randn(M, N, generator=g, device=dev).to(torch.bfloat16)
+        for _ in range(steps):
+            gemm(a, w, epi, residual=r if epi == "residual" else None, alpha=0.5)
+    torch.cuda.synchronize()
+    return {"profile_run": model, "op": "gemm", "steps": steps,
+            "device_error_word": gemm_error_word(dev)}
+
+
 def profile_features(model, steps, dev):
     """First push, then `steps` steady pushes of the log-mel kernel (the
     configuration of feature_step), nothing else: a short launch list for ncu."""
@@ -683,6 +774,9 @@ def main():
     if args.profile_op == "features":   # the log-mel kernel alone, for ncu
         print(json.dumps(profile_features(args.model, args.steps, dev)))
         return
+    if args.profile_op == "gemm":       # the projection GEMMs alone, for ncu
+        print(json.dumps(profile_gemm(args.model, args.steps, dev)))
+        return
     if args.profile_op == "streaming":  # --steps audio -> tokens steps inside a profiler range
         print(json.dumps(streaming_step(args.model, args.steps, dev, profile=True)))
         return
@@ -818,12 +912,13 @@ def main():
             dist.barrier()
         ms = g0.elapsed_time(g1) / K
     clk = clocks.stop()
-    enc_line = dec_line = pre_line = fe_line = pipe_line = None
+    enc_line = dec_line = pre_line = fe_line = pipe_line = gemm_line = None
     if rank == 0 and not args.no_breakdown:
         enc_line = encoder_step(args.model, 160 if args.model == "small" else 480, 20, dev)
         dec_line = rnnt_decode_step(args.model, 10, dev)
         pre_line = pre_encode_step(args.model, 10, dev)
         fe_line = feature_step(args.model, 50, dev)
+        gemm_line = {m: gemm_step(m, 20, dev) for m in ("small", "large")}
         pipe_line = streaming_step(args.model, 10, dev)
     err = pool.read_error()
 
@@ -978,6 +1073,7 @@ def main():
             "rnnt_decode": dec_line,
             "pre_encode": pre_line,
             "features": fe_line,
+            "gemm": gemm_line,
             "streaming_step": pipe_line,
         }
         print(json.dumps(line), flush=True)

@@ -252,6 +252,24 @@ int pk_lstm_cell(const void *gates, int64_t gates_ld, void *h, void *c, int64_t 
                  const int32_t *emit, int32_t batch, int32_t hidden, int32_t dtype,
                  void *stream);
 
+/* bf16 GEMM on the tcgen05 tensor cores (fp32 accumulation in tensor
+ * memory) with the encoder's epilogues:
+ *   C[m][n] = epi(acc[m][n]),  acc = sum_k A[m][k] * W[n][k]
+ *   PK_GEMM_STORE: acc;  PK_GEMM_SILU: acc * sigmoid(acc);
+ *   PK_GEMM_RESIDUAL: R[m][n] + alpha * acc (R may be C).
+ * A [M][K] (row stride lda), W [N][K] (ldw, an nn.Linear weight), C and R
+ * [M][N] (ldc, ldr), all bf16, 16-byte aligned, strides multiples of 8;
+ * K a multiple of 64, N a multiple of 64.  Replaces the Linear -> SiLU ->
+ * Linear of ConformerFeedForward (parakeet/modules/feedforward.py) and the
+ * residual adds of ConformerLayer.forward (parakeet/modules/encoder.py:60-81)
+ * around the attention and conv projections. */
+#define PK_GEMM_STORE 0
+#define PK_GEMM_SILU 1
+#define PK_GEMM_RESIDUAL 2
+int pk_gemm_bf16(const void *A, int64_t lda, const void *W, int64_t ldw, int32_t M, int32_t N,
+                 int32_t K, void *C, int64_t ldc, int32_t epilogue, const void *R, int64_t ldr,
+                 float alpha, int32_t *error, void *stream);
+
 /* LayerNorm over the last dimension of `rows` rows (row strides x_ld, y_ld
  * elements): y = (x - mean) / sqrt(var + eps) * gamma + beta, fp32 statistics
  * (exact two-pass).  With gamma2 != NULL the same launch also writes

@@ -402,6 +402,39 @@ int pk_lstm_cell(const void *gates, int64_t gates_ld, void *h, void *c, int64_t 
                             static_cast<cudaStream_t>(stream));
 }
 
+int pk_gemm_bf16(const void *A, int64_t lda, const void *W, int64_t ldw, int32_t M, int32_t N,
+                 int32_t K, void *C, int64_t ldc, int32_t epilogue, const void *R, int64_t ldr,
+                 float alpha, int32_t *error, void *stream) {
+    PK_CHECK(M >= 0 && N > 0 && K > 0, "bad shape %d x %d x %d", M, N, K);
+    if (M == 0) return PK_OK;
+    PK_CHECK(K % 64 == 0 && N % 64 == 0, "K (%d) and N (%d) must be multiples of 64", K, N);
+    PK_CHECK(epilogue == PK_GEMM_STORE || epilogue == PK_GEMM_SILU ||
+                 epilogue == PK_GEMM_RESIDUAL, "bad epilogue %d", epilogue);
+    PK_CHECK(A && W && C && error, "null pointer");
+    PK_CHECK(aligned16(A) && aligned16(W) && aligned16(C), "operands must be 16-byte aligned");
+    PK_CHECK(lda >= K && ldw >= K && ldc >= N && lda % 8 == 0 && ldw % 8 == 0 && ldc % 8 == 0,
+             "row strides must cover the rows and be multiples of 8 elements");
+    if (epilogue == PK_GEMM_RESIDUAL)
+        PK_CHECK(R && aligned16(R) && ldr >= N && ldr % 8 == 0, "bad residual operand");
+    PK_CHECK(M <= 65535 * 128, "M too large");
+    GemmArgs g;
+    g.A = A;
+    g.W = W;
+    g.lda = lda;
+    g.ldw = ldw;
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    g.epilogue = epilogue;
+    g.C = C;
+    g.ldc = ldc;
+    g.R = R;
+    g.ldr = ldr;
+    g.alpha = alpha;
+    g.error = error;
+    return launch_gemm(g, static_cast<cudaStream_t>(stream));
+}
+
 int pk_layer_norm(const void *x, int64_t x_ld, int32_t rows, int32_t dim, const void *gamma,
                   const void *beta, float eps, void *y, int64_t y_ld, const void *gamma2,
                   const void *beta2, float eps2, void *y2, int64_t y2_ld, int32_t dtype,

@@ -1,0 +1,298 @@
+// bf16 GEMM on the 5th-generation tensor cores with the encoder's epilogues.
+//
+//   C[m][n] = epilogue( sum_k A[m][k] * W[n][k] ),  A, W, C bf16, fp32 accumulation
+//   epilogue: store | SiLU | R[m][n] + alpha * acc
+//
+// These are the Conformer layer's projections (parakeet/modules/feedforward.py:
+// Linear -> SiLU -> Linear; attention.py qkv / linear_out; convolution.py
+// pointwise convs), with the activation and the residual add of
+// ConformerLayer.forward (encoder.py:60-81: x + 0.5 * ff, x + attn, x + conv)
+// done on the accumulator instead of by separate elementwise launches.
+//
+// One CTA computes a 128 x BN tile (128 threads).  Lane 0 of warp 0 streams
+// 64-wide K blocks of A and W into a ring of NS shared-memory stages with TMA
+// (128B swizzle, the layout the tensor-core descriptors read); lane 0 of warp 1
+// issues tcgen05.mma (M = 128, N = BN, K = 16, four per stage) into a TMEM
+// accumulator of BN fp32 columns and releases each stage with tcgen05.commit;
+// after the last commit all four warps read their 32 TMEM lanes (= tile rows)
+// with tcgen05.ld, apply the epilogue and store.  The weights do not depend on
+// the previous kernel, so their first stages are requested before the
+// programmatic-dependent-launch wait.  Every wait is bounded (PK_DEV_TIMEOUT).
+#include "pk_common.cuh"
+#include "pk_internal.h"
+
+namespace pk {
+namespace {
+
+constexpr int kBM = 128, kBK = 64, kThreads = 128;
+constexpr int kABytes = kBM * kBK * 2;   // 16 KB per stage
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar,
+                                            int32_t c0, int32_t c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major operand tile written by TMA
+// with 128B swizzle (rows of 128 bytes, 8-row swizzle atoms of 1024 bytes):
+// start address >> 4, leading byte offset 1 (unused for swizzled K-major),
+// stride byte offset 1024 >> 4 between 8-row groups, descriptor version 1,
+// layout type 2 = 128B swizzle.  The tile base is 1024-byte aligned, so the
+// base offset is 0; a K step of 16 elements inside the atom advances the start
+// address by 32 bytes.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) |
+           ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor, kind::f16: D fp32 (bits 4-5 = 1), A and B bf16
+// (bits 7-9, 10-12 = 1), both K-major (bits 15, 16 = 0), N >> 3 at bit 17,
+// M >> 4 at bit 24.
+constexpr uint32_t idesc_bf16(int m, int n) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) |
+           ((uint32_t)(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                          uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// arrive on `bar` when every tcgen05.mma issued so far by this thread is done
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t *dst, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(dst)),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// 32 consecutive fp32 columns of this thread's TMEM lane
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+        "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+        "%28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+          "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+          "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+template <int BN, int NS, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w,
+                     int M, int K, __nv_bfloat16 *C, int64_t ldc, const __nv_bfloat16 *R,
+                     int64_t ldr, float alpha, int32_t *error) {
+    constexpr int kBBytes = BN * kBK * 2;
+    extern __shared__ uint8_t gemm_smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(gemm_smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *sA = smem, *sB = smem + NS * kABytes;
+    __shared__ __align__(8) uint64_t full[NS], empty[NS], done;
+    __shared__ uint32_t tmem_base;
+    __shared__ int failed;
+
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int m0 = blockIdx.y * kBM, n0 = blockIdx.x * BN;
+    const int nk = K / kBK;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(&done, 1);
+        failed = 0;
+        fence_mbar_init();
+        prefetch_tmap(&tm_a);
+        prefetch_tmap(&tm_w);
+    }
+    if (warp == 0) {
+        tmem_alloc(&tmem_base, BN);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base;
+
+    if (warp == 0 && lane == 0) {
+        // producer: the weights of the first stages before the wait on the
+        // previous kernel (they are constants), then A, then the steady ring
+        const int pre = nk < NS ? nk : NS;
+        for (int kb = 0; kb < pre; ++kb) {
+            mbar_arrive_expect_tx(&full[kb], kABytes + kBBytes);
+            tma_load_2d(sB + kb * kBBytes, &tm_w, &full[kb], kb * kBK, n0);
+        }
+        grid_dep_wait();
+        for (int kb = 0; kb < pre; ++kb)
+            tma_load_2d(sA + kb * kABytes, &tm_a, &full[kb], kb * kBK, m0);
+        for (int kb = NS; kb < nk; ++kb) {
+            const int s = kb % NS;
+            if (!mbar_wait_bounded(&empty[s], ((kb / NS) - 1) & 1, kWaitLimitNs)) {
+                raise(error, PK_DEV_TIMEOUT);
+                failed = 1;
+                break;
+            }
+            mbar_arrive_expect_tx(&full[s], kABytes + kBBytes);
+            tma_load_2d(sB + s * kBBytes, &tm_w, &full[s], kb * kBK, n0);
+            tma_load_2d(sA + s * kABytes, &tm_a, &full[s], kb * kBK, m0);
+        }
+    } else if (warp == 1 && lane == 0) {
+        // MMA issuer
+        constexpr uint32_t idesc = idesc_bf16(kBM, BN);
+        grid_dep_wait();
+        for (int kb = 0; kb < nk; ++kb) {
+            const int s = kb % NS;
+            if (!mbar_wait_bounded(&full[s], (kb / NS) & 1, kWaitLimitNs)) {
+                raise(error, PK_DEV_TIMEOUT);
+                failed = 1;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t a0 = smem_u32(sA + s * kABytes), b0 = smem_u32(sB + s * kBBytes);
+#pragma unroll
+            for (int kk = 0; kk < kBK / 16; ++kk)
+                umma_bf16(tmem, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32), idesc,
+                          (kb | kk) != 0);
+            umma_commit(&empty[s]);
+        }
+        umma_commit(&done);
+    } else {
+        grid_dep_wait();   // the residual rows may come from the previous kernel
+    }
+    __syncwarp();
+
+    // epilogue: warp w owns TMEM lanes (tile rows) 32w .. 32w + 31
+    const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(&done, 0, kWaitLimitNs));
+    if (!ok && lane == 0) raise(error, PK_DEV_TIMEOUT);
+    tc_fence_after();
+    grid_dep_launch();
+    const int row = m0 + warp * 32 + lane;
+    if (ok && !failed) {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+            float v[32];
+            tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + c * 32, v);
+            if (row < M) {
+                const int col = n0 + c * 32;
+                if (EPI == PK_GEMM_SILU) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) v[i] = __fdividef(v[i], 1.f + __expf(-v[i]));
+                } else if (EPI == PK_GEMM_RESIDUAL) {
+                    const uint4 *rp = reinterpret_cast<const uint4 *>(R + (int64_t)row * ldr + col);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        float f[8];
+                        unpack16(rp[q], f, R);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) v[q * 8 + i] = f[i] + alpha * v[q * 8 + i];
+                    }
+                }
+                uint4 *cp = reinterpret_cast<uint4 *>(C + (int64_t)row * ldc + col);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    uint4 o;
+                    __nv_bfloat162 *h = reinterpret_cast<__nv_bfloat162 *>(&o);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        h[i] = __floats2bfloat162_rn(v[q * 8 + 2 * i], v[q * 8 + 2 * i + 1]);
+                    cp[q] = o;
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, BN);
+    }
+}
+
+template <int BN, int NS, int EPI>
+int launch_gemm_t(const GemmArgs &g, const CUtensorMap &ta, const CUtensorMap &tw,
+                  cudaStream_t s) {
+    auto k = gemm_bf16_kernel<BN, NS, EPI>;
+    const size_t smem = (size_t)NS * (kABytes + BN * kBK * 2) + 1024;
+    static bool attr = false;
+    if (!attr) {
+        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(gemm)");
+        attr = true;
+    }
+    const dim3 grid(g.N / BN, (g.M + kBM - 1) / kBM);
+    cudaError_t e = launch_pdl(k, grid, dim3(kThreads), smem, s, ta, tw, g.M, g.K,
+                               static_cast<__nv_bfloat16 *>(g.C), g.ldc,
+                               static_cast<const __nv_bfloat16 *>(g.R), g.ldr, g.alpha, g.error);
+    return cuda_status(e, "gemm_bf16_kernel");
+}
+
+template <int BN, int NS>
+int launch_gemm_epi(const GemmArgs &g, const CUtensorMap &ta, const CUtensorMap &tw,
+                    cudaStream_t s) {
+    switch (g.epilogue) {
+        case PK_GEMM_SILU: return launch_gemm_t<BN, NS, PK_GEMM_SILU>(g, ta, tw, s);
+        case PK_GEMM_RESIDUAL: return launch_gemm_t<BN, NS, PK_GEMM_RESIDUAL>(g, ta, tw, s);
+        default: return launch_gemm_t<BN, NS, PK_GEMM_STORE>(g, ta, tw, s);
+    }
+}
+
+}  // namespace
+
+int launch_gemm(const GemmArgs &g, cudaStream_t s) {
+    if (g.M == 0) return PK_OK;
+    // N tile: narrow tiles when there are few row tiles (more CTAs for the
+    // weight stream), wide ones otherwise
+    const int mtiles = (g.M + kBM - 1) / kBM;
+    int bn = mtiles * (g.N / 256) >= 148 && g.N % 256 == 0 ? 256
+             : (mtiles * (g.N / 128) >= 148 && g.N % 128 == 0 ? 128 : 64);
+    CUtensorMap ta, tw;
+    const uint64_t adims[2] = {(uint64_t)g.K, (uint64_t)g.M}, astr[1] = {(uint64_t)g.lda * 2};
+    const uint64_t wdims[2] = {(uint64_t)g.K, (uint64_t)g.N}, wstr[1] = {(uint64_t)g.ldw * 2};
+    const uint32_t abox[2] = {kBK, kBM}, wbox[2] = {kBK, (uint32_t)bn};
+    int st = encode_tmap(&ta, PK_DTYPE_BF16, g.A, 2, adims, astr, abox);
+    if (st != PK_OK) return st;
+    st = encode_tmap(&tw, PK_DTYPE_BF16, g.W, 2, wdims, wstr, wbox);
+    if (st != PK_OK) return st;
+    switch (bn) {
+        case 256: return launch_gemm_epi<256, 3>(g, ta, tw, s);
+        case 128: return launch_gemm_epi<128, 4>(g, ta, tw, s);
+        default: return launch_gemm_epi<64, 6>(g, ta, tw, s);
+    }
+}
+
+}  // namespace pk

@@ -131,6 +131,20 @@ struct LnArgs {
 };
 int launch_layer_norm(const LnArgs &a, cudaStream_t s);
 
+// pk_gemm.cu
+struct GemmArgs {
+    const void *A, *W;
+    int64_t lda, ldw;
+    int M, N, K, epilogue;
+    void *C;
+    int64_t ldc;
+    const void *R;
+    int64_t ldr;
+    float alpha;
+    int32_t *error;
+};
+int launch_gemm(const GemmArgs &g, cudaStream_t s);
+
 // pk_features.cu.  Table block: int32 header[kFeHeader], then float2
 // twiddle[n_fft] (exp(-2 pi i u / n_fft)), float window[n_fft], int32 lo[n_mels],
 // cnt[n_mels], off[n_mels] (first bin, length and offset of each filter's

@@ -12,16 +12,6 @@
 namespace pk {
 namespace {
 
-// Element offset of (page, layer, K|V, row, model column) in the head-major
-// pool [pages][layers][2][heads][page_size][head_dim].
-__device__ __forceinline__ int64_t pool_offset(const pk_paged_kv_desc &d, int page, int layer,
-                                               int kvi, int row, int col) {
-    const int dh = d.dim / d.num_heads;
-    const int h = col / dh;
-    return (((((int64_t)page * d.num_layers + layer) * 2 + kvi) * d.num_heads + h) * d.page_size +
-            row) * dh + (col - h * dh);
-}
-
 // A stream's step context in shared memory: its slot, rows written so far
 // (meta) and its page-table ring, read once per CTA.  Loads that do not depend
 // on it are issued before it (they overlap its two dependent round trips).

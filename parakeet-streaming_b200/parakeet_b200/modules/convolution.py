@@ -15,6 +15,7 @@ import torch.nn.functional as F
 from torch import Tensor, nn
 
 from .cache import ConvCacheRef
+from .feedforward import residual_linear
 
 
 class ConformerConvolution(nn.Module):
@@ -49,10 +50,7 @@ class ConformerConvolution(nn.Module):
         h = F.linear(x, self.pointwise_conv1.weight[:, :, 0])            # [B, T, 2D]
         y = c.pool.conv_step(cache.layer_idx, h, self.depthwise_conv.weight, c.slots, c.lengths,
                              self.batch_norm.weight, self.batch_norm.bias, self.batch_norm.eps)
-        w2 = self.pointwise_conv2.weight[:, :, 0]
-        shape = res.shape
-        return torch.addmm(res.reshape(-1, shape[-1]), y.reshape(-1, y.shape[-1]), w2.t(),
-                           beta=1, alpha=1).reshape(shape)
+        return residual_linear(res, y, None, weight=self.pointwise_conv2.weight[:, :, 0])
 
 
 __all__ = ["ConformerConvolution"]

@@ -57,6 +57,56 @@ def layer_norm(x: torch.Tensor, ln, ln2=None):
     return y if ln2 is None else (y, y2.reshape(x.shape))
 
 
+GEMM_EPILOGUES = {"store": _lib.PK_GEMM_STORE, "silu": _lib.PK_GEMM_SILU,
+                  "residual": _lib.PK_GEMM_RESIDUAL}
+_gemm_error: dict = {}
+
+
+def _rows(t: torch.Tensor, width: int) -> torch.Tensor:
+    """t as [rows, width] with unit column stride, 16-byte aligned rows."""
+    t2 = t.reshape(-1, width)
+    if t2.stride(-1) != 1 or t2.stride(0) % 8 or t2.data_ptr() % 16:
+        t2 = t2.contiguous()
+    return t2
+
+
+def gemm_supported(a: torch.Tensor, weight: torch.Tensor) -> bool:
+    """Shapes and types pk_gemm_bf16 takes: bf16 CUDA operands, K and N
+    multiples of 64, the weight's rows contiguous and 16-byte aligned."""
+    return (a.is_cuda and a.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16
+            and weight.dim() == 2 and a.shape[-1] == weight.shape[1]
+            and weight.shape[1] % 64 == 0 and weight.shape[0] % 64 == 0
+            and weight.stride(1) == 1 and weight.stride(0) % 8 == 0
+            and weight.data_ptr() % 16 == 0)
+
+
+def gemm(a: torch.Tensor, weight: torch.Tensor, epilogue: str = "store",
+         residual: torch.Tensor | None = None, alpha: float = 1.0) -> torch.Tensor:
+    """epilogue(a @ weight.T) on the tcgen05 tensor cores (pk_gemm_bf16):
+    "store" -> acc, "silu" -> acc * sigmoid(acc), "residual" -> residual +
+    alpha * acc.  a [..., K], weight [N, K] (an nn.Linear weight), bf16."""
+    K, N = weight.shape[1], weight.shape[0]
+    a2 = _rows(a, K)
+    M = a2.shape[0]
+    out = torch.empty((M, N), dtype=a.dtype, device=a.device)
+    r2 = None
+    if epilogue == "residual":
+        r2 = _rows(residual, N)
+    err = _gemm_error.get(a.device)
+    if err is None:
+        err = _gemm_error[a.device] = torch.zeros(1, dtype=torch.int32, device=a.device)
+    check(lib().pk_gemm_bf16(a2.data_ptr(), a2.stride(0), weight.data_ptr(), weight.stride(0), M,
+                             N, K, out.data_ptr(), N, GEMM_EPILOGUES[epilogue], _ptr(r2),
+                             r2.stride(0) if r2 is not None else 0, float(alpha), err.data_ptr(),
+                             _stream(a.device)), "pk_gemm_bf16")
+    return out.reshape(*a.shape[:-1], N)
+
+
+def gemm_error_word(device) -> int:
+    err = _gemm_error.get(torch.device(device))
+    return 0 if err is None else int(err.item())
+
+
 def pages_per_stream(left: int, chunk: int, page_size: int) -> int:
     return int(lib().pk_pages_per_stream(left, chunk, page_size))
 
