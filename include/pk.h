@@ -222,6 +222,31 @@ int pk_pre_encode_window(void *cache, int32_t num_slots, const void *feats,
                          int32_t csize, int32_t prefix_frames, void *out, int32_t dtype,
                          int32_t *error, void *stream);
 
+/* The strided convs of ConvSubsampling (parakeet/modules/subsample.py:
+ * 61-179, dw_striding; every conv causal: CausalConv2D, convolution.py:55-104,
+ * output (o, p) reads input rows 2o-2 .. 2o and columns 2p-2 .. 2p, zero
+ * outside).  pk_subsample_stage12: conv1 (1 -> C, 3x3 stride 2, bias, ReLU)
+ * and the depthwise conv2 (3x3 stride 2, bias) in one launch, conv1's
+ * activation kept in shared memory; x[b][f][t] at b*x_batch_stride +
+ * f*x_feat_stride + t*x_time_stride (the pre-encode window, frames x feat
+ * per row); y channels-last [batch][T2 - first_row][F2][C] with T2, F2 the
+ * conv2 output sizes, holding conv2 rows first_row .. T2-1.  C a multiple of
+ * 16.  w1, w2 are [C][1][3][3], b1, b2 [C]. */
+int pk_subsample_stage12(const void *x, int64_t x_batch_stride, int64_t x_feat_stride,
+                         int64_t x_time_stride, int32_t batch, int32_t frames, int32_t feat,
+                         const void *w1, const void *b1, const void *w2, const void *b2,
+                         int32_t channels, int32_t first_row, void *y, int32_t dtype,
+                         void *stream);
+
+/* Depthwise 3x3 stride-2 causal conv + bias over channels-last rows: x
+ * [batch][rows_in - first_in][cols_in][C] holds input rows first_in ..
+ * rows_in-1 (earlier rows are never read: first_in <= max(0, 2*first_out - 2));
+ * y [batch][R - first_out][Cout][C] gets output rows first_out .. R-1 (R =
+ * rows_in / 2 + 1, Cout = cols_in / 2 + 1).  w [C][1][3][3], b [C]. */
+int pk_subsample_dw(const void *x, int32_t batch, int32_t rows_in, int32_t first_in,
+                    int32_t cols_in, const void *w, const void *b, int32_t channels,
+                    int32_t first_out, void *y, int32_t dtype, void *stream);
+
 /* ---------------- batched greedy RNNT decode (device-side bookkeeping) ----
  * A chunk's decode runs, for every frame f < frames and symbol s <
  * max_symbols, joint -> pk_rnnt_pick -> prediction step -> pk_lstm_cell, all

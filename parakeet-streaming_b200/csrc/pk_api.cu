@@ -372,6 +372,68 @@ int pk_pre_encode_window(void *cache, int32_t num_slots, const void *feats,
                                     static_cast<cudaStream_t>(stream));
 }
 
+int pk_subsample_stage12(const void *x, int64_t x_batch_stride, int64_t x_feat_stride,
+                         int64_t x_time_stride, int32_t batch, int32_t frames, int32_t feat,
+                         const void *w1, const void *b1, const void *w2, const void *b2,
+                         int32_t channels, int32_t first_row, void *y, int32_t dtype,
+                         void *stream) {
+    PK_CHECK(dtype == PK_DTYPE_F32 || dtype == PK_DTYPE_BF16, "bad dtype %d", dtype);
+    PK_CHECK(batch >= 0, "negative batch");
+    if (batch == 0) return PK_OK;
+    PK_CHECK(x && w1 && b1 && w2 && b2 && y, "null pointer");
+    PK_CHECK(frames > 0 && feat > 0 && feat <= 1024, "bad window %d x %d", frames, feat);
+    PK_CHECK(channels > 0 && channels % 16 == 0, "channels %d: a multiple of 16", channels);
+    const int t2 = (frames / 2 + 1) / 2 + 1;
+    PK_CHECK(first_row >= 0 && first_row < t2, "first_row %d outside [0, %d)", first_row, t2);
+    PK_CHECK(frames <= 4096 && batch <= 65535, "window or batch too large");
+    SubsampleArgs a = {};
+    a.x = x;
+    a.xb = x_batch_stride;
+    a.xf = x_feat_stride;
+    a.xt = x_time_stride;
+    a.batch = batch;
+    a.frames = frames;
+    a.feat = feat;
+    a.channels = channels;
+    a.dtype = dtype;
+    a.w1 = w1;
+    a.b1 = b1;
+    a.w2 = w2;
+    a.b2 = b2;
+    a.first = first_row;
+    a.y = y;
+    return launch_subsample_stage12(a, static_cast<cudaStream_t>(stream));
+}
+
+int pk_subsample_dw(const void *x, int32_t batch, int32_t rows_in, int32_t first_in,
+                    int32_t cols_in, const void *w, const void *b, int32_t channels,
+                    int32_t first_out, void *y, int32_t dtype, void *stream) {
+    PK_CHECK(dtype == PK_DTYPE_F32 || dtype == PK_DTYPE_BF16, "bad dtype %d", dtype);
+    PK_CHECK(batch >= 0, "negative batch");
+    if (batch == 0) return PK_OK;
+    PK_CHECK(x && w && b && y, "null pointer");
+    PK_CHECK(rows_in > 0 && cols_in > 0 && channels > 0, "bad shape");
+    const int rows_out = rows_in / 2 + 1;
+    PK_CHECK(first_out >= 0 && first_out < rows_out, "first_out %d outside [0, %d)", first_out,
+             rows_out);
+    const int need = 2 * first_out - 2 > 0 ? 2 * first_out - 2 : 0;
+    PK_CHECK(first_in >= 0 && first_in <= need && first_in < rows_in,
+             "first_in %d: rows the outputs read must be present (<= %d)", first_in, need);
+    SubsampleArgs a = {};
+    a.x = x;
+    a.batch = batch;
+    a.frames = rows_in;
+    a.first = first_in;
+    a.feat = cols_in;
+    a.w2 = w;
+    a.b2 = b;
+    a.channels = channels;
+    a.first_out = first_out;
+    a.dtype = dtype;
+    a.y = y;
+    return launch_subsample_dw(a, static_cast<cudaStream_t>(stream));
+}
+
 int pk_rnnt_pick(const void *logits, int64_t logits_ld, int32_t dtype, int32_t batch,
                  int32_t num_classes, int32_t blank, const int32_t *lengths, int32_t frame,
                  int32_t symbol, int32_t max_symbols, int32_t frames, int32_t *done,

@@ -145,6 +145,18 @@ struct GemmArgs {
 };
 int launch_gemm(const GemmArgs &g, cudaStream_t s);
 
+// pk_subsample.cu
+struct SubsampleArgs {
+    const void *x;
+    int64_t xb, xf, xt;      // stage12: x[b][f][t] strides (elements)
+    int batch, frames, feat, channels, dtype;
+    const void *w1, *b1, *w2, *b2;   // dw: w2 / b2 are the depthwise conv's
+    int first, first_out;
+    void *y;
+};
+int launch_subsample_stage12(const SubsampleArgs &a, cudaStream_t s);
+int launch_subsample_dw(const SubsampleArgs &a, cudaStream_t s);
+
 // pk_features.cu.  Table block: int32 header[kFeHeader], then float2
 // twiddle[n_fft] (exp(-2 pi i u / n_fft)), float window[n_fft], int32 lo[n_mels],
 // cnt[n_mels], off[n_mels] (first bin, length and offset of each filter's

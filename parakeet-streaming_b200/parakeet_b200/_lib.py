@@ -96,6 +96,9 @@ SIGNATURES = {
                      ctypes.c_float, _P, _P, _I32, _P, _P, _P],
     "pk_gemm_bf16": [_P, _I64, _P, _I64, _I32, _I32, _I32, _P, _I64, _I32, _P, _I64,
                      ctypes.c_float, _P, _P],
+    "pk_subsample_stage12": [_P, _I64, _I64, _I64, _I32, _I32, _I32, _P, _P, _P, _P, _I32,
+                             _I32, _P, _I32, _P],
+    "pk_subsample_dw": [_P, _I32, _I32, _I32, _I32, _P, _P, _I32, _I32, _P, _I32, _P],
     "pk_layer_norm": [_P, _I64, _I32, _I32, _P, _P, ctypes.c_float, _P, _I64, _P, _P,
                       ctypes.c_float, _P, _I64, _I32, _P],
     "pk_features_tables": [_I32, _I32, _I32, _I32, ctypes.c_double, ctypes.c_double, _I32, _P,

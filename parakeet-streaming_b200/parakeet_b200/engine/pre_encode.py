@@ -53,10 +53,11 @@ class BatchedPreEncoder:
                                          sl.data_ptr(), B, M, F, self.cache_size, pre,
                                          x.data_ptr(), DTYPES[self.dtype], self.error.data_ptr(),
                                          _stream(self.device)), "pk_pre_encode_window")
+        drop = 0 if first else self.drop_extra
+        if self.module.stream_supported(x):
+            return self.module.forward_stream(x, drop)      # fused convs, dropped rows skipped
         y = self.module.forward_full(x.transpose(1, 2))   # every row spans all frames
-        if not first and self.drop_extra > 0:
-            y = y[:, self.drop_extra:]
-        return y
+        return y[:, drop:] if drop else y
 
 
 __all__ = ["BatchedPreEncoder"]

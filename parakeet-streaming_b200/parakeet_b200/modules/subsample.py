@@ -16,6 +16,9 @@ import torch
 import torch.nn.functional as F
 from torch import Tensor, nn
 
+from .._lib import check, lib
+from ..ops import DTYPES, _stream
+
 
 class ConvSubsampling(nn.Module):
     def __init__(self, hidden_size: int, subsampling_conv_channels: int, feat_in: int,
@@ -80,6 +83,64 @@ class ConvSubsampling(nn.Module):
                 x = layer(x)
         b, c, t, f = x.shape
         return self.out(x.permute(0, 2, 1, 3).reshape(b, t, c * f))
+
+    def stream_supported(self, x: Tensor) -> bool:
+        """The fused streaming path takes the 8x dw_striding stack with 3x3
+        stride-2 convs and channels in multiples of 16, on CUDA."""
+        return (x.is_cuda and x.dtype in DTYPES and self.sampling_num == 3
+                and self._kernel_size == 3 and self._stride == 2
+                and self._conv_channels % 16 == 0
+                and self.conv[0].weight.dtype == x.dtype)
+
+    def _out_weight(self) -> Tensor:
+        """``out.weight`` with its columns reordered from (channel, frequency)
+        to (frequency, channel), so channels-last rows multiply it directly;
+        cached while the weight is unchanged."""
+        w = self.out.weight
+        try:
+            version = w._version
+        except RuntimeError:   # an inference-mode tensor has no version counter
+            version = None
+        key = (w.data_ptr(), version, w.dtype)
+        if getattr(self, "_outw_key", None) != key:
+            C = self._conv_channels
+            f3 = w.shape[1] // C
+            self._outw = w.reshape(w.shape[0], C, f3).transpose(1, 2).reshape(w.shape[0], -1).contiguous()
+            self._outw_key = key
+        return self._outw
+
+    def forward_stream(self, xw: Tensor, drop: int = 0) -> Tensor:
+        """``forward_full`` for a batch of streaming windows given as the
+        pre-encode cache kernel writes them, xw [B, feat_in, frames], minus
+        the first ``drop`` output frames: [B, frames' - drop, hidden].  conv1
+        and the depthwise conv2 run as one libpk launch (conv1's activation
+        stays in shared memory), the depthwise conv3 as another, the
+        pointwise convs and ``out`` as GEMMs over channels-last rows; only the
+        rows the kept outputs read are computed."""
+        B, Fi, W = xw.shape
+        C = self._conv_channels
+        t1, f1 = W // 2 + 1, Fi // 2 + 1
+        t2, f2 = t1 // 2 + 1, f1 // 2 + 1
+        t3, f3 = t2 // 2 + 1, f2 // 2 + 1
+        if not 0 <= drop < t3:
+            raise ValueError(f"drop {drop} of {t3} output frames")
+        first3 = drop
+        first2 = max(0, 2 * first3 - 2)
+        dt, dev, st = DTYPES[xw.dtype], xw.device, _stream(xw.device)
+        c0, dw2, pw2, dw3, pw3 = self.conv[0], self.conv[2], self.conv[3], self.conv[5], self.conv[6]
+        y2 = torch.empty(B, t2 - first2, f2, C, dtype=xw.dtype, device=dev)
+        check(lib().pk_subsample_stage12(
+            xw.data_ptr(), xw.stride(0), xw.stride(1), xw.stride(2), B, W, Fi,
+            c0.weight.data_ptr(), c0.bias.data_ptr(), dw2.weight.data_ptr(), dw2.bias.data_ptr(),
+            C, first2, y2.data_ptr(), dt, st), "pk_subsample_stage12")
+        h2 = torch.addmm(pw2.bias, y2.view(-1, C), pw2.weight.view(C, C).t()).relu_()
+        y3 = torch.empty(B, t3 - first3, f3, C, dtype=xw.dtype, device=dev)
+        check(lib().pk_subsample_dw(
+            h2.data_ptr(), B, t2, first2, f2, dw3.weight.data_ptr(), dw3.bias.data_ptr(), C,
+            first3, y3.data_ptr(), dt, st), "pk_subsample_dw")
+        h3 = torch.addmm(pw3.bias, y3.view(-1, C), pw3.weight.view(C, C).t()).relu_()
+        out = torch.addmm(self.out.bias, h3.view(-1, f3 * C), self._out_weight().t())
+        return out.view(B, t3 - first3, -1)
 
 
 __all__ = ["ConvSubsampling"]

@@ -56,3 +56,30 @@ def test_batched_pre_encode_matches_reference(cfg, name):
                     assert rel_l2(y[r], g[f"y_{step}_{i}"]) <= 1e-5, (step, i, first)
                     held[i] = min(cfg["cache"], pre + F)
     assert int(pe.error.item()) == 0
+
+
+@pytest.mark.parametrize("frames", [8, 9, 24, 25, 104, 121])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_fused_stream_path_equals_full_path(frames, dtype):
+    """forward_stream (conv1 + depthwise conv2 in one launch, conv3 depthwise,
+    pointwise convs and out as GEMMs over channels-last rows, dropped rows
+    skipped) against forward_full (cuDNN convs) on the same windows."""
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    cfg = PRE_SMALL if frames < 100 else PRE_LARGE
+    m = ConvSubsampling(cfg["hidden"], cfg["channels"], cfg["feat_in"], 8)
+    sd = random_pre_encode_state_dict(cfg["seed"], cfg["feat_in"], cfg["channels"], cfg["hidden"])
+    m.load_state_dict({k: torch.from_numpy(v) for k, v in sd.items()}, strict=True)
+    m = m.to("cuda", dtype).eval()
+    g = torch.Generator(device="cuda").manual_seed(frames)
+    xw = torch.randn(5, cfg["feat_in"], frames, generator=g, device="cuda").to(dtype)
+    with torch.inference_mode():
+        full = m.forward_full(xw.transpose(1, 2)).float()
+        for drop in (0, 2):
+            if drop >= full.shape[1]:
+                continue
+            got = m.forward_stream(xw, drop).float()
+            ref = full[:, drop:]
+            assert got.shape == ref.shape
+            err = float((got - ref).norm() / ref.norm())
+            assert err <= (1e-5 if dtype == torch.float32 else 2e-2), (drop, err)
