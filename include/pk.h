@@ -268,32 +268,39 @@ int pk_rnnt_pick(const void *logits, int64_t logits_ld, int32_t dtype, int32_t b
                  int32_t *emit, int64_t *ids, int32_t *tokens, int32_t *counts, void *stream);
 
 /* One LSTM cell step from precomputed gates [batch][4 * hidden] (x W_ih^T +
- * h W_hh^T + biases, PyTorch order i, f, g, o; row stride `gates_ld`) into the
- * state rows h, c (row stride `state_ld`), only for rows with emit[b] != 0;
- * other rows keep their state.  Replaces the nn.LSTM step of
- * Predictor.forward (parakeet/modules/decoder.py:44-50) and the torch.where of
- * model_runner.py:433-445. */
-int pk_lstm_cell(const void *gates, int64_t gates_ld, void *h, void *c, int64_t state_ld,
-                 const int32_t *emit, int32_t batch, int32_t hidden, int32_t dtype,
-                 void *stream);
+ * h W_hh^T + biases, PyTorch order i, f, g, o; row stride `gates_ld`), plus,
+ * when xtab != NULL, the row xtab[ids[b]] (row stride xtab_ld: a per-token
+ * table of the embedding times W_ih plus the biases), into the state rows
+ * h, c (row stride `state_ld`), only for rows with emit[b] != 0; other rows
+ * keep their state.  Replaces the embedding and nn.LSTM step of
+ * Predictor.forward (parakeet/modules/decoder.py:44-50) and the torch.where
+ * of model_runner.py:433-445. */
+int pk_lstm_cell(const void *gates, int64_t gates_ld, const void *xtab, int64_t xtab_ld,
+                 const int64_t *ids, void *h, void *c, int64_t state_ld, const int32_t *emit,
+                 int32_t batch, int32_t hidden, int32_t dtype, void *stream);
 
 /* bf16 GEMM on the tcgen05 tensor cores (fp32 accumulation in tensor
  * memory) with the encoder's epilogues:
  *   C[m][n] = epi(acc[m][n]),  acc = sum_k A[m][k] * W[n][k]
  *   PK_GEMM_STORE: acc;  PK_GEMM_SILU: acc * sigmoid(acc);
- *   PK_GEMM_RESIDUAL: R[m][n] + alpha * acc (R may be C).
+ *   PK_GEMM_RESIDUAL: R[m][n] + alpha * acc (R may be C);
+ *   PK_GEMM_RESIDUAL_RELU: max(R[m][n] + alpha * acc, 0);
+ *   PK_GEMM_BIAS: acc + bias[n].
  * A [M][K] (row stride lda), W [N][K] (ldw, an nn.Linear weight), C and R
- * [M][N] (ldc, ldr), all bf16, 16-byte aligned, strides multiples of 8;
- * K a multiple of 64, N a multiple of 64.  Replaces the Linear -> SiLU ->
- * Linear of ConformerFeedForward (parakeet/modules/feedforward.py) and the
- * residual adds of ConformerLayer.forward (parakeet/modules/encoder.py:60-81)
- * around the attention and conv projections. */
+ * [M][N] (ldc, ldr), bias [N], all bf16, 16-byte aligned, strides multiples
+ * of 8; K a multiple of 64, N a multiple of 64.  Replaces the Linear -> SiLU
+ * -> Linear of ConformerFeedForward (parakeet/modules/feedforward.py), the
+ * residual adds of ConformerLayer.forward (parakeet/modules/encoder.py:
+ * 60-81) and the joint network's enc + pred -> ReLU -> Linear
+ * (parakeet/modules/decoder.py:82-86). */
 #define PK_GEMM_STORE 0
 #define PK_GEMM_SILU 1
 #define PK_GEMM_RESIDUAL 2
+#define PK_GEMM_RESIDUAL_RELU 3
+#define PK_GEMM_BIAS 4
 int pk_gemm_bf16(const void *A, int64_t lda, const void *W, int64_t ldw, int32_t M, int32_t N,
                  int32_t K, void *C, int64_t ldc, int32_t epilogue, const void *R, int64_t ldr,
-                 float alpha, int32_t *error, void *stream);
+                 const void *bias, float alpha, int32_t *error, void *stream);
 
 /* LayerNorm over the last dimension of `rows` rows (row strides x_ld, y_ld
  * elements): y = (x - mean) / sqrt(var + eps) * gamma + beta, fp32 statistics

@@ -452,32 +452,33 @@ int pk_rnnt_pick(const void *logits, int64_t logits_ld, int32_t dtype, int32_t b
                             static_cast<cudaStream_t>(stream));
 }
 
-int pk_lstm_cell(const void *gates, int64_t gates_ld, void *h, void *c, int64_t state_ld,
-                 const int32_t *emit, int32_t batch, int32_t hidden, int32_t dtype,
-                 void *stream) {
+int pk_lstm_cell(const void *gates, int64_t gates_ld, const void *xtab, int64_t xtab_ld,
+                 const int64_t *ids, void *h, void *c, int64_t state_ld, const int32_t *emit,
+                 int32_t batch, int32_t hidden, int32_t dtype, void *stream) {
     PK_CHECK(dtype == PK_DTYPE_F32 || dtype == PK_DTYPE_BF16, "bad dtype %d", dtype);
     PK_CHECK(batch >= 0 && hidden >= 0, "negative shape");
     if (batch == 0 || hidden == 0) return PK_OK;
     PK_CHECK(gates && h && c && emit, "null pointer");
     PK_CHECK(gates_ld >= 4 * (int64_t)hidden && state_ld >= hidden, "bad strides");
-    return launch_lstm_cell(gates, gates_ld, h, c, state_ld, emit, batch, hidden, dtype,
-                            static_cast<cudaStream_t>(stream));
+    PK_CHECK(!xtab || (ids && xtab_ld >= 4 * (int64_t)hidden), "xtab needs ids and a row stride");
+    return launch_lstm_cell(gates, gates_ld, xtab, xtab_ld, ids, h, c, state_ld, emit, batch,
+                            hidden, dtype, static_cast<cudaStream_t>(stream));
 }
 
 int pk_gemm_bf16(const void *A, int64_t lda, const void *W, int64_t ldw, int32_t M, int32_t N,
                  int32_t K, void *C, int64_t ldc, int32_t epilogue, const void *R, int64_t ldr,
-                 float alpha, int32_t *error, void *stream) {
+                 const void *bias, float alpha, int32_t *error, void *stream) {
     PK_CHECK(M >= 0 && N > 0 && K > 0, "bad shape %d x %d x %d", M, N, K);
     if (M == 0) return PK_OK;
     PK_CHECK(K % 64 == 0 && N % 64 == 0, "K (%d) and N (%d) must be multiples of 64", K, N);
-    PK_CHECK(epilogue == PK_GEMM_STORE || epilogue == PK_GEMM_SILU ||
-                 epilogue == PK_GEMM_RESIDUAL, "bad epilogue %d", epilogue);
+    PK_CHECK(epilogue >= PK_GEMM_STORE && epilogue <= PK_GEMM_BIAS, "bad epilogue %d", epilogue);
     PK_CHECK(A && W && C && error, "null pointer");
     PK_CHECK(aligned16(A) && aligned16(W) && aligned16(C), "operands must be 16-byte aligned");
     PK_CHECK(lda >= K && ldw >= K && ldc >= N && lda % 8 == 0 && ldw % 8 == 0 && ldc % 8 == 0,
              "row strides must cover the rows and be multiples of 8 elements");
-    if (epilogue == PK_GEMM_RESIDUAL)
+    if (epilogue == PK_GEMM_RESIDUAL || epilogue == PK_GEMM_RESIDUAL_RELU)
         PK_CHECK(R && aligned16(R) && ldr >= N && ldr % 8 == 0, "bad residual operand");
+    if (epilogue == PK_GEMM_BIAS) PK_CHECK(bias && aligned16(bias), "bad bias operand");
     PK_CHECK(M <= 65535 * 128, "M too large");
     GemmArgs g;
     g.A = A;
@@ -492,6 +493,7 @@ int pk_gemm_bf16(const void *A, int64_t lda, const void *W, int64_t ldw, int32_t
     g.ldc = ldc;
     g.R = R;
     g.ldr = ldr;
+    g.bias = bias;
     g.alpha = alpha;
     g.error = error;
     return launch_gemm(g, static_cast<cudaStream_t>(stream));

@@ -1,7 +1,7 @@
 // bf16 GEMM on the 5th-generation tensor cores with the encoder's epilogues.
 //
 //   C[m][n] = epilogue( sum_k A[m][k] * W[n][k] ),  A, W, C bf16, fp32 accumulation
-//   epilogue: store | SiLU | R[m][n] + alpha * acc
+//   epilogue: store | SiLU | R[m][n] + alpha * acc (optionally ReLU'd) | acc + bias[n]
 //
 // These are the Conformer layer's projections (parakeet/modules/feedforward.py:
 // Linear -> SiLU -> Linear; attention.py qkv / linear_out; convolution.py
@@ -116,7 +116,7 @@ template <int BN, int NS, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w,
                      int M, int K, __nv_bfloat16 *C, int64_t ldc, const __nv_bfloat16 *R,
-                     int64_t ldr, float alpha, int32_t *error) {
+                     int64_t ldr, const __nv_bfloat16 *bias, float alpha, int32_t *error) {
     constexpr int kBBytes = BN * kBK * 2;
     extern __shared__ uint8_t gemm_smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
@@ -212,14 +212,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (EPI == PK_GEMM_SILU) {
 #pragma unroll
                     for (int i = 0; i < 32; ++i) v[i] = __fdividef(v[i], 1.f + __expf(-v[i]));
-                } else if (EPI == PK_GEMM_RESIDUAL) {
+                } else if (EPI == PK_GEMM_RESIDUAL || EPI == PK_GEMM_RESIDUAL_RELU) {
                     const uint4 *rp = reinterpret_cast<const uint4 *>(R + (int64_t)row * ldr + col);
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
                         float f[8];
                         unpack16(rp[q], f, R);
 #pragma unroll
-                        for (int i = 0; i < 8; ++i) v[q * 8 + i] = f[i] + alpha * v[q * 8 + i];
+                        for (int i = 0; i < 8; ++i) {
+                            const float t = f[i] + alpha * v[q * 8 + i];
+                            v[q * 8 + i] = EPI == PK_GEMM_RESIDUAL_RELU ? fmaxf(t, 0.f) : t;
+                        }
+                    }
+                } else if (EPI == PK_GEMM_BIAS) {
+                    const uint4 *bp = reinterpret_cast<const uint4 *>(bias + col);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        float f[8];
+                        unpack16(bp[q], f, bias);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) v[q * 8 + i] += f[i];
                     }
                 }
                 uint4 *cp = reinterpret_cast<uint4 *>(C + (int64_t)row * ldc + col);
@@ -257,7 +269,8 @@ int launch_gemm_t(const GemmArgs &g, const CUtensorMap &ta, const CUtensorMap &t
     const dim3 grid(g.N / BN, (g.M + kBM - 1) / kBM);
     cudaError_t e = launch_pdl(k, grid, dim3(kThreads), smem, s, ta, tw, g.M, g.K,
                                static_cast<__nv_bfloat16 *>(g.C), g.ldc,
-                               static_cast<const __nv_bfloat16 *>(g.R), g.ldr, g.alpha, g.error);
+                               static_cast<const __nv_bfloat16 *>(g.R), g.ldr,
+                               static_cast<const __nv_bfloat16 *>(g.bias), g.alpha, g.error);
     return cuda_status(e, "gemm_bf16_kernel");
 }
 
@@ -267,6 +280,9 @@ int launch_gemm_epi(const GemmArgs &g, const CUtensorMap &ta, const CUtensorMap 
     switch (g.epilogue) {
         case PK_GEMM_SILU: return launch_gemm_t<BN, NS, PK_GEMM_SILU>(g, ta, tw, s);
         case PK_GEMM_RESIDUAL: return launch_gemm_t<BN, NS, PK_GEMM_RESIDUAL>(g, ta, tw, s);
+        case PK_GEMM_RESIDUAL_RELU:
+            return launch_gemm_t<BN, NS, PK_GEMM_RESIDUAL_RELU>(g, ta, tw, s);
+        case PK_GEMM_BIAS: return launch_gemm_t<BN, NS, PK_GEMM_BIAS>(g, ta, tw, s);
         default: return launch_gemm_t<BN, NS, PK_GEMM_STORE>(g, ta, tw, s);
     }
 }

@@ -112,8 +112,9 @@ int launch_rnnt_pick(const void *logits, int64_t ld, int dtype, int batch, int n
                      const int32_t *lengths, int frame, int symbol, int max_symbols, int frames,
                      int32_t *done, int32_t *emit, int64_t *ids, int32_t *tokens, int32_t *counts,
                      cudaStream_t s);
-int launch_lstm_cell(const void *gates, int64_t gld, void *h, void *c, int64_t sld,
-                     const int32_t *emit, int batch, int hidden, int dtype, cudaStream_t s);
+int launch_lstm_cell(const void *gates, int64_t gld, const void *xtab, int64_t xld,
+                     const int64_t *ids, void *h, void *c, int64_t sld, const int32_t *emit,
+                     int batch, int hidden, int dtype, cudaStream_t s);
 
 // pk_norm.cu
 struct LnArgs {
@@ -140,6 +141,7 @@ struct GemmArgs {
     int64_t ldc;
     const void *R;
     int64_t ldr;
+    const void *bias;
     float alpha;
     int32_t *error;
 };

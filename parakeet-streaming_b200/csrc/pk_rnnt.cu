@@ -64,18 +64,27 @@ __global__ void __launch_bounds__(kPickWarps * 32)
 
 __device__ __forceinline__ float sigmoidf(float x) { return 1.f / (1.f + expf(-x)); }
 
-// one thread per (row, hidden unit); rows that did not emit keep their state
+// one thread per (row, hidden unit); rows that did not emit keep their state.
+// xtab (optional): a per-token addend row of the gates, xtab[ids[b]] (the
+// embedding already multiplied by W_ih, plus both biases)
 template <typename T>
 __global__ void __launch_bounds__(256)
-    lstm_cell_kernel(const T *gates, int64_t gld, T *h, T *c, int64_t sld, const int32_t *emit,
-                     int batch, int hidden) {
+    lstm_cell_kernel(const T *gates, int64_t gld, const T *xtab, int64_t xld, const int64_t *ids,
+                     T *h, T *c, int64_t sld, const int32_t *emit, int batch, int hidden) {
     const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= (int64_t)batch * hidden) return;
     const int b = (int)(idx / hidden), j = (int)(idx - (int64_t)b * hidden);
     if (!emit[b]) return;
     const T *g = gates + (int64_t)b * gld;
-    const float gi = Elem<T>::to_f(g[j]), gf = Elem<T>::to_f(g[hidden + j]);
-    const float gg = Elem<T>::to_f(g[2 * hidden + j]), go = Elem<T>::to_f(g[3 * hidden + j]);
+    float gi = Elem<T>::to_f(g[j]), gf = Elem<T>::to_f(g[hidden + j]);
+    float gg = Elem<T>::to_f(g[2 * hidden + j]), go = Elem<T>::to_f(g[3 * hidden + j]);
+    if (xtab) {
+        const T *x = xtab + ids[b] * xld;
+        gi += Elem<T>::to_f(x[j]);
+        gf += Elem<T>::to_f(x[hidden + j]);
+        gg += Elem<T>::to_f(x[2 * hidden + j]);
+        go += Elem<T>::to_f(x[3 * hidden + j]);
+    }
     T *cp = c + (int64_t)b * sld + j;
     const float cn = sigmoidf(gf) * Elem<T>::to_f(*cp) + sigmoidf(gi) * tanhf(gg);
     const T cq = Elem<T>::from_f(cn);
@@ -102,18 +111,20 @@ int launch_rnnt_pick(const void *logits, int64_t ld, int dtype, int batch, int n
     return cuda_status(cudaGetLastError(), "rnnt_pick_kernel");
 }
 
-int launch_lstm_cell(const void *gates, int64_t gld, void *h, void *c, int64_t sld,
-                     const int32_t *emit, int batch, int hidden, int dtype, cudaStream_t s) {
+int launch_lstm_cell(const void *gates, int64_t gld, const void *xtab, int64_t xld,
+                     const int64_t *ids, void *h, void *c, int64_t sld, const int32_t *emit,
+                     int batch, int hidden, int dtype, cudaStream_t s) {
     const int64_t n = (int64_t)batch * hidden;
     if (n == 0) return PK_OK;
     const dim3 grid((unsigned)((n + 255) / 256));
     if (dtype == PK_DTYPE_BF16)
-        lstm_cell_kernel<<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16 *>(gates), gld,
-                                              static_cast<__nv_bfloat16 *>(h),
-                                              static_cast<__nv_bfloat16 *>(c), sld, emit, batch,
-                                              hidden);
+        lstm_cell_kernel<<<grid, 256, 0, s>>>(
+            static_cast<const __nv_bfloat16 *>(gates), gld,
+            static_cast<const __nv_bfloat16 *>(xtab), xld, ids, static_cast<__nv_bfloat16 *>(h),
+            static_cast<__nv_bfloat16 *>(c), sld, emit, batch, hidden);
     else
         lstm_cell_kernel<<<grid, 256, 0, s>>>(static_cast<const float *>(gates), gld,
+                                              static_cast<const float *>(xtab), xld, ids,
                                               static_cast<float *>(h), static_cast<float *>(c),
                                               sld, emit, batch, hidden);
     return cuda_status(cudaGetLastError(), "lstm_cell_kernel");

@@ -50,51 +50,66 @@ __global__ void __launch_bounds__(kThreads)
     const int s1w = f1n + 3;                          // stage-1 columns -2 .. f1n
     grid_dep_wait();
     const T *xrow = x + (int64_t)b * xb;
+    // time fastest: the window is stored frames-contiguous per feature bin
     for (int i = threadIdx.x; i < nin * fpad; i += kThreads) {
-        const int r = i / fpad, f = i - r * fpad - 2;
-        const int t = t_lo + r;
+        const int j = i / nin, r = i - j * nin;
+        const int t = t_lo + r, f = j - 2;
         float v = 0.f;
         if (t >= 0 && t < frames && f >= 0 && f < feat)
             v = Elem<T>::to_f(xrow[(int64_t)f * xf + (int64_t)t * xt]);
-        xs[i] = v;
+        xs[r * fpad + j] = v;
     }
     __syncthreads();
+    // thread = (channel c of the block, position lane l of kLanes): the
+    // channel's taps stay in registers, positions are walked without divisions
+    constexpr int kLanes = kThreads / kCB;
+    const int c = threadIdx.x % kCB, l = threadIdx.x / kCB;
+    float wa[9];
+#pragma unroll
+    for (int i = 0; i < 9; ++i) wa[i] = Elem<T>::to_f(w1[(c0 + c) * 9 + i]);
+    const float ba = Elem<T>::to_f(b1[c0 + c]);
     // conv1 + bias + ReLU, zero outside the stage-1 grid (the next conv's padding)
-    for (int i = threadIdx.x; i < kCB * nr1 * s1w; i += kThreads) {
-        const int c = i / (nr1 * s1w), rem = i - c * nr1 * s1w;
-        const int r = rem / s1w, q = rem - r * s1w - 2;
+    float *s1c = s1 + c * nr1 * s1w;
+    for (int r = 0; r < nr1; ++r) {
         const int ra = r_lo + r;
-        float v = 0.f;
-        if (ra >= 0 && ra < t1n && q >= 0 && q < f1n) {
-            const T *w = w1 + (c0 + c) * 9;
-            const float *xa = xs + (2 * ra - 2 - t_lo) * fpad + (2 * q - 2 + 2);
-            float acc = Elem<T>::to_f(b1[c0 + c]);
+        const bool row_ok = ra >= 0 && ra < t1n;
+        const float *xr = xs + (2 * ra - 2 - t_lo) * fpad;
+        for (int col = l; col < s1w; col += kLanes) {
+            const int q = col - 2;
+            float v = 0.f;
+            if (row_ok && q >= 0 && q < f1n) {
+                const float *xa = xr + 2 * q;              // input columns 2q-2 .. 2q
+                float acc = ba;
 #pragma unroll
-            for (int di = 0; di < 3; ++di)
+                for (int di = 0; di < 3; ++di)
 #pragma unroll
-                for (int dj = 0; dj < 3; ++dj)
-                    acc = fmaf(Elem<T>::to_f(w[di * 3 + dj]), xa[di * fpad + dj], acc);
-            v = fmaxf(acc, 0.f);
+                    for (int dj = 0; dj < 3; ++dj)
+                        acc = fmaf(wa[di * 3 + dj], xa[di * fpad + dj], acc);
+                v = fmaxf(acc, 0.f);
+            }
+            s1c[r * s1w + col] = v;
         }
-        s1[i] = v;
     }
+#pragma unroll
+    for (int i = 0; i < 9; ++i) wa[i] = Elem<T>::to_f(w2[(c0 + c) * 9 + i]);
+    const float bb = Elem<T>::to_f(b2[c0 + c]);
     __syncthreads();
     grid_dep_launch();
     // depthwise conv2 + bias, channels-last output rows o0 .. o1-1
     const int no = o1 - o0;
-    for (int i = threadIdx.x; i < no * f2n * kCB; i += kThreads) {
-        const int c = i % kCB, op = i / kCB;
-        const int o = op / f2n, p = op - o * f2n;
-        const T *w = w2 + (c0 + c) * 9;
-        const float *sa = s1 + (c * nr1 + 2 * o) * s1w + 2 * p;   // rows 2o..2o+2 (local), cols 2p-2..
-        float acc = Elem<T>::to_f(b2[c0 + c]);
+    T *yb = y + ((int64_t)b * (t2n - first2) + (o0 - first2)) * f2n * C + c0 + c;
+    for (int o = 0; o < no; ++o) {
+        const float *sr = s1c + 2 * o * s1w;            // stage-1 rows 2o .. 2o+2 (local)
+        for (int p = l; p < f2n; p += kLanes) {
+            const float *sa = sr + 2 * p;               // stage-1 columns 2p-2 .. 2p
+            float acc = bb;
 #pragma unroll
-        for (int di = 0; di < 3; ++di)
+            for (int di = 0; di < 3; ++di)
 #pragma unroll
-            for (int dj = 0; dj < 3; ++dj)
-                acc = fmaf(Elem<T>::to_f(w[di * 3 + dj]), sa[di * s1w + dj], acc);
-        y[(((int64_t)b * (t2n - first2) + (o0 + o - first2)) * f2n + p) * C + c0 + c] =
-            Elem<T>::from_f(acc);
+                for (int dj = 0; dj < 3; ++dj)
+                    acc = fmaf(wa[di * 3 + dj], sa[di * s1w + dj], acc);
+            yb[((int64_t)o * f2n + p) * C] = Elem<T>::from_f(acc);
+        }
     }
 }
 

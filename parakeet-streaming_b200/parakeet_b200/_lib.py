@@ -18,7 +18,7 @@ PK_OK, PK_EINVAL, PK_ECUDA, PK_ENOTSUP = 0, 1, 2, 3
 PK_DTYPE_F32, PK_DTYPE_BF16 = 0, 1
 PK_DEV_POOL_EXHAUSTED, PK_DEV_BAD_PAGE, PK_DEV_TIMEOUT, PK_DEV_BAD_SLOT = 1, 2, 4, 8
 PK_DEV_BAD_COUNT = 16
-PK_GEMM_STORE, PK_GEMM_SILU, PK_GEMM_RESIDUAL = 0, 1, 2
+PK_GEMM_STORE, PK_GEMM_SILU, PK_GEMM_RESIDUAL, PK_GEMM_RESIDUAL_RELU, PK_GEMM_BIAS = 0, 1, 2, 3, 4
 PK_FE_HIST, PK_FE_META_STRIDE, PK_FE_FIRST, PK_FE_FINAL = 512, 4, 1, 2
 META_FIRST, META_NEXT, META_WRITTEN, META_PROCESSED, META_CACHE_LEN = 0, 1, 2, 3, 4
 META_STRIDE = 8
@@ -88,13 +88,13 @@ SIGNATURES = {
     "pk_gather_windows": [_P, _I32, _I32, _P, _I32, _P, _P, _I64, _P],
     "pk_rnnt_pick": [_P, _I64, _I32, _I32, _I32, _I32, _P, _I32, _I32, _I32, _I32, _P, _P, _P, _P,
                      _P, _P],
-    "pk_lstm_cell": [_P, _I64, _P, _P, _I64, _P, _I32, _I32, _I32, _P],
+    "pk_lstm_cell": [_P, _I64, _P, _I64, _P, _P, _P, _I64, _P, _I32, _I32, _I32, _P],
     "pk_pre_encode_window": [_P, _I32, _P, _P, _I32, _I32, _I32, _I32, _I32, _P, _I32, _P, _P],
     "pk_paged_attention": [_P, _I32, _I32, _P, _I64, _I64, _I64, _P, _P, _P, _I64, _P, _P,
                            _I64, _P, _P, _I32, _P, _I64, _I64, _I64, _P],
     "pk_conv_step": [_P, _I32, _I32, _I32, _I32, _I32, _I32, _I32, _P, _I64, _I64, _P, _P, _P,
                      ctypes.c_float, _P, _P, _I32, _P, _P, _P],
-    "pk_gemm_bf16": [_P, _I64, _P, _I64, _I32, _I32, _I32, _P, _I64, _I32, _P, _I64,
+    "pk_gemm_bf16": [_P, _I64, _P, _I64, _I32, _I32, _I32, _P, _I64, _I32, _P, _I64, _P,
                      ctypes.c_float, _P, _P],
     "pk_subsample_stage12": [_P, _I64, _I64, _I64, _I32, _I32, _I32, _P, _P, _P, _P, _I32,
                              _I32, _P, _I32, _P],

@@ -7,9 +7,14 @@ prediction state into batch tensors every frame (``_stack_states``), and per
 symbol reads ``bool(blank_mask.all())`` and ``ids.tolist()`` on the host.  Here
 each slot's LSTM state lives in a pool indexed by the encoder slot id, the
 chunk's frames are one [B, T, D] tensor, and every (frame, symbol) step is
-joint GEMMs (cuBLAS) -> ``pk_rnnt_pick`` (argmax, blank mask, token lists, row
+joint GEMMs -> ``pk_rnnt_pick`` (argmax, blank mask, token lists, row
 bookkeeping) -> prediction GEMMs -> ``pk_lstm_cell`` (cell update fused with the
-keep-state-on-blank select).  Nothing is read back until the chunk's tokens are
+keep-state-on-blank select).  The first LSTM layer's input half of the gates
+(embedding x W_ih + biases) is a per-token table computed once, which the cell
+kernel adds by token id, so no embedding lookup or input GEMM runs per step.
+In bf16 the joint is two tcgen05 GEMMs: relu(enc + pred_out W_pred) in the
+first one's epilogue, the output bias in the second's (the classes padded to
+a multiple of 64 with zero rows that the argmax never reads).  Nothing is read back until the chunk's tokens are
 complete, so the whole decode of a chunk is one stream of launches (and can be
 captured in a CUDA graph).  The prediction network's output is the last LSTM
 layer's h, so no separate ``pred_out`` is kept.
@@ -20,7 +25,7 @@ import torch
 import torch.nn.functional as F
 
 from .._lib import check, lib
-from ..ops import DTYPES, _stream
+from ..ops import DTYPES, _ptr, _stream, gemm, gemm_supported
 
 
 class BatchedGreedyDecoder:
@@ -44,6 +49,18 @@ class BatchedGreedyDecoder:
         self.w_out, self.b_out = out.weight.detach(), out.bias.detach()
         self.classes = self.w_out.shape[0]
         L, H = self.layers, self.hidden
+        # first layer's input half of the gates for every token id (the blank
+        # id's embedding row is the padding row)
+        self.xtab = torch.addmm(self.b[0], self.emb, self.w_ih[0].t()).contiguous()
+        # bf16: the joint and the recurrent GEMM on the tcgen05 kernel (its K
+        # and N must be multiples of 64: joint width, hidden, 4 x hidden)
+        probe = self.w_pred.new_empty(0, H)
+        self.fast = (self.dtype == torch.bfloat16 and gemm_supported(probe, self.w_pred)
+                     and self.w_out.shape[1] % 64 == 0
+                     and gemm_supported(probe, self.w_hh[0]))
+        pad = (-self.classes) % 64
+        self.w_out_p = F.pad(self.w_out, (0, 0, 0, pad)).contiguous()
+        self.b_out_p = F.pad(self.b_out, (0, pad)).contiguous()
         self.h = torch.zeros(L, num_slots, H, device=self.device, dtype=self.dtype)
         self.c = torch.zeros_like(self.h)
         # create_sequence (model_runner.py:66-80): zero state, one step on blank
@@ -64,14 +81,20 @@ class BatchedGreedyDecoder:
     def _predict(self, ids, h, c, emit) -> None:
         """One prediction step for rows with emit != 0 (decoder.py:44-50)."""
         B, H = ids.numel(), self.hidden
-        x = F.embedding(ids, self.emb)
         dt = DTYPES[self.dtype]
+        x = None
         for k in range(self.layers):
-            gates = torch.addmm(self.b[k], x, self.w_ih[k].t())
-            gates.addmm_(h[k], self.w_hh[k].t())
-            check(lib().pk_lstm_cell(gates.data_ptr(), 4 * H, h[k].data_ptr(), c[k].data_ptr(),
-                                     H, emit.data_ptr(), B, H, dt, _stream(self.device)),
-                  "pk_lstm_cell")
+            if k == 0:   # the token's half comes from the table, in the cell kernel
+                gates = (gemm(h[0], self.w_hh[0]) if self.fast
+                         else torch.mm(h[0], self.w_hh[0].t()))
+                xtab, xld = self.xtab, 4 * H
+            else:
+                gates = torch.addmm(self.b[k], x, self.w_ih[k].t())
+                gates.addmm_(h[k], self.w_hh[k].t())
+                xtab, xld = None, 0
+            check(lib().pk_lstm_cell(gates.data_ptr(), 4 * H, _ptr(xtab), xld, ids.data_ptr(),
+                                     h[k].data_ptr(), c[k].data_ptr(), H, emit.data_ptr(), B, H,
+                                     dt, _stream(self.device)), "pk_lstm_cell")
             x = h[k]
 
     def decode(self, enc: torch.Tensor, lengths: torch.Tensor, slots: torch.Tensor):
@@ -93,11 +116,16 @@ class BatchedGreedyDecoder:
         emit = torch.empty(B, dtype=torch.int32, device=self.device)
         ids = torch.empty(B, dtype=torch.int64, device=self.device)
         dt, st = DTYPES[self.dtype], _stream(self.device)
+        ld = self.w_out_p.shape[0] if self.fast else self.classes
         for t in range(T):
             for s in range(S):
-                z = torch.addmm(encp[:, t], h[L - 1], self.w_pred.t()).relu_()
-                logits = torch.addmm(self.b_out, z, self.w_out.t())
-                check(lib().pk_rnnt_pick(logits.data_ptr(), self.classes, dt, B, self.classes,
+                if self.fast:
+                    z = gemm(h[L - 1], self.w_pred, "residual_relu", residual=encp[:, t])
+                    logits = gemm(z, self.w_out_p, "bias", bias=self.b_out_p)
+                else:
+                    z = torch.addmm(encp[:, t], h[L - 1], self.w_pred.t()).relu_()
+                    logits = torch.addmm(self.b_out, z, self.w_out.t())
+                check(lib().pk_rnnt_pick(logits.data_ptr(), ld, dt, B, self.classes,
                                          self.blank, lengths.data_ptr(), t, s, S, T,
                                          done.data_ptr(), emit.data_ptr(), ids.data_ptr(),
                                          tokens.data_ptr(), counts.data_ptr(), st), "pk_rnnt_pick")

@@ -58,7 +58,8 @@ def layer_norm(x: torch.Tensor, ln, ln2=None):
 
 
 GEMM_EPILOGUES = {"store": _lib.PK_GEMM_STORE, "silu": _lib.PK_GEMM_SILU,
-                  "residual": _lib.PK_GEMM_RESIDUAL}
+                  "residual": _lib.PK_GEMM_RESIDUAL, "residual_relu": _lib.PK_GEMM_RESIDUAL_RELU,
+                  "bias": _lib.PK_GEMM_BIAS}
 _gemm_error: dict = {}
 
 
@@ -81,24 +82,32 @@ def gemm_supported(a: torch.Tensor, weight: torch.Tensor) -> bool:
 
 
 def gemm(a: torch.Tensor, weight: torch.Tensor, epilogue: str = "store",
-         residual: torch.Tensor | None = None, alpha: float = 1.0) -> torch.Tensor:
+         residual: torch.Tensor | None = None, alpha: float = 1.0,
+         bias: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
     """epilogue(a @ weight.T) on the tcgen05 tensor cores (pk_gemm_bf16):
     "store" -> acc, "silu" -> acc * sigmoid(acc), "residual" -> residual +
-    alpha * acc.  a [..., K], weight [N, K] (an nn.Linear weight), bf16."""
+    alpha * acc, "residual_relu" -> max(residual + alpha * acc, 0), "bias" ->
+    acc + bias.  a [..., K], weight [N, K] (an nn.Linear weight), bf16;
+    ``residual`` [..., N] may have strided rows; ``out`` a contiguous [M, N]."""
     K, N = weight.shape[1], weight.shape[0]
     a2 = _rows(a, K)
     M = a2.shape[0]
-    out = torch.empty((M, N), dtype=a.dtype, device=a.device)
+    if out is None:
+        out = torch.empty((M, N), dtype=a.dtype, device=a.device)
+    elif not out.is_contiguous() or out.numel() != M * N:
+        raise ValueError("out must be a contiguous [M, N] tensor")
     r2 = None
-    if epilogue == "residual":
+    if epilogue in ("residual", "residual_relu"):
         r2 = _rows(residual, N)
+    if epilogue == "bias" and (bias is None or not bias.is_contiguous()):
+        raise ValueError("the bias epilogue needs a contiguous bias")
     err = _gemm_error.get(a.device)
     if err is None:
         err = _gemm_error[a.device] = torch.zeros(1, dtype=torch.int32, device=a.device)
     check(lib().pk_gemm_bf16(a2.data_ptr(), a2.stride(0), weight.data_ptr(), weight.stride(0), M,
                              N, K, out.data_ptr(), N, GEMM_EPILOGUES[epilogue], _ptr(r2),
-                             r2.stride(0) if r2 is not None else 0, float(alpha), err.data_ptr(),
-                             _stream(a.device)), "pk_gemm_bf16")
+                             r2.stride(0) if r2 is not None else 0, _ptr(bias), float(alpha),
+                             err.data_ptr(), _stream(a.device)), "pk_gemm_bf16")
     return out.reshape(*a.shape[:-1], N)
 
 

@@ -69,3 +69,32 @@ def test_gemm_strided_operand_and_graph():
     g.replay()
     torch.cuda.synchronize()
     check_close(out, ref)
+
+
+@pytest.mark.parametrize("M", [1, 160, 480])
+def test_gemm_residual_relu_strided_rows(M):
+    """The joint network's hidden: relu(enc[:, t] + h W_pred^T), the residual
+    rows taken from a [B, T, 640] tensor (row stride T * 640)."""
+    T, D = 14, 640
+    a, w, _ = operands(M, D, D, 5 * M)
+    g = torch.Generator(device="cuda").manual_seed(M)
+    enc = torch.randn(M, T, D, generator=g, device="cuda").to(torch.bfloat16)
+    for t in (0, 5, T - 1):
+        ref = torch.relu(enc[:, t].float() + a.float() @ w.float().t())
+        check_close(gemm(a, w, "residual_relu", residual=enc[:, t]), ref)
+
+
+@pytest.mark.parametrize("M,classes", [(160, 1026), (480, 1025)])
+def test_gemm_bias_padded_classes(M, classes):
+    """The joint output layer with its classes padded to a multiple of 64
+    (zero weight rows): the real classes equal z W_out^T + b."""
+    K = 640
+    a, w, _ = operands(M, classes, K, classes)
+    g = torch.Generator(device="cuda").manual_seed(classes)
+    b = torch.randn(classes, generator=g, device="cuda").to(torch.bfloat16)
+    pad = (-classes) % 64
+    wp = torch.nn.functional.pad(w, (0, 0, 0, pad)).contiguous()
+    bp = torch.nn.functional.pad(b, (0, pad)).contiguous()
+    out = gemm(a, wp, "bias", bias=bp)
+    ref = a.float() @ w.float().t() + b.float()
+    check_close(out[:, :classes], ref)
