@@ -508,13 +508,17 @@ def feature_step(model, steps, dev, cpu_sample=8):
     return res
 
 
-GEMM_SHAPES = {   # (name, M, N, K, epilogue): the FF GEMMs of one encoder step's layer
+GEMM_SHAPES = {   # (name, M, N, K, epilogue): the GEMMs of one encoder layer at the streaming batch
     "small": [("ff_linear1+silu", 320, 2048, 512, "silu"),
               ("ff_linear2+residual", 320, 512, 2048, "residual"),
-              ("qkv", 320, 1536, 512, "store")],
+              ("qkv", 320, 1536, 512, "store"),
+              ("out_proj+residual", 320, 512, 512, "residual"),
+              ("pointwise_conv1", 320, 1024, 512, "store")],
     "large": [("ff_linear1+silu", 6720, 4096, 1024, "silu"),
               ("ff_linear2+residual", 6720, 1024, 4096, "residual"),
-              ("qkv", 6720, 3072, 1024, "store")],
+              ("qkv", 6720, 3072, 1024, "store"),
+              ("out_proj+residual", 6720, 1024, 1024, "residual"),
+              ("pointwise_conv1", 6720, 2048, 1024, "store")],
 }
 
 

@@ -206,6 +206,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
             float v[32];
+            __syncwarp();
             tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + c * 32, v);
             if (row < M) {
                 const int col = n0 + c * 32;
