@@ -917,7 +917,9 @@ def main():
         ms = g0.elapsed_time(g1) / K
     clk = clocks.stop()
     enc_line = dec_line = pre_line = fe_line = pipe_line = gemm_line = None
-    if rank == 0 and not args.no_breakdown:
+    # the model-level lines are one GPU's measurements: run them on single-GPU
+    # runs only, so that no rank waits in a collective while rank 0 measures
+    if world == 1 and not args.no_breakdown:
         enc_line = encoder_step(args.model, 160 if args.model == "small" else 480, 20, dev)
         dec_line = rnnt_decode_step(args.model, 10, dev)
         pre_line = pre_encode_step(args.model, 10, dev)
