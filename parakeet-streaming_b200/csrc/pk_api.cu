@@ -349,6 +349,9 @@ int pk_conv_step(void *conv_state, int32_t num_slots, int32_t num_layers, int32_
     a.batch = batch;
     a.y = y;
     a.error = error;
+    const int vec = 16 / es;   // elements per 16-byte vector
+    a.x_vec = aligned16(x) && x_batch_stride % vec == 0 && x_row_stride % vec == 0 &&
+              (2 * dim) % vec == 0;
     int st = launch_conv(a, static_cast<cudaStream_t>(stream));
     if (st == PK_ENOTSUP) pk::set_error("conv configuration not handled (kernel 9, chunk <= 16)");
     return st;

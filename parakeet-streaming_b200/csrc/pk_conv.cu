@@ -74,60 +74,73 @@ __device__ __forceinline__ float sigmoid(float x) { return __fdividef(1.f, 1.f +
 
 constexpr int kCpt = 2;   // channels per thread in the conv phase
 
-// One CTA per stream.  Conv phase: kCpt channels per thread, TM >= chunk frames in
-// registers; every load that does not depend on the slot id goes out first and
-// the cache follows the slot.  LayerNorm phase: the conv outputs [chunk][D] sit
-// in shared memory and one warp per frame takes the exact two-pass mean and
-// variance, then writes the frame's normalised SiLU output with coalesced stores.
+// One CTA per stream, D / 2 threads.  The stream's GLU input rows [chunk][2D]
+// are staged in shared memory with 16-byte loads (the loads do not depend on
+// the slot, the cache load follows the slot id); each thread then takes its two
+// channels one at a time: GLU, pad mask, depthwise conv over cat(cache, x) with
+// TM >= chunk frames of history in registers, the next cache; the conv outputs
+// go to shared memory in the element type (the reference's conv output is a
+// tensor of the model dtype), and one warp per frame takes the exact two-pass
+// LayerNorm statistics and writes the frame's SiLU output with coalesced stores.
+// Keeping the inputs out of registers holds a thread to a few dozen registers,
+// so two CTAs of 512 threads share an SM at the large model's width.
 template <typename T, int K, int TM>
 __global__ void __launch_bounds__(512) conv_step_kernel(const ConvArgs a) {
     constexpr int KC = K - 1;
-    extern __shared__ float ys[];   // [chunk][D] conv outputs (LayerNorm only)
+    extern __shared__ __align__(16) char conv_smem[];
     const int b = blockIdx.x;
     const int D = a.dim, chunk = a.chunk;
-    const int c0 = threadIdx.x * kCpt;
-    const bool active = c0 < D;
+    T *xs = reinterpret_cast<T *>(conv_smem);            // [chunk][2D] GLU inputs
+    T *ys = xs + (size_t)chunk * 2 * D;                  // [chunk][D] conv outputs
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, nw = blockDim.x / 32;
 
-    // inputs that do not depend on the slot: the GLU input rows and the taps
-    float va[TM][kCpt], vg[TM][kCpt], wk[kCpt][K];
     grid_dep_wait();     // x and the cache may come from the previous kernel
-    grid_dep_launch();   // one wave: the next kernel may be scheduled (it waits for us)
+    grid_dep_launch();   // the next kernel may be scheduled (it waits for us)
     const int s = a.slots[b];
     const int n = a.lengths[b];
-    if (active) {
+    {
         const T *xb = static_cast<const T *>(a.x) + (int64_t)b * a.x_bs;
-#pragma unroll
-        for (int t = 0; t < TM; ++t) {
-            if (t >= chunk) break;
-            load2<T>(xb + (int64_t)t * a.x_rs + c0, va[t]);
-            load2<T>(xb + (int64_t)t * a.x_rs + D + c0, vg[t]);
+        constexpr int kVec = 16 / sizeof(T);
+        const int per_row = 2 * D / kVec;
+        if (a.x_vec) {
+            for (int i = threadIdx.x; i < chunk * per_row; i += blockDim.x) {
+                const int t = i / per_row, j = i - t * per_row;
+                *reinterpret_cast<uint4 *>(xs + (size_t)t * 2 * D + j * kVec) =
+                    *reinterpret_cast<const uint4 *>(xb + (int64_t)t * a.x_rs + j * kVec);
+            }
+        } else {
+            for (int i = threadIdx.x; i < chunk * 2 * D; i += blockDim.x) {
+                const int t = i / (2 * D), j = i - t * 2 * D;
+                xs[i] = xb[(int64_t)t * a.x_rs + j];
+            }
         }
-        const T *wt = static_cast<const T *>(a.w) + (int64_t)c0 * K;
-#pragma unroll
-        for (int ch = 0; ch < kCpt; ++ch)
-#pragma unroll
-            for (int k = 0; k < K; ++k) wk[ch][k] = Elem<T>::to_f(wt[ch * K + k]);
     }
     const bool slot_ok = s >= 0 && s < a.num_slots;   // block-uniform
     if (!slot_ok) {
         if (threadIdx.x == 0) raise(a.error, PK_DEV_BAD_SLOT);
         return;
     }
+    __syncthreads();
 
+    const int c0 = threadIdx.x * kCpt;
     T *yb = static_cast<T *>(a.y) + (int64_t)b * chunk * D;
-    if (active) {
+    if (c0 < D) {
         T *cache = static_cast<T *>(a.state) + (((int64_t)s * a.num_layers + a.layer) * D + c0) * KC;
-        float y[kCpt][TM];
-#pragma unroll
+        const T *wt = static_cast<const T *>(a.w) + (int64_t)c0 * K;
+#pragma unroll 1
         for (int ch = 0; ch < kCpt; ++ch) {
-            float hist[KC + TM];
+            const int c = c0 + ch;
+            float wk[K], hist[KC + TM];
+#pragma unroll
+            for (int k = 0; k < K; ++k) wk[k] = Elem<T>::to_f(wt[ch * K + k]);
             load_cache<T, KC>(cache + ch * KC, hist);
 #pragma unroll
             for (int t = 0; t < TM; ++t) {
                 if (t >= chunk) break;
                 // F.glu then masked_fill(pad_mask, 0) (convolution.py:153-155)
-                const float v = round_to(va[t][ch] * sigmoid(vg[t][ch]), static_cast<const T *>(nullptr));
+                const float va = Elem<T>::to_f(xs[(size_t)t * 2 * D + c]);
+                const float vg = Elem<T>::to_f(xs[(size_t)t * 2 * D + D + c]);
+                const float v = round_to(va * sigmoid(vg), static_cast<const T *>(nullptr));
                 hist[KC + t] = t < n ? v : 0.f;
             }
 #pragma unroll
@@ -135,8 +148,11 @@ __global__ void __launch_bounds__(512) conv_step_kernel(const ConvArgs a) {
                 if (t >= chunk) break;
                 float acc = 0.f;
 #pragma unroll
-                for (int k = 0; k < K; ++k) acc = fmaf(wk[ch][k], hist[t + k], acc);
-                y[ch][t] = acc;
+                for (int k = 0; k < K; ++k) acc = fmaf(wk[k], hist[t + k], acc);
+                if (a.ln_w)
+                    ys[(size_t)t * D + c] = Elem<T>::from_f(acc);
+                else
+                    yb[(int64_t)t * D + c] = Elem<T>::from_f(acc);
             }
             // next cache: the last K-1 entries of cat(cache, x)
             float nc[KC];
@@ -150,16 +166,6 @@ __global__ void __launch_bounds__(512) conv_step_kernel(const ConvArgs a) {
             }
             store_cache<T, KC>(cache + ch * KC, nc);
         }
-#pragma unroll
-        for (int t = 0; t < TM; ++t) {
-            if (t >= chunk) break;
-            if (a.ln_w) {
-                *reinterpret_cast<float2 *>(ys + t * D + c0) = make_float2(y[0][t], y[1][t]);
-            } else {
-                const float o[kCpt] = {y[0][t], y[1][t]};
-                store2<T>(yb + (int64_t)t * D + c0, o);
-            }
-        }
     }
     if (!a.ln_w) return;
     __syncthreads();
@@ -167,30 +173,32 @@ __global__ void __launch_bounds__(512) conv_step_kernel(const ConvArgs a) {
     // LayerNorm over channels (the module's "batch_norm", convolution.py:138,157), then SiLU
     const T *lw = static_cast<const T *>(a.ln_w), *lb = static_cast<const T *>(a.ln_b);
     for (int t = warp; t < chunk; t += nw) {
-        const float *row = ys + t * D;
+        const T *row = ys + (size_t)t * D;
         float sum = 0.f;
         for (int c = 2 * lane; c < D; c += 64) {
-            const float2 v = *reinterpret_cast<const float2 *>(row + c);
-            sum += v.x + v.y;
+            float v[2];
+            load2<T>(row + c, v);
+            sum += v[0] + v[1];
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
         const float mean = sum / D;
         float sq = 0.f;
         for (int c = 2 * lane; c < D; c += 64) {
-            const float2 v = *reinterpret_cast<const float2 *>(row + c);
-            sq += (v.x - mean) * (v.x - mean) + (v.y - mean) * (v.y - mean);
+            float v[2];
+            load2<T>(row + c, v);
+            sq += (v[0] - mean) * (v[0] - mean) + (v[1] - mean) * (v[1] - mean);
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
         const float inv = rsqrtf(sq / D + a.eps);
         for (int c = 2 * lane; c < D; c += 64) {
-            const float2 v = *reinterpret_cast<const float2 *>(row + c);
-            float gw[2], gb[2];
+            float v[2], gw[2], gb[2];
+            load2<T>(row + c, v);
             load2<T>(lw + c, gw);
             load2<T>(lb + c, gb);
-            const float z0 = (v.x - mean) * inv * gw[0] + gb[0];
-            const float z1 = (v.y - mean) * inv * gw[1] + gb[1];
+            const float z0 = (v[0] - mean) * inv * gw[0] + gb[0];
+            const float z1 = (v[1] - mean) * inv * gw[1] + gb[1];
             const float o[2] = {z0 * sigmoid(z0), z1 * sigmoid(z1)};
             store2<T>(yb + (int64_t)t * D + c, o);
         }
@@ -209,8 +217,9 @@ int launch_conv(const ConvArgs &a, cudaStream_t s) {
         using T = decltype(tag);
         auto kernel = tm == 2 ? conv_step_kernel<T, 9, 2> : tm == 4 ? conv_step_kernel<T, 9, 4>
                     : tm == 8 ? conv_step_kernel<T, 9, 8> : conv_step_kernel<T, 9, 16>;
-        const size_t smem = a.ln_w ? (size_t)a.chunk * a.dim * sizeof(float) : 0;
-        if (smem > 48 * 1024) {   // at most 64 KB: chunk <= 16, dim <= 1024
+        // GLU inputs [chunk][2D] and conv outputs [chunk][D] in the element type
+        const size_t smem = (size_t)a.chunk * 3 * a.dim * sizeof(T);
+        if (smem > 48 * 1024) {   // at most 96 KB in bf16: chunk <= 16, dim <= 1024
             const cudaError_t e = cudaFuncSetAttribute(
                 kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
             if (e != cudaSuccess) return e;

@@ -99,6 +99,7 @@ struct ConvArgs {
     int batch;
     void *y;
     int32_t *error;
+    int x_vec;   // x rows 16-byte aligned (base, row and batch strides): vector staging
 };
 int launch_conv(const ConvArgs &a, cudaStream_t s);
 
