@@ -66,6 +66,11 @@ __device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint6
         : "memory");
 }
 
+__device__ __forceinline__ void mbar_arrive_cta(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
 // arrive on `bar` when every tcgen05.mma issued so far by this thread is done
 __device__ __forceinline__ void umma_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -256,6 +261,225 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// apply the epilogue to 32 accumulator columns of one row and store them as bf16
+template <int EPI>
+__device__ __forceinline__ void epilogue_store(float (&v)[32], int row, int col, __nv_bfloat16 *C,
+                                               int64_t ldc, const __nv_bfloat16 *R, int64_t ldr,
+                                               const __nv_bfloat16 *bias, float alpha) {
+    if (EPI == PK_GEMM_SILU) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __fdividef(v[i], 1.f + __expf(-v[i]));
+    } else if (EPI == PK_GEMM_RESIDUAL || EPI == PK_GEMM_RESIDUAL_RELU) {
+        const uint4 *rp = reinterpret_cast<const uint4 *>(R + (int64_t)row * ldr + col);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            float f[8];
+            unpack16(rp[q], f, R);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float t = f[i] + alpha * v[q * 8 + i];
+                v[q * 8 + i] = EPI == PK_GEMM_RESIDUAL_RELU ? fmaxf(t, 0.f) : t;
+            }
+        }
+    } else if (EPI == PK_GEMM_BIAS) {
+        const uint4 *bp = reinterpret_cast<const uint4 *>(bias + col);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            float f[8];
+            unpack16(bp[q], f, bias);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[q * 8 + i] += f[i];
+        }
+    }
+    uint4 *cp = reinterpret_cast<uint4 *>(C + (int64_t)row * ldc + col);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        uint4 o;
+        __nv_bfloat162 *h = reinterpret_cast<__nv_bfloat162 *>(&o);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            h[i] = __floats2bfloat162_rn(v[q * 8 + 2 * i], v[q * 8 + 2 * i + 1]);
+        cp[q] = o;
+    }
+}
+
+// Persistent form for many tiles: one CTA per SM walks tiles t = blockIdx.x +
+// k * gridDim.x (row tiles fastest, so the CTAs at work share a weight tile in
+// L2).  Warp 0 lane 0 streams K blocks through the stage ring across tiles,
+// warp 1 lane 0 issues the MMAs into one of two TMEM accumulators (2 x BN
+// columns), and warps 2-5 drain the other accumulator through the epilogue, so
+// a tile's epilogue runs under the next tile's mainloop.  tmem_full[a] (MMA ->
+// epilogue, by tcgen05.commit) and tmem_empty[a] (4 epilogue warps -> MMA)
+// hand the accumulators over.  Warp w of the epilogue reads TMEM lanes
+// 32 * (w % 4) .. + 31.
+constexpr int kPThreads = 192;
+
+template <int BN, int NS, int EPI>
+__global__ void __launch_bounds__(kPThreads, 1)
+    gemm_bf16_persistent_kernel(const __grid_constant__ CUtensorMap tm_a,
+                                const __grid_constant__ CUtensorMap tm_w, int M, int N, int K,
+                                __nv_bfloat16 *C, int64_t ldc, const __nv_bfloat16 *R, int64_t ldr,
+                                const __nv_bfloat16 *bias, float alpha, int32_t *error) {
+    constexpr int kBBytes = BN * kBK * 2;
+    extern __shared__ uint8_t gemm_smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(gemm_smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *sA = smem, *sB = smem + NS * kABytes;
+    __shared__ __align__(8) uint64_t full[NS], empty[NS], tmem_full[2], tmem_empty[2];
+    __shared__ uint32_t tmem_base;
+    __shared__ volatile int failed;
+
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int mtiles = (M + kBM - 1) / kBM, tiles = mtiles * (N / BN), nk = K / kBK;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tmem_full[a], 1);
+            mbar_init(&tmem_empty[a], 4);
+        }
+        failed = 0;
+        fence_mbar_init();
+        prefetch_tmap(&tm_a);
+        prefetch_tmap(&tm_w);
+    }
+    if (warp == 0) {
+        tmem_alloc(&tmem_base, 2 * BN);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // producer: K blocks of every tile of this CTA through the ring
+            grid_dep_wait();
+            int g = 0;
+            for (int tile = blockIdx.x; tile < tiles && !failed; tile += gridDim.x) {
+                const int m0 = (tile % mtiles) * kBM, n0 = (tile / mtiles) * BN;
+                for (int kb = 0; kb < nk; ++kb, ++g) {
+                    const int s = g % NS, u = g / NS;
+                    if (u >= 1 && !mbar_wait_bounded(&empty[s], (u - 1) & 1, kWaitLimitNs)) {
+                        raise(error, PK_DEV_TIMEOUT);
+                        failed = 1;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&full[s], kABytes + kBBytes);
+                    tma_load_2d(sB + s * kBBytes, &tm_w, &full[s], kb * kBK, n0);
+                    tma_load_2d(sA + s * kABytes, &tm_a, &full[s], kb * kBK, m0);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // MMA issuer: accumulator t & 1 for the CTA's t-th tile
+            constexpr uint32_t idesc = idesc_bf16(kBM, BN);
+            int g = 0, t = 0;
+            for (int tile = blockIdx.x; tile < tiles && !failed; tile += gridDim.x, ++t) {
+                const int acc = t & 1, use = t >> 1;
+                if (use >= 1 && !mbar_wait_bounded(&tmem_empty[acc], (use - 1) & 1, kWaitLimitNs)) {
+                    raise(error, PK_DEV_TIMEOUT);
+                    failed = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem + acc * BN;
+                for (int kb = 0; kb < nk; ++kb, ++g) {
+                    const int s = g % NS;
+                    if (!mbar_wait_bounded(&full[s], (g / NS) & 1, kWaitLimitNs)) {
+                        raise(error, PK_DEV_TIMEOUT);
+                        failed = 1;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(sA + s * kABytes), b0 = smem_u32(sB + s * kBBytes);
+#pragma unroll
+                    for (int kk = 0; kk < kBK / 16; ++kk)
+                        umma_bf16(d, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32), idesc,
+                                  (kb | kk) != 0);
+                    umma_commit(&empty[s]);
+                }
+                umma_commit(&tmem_full[acc]);
+            }
+        }
+    } else {
+        // epilogue warps 2..5
+        grid_dep_wait();   // the residual rows may come from the previous kernel
+        const int q = warp & 3;
+        int t = 0;
+        for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
+            const int acc = t & 1, use = t >> 1;
+            const bool ok = __all_sync(0xffffffffu,
+                                       mbar_wait_bounded(&tmem_full[acc], use & 1, kWaitLimitNs));
+            if (!ok) {
+                if (lane == 0) raise(error, PK_DEV_TIMEOUT);
+                failed = 1;
+                break;
+            }
+            tc_fence_after();
+            if (tile + (int)gridDim.x >= tiles) grid_dep_launch();
+            const int m0 = (tile % mtiles) * kBM, n0 = (tile / mtiles) * BN;
+            const int row = m0 + q * 32 + lane;
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                float v[32];
+                __syncwarp();
+                tmem_ld32(tmem + acc * BN + ((uint32_t)(q * 32) << 16) + c * 32, v);
+                if (row < M) epilogue_store<EPI>(v, row, n0 + c * 32, C, ldc, R, ldr, bias, alpha);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cta(&tmem_empty[acc]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 2 * BN);
+    }
+}
+
+template <int BN, int NS, int EPI>
+int launch_gemm_persistent_t(const GemmArgs &g, const CUtensorMap &ta, const CUtensorMap &tw,
+                             int num_sms, cudaStream_t s) {
+    auto k = gemm_bf16_persistent_kernel<BN, NS, EPI>;
+    const size_t smem = (size_t)NS * (kABytes + BN * kBK * 2) + 1024;
+    static bool attr = false;
+    if (!attr) {
+        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(gemm persistent)");
+        attr = true;
+    }
+    const int tiles = ((g.M + kBM - 1) / kBM) * (g.N / BN);
+    const dim3 grid(tiles < num_sms ? tiles : num_sms);
+    cudaError_t e = launch_pdl(k, grid, dim3(kPThreads), smem, s, ta, tw, g.M, g.N, g.K,
+                               static_cast<__nv_bfloat16 *>(g.C), g.ldc,
+                               static_cast<const __nv_bfloat16 *>(g.R), g.ldr,
+                               static_cast<const __nv_bfloat16 *>(g.bias), g.alpha, g.error);
+    return cuda_status(e, "gemm_bf16_persistent_kernel");
+}
+
+template <int BN, int NS>
+int launch_gemm_persistent(const GemmArgs &g, const CUtensorMap &ta, const CUtensorMap &tw,
+                           int num_sms, cudaStream_t s) {
+    switch (g.epilogue) {
+        case PK_GEMM_SILU:
+            return launch_gemm_persistent_t<BN, NS, PK_GEMM_SILU>(g, ta, tw, num_sms, s);
+        case PK_GEMM_RESIDUAL:
+            return launch_gemm_persistent_t<BN, NS, PK_GEMM_RESIDUAL>(g, ta, tw, num_sms, s);
+        case PK_GEMM_RESIDUAL_RELU:
+            return launch_gemm_persistent_t<BN, NS, PK_GEMM_RESIDUAL_RELU>(g, ta, tw, num_sms, s);
+        case PK_GEMM_BIAS:
+            return launch_gemm_persistent_t<BN, NS, PK_GEMM_BIAS>(g, ta, tw, num_sms, s);
+        default: return launch_gemm_persistent_t<BN, NS, PK_GEMM_STORE>(g, ta, tw, num_sms, s);
+    }
+}
+
 template <int BN, int NS, int EPI>
 int launch_gemm_t(const GemmArgs &g, const CUtensorMap &ta, const CUtensorMap &tw,
                   cudaStream_t s) {
@@ -292,11 +516,25 @@ int launch_gemm_epi(const GemmArgs &g, const CUtensorMap &ta, const CUtensorMap 
 
 int launch_gemm(const GemmArgs &g, cudaStream_t s) {
     if (g.M == 0) return PK_OK;
+    static int num_sms = 0;
+    if (num_sms == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+            num_sms = 148;
+    }
     // N tile: narrow tiles when there are few row tiles (more CTAs for the
-    // weight stream), wide ones otherwise
+    // weight stream), wide ones otherwise; with more 256-wide tiles than two
+    // waves the persistent kernel takes over
     const int mtiles = (g.M + kBM - 1) / kBM;
     int bn = mtiles * (g.N / 256) >= 148 && g.N % 256 == 0 ? 256
              : (mtiles * (g.N / 128) >= 148 && g.N % 128 == 0 ? 128 : 64);
+    // persistent when the tiles make more than two waves: 256-wide, or 128-wide
+    // when the 256-wide tiling is too short (an N = 1024 output)
+    int pbn = 0;
+    if (g.N % 256 == 0 && mtiles * (g.N / 256) >= 2 * num_sms) pbn = 256;
+    else if (g.N % 128 == 0 && mtiles * (g.N / 128) >= 2 * num_sms) pbn = 128;
+    if (pbn) bn = pbn;
     CUtensorMap ta, tw;
     const uint64_t adims[2] = {(uint64_t)g.K, (uint64_t)g.M}, astr[1] = {(uint64_t)g.lda * 2};
     const uint64_t wdims[2] = {(uint64_t)g.K, (uint64_t)g.N}, wstr[1] = {(uint64_t)g.ldw * 2};
@@ -305,6 +543,8 @@ int launch_gemm(const GemmArgs &g, cudaStream_t s) {
     if (st != PK_OK) return st;
     st = encode_tmap(&tw, PK_DTYPE_BF16, g.W, 2, wdims, wstr, wbox);
     if (st != PK_OK) return st;
+    if (pbn == 256) return launch_gemm_persistent<256, 4>(g, ta, tw, num_sms, s);
+    if (pbn == 128) return launch_gemm_persistent<128, 6>(g, ta, tw, num_sms, s);
     switch (bn) {
         case 256: return launch_gemm_epi<256, 3>(g, ta, tw, s);
         case 128: return launch_gemm_epi<128, 4>(g, ta, tw, s);

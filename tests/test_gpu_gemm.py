@@ -1,4 +1,6 @@
-"""pk_gemm_bf16 (tcgen05 tensor cores, TMEM accumulator; through the C ABI)
+"""pk_gemm_bf16 (tcgen05 tensor cores, TMEM accumulator; through the C ABI;
+the persistent two-accumulator form takes the shapes with more than two waves
+of 128 x 256 tiles)
 against an fp32 matmul of the same bf16 operands: the output is the fp32
 result rounded once to bf16, so each element is within 2^-8 relative (plus
 the accumulation-order difference, far below that) of the reference."""
@@ -28,7 +30,8 @@ def check_close(out, ref):
 
 @pytest.mark.parametrize("M,N,K", [(1, 64, 64), (7, 512, 512), (128, 128, 64), (320, 2048, 512),
                                    (320, 512, 2048), (320, 1536, 512), (1000, 1024, 1024),
-                                   (6720, 4096, 1024), (6720, 1024, 4096)])
+                                   (6720, 4096, 1024), (6720, 1024, 4096), (6720, 3072, 1024),
+                                   (6720, 2048, 1024), (6700, 2048, 128)])
 def test_gemm_store(M, N, K):
     a, w, _ = operands(M, N, K, M + N + K)
     ref = a.float() @ w.float().t()
@@ -43,7 +46,8 @@ def test_gemm_silu(M, N, K):
     check_close(gemm(a, w, "silu"), acc * torch.sigmoid(acc))
 
 
-@pytest.mark.parametrize("M,N,K", [(320, 512, 2048), (6720, 1024, 4096), (5, 64, 64)])
+@pytest.mark.parametrize("M,N,K", [(320, 512, 2048), (6720, 1024, 4096), (5, 64, 64),
+                                   (6720, 3072, 1024)])
 def test_gemm_residual(M, N, K):
     a, w, r = operands(M, N, K, 3 * M + K)
     ref = r.float() + 0.5 * (a.float() @ w.float().t())
