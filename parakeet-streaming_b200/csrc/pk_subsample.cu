@@ -29,6 +29,87 @@ constexpr int kThreads = 256;
 
 __host__ __device__ constexpr int conv_out(int n) { return n / 2 + 1; }   // (n + 3 - 3) / 2 + 1
 
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&v);
+}
+
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, "
+        "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// conv1 of a bf16 model on the tensor cores: an im2col product per block of 16
+// stage-1 positions (rows of A: positions (r, q) in row-major order; columns:
+// the 9 taps, padded to 16 with zeros) and the block's 16 channels (two n8
+// tiles of B = the taps of each channel).  Inputs and taps are bf16 values, so
+// the products are exact and only the fp32 accumulation order differs from a
+// direct convolution.  Writes ReLU(acc + bias) for positions inside the
+// stage-1 grid and 0 elsewhere (rows outside it, the padding columns).
+__device__ __forceinline__ void conv1_tensor_core(const float *xs, int fpad,
+                                                  const __nv_bfloat16 *w1, const __nv_bfloat16 *b1,
+                                                  int t_lo, int r_lo, int nr1, int t1n, int f1n,
+                                                  float *s1, int s1w) {
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int gq = lane / 4, tq = lane % 4;
+    // B: (tap k, channel n) = w1[n][k]; b0 holds taps 2tq, 2tq+1, b1 taps 2tq+8, 2tq+9
+    auto tap = [&](int n, int k) { return k < 9 ? __bfloat162float(w1[n * 9 + k]) : 0.f; };
+    uint32_t bw[2][2];
+    float bias[2][2];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+        const int n = nt * 8 + gq;
+        bw[nt][0] = pack_bf16(tap(n, 2 * tq), tap(n, 2 * tq + 1));
+        bw[nt][1] = pack_bf16(tap(n, 2 * tq + 8), tap(n, 2 * tq + 9));
+        bias[nt][0] = __bfloat162float(b1[nt * 8 + 2 * tq]);
+        bias[nt][1] = __bfloat162float(b1[nt * 8 + 2 * tq + 1]);
+    }
+    const int npos = nr1 * f1n, ntiles = (npos + 15) / 16;
+    for (int mt = warp; mt < ntiles; mt += kThreads / 32) {
+        uint32_t a[4];
+        int pr[2], pq[2];
+        bool ok[2];
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+            const int p = mt * 16 + gq + 8 * half;
+            const int pp = p < npos ? p : 0;
+            const int r = pp / f1n, q = pp - r * f1n;
+            const int ra = r_lo + r;
+            pr[half] = r;
+            pq[half] = q;
+            ok[half] = p < npos && ra >= 0 && ra < t1n;
+            const float *xb = xs + (2 * ra - 2 - t_lo) * fpad + 2 * q;   // input columns 2q-2 ..
+            auto x = [&](int k) { return k < 9 ? xb[(k / 3) * fpad + k % 3] : 0.f; };
+            a[half] = pack_bf16(x(2 * tq), x(2 * tq + 1));
+            a[2 + half] = pack_bf16(x(2 * tq + 8), x(2 * tq + 9));
+        }
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+            float c[4] = {0.f, 0.f, 0.f, 0.f};
+            mma16816(c, a, bw[nt][0], bw[nt][1]);
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                if (mt * 16 + gq + 8 * half >= npos) continue;
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const int ch = nt * 8 + 2 * tq + e;
+                    const float v = ok[half] ? fmaxf(c[2 * half + e] + bias[nt][e], 0.f) : 0.f;
+                    s1[(ch * nr1 + pr[half]) * s1w + pq[half] + 2] = v;
+                }
+            }
+        }
+    }
+    // the padding columns q = -2, -1 and f1n of every row and channel
+    for (int i = threadIdx.x; i < kCB * nr1 * 3; i += kThreads) {
+        const int rc = i / 3, k = i - rc * 3;
+        s1[rc * s1w + (k < 2 ? k : s1w - 1)] = 0.f;
+    }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads)
     subsample_stage12_kernel(const T *x, int64_t xb, int64_t xf, int64_t xt, int frames, int feat,
@@ -65,11 +146,14 @@ __global__ void __launch_bounds__(kThreads)
     constexpr int kLanes = kThreads / kCB;
     const int c = threadIdx.x % kCB, l = threadIdx.x / kCB;
     float wa[9];
+    float *s1c = s1 + c * nr1 * s1w;
+    if constexpr (sizeof(T) == 2) {
+        conv1_tensor_core(xs, fpad, w1 + c0 * 9, b1 + c0, t_lo, r_lo, nr1, t1n, f1n, s1, s1w);
+    } else {
 #pragma unroll
     for (int i = 0; i < 9; ++i) wa[i] = Elem<T>::to_f(w1[(c0 + c) * 9 + i]);
     const float ba = Elem<T>::to_f(b1[c0 + c]);
     // conv1 + bias + ReLU, zero outside the stage-1 grid (the next conv's padding)
-    float *s1c = s1 + c * nr1 * s1w;
     for (int r = 0; r < nr1; ++r) {
         const int ra = r_lo + r;
         const bool row_ok = ra >= 0 && ra < t1n;
@@ -89,6 +173,7 @@ __global__ void __launch_bounds__(kThreads)
             }
             s1c[r * s1w + col] = v;
         }
+    }
     }
 #pragma unroll
     for (int i = 0; i < 9; ++i) wa[i] = Elem<T>::to_f(w2[(c0 + c) * 9 + i]);
