@@ -729,6 +729,23 @@ def streaming_step(model, steps, dev, profile=False):
         except Exception as e:   # informative; keep the run going
             out["graph_error"] = str(e)[:200]
         out["tokens_per_frame"] = round(float(cnt.float().mean()), 2)
+        try:   # chunk k's decode on a second stream under chunk k+1's encoder
+            from parakeet_b200.engine import OverlappedStreamingRunner
+            runner = OverlappedStreamingRunner(pipe, slots, n)
+            for _ in range(3):
+                runner.step(nxt)
+            runner.drain()
+            torch.cuda.synchronize()
+            a.record()
+            for _ in range(steps):
+                runner.step(nxt)
+            runner.drain()
+            b.record()
+            torch.cuda.synchronize()
+            out["ms_per_step_overlapped"] = round(a.elapsed_time(b) / steps, 4)
+            del runner
+        except Exception as e:   # informative; keep the run going
+            out["overlap_error"] = str(e)[:200]
         try:
             out["stage_ms_graph"] = stage_times(pipe, nxt, slots, steps)
         except Exception as e:   # informative; keep the run going

@@ -79,6 +79,13 @@ class StreamingPipeline:
         holds; default the engine's first chunk, (1 + 8 * lookahead) hops).
         Returns tokens int32 [B, T, max_symbols] (-1 = none) and counts int32
         [B, T]."""
+        y, lengths = self.encode_audio(samples, slots, push, first_samples)
+        return self.dec.decode(y, lengths, slots)
+
+    def encode_audio(self, samples: torch.Tensor, slots: torch.Tensor, push: int,
+                     first_samples: int | None = None):
+        """The features, pre-encode and encoder half of ``step_audio``:
+        returns the encoder output [B, T, D] and the frame counts int32 [B]."""
         B, n = samples.shape
         first = push == 0
         F = self.frames_per_push(n, first)
@@ -100,7 +107,7 @@ class StreamingPipeline:
             self._fe_bufs[key] = bufs
         ns, flags, feats, nframes = bufs
         self.fe.launch(samples, ns, flags, slots, feats, F, nframes)
-        return self.step(feats, slots, first, prefix=prefix)
+        return self.encode(feats, slots, first, prefix=prefix)
 
     def end_streams(self, slots) -> None:
         """Finished streams: their pages return to the pool at the next step."""
@@ -114,12 +121,90 @@ class StreamingPipeline:
         the cached feature frames to prepend (BatchedPreEncoder.pre_encode).
         Returns tokens int32 [B, T, max_symbols] (-1 = none) and counts int32
         [B, T]."""
+        y, lengths = self.encode(feats, slots, first, prefix)
+        return self.dec.decode(y, lengths, slots)
+
+    def encode(self, feats: torch.Tensor, slots: torch.Tensor, first: bool,
+               prefix: int | None = None):
+        """Pre-encode and encoder half of ``step``: the encoder output [B, T, D]
+        and the frame counts int32 [B]."""
         x = self.pre.pre_encode(feats, slots, first, prefix)         # [B, T, D]
         state = StreamingState(PagedModelCache(self.pool, slots))
         y, _ = self.encoder(x, state, bypass_pre_encode=True)        # [B, D, T]
         B, T = x.shape[:2]
         lengths = torch.full((B,), T, dtype=torch.int32, device=self.device)
-        return self.dec.decode(y.transpose(1, 2), lengths, slots)
+        return y.transpose(1, 2), lengths
 
 
-__all__ = ["StreamingPipeline"]
+class OverlappedStreamingRunner:
+    """Steady-state audio steps (push index 2 on) of one batch of streams, with
+    chunk k's greedy decode on a second stream running under chunk k+1's
+    features, pre-encode and encoder - the reference engine's separate encode
+    and decode loops (parakeet/engine/model_runner.py:150-171) as two streams
+    of CUDA graphs.  Two sets of graphs and buffers alternate (step k uses set
+    k % 2); step k's encoder graph waits for step k-2's decode, the only one
+    that read that set's encoder output.  Call after the pipeline has run at
+    least one steady step eagerly for this batch (the capture needs its
+    workspaces); ``slots`` and the batch stay fixed."""
+
+    def __init__(self, pipe: StreamingPipeline, slots: torch.Tensor, samples_per_chunk: int):
+        dev = pipe.device
+        B = int(slots.numel())
+        self.pipe, self.slots, self.device = pipe, slots, dev
+        self.audio = [torch.zeros(B, samples_per_chunk, dtype=torch.float32, device=dev)
+                      for _ in range(2)]
+        self.dec_stream = torch.cuda.Stream(dev)
+        self.enc_done = [torch.cuda.Event() for _ in range(2)]
+        self.dec_done = [torch.cuda.Event() for _ in range(2)]
+        self.g_enc, self.g_dec, self.out, self._y = [], [], [], []
+        self.k = 0
+        # The two sides are captured on different streams: library handles
+        # that keep a workspace per stream (cuBLAS) then bake different
+        # workspaces into the encoder and the decode graphs, which run at once.
+        cap_e, cap_d = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        for cap in (cap_e, cap_d):
+            cap.wait_stream(torch.cuda.current_stream(dev))
+        for j in range(2):
+            ge, gd = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+            with torch.cuda.graph(ge, stream=cap_e):
+                y, lengths = pipe.encode_audio(self.audio[j], slots, 2)
+            cap_d.wait_stream(cap_e)
+            with torch.cuda.graph(gd, stream=cap_d):
+                tokens, counts = pipe.dec.decode(y, lengths, slots)
+            self.g_enc.append(ge)
+            self.g_dec.append(gd)
+            self._y.append((y, lengths))
+            self.out.append((tokens, counts))
+        for cap in (cap_e, cap_d):
+            torch.cuda.current_stream(dev).wait_stream(cap)
+
+    def step(self, samples: torch.Tensor | None = None):
+        """One steady step: copies ``samples`` (float32 [B, n], host or device)
+        into this step's input set, launches its encoder side on the current
+        stream and its decode on the decode stream.  Returns (tokens, counts,
+        event): the tensors are final once ``event`` has completed and stay so
+        until the call after next."""
+        j = self.k % 2
+        main = torch.cuda.current_stream(self.device)
+        if self.k >= 2:
+            main.wait_event(self.dec_done[j])
+        if samples is not None:
+            self.audio[j].copy_(samples, non_blocking=True)
+        self.g_enc[j].replay()
+        self.enc_done[j].record(main)
+        self.dec_stream.wait_event(self.enc_done[j])
+        with torch.cuda.stream(self.dec_stream):
+            self.g_dec[j].replay()
+        self.dec_done[j].record(self.dec_stream)
+        self.k += 1
+        tokens, counts = self.out[j]
+        return tokens, counts, self.dec_done[j]
+
+    def drain(self) -> None:
+        """Make the current stream wait for every launched decode."""
+        main = torch.cuda.current_stream(self.device)
+        for e in self.dec_done:
+            main.wait_event(e)
+
+
+__all__ = ["StreamingPipeline", "OverlappedStreamingRunner"]

@@ -4,12 +4,13 @@ stepping it alone (slot isolation of the three per-slot states: mel cache,
 K/V pages + conv cache, prediction state), in fp32, over a first chunk and
 later chunks; and one steady-state step replays as a CUDA graph with the same
 result.  The same for the audio -> tokens step (sample history as a fourth
-per-slot state)."""
+per-slot state), and for the overlapped runner that decodes chunk k on a second
+stream under chunk k+1's encoder."""
 import numpy as np
 import pytest
 import torch
 
-from parakeet_b200.engine import StreamingPipeline
+from parakeet_b200.engine import OverlappedStreamingRunner, StreamingPipeline
 from parakeet_b200.modules import ConformerEncoder, ConvSubsampling, Joiner, Predictor
 from parakeet_b200.weights import (random_decoder_state_dict, random_encoder_layers,
                                    random_pre_encode_state_dict)
@@ -175,3 +176,39 @@ def test_audio_steady_step_replays_as_cuda_graph():
     g.replay()
     torch.cuda.synchronize()
     assert torch.equal(tok, want[0]) and torch.equal(cnt, want[1])
+
+
+def test_overlapped_runner_equals_sequential_steps():
+    """OverlappedStreamingRunner: chunk k's decode on the decode stream under
+    chunk k+1's features + encoder gives every chunk the tokens of plain
+    sequential step_audio calls; outputs of step k are read only after its
+    event, and before the step two calls later reuses its buffers."""
+    pipe, ref_pipe = make(3), make(3)
+    slots_l = [2, 0, 1]
+    pipe.start_streams(slots_l)
+    ref_pipe.start_streams(slots_l)
+    slots = torch.tensor(slots_l, dtype=torch.int32, device="cuda")
+    n = 7
+    xs = [torch.cat([audio(p, i) for i in range(3)]).cuda() for p in range(2 + n)]
+    with torch.inference_mode():
+        for push in range(2):
+            pipe.step_audio(xs[push], slots, push)
+            ref_pipe.step_audio(xs[push], slots, push)
+        want = [ref_pipe.step_audio(xs[2 + k], slots, 2) for k in range(n)]
+        want = [(t.clone(), c.clone()) for t, c in want]
+        runner = OverlappedStreamingRunner(pipe, slots, SMALL_NEXT)
+        main = torch.cuda.current_stream()
+        got, prev = [], None
+        for k in range(n):
+            cur = runner.step(xs[2 + k])
+            if prev is not None:
+                main.wait_event(prev[2])
+                got.append((prev[0].clone(), prev[1].clone()))
+            prev = cur
+        runner.drain()
+        got.append((prev[0].clone(), prev[1].clone()))
+        torch.cuda.synchronize()
+    for k in range(n):
+        assert torch.equal(got[k][0], want[k][0]) and torch.equal(got[k][1], want[k][1]), k
+    assert sum(int(c.sum()) for _, c in want) > 0
+    assert pipe.pool.read_error() == 0 and pipe.fe.error_bits() == 0
