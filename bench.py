@@ -65,6 +65,8 @@ def parse():
     ap.add_argument("--streams", type=int, default=80)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-breakdown", action="store_true")
+    ap.add_argument("--no-serve", action="store_true",
+                    help="skip the paced serving search (streams at p99 <= 160 ms)")
     ap.add_argument("--no-graph", action="store_true", help="time eager launches only")
     ap.add_argument("--profile", action="store_true",
                     help="prefill + warmup + --steps steps only (for ncu), no report")
@@ -653,14 +655,9 @@ def stage_times(pipe, samples, slots, reps):
     return res
 
 
-def streaming_step(model, steps, dev, profile=False):
-    """Audio -> tokens for every stream of configs[2] (small, 160 streams) or
-    configs[3] on one GPU (large, 480 streams): batched log-mel features ->
-    batched pre-encode -> paged encoder -> batched greedy decode
-    (engine.pipeline.StreamingPipeline.step_audio), random bf16 weights,
-    synthetic audio of configs[2], as one CUDA graph per steady-state step.
-    Streams that one GPU sustains in real time at this batch = batch x audio
-    per step / step time."""
+def build_streaming_pipeline(model, dev, num_slots, feature_kw=None):
+    """StreamingPipeline of configs[2] (small) / configs[3] (large) with random
+    bf16 weights over ``num_slots`` stream slots."""
     import torch
 
     from parakeet_b200.engine import StreamingPipeline
@@ -669,7 +666,7 @@ def streaming_step(model, steps, dev, profile=False):
                                        random_pre_encode_state_dict)
     c, d = SHAPES[model], DECODE_CFG[model]
     L, D, H, att = c["layers"], c["dim"], c["heads"], c["att"]
-    la, B, V = att[1], d["streams"], d["vocab"]
+    V = d["vocab"]
     enc = ConformerEncoder(feat_in=128, hidden_size=D, ff_expansion_factor=4, num_layers=L,
                            num_heads=H, subsampling_factor=8, pos_emb_max_len=5000,
                            conv_kernel_size=9, att_context_size=att, subsampling_conv_channels=256,
@@ -685,7 +682,22 @@ def streaming_step(model, steps, dev, profile=False):
     join.load_state_dict({k[7:]: torch.from_numpy(v) for k, v in sd.items()
                           if k.startswith("joiner.")})
     mods = [m.to(dev, torch.bfloat16).eval() for m in (enc, pre, pred, join)]
-    pipe = StreamingPipeline(*mods, blank_id=V, num_slots=B)
+    return StreamingPipeline(*mods, blank_id=V, num_slots=num_slots, feature_kw=feature_kw)
+
+
+def streaming_step(model, steps, dev, profile=False):
+    """Audio -> tokens for every stream of configs[2] (small, 160 streams) or
+    configs[3] on one GPU (large, 480 streams): batched log-mel features ->
+    batched pre-encode -> paged encoder -> batched greedy decode
+    (engine.pipeline.StreamingPipeline.step_audio), random bf16 weights,
+    synthetic audio of configs[2], as one CUDA graph per steady-state step.
+    Streams that one GPU sustains in real time at this batch = batch x audio
+    per step / step time."""
+    import torch
+
+    pipe = build_streaming_pipeline(model, dev, DECODE_CFG[model]["streams"])
+    att, B = SHAPES[model]["att"], DECODE_CFG[model]["streams"]
+    la = att[1]
     slots = torch.arange(B, dtype=torch.int32, device=dev)
     pipe.start_streams(slots)
     n0, n = (1 + 8 * la) * 160, (8 + 8 * la) * 160
@@ -754,6 +766,177 @@ def streaming_step(model, steps, dev, profile=False):
     out["realtime_streams_at_this_batch"] = int(B * out["audio_ms_per_step"] / best)
     out["device_error_word"] = pipe.pool.read_error() | pipe.fe.error_bits()
     return out
+
+
+def serve_trial(pipe, N, period, banks, hbufs, dbufs, hslots, dslots, htok, hcnt,
+                warm_periods, meas_periods, seed, max_batch=2048):
+    """N streams paced in real time: stream i's chunk k completes at
+    t0 + phase_i + k * period (phases uniform over one period).  The loop takes
+    every chunk that has completed (one per stream per iteration), groups them
+    by push index (first, second, later; batches of at most 2048 streams), copies
+    their samples
+    and slots in from pinned host memory, runs ``step_audio`` eagerly and
+    copies the tokens back to pinned host memory; a chunk's latency is the
+    wall time from its completion to its tokens being on the host (the
+    reference's push_samples -> DecodeResult, model_runner.py:150-171).
+    Returns latencies (s) of the chunks completed in the measured periods and
+    the loop's statistics."""
+    import numpy as np
+    import torch
+
+    dev = pipe.device
+    rng = np.random.default_rng(seed)
+    phase = rng.uniform(0.0, period, N)
+    k = np.zeros(N, np.int64)
+    slots_all = torch.arange(N, dtype=torch.int32)
+    pipe.start_streams(slots_all)
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter() + 0.02
+    t_meas, t_end = t0 + warm_periods * period, t0 + (warm_periods + meas_periods) * period
+    lats, steps, rows, launches = [], 0, 0, 0
+    ev = torch.cuda.Event()
+    while True:
+        now = time.perf_counter()
+        if now >= t_end:
+            break
+        arr = t0 + phase + k * period
+        ready = np.flatnonzero(arr <= now)
+        if ready.size == 0:
+            time.sleep(max(0.0, min(float(arr.min()), t_end) - now))
+            continue
+        cls = np.minimum(k[ready], 2)
+        launched = []
+        for c in (0, 1, 2):
+            sel = ready[cls == c]
+            sel = sel[np.argsort(arr[sel], kind="stable")]
+            # batches of at most 2048 rows (the step's allocator), oldest first,
+            # each in its own rows of the buffers (copies are still in flight)
+            for off in range(0, sel.size, max_batch):
+                part = sel[off:off + max_batch]
+                B = part.size
+                rs = slice(off, off + B)
+                bank = banks[c]
+                torch.index_select(bank, 0, torch.from_numpy((part + k[part]) % bank.shape[0]),
+                                   out=hbufs[c][rs])
+                hslots[c][rs].numpy()[:] = part
+                dx = dbufs[c][rs]
+                dx.copy_(hbufs[c][rs], non_blocking=True)
+                ds = dslots[c][rs]
+                ds.copy_(hslots[c][rs], non_blocking=True)
+                tok, cnt = pipe.step_audio(dx, ds, c)
+                htok[c][rs].copy_(tok.view(B, -1), non_blocking=True)
+                hcnt[c][rs].copy_(cnt, non_blocking=True)
+                rows += B
+                launches += 1
+            if sel.size:
+                launched.append((sel, arr[sel]))
+        ev.record()
+        ev.synchronize()
+        t_done = time.perf_counter()
+        for sel, a in launched:
+            lats.append(t_done - a[a >= t_meas])
+            k[sel] += 1
+        steps += 1
+    backlog = int(np.max(np.floor((t_end - t0 - phase) / period) + 1 - k))
+    pipe.end_streams(slots_all)
+    lat = np.concatenate(lats) if lats else np.zeros(0)
+    return lat, {"iterations": steps, "steps": launches,
+                 "mean_batch": round(rows / max(launches, 1), 1),
+                 "backlog_chunks_at_end": backlog}
+
+
+def serving_search(model, dev, measure_s=3.0, max_trials=9, limit_ms=160.0):
+    """Metric 1 of the survey: the most concurrent streams one GPU serves with
+    p99 chunk latency <= 160 ms, streams paced in real time (configs[2] /
+    configs[3] audio, random bf16 weights).  Doubling from 1024 streams until
+    a trial fails (p99 above the limit, or chunks left waiting at the end),
+    then bisection, a failing trial repeated once; the slot count is capped by
+    85 % of the free device memory (every slot holds its K/V pages).  Eager
+    steps (batch sizes vary from step to step)."""
+    import numpy as np
+    import torch
+
+    from parakeet_b200.ops import pages_per_stream
+    c = SHAPES[model]
+    L, D, att = c["layers"], c["dim"], c["att"]
+    la = att[1]
+    T = la + 1
+    period = (la + 1) * 0.08
+    n0, n = (1 + 8 * la) * 160, (8 + 8 * la) * 160
+    per_slot = (pages_per_stream(att[0], T, PAGE) * L * 2 * PAGE * D * 2 + L * D * 8 * 2
+                + 128 * 9 * 2 + 4096)
+    torch.cuda.empty_cache()
+    free = torch.cuda.mem_get_info(dev)[0]
+    cap = int(min(65536, 0.85 * free / per_slot)) // 256 * 256
+    pipe = build_streaming_pipeline(model, dev, cap)
+    S = pipe.dec.max_symbols
+    audio = synth_audio_batch(64, n0 + 2 * n, seed=11)
+    banks = [torch.from_numpy(np.ascontiguousarray(a))
+             for a in (audio[:, :n0], audio[:, n0:n0 + n], audio[:, n0 + n:])]
+    hbufs = [torch.empty(cap, b.shape[1], dtype=torch.float32).pin_memory() for b in banks]
+    dbufs = [torch.empty(cap, b.shape[1], dtype=torch.float32, device=dev) for b in banks]
+    hslots = [torch.empty(cap, dtype=torch.int32).pin_memory() for _ in range(3)]
+    dslots = [torch.empty(cap, dtype=torch.int32, device=dev) for _ in range(3)]
+    htok = [torch.empty(cap, T * S, dtype=torch.int32).pin_memory() for _ in range(3)]
+    hcnt = [torch.empty(cap, T, dtype=torch.int32).pin_memory() for _ in range(3)]
+    meas = max(3, int(round(measure_s / period)))
+    trials, ok_n, bad_n = [], 0, None
+    N = min(1024, cap)
+    with torch.inference_mode():
+        # Warm-up: one first, second and later step at batch sizes 1 ... wcap
+        # (ratio 1.5), so that every kernel the trials' batch sizes select is
+        # loaded (modules load at first launch) and the allocator holds blocks.
+        wcap = min(cap, 2048)
+        sizes = sorted({min(wcap, int(1.5 ** i)) for i in range(64) if 1.5 ** (i - 1) < wcap})
+        for B in sizes:
+            sl = torch.arange(B, dtype=torch.int32)
+            pipe.start_streams(sl)
+            for c in range(3):
+                dbufs[c][:B].copy_(banks[c][torch.arange(B) % banks[c].shape[0]])
+                dslots[c][:B].copy_(sl)
+                pipe.step_audio(dbufs[c][:B], dslots[c][:B], c)
+            pipe.end_streams(sl)
+        torch.cuda.synchronize(dev)
+        serve_trial(pipe, min(64, cap), period, banks, hbufs, dbufs, hslots, dslots, htok, hcnt,
+                    3, 1, seed=0)
+
+        def run(N, seed):
+            lat, st = serve_trial(pipe, N, period, banks, hbufs, dbufs, hslots, dslots, htok, hcnt,
+                                  3, meas, seed=seed)
+            p99 = float(np.percentile(lat, 99)) * 1e3 if lat.size else float("inf")
+            ok = p99 <= limit_ms and st["backlog_chunks_at_end"] <= 1
+            return ok, {"streams": N, "ok": ok, "p50_ms": round(float(np.median(lat)) * 1e3, 2),
+                        "p99_ms": round(p99, 2), "chunks": int(lat.size), **st}
+
+        while len(trials) < max_trials:
+            ok, rec = run(N, len(trials) + 1)
+            if not ok:   # a trial fails only if its repeat fails too
+                ok, rec2 = run(N, 100 + len(trials))
+                rec = {**rec2, "first_attempt_p99_ms": rec["p99_ms"]}
+            trials.append(rec)
+            if ok:
+                ok_n = N
+            else:
+                bad_n = N
+            if bad_n is None:
+                if N >= cap:
+                    break
+                N = min(2 * N, cap)
+            else:
+                if bad_n - ok_n <= max(64, ok_n // 16):
+                    break
+                N = (ok_n + bad_n) // 2 // 32 * 32
+    err = pipe.pool.read_error() | pipe.fe.error_bits()
+    del pipe
+    torch.cuda.empty_cache()
+    best = next((t for t in trials if t["streams"] == ok_n), None)
+    return {"model": model, "limit_ms": limit_ms, "streams_max": ok_n,
+            "capped_by_memory": bad_n is None and ok_n == cap, "slot_cap": cap,
+            "p99_ms_at_max": best["p99_ms"] if best else None,
+            "audio_ms_per_chunk": period * 1e3, "measured_s_per_trial": round(meas * period, 2),
+            "trials": trials, "device_error_word": err,
+            "method": "streams paced in real time, eager batched steps over every completed "
+                      "chunk, latency = chunk completion -> tokens in pinned host memory"}
 
 
 def max_over_ranks(vals, device):
@@ -933,7 +1116,7 @@ def main():
             dist.barrier()
         ms = g0.elapsed_time(g1) / K
     clk = clocks.stop()
-    enc_line = dec_line = pre_line = fe_line = pipe_line = gemm_line = None
+    enc_line = dec_line = pre_line = fe_line = pipe_line = gemm_line = serve_line = None
     # the model-level lines are one GPU's measurements: run them on single-GPU
     # runs only, so that no rank waits in a collective while rank 0 measures
     if world == 1 and not args.no_breakdown:
@@ -943,6 +1126,8 @@ def main():
         fe_line = feature_step(args.model, 50, dev)
         gemm_line = {m: gemm_step(m, 20, dev) for m in ("small", "large")}
         pipe_line = streaming_step(args.model, 10, dev)
+        if not args.no_serve:
+            serve_line = serving_search(args.model, dev)
     err = pool.read_error()
 
     # ---- end to end through the public API, as a serving loop runs it: every step
@@ -1098,6 +1283,7 @@ def main():
             "features": fe_line,
             "gemm": gemm_line,
             "streaming_step": pipe_line,
+            "streams_at_p99_160ms": serve_line,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -54,8 +54,8 @@ class StreamingPipeline:
         """Fresh state for new streams in ``slots`` (their pages start empty;
         conv cache and prediction state as ``create_sequence`` leaves them; the
         feature history restarts with their first ``step_audio``)."""
-        for s in torch.as_tensor(slots).reshape(-1).tolist():
-            self.pool.zero_conv_slot(int(s))
+        idx = torch.as_tensor(slots, dtype=torch.int64).reshape(-1).to(self.device)
+        self.pool.conv.index_fill_(0, idx, 0)
         self.dec.reset_slots(slots)
         self.fe.reset_slots(slots)
 
@@ -96,15 +96,17 @@ class StreamingPipeline:
                 first_samples = (1 + 8 * la) * self.fe.hop_length
             prefix = min(self.frames_per_push(first_samples, True), self.pre.cache_size)
         key = (B, n, first)
-        bufs = self._fe_bufs.get(key)
+        bufs = self._fe_bufs.pop(key, None)
         if bufs is None:
+            while len(self._fe_bufs) >= 16:   # batches of many sizes: keep the recent ones
+                self._fe_bufs.pop(next(iter(self._fe_bufs)))
             dev = self.device
             bufs = (torch.full((B,), n, dtype=torch.int32, device=dev),
                     torch.full((B,), _lib.PK_FE_FIRST if first else 0, dtype=torch.int32,
                                device=dev),
                     torch.empty(B, self.fe.n_mels, F, dtype=self.dtype, device=dev),
                     torch.empty(B, dtype=torch.int32, device=dev))
-            self._fe_bufs[key] = bufs
+        self._fe_bufs[key] = bufs
         ns, flags, feats, nframes = bufs
         self.fe.launch(samples, ns, flags, slots, feats, F, nframes)
         return self.encode(feats, slots, first, prefix=prefix)
