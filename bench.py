@@ -5,9 +5,13 @@ Workload: one isolated paged-attention step of the
 small model, bf16 - 80 streams x 17 layers, 8 heads of 64, chunk of 2 frames
 over 70 cached left-context frames (window 72), 16-frame pages, the free
 list a random permutation of the pool (seed 1), Q/K/V and the rel-pos
-projection N(0,1)/8.  A step is three launches: step start (page allocator
-and window descriptors) -> paged rel-pos attention for all 17 layers with the
-chunk's K/V append fused in -> counter update (end).  Streams are
+projection N(0,1)/8.  A step is four launches: the rel-pos term of every
+(layer, stream, head, query) in one pre-pass (each layer's pos rows read
+once, not once per stream) -> step start (page allocator and window
+descriptors) -> paged rel-pos attention for all 17 layers with the chunk's
+K/V append fused in -> counter update (end); ``--relpos in-kernel`` computes
+the rel-pos term inside the attention kernel instead (three launches).
+Streams are
 independent, so N GPUs run N replicas with no collective on the data path
 (weak scaling): each rank owns its own pool and streams, and the only
 collectives are the timing barriers and one max-reduce of the timings.
@@ -65,6 +69,9 @@ def parse():
     ap.add_argument("--streams", type=int, default=80)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-breakdown", action="store_true")
+    ap.add_argument("--relpos", choices=["prepass", "in-kernel"], default="prepass",
+                    help="rel-pos term: all-stream pre-pass (pk_relpos_bd) or inside the "
+                         "attention kernel")
     ap.add_argument("--no-serve", action="store_true",
                     help="skip the paced serving search (streams at p99 <= 160 ms)")
     ap.add_argument("--no-graph", action="store_true", help="time eager launches only")
@@ -1009,16 +1016,34 @@ def main():
     units = B * L
     step_bytes = (nb["append"] + nb["attention"]) * units
 
-    def step(buf, ev=None):
+    # the rel-pos term of every (layer, stream, head, query) in one pre-pass
+    # that reads each layer's pos rows once, instead of once per stream inside
+    # the attention kernel (where they are L2 traffic 1.5x the K/V bytes' size)
+    prepass = args.relpos == "prepass" and pool.relpos_bd_cols > 0
+    bd_buf = (torch.empty(L, B, H, T, pool.relpos_bd_cols, dtype=torch.float32, device=dev)
+              if prepass else None)
+
+    def run_step(x, o, ev=None):
+        # (on a side stream, concurrent with the step start, it measured slower:
+        # the join costs the programmatic overlap of step start and attention)
+        if ev is not None:
+            ev[2].record()
+        if prepass:
+            pool.relpos_bd(0, x[..., :D], pos, bv, out=bd_buf)
+        if ev is not None:
+            ev[3].record()
         pool.begin_step(slots, lengths)
         if ev is not None:
             ev[0].record()
         # append of the chunk's K/V rows fused into the attention call
-        pool.attention(0, buf[..., :D], pos, bu, bv, slots, lengths, out,
-                       key=buf[..., D:2 * D], value=buf[..., 2 * D:])
+        pool.attention(0, x[..., :D], pos, bu, bv, slots, lengths, o,
+                       key=x[..., D:2 * D], value=x[..., 2 * D:], bd=bd_buf)
         if ev is not None:
             ev[1].record()
         pool.end_step(slots, lengths)
+
+    def step(buf, ev=None):
+        run_step(buf, out, ev)
 
     def make_ops():
         """The per-op breakdown: name -> (launch fn, algorithmic bytes, launches)."""
@@ -1076,8 +1101,7 @@ def main():
 
     K = args.steps
     # (a) eager steps with CUDA events around the attention kernel: roofline timing
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(K)]
+    evs = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(4)) for _ in range(K)]
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
         dist.barrier()
@@ -1090,7 +1114,8 @@ def main():
     if world > 1:
         dist.barrier()
     eager_ms = e0.elapsed_time(e1) / K
-    attn_ms = sum(a.elapsed_time(b) for a, b in evs) / K
+    attn_ms = sum(e[0].elapsed_time(e[1]) for e in evs) / K
+    bd_ms = sum(e[2].elapsed_time(e[3]) for e in evs) / K if prepass else 0.0
 
     # (b) the same steps replayed as CUDA graphs (one graph per input buffer): `value`
     ms = eager_ms
@@ -1147,10 +1172,7 @@ def main():
     ev_out = [torch.cuda.Event() for _ in range(NB2)]
 
     def api_step(x, o):
-        pool.begin_step(slots, lengths)
-        pool.attention(0, x[..., :D], pos, bu, bv, slots, lengths, o,
-                       key=x[..., D:2 * D], value=x[..., 2 * D:])
-        pool.end_step(slots, lengths)
+        run_step(x, o)
 
     def e2e_issue(i):
         k = i % NB2
@@ -1273,7 +1295,10 @@ def main():
                     "h2d_bytes_per_step": qkv[0].numel() * 2, "d2h_bytes_per_step": out.numel() * 2,
                     "ms_per_step": round(e2e_ms, 4),
                     "pipeline": "copy-in, compute and copy-out streams, 3 buffer sets, eager API calls"},
-            "gpu_launches": 3 * K,   # per step: allocator+windows, attention+append, counters
+            # per step: [rel-pos pre-pass,] allocator+windows, attention+append, counters
+            "gpu_launches": (4 if prepass else 3) * K,
+            "relpos": {"mode": "prepass" if prepass else "in-kernel",
+                       "prepass_ms": round(bd_ms, 4) if prepass else None},
             "clocks": clk,
             "device_error_word": err,
             "ops": breakdown,

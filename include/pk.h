@@ -190,6 +190,42 @@ int pk_paged_attention(pk_paged_kv *kv, int32_t layer0, int32_t num_layers,
                        int64_t out_layer_stride, int64_t out_batch_stride,
                        int64_t out_row_stride, void *stream);
 
+/* Row length (floats) of the rel-pos term pk_relpos_bd writes for this pool:
+ * 16 * ceil((left + 2 * chunk - 1) / 16); 0 when the pool's shape has no
+ * pre-pass (it needs bf16, head_dim 64, heads a multiple of 4, 4 * chunk <= 16
+ * and 16-frame pages; pk_paged_attention covers every shape). */
+int32_t pk_relpos_bd_cols(const pk_paged_kv *kv);
+
+/* The rel-pos term of the attention logits for every (layer, stream, head,
+ * query row) of a step, before its 1/sqrt(head_dim) scale:
+ *   bd[l][b][h][t][r] = sum_d bf16(q[l][b][t][h*dh + d] + bias_v[l][h][d])
+ *                             * pos_proj[l][r][h*dh + d]      (fp32)
+ * for r < pk_relpos_bd_cols(kv) (rows >= 2*(left+chunk)-1 read as zero);
+ * query / pos_proj / bias_v as in pk_paged_attention, bd 16-byte aligned with
+ * num_layers * batch * heads * chunk * cols floats.  Every stream of a layer
+ * uses the same pos_proj rows, so this pass reads them once per (layer, head)
+ * instead of once per stream.  It is the (q + pos_bias_v) pos^T product of
+ * ConformerAttention.forward lines 108-110 (parakeet/modules/attention.py),
+ * before rel_shift. */
+int pk_relpos_bd(pk_paged_kv *kv, int32_t layer0, int32_t num_layers,
+                 const void *query, int64_t q_layer_stride, int64_t q_batch_stride,
+                 int64_t q_row_stride, const void *pos_proj, int64_t pos_layer_stride,
+                 const void *bias_v, int64_t bias_layer_stride, int32_t batch,
+                 float *bd, void *stream);
+
+/* pk_paged_attention with the rel-pos term taken from pk_relpos_bd's output
+ * for the same query, layers and batch (in place of pos_proj and bias_v).
+ * Same outputs, same replaced calls; for the shapes pk_relpos_bd_cols
+ * accepts. */
+int pk_paged_attention_bd(pk_paged_kv *kv, int32_t layer0, int32_t num_layers,
+                          const void *query, int64_t q_layer_stride,
+                          int64_t q_batch_stride, int64_t q_row_stride,
+                          const void *key, const void *value, const float *bd,
+                          const void *bias_u, int64_t bias_layer_stride,
+                          const int32_t *slots, const int32_t *lengths, int32_t batch,
+                          void *out, int64_t out_layer_stride, int64_t out_batch_stride,
+                          int64_t out_row_stride, void *stream);
+
 /* Depthwise causal conv step with its time cache, one layer:
  *   GLU over the pw-conv1 output x (l=0: [batch][chunk][2*dim] with
  *   x_batch_stride / x_row_stride) -> zero rows t >= length -> depthwise conv

@@ -272,6 +272,10 @@ int pk_paged_attention(pk_paged_kv *kv, int32_t layer0, int32_t num_layers, cons
     a.bias_u = bias_u;
     a.bias_v = bias_v;
     a.bias_ls = bias_layer_stride;
+    a.pos = pos_proj;
+    a.pos_ls = (int64_t)(lstride / es);
+    a.pos_rows = P;
+    a.bd = nullptr;
     a.slots = slots;
     a.lengths = lengths;
     a.batch = batch;
@@ -309,6 +313,95 @@ int pk_paged_attention(pk_paged_kv *kv, int32_t layer0, int32_t num_layers, cons
     st = launch_attention(kv, pos_map, a, s);
     if (st == PK_ENOTSUP) pk::set_error("attention configuration not handled (smem or boxes)");
     return st;
+}
+
+int32_t pk_relpos_bd_cols(const pk_paged_kv *kv) {
+    return kv ? relpos_bd_cols(kv) : 0;
+}
+
+int pk_relpos_bd(pk_paged_kv *kv, int32_t layer0, int32_t num_layers, const void *query,
+                 int64_t q_layer_stride, int64_t q_batch_stride, int64_t q_row_stride,
+                 const void *pos_proj, int64_t pos_layer_stride, const void *bias_v,
+                 int64_t bias_layer_stride, int32_t batch, float *bd, void *stream) {
+    PK_CHECK(kv, "null pool");
+    PK_CHECK(batch >= 0 && num_layers >= 0 && layer0 >= 0 &&
+                 layer0 + num_layers <= kv->d.num_layers,
+             "layer range outside the pool");
+    PK_CHECK(relpos_bd_cols(kv) > 0, "no all-stream rel-pos pre-pass for this pool's shape");
+    if (batch == 0 || num_layers == 0) return PK_OK;
+    PK_CHECK(query && pos_proj && bias_v && bd, "null pointer");
+    const int es = kv->esize;
+    PK_CHECK(aligned16(query) && (q_row_stride * es) % 16 == 0 &&
+                 (q_batch_stride * es) % 16 == 0 && (q_layer_stride * es) % 16 == 0,
+             "query must be 16-byte aligned with 16-byte strides");
+    PK_CHECK(aligned16(pos_proj) && aligned16(bd), "pos_proj / bd not 16-byte aligned");
+    PK_CHECK((reinterpret_cast<uintptr_t>(bias_v) & 3u) == 0, "bias_v not 4-byte aligned");
+    const int P = 2 * (kv->d.left + kv->d.chunk) - 1;
+    const uint64_t row = (uint64_t)kv->d.dim * es;
+    uint64_t lstride = (uint64_t)pos_layer_stride * es;
+    if (num_layers == 1) lstride = row * P;
+    PK_CHECK(lstride % 16 == 0 && lstride >= row * P, "bad pos_layer_stride");
+    AttnArgs a{};
+    a.q = query;
+    a.q_ls = q_layer_stride;
+    a.q_bs = q_batch_stride;
+    a.q_rs = q_row_stride;
+    a.bias_v = bias_v;
+    a.bias_ls = bias_layer_stride;
+    a.pos = pos_proj;
+    a.pos_ls = (int64_t)(lstride / es);
+    a.pos_rows = P;
+    a.batch = batch;
+    a.layer0 = layer0;
+    a.nlayers = num_layers;
+    return launch_relpos_bd(kv, a, bd, static_cast<cudaStream_t>(stream));
+}
+
+int pk_paged_attention_bd(pk_paged_kv *kv, int32_t layer0, int32_t num_layers, const void *query,
+                          int64_t q_layer_stride, int64_t q_batch_stride, int64_t q_row_stride,
+                          const void *key, const void *value, const float *bd,
+                          const void *bias_u, int64_t bias_layer_stride, const int32_t *slots,
+                          const int32_t *lengths, int32_t batch, void *out,
+                          int64_t out_layer_stride, int64_t out_batch_stride,
+                          int64_t out_row_stride, void *stream) {
+    PK_CHECK(kv, "null pool");
+    PK_CHECK(batch >= 0 && num_layers >= 0 && layer0 >= 0 &&
+                 layer0 + num_layers <= kv->d.num_layers,
+             "layer range outside the pool");
+    PK_CHECK(relpos_bd_cols(kv) > 0, "no attention over a precomputed rel-pos term for this pool's shape");
+    if (batch == 0 || num_layers == 0) return PK_OK;
+    PK_CHECK(query && bd && bias_u && slots && lengths && out, "null pointer");
+    PK_CHECK((key == nullptr) == (value == nullptr), "key and value go together");
+    PK_CHECK(aligned16(bd), "bd not 16-byte aligned");
+    PK_CHECK(out_row_stride % 2 == 0 && out_batch_stride % 2 == 0 && out_layer_stride % 2 == 0 &&
+                 (reinterpret_cast<uintptr_t>(out) % (2 * kv->esize)) == 0,
+             "out must allow 2-element stores");
+    const int es = kv->esize;
+    PK_CHECK(aligned16(query) && (q_row_stride * es) % 16 == 0 &&
+                 (q_batch_stride * es) % 16 == 0 && (q_layer_stride * es) % 16 == 0,
+             "query must be 16-byte aligned with 16-byte strides");
+    PK_CHECK(!key || (aligned16(key) && aligned16(value)), "key/value not 16-byte aligned");
+    AttnArgs a{};
+    a.q = query;
+    a.q_ls = q_layer_stride;
+    a.q_bs = q_batch_stride;
+    a.q_rs = q_row_stride;
+    a.k_new = key;
+    a.v_new = value;
+    a.bias_u = bias_u;
+    a.bias_ls = bias_layer_stride;
+    a.bd = bd;
+    a.slots = slots;
+    a.lengths = lengths;
+    a.batch = batch;
+    a.out = out;
+    a.o_ls = out_layer_stride;
+    a.o_bs = out_batch_stride;
+    a.o_rs = out_row_stride;
+    a.layer0 = layer0;
+    a.nlayers = num_layers;
+    CUtensorMap unused{};
+    return launch_attention_stacked(kv, unused, a, static_cast<cudaStream_t>(stream));
 }
 
 int pk_conv_step(void *conv_state, int32_t num_slots, int32_t num_layers, int32_t layer,

@@ -9,14 +9,16 @@
 // 14 padding rows of every m16 tile.  Here:
 //
 // * a producer warp streams 8 KB blocks through an NS-stage ring with
-//   128B-swizzled TMA tile loads (cp.async.bulk.tensor, one box per head;
-//   pages with an L2 evict-first policy, rel-pos rows evict-last):
-//   the stream's K pages first (DRAM), then the rel-pos rows in blocks of 16
-//   (L2-resident), then its V pages - each page box shifted so that rows
-//   outside the window are zero-filled without being read;
-// * consumer warp h owns head h: BD = (q+v) P^T and S = (q+u) K^T on tensor
-//   cores (mma.sync m16n8k16, bf16 in, fp32 accumulate), written to shared
-//   memory in the stacked [head * T + query] row order;
+//   128B-swizzled TMA tile loads (cp.async.bulk.tensor, one box per head,
+//   L2 evict-first): the stream's K pages, then its V pages - each page box
+//   shifted so that rows outside the window are zero-filled without being
+//   read;
+// * meanwhile consumer warp h computes its head's BD = (q+v) P^T from the
+//   rel-pos rows P read straight from global memory (L2-resident: every
+//   stream of the layer reads the same rows), so they take no turns of the
+//   ring; then S = (q+u) K^T as the K pages arrive; both on tensor cores
+//   (mma.sync m16n8k16, bf16 in, fp32 accumulate), written to shared memory
+//   in the stacked [head * T + query] row order;
 // * one dense softmax over the group's rows (16 threads per row) with the
 //   reference's -1e5 masked fill, probabilities kept as bf16 per page box;
 // * O_h = P V_h on tensor cores, normalised by the row sums;
@@ -78,10 +80,83 @@ __device__ __forceinline__ void consumer_sync() {
     asm volatile("bar.sync 1, %0;" ::"n"(kH * 32) : "memory");
 }
 
+// ---- rel-pos term BD = bf16(q + v) P^T on tensor cores, P (the layer's
+// linear_pos rows) read straight from global memory.  The MMA's k index is
+// permuted alike in both operands (a sum over k does not depend on its order)
+// so that each lane's A and B fragments are the 32 contiguous bytes
+// [16 tq, 16 tq + 16) of a row: logical k = 16 ks + 2 tq + 8 half + e sits in
+// column 16 tq + 4 ks + 2 half + e.  The attention kernel and the all-stream
+// pre-pass both use these two helpers, so their BD values are identical.
+
+// One query row's A-fragment words: bf16(q + v) at columns [16 tq, 16 tq + 16)
+// (q_row and bias_v2 already offset by the head and by 16 tq); zeros without q_row.
+__device__ __forceinline__ void bd_a_words(const __nv_bfloat16 *q_row,
+                                           const __nv_bfloat162 *bias_v2, uint32_t (&x)[8]) {
+    uint4 q0 = make_uint4(0, 0, 0, 0), q1 = q0;
+    if (q_row) {
+        q0 = reinterpret_cast<const uint4 *>(q_row)[0];
+        q1 = reinterpret_cast<const uint4 *>(q_row)[1];
+    }
+    const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        uint32_t xv = 0u;
+        if (q_row) {
+            const float2 q = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&qw[j]));
+            const float2 v = __bfloat1622float2(__ldg(bias_v2 + j));
+            __nv_bfloat162 t2 = __floats2bfloat162_rn(q.x + v.x, q.y + v.y);
+            xv = *reinterpret_cast<uint32_t *>(&t2);
+        }
+        x[j] = xv;
+    }
+}
+
+// n-tiles (8 rel-pos rows) whose B fragments one batch of loads brings in:
+// 5 inside the attention kernel (register budget), 10 (all of them at the
+// small config) in the pre-pass
+constexpr int kBdBatch = 5;
+constexpr int kBdBatchPrepass = 10;
+
+// BD of the m16 tile's rows gq (xa) and gq + 8 (xb) against rel-pos rows
+// [0, 8 * ntiles) (rows >= pos_rows read as zero); p_base = the layer's P at
+// row 0, offset by the head and by 16 tq, rows dim elements apart.
+// store(nt, c) receives n-tile nt's accumulators (row gq: c[0..1], row gq + 8:
+// c[2..3], columns nt * 8 + 2 tq + {0, 1}).
+template <int NB, class Store>
+__device__ __forceinline__ void bd_tile(const uint32_t (&xa)[8], const uint32_t (&xb)[8],
+                                        const __nv_bfloat16 *p_base, int dim, int pos_rows,
+                                        int ntiles, int gq, Store store) {
+    for (int nt0 = 0; nt0 < ntiles; nt0 += NB) {
+        uint4 pw[NB][2];
+#pragma unroll
+        for (int i = 0; i < NB; ++i) {
+            const int r = (nt0 + i) * 8 + gq;
+            pw[i][0] = pw[i][1] = make_uint4(0, 0, 0, 0);
+            if (nt0 + i < ntiles && r < pos_rows) {
+                const uint4 *src = reinterpret_cast<const uint4 *>(p_base + (int64_t)r * dim);
+                pw[i][0] = __ldg(src);
+                pw[i][1] = __ldg(src + 1);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < NB; ++i) {
+            if (nt0 + i >= ntiles) break;
+            const uint32_t pv[8] = {pw[i][0].x, pw[i][0].y, pw[i][0].z, pw[i][0].w,
+                                    pw[i][1].x, pw[i][1].y, pw[i][1].z, pw[i][1].w};
+            float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+                const uint32_t af[4] = {xa[2 * ks], xb[2 * ks], xa[2 * ks + 1], xb[2 * ks + 1]};
+                mma_bf16(c, af, pv[2 * ks], pv[2 * ks + 1]);
+            }
+            store(nt0 + i, c);
+        }
+    }
+}
+
 template <int NS>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
-    paged_attn_stacked_kernel(const __grid_constant__ CUtensorMap kv_map,
-                              const __grid_constant__ CUtensorMap pos_map, const SGeom g,
+    paged_attn_stacked_kernel(const __grid_constant__ CUtensorMap kv_map, const SGeom g,
                               const pk_paged_kv_desc d, const AttnArgs a) {
     using T = __nv_bfloat16;
     extern __shared__ char smem_raw[];
@@ -130,7 +205,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     }
     __syncthreads();
     const int nb = s_nb, w = s_w, nfirst = s_nfirst;
-    const int nblocks = npb + 2 * nb;
+    const int nblocks = 2 * nb;   // K pages, then V pages
     T *out_base = static_cast<T *>(a.out) + (int64_t)lrel * a.o_ls + (int64_t)b * a.o_bs + hg0 * 64;
     if (!s_ok) {
         for (int idx = tid; idx < chunk * kH * 64; idx += kThreads)
@@ -139,7 +214,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     }
 
     if (warp == kH) {
-        // ================= producer: K pages, rel-pos blocks, V pages =================
+        // ======================= producer: K pages, then V pages =======================
         int last_n[NS];
 #pragma unroll
         for (int s = 0; s < NS; ++s) last_n[s] = -1;
@@ -159,14 +234,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
             __syncwarp();
             if (lane < kH) {
                 char *dst = smem + s * g.stage_bytes + lane * kBox;
-                if (n >= nb && n < nb + npb) {
-                    tma_load_3d_hint(dst, &pos_map, &full[s], (hg0 + lane) * 64, (n - nb) * 16, lrel,
-                                     l2_evict_last());
-                } else {
-                    const int i = n < nb ? n : n - nb - npb, kvi = n < nb ? 0 : 1;
-                    const int plane = ((s_page[i] * d.num_layers + layer) * 2 + kvi) * d.num_heads + hg0 + lane;
-                    tma_load_3d_hint(dst, &kv_map, &full[s], 0, s_start[i], plane, l2_evict_first());
-                }
+                const int i = n < nb ? n : n - nb, kvi = n < nb ? 0 : 1;
+                const int plane = ((s_page[i] * d.num_layers + layer) * 2 + kvi) * d.num_heads + hg0 + lane;
+                tma_load_3d_hint(dst, &kv_map, &full[s], 0, s_start[i], plane, l2_evict_first());
             }
             last_n[s] = n;
         }
@@ -184,33 +254,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     const float scale = 0.125f;  // 1 / sqrt(64)
     const int bds = g.bd_stride;
 
-    // A fragments: rows 0..chunk-1 of the m16 tile are this head's queries
-    uint32_t fu[4][4], fv[4][4];
-    {
-        const int hh = hg0 + h;
-        const T *qb = static_cast<const T *>(a.q) + (int64_t)lrel * a.q_ls + (int64_t)b * a.q_bs + hh * 64;
-        const T *bu = static_cast<const T *>(a.bias_u) + (int64_t)lrel * a.bias_ls + hh * 64;
-        const T *bv = static_cast<const T *>(a.bias_v) + (int64_t)lrel * a.bias_ls + hh * 64;
-#pragma unroll
-        for (int ks = 0; ks < 4; ++ks)
-#pragma unroll
-            for (int r = 0; r < 4; ++r) {
-                const int row = gq + (r & 1) * 8, col = ks * 16 + (r >> 1) * 8 + 2 * tq;
-                uint32_t pu = 0u, pv = 0u;
-                if (row < chunk) {
-                    const float2 q = __bfloat1622float2(
-                        *reinterpret_cast<const __nv_bfloat162 *>(qb + (int64_t)row * a.q_rs + col));
-                    const float2 u = __bfloat1622float2(__ldg(reinterpret_cast<const __nv_bfloat162 *>(bu + col)));
-                    const float2 v = __bfloat1622float2(__ldg(reinterpret_cast<const __nv_bfloat162 *>(bv + col)));
-                    __nv_bfloat162 xu = __floats2bfloat162_rn(q.x + u.x, q.y + u.y);
-                    __nv_bfloat162 xv = __floats2bfloat162_rn(q.x + v.x, q.y + v.y);
-                    pu = *reinterpret_cast<uint32_t *>(&xu);
-                    pv = *reinterpret_cast<uint32_t *>(&xv);
-                }
-                fu[ks][r] = pu;
-                fv[ks][r] = pv;
-            }
-    }
+    const int hh = hg0 + h;
+    const T *qb = static_cast<const T *>(a.q) + (int64_t)lrel * a.q_ls + (int64_t)b * a.q_bs + hh * 64;
 
     // this step's new K/V rows of head h, 16 bytes per lane (chunk * 8 <= 16 lanes),
     // fetched now so that the append below does not wait on memory
@@ -222,6 +267,49 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         knew = *reinterpret_cast<const uint4 *>(static_cast<const T *>(a.k_new) + off);
         vnew = *reinterpret_cast<const uint4 *>(static_cast<const T *>(a.v_new) + off);
     }
+    // ---- BD rows of this CTA's heads: from the all-stream pre-pass when given
+    // (a contiguous [head][query][bds] block), else computed here by warp h from
+    // the rel-pos rows, while the producer's first K pages are in flight
+    if (a.bd) {   // (its latency overlaps that of the first K pages)
+        const float4 *src = reinterpret_cast<const float4 *>(
+            a.bd + ((((int64_t)lrel * a.batch + b) * d.num_heads + hg0) * chunk) * bds);
+        float4 *dst = reinterpret_cast<float4 *>(sBD);
+        for (int i = tid; i < kH * chunk * bds / 4; i += kH * 32) dst[i] = src[i];
+    } else {
+        uint32_t xa[8], xb[8];   // query rows gq and gq + 8
+        const __nv_bfloat162 *bv2 = reinterpret_cast<const __nv_bfloat162 *>(
+            static_cast<const T *>(a.bias_v) + (int64_t)lrel * a.bias_ls + hh * 64 + 16 * tq);
+        bd_a_words(gq < chunk ? qb + (int64_t)gq * a.q_rs + 16 * tq : nullptr, bv2, xa);
+        bd_a_words(gq + 8 < chunk ? qb + (int64_t)(gq + 8) * a.q_rs + 16 * tq : nullptr, bv2, xb);
+        const T *p_base = static_cast<const T *>(a.pos) + (int64_t)lrel * a.pos_ls + hh * 64 + 16 * tq;
+        bd_tile<kBdBatch>(xa, xb, p_base, d.dim, a.pos_rows, 2 * npb, gq, [&](int nt, const float (&c)[4]) {
+            if (gq < chunk)
+                *reinterpret_cast<float2 *>(sBD + (h * chunk + gq) * bds + nt * 8 + 2 * tq) =
+                    make_float2(c[0], c[1]);
+        });
+    }
+
+    // A fragments of S: rows 0..chunk-1 of the m16 tile are this head's queries
+    uint32_t fu[4][4];
+    {
+        const T *bu = static_cast<const T *>(a.bias_u) + (int64_t)lrel * a.bias_ls + hh * 64;
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                const int row = gq + (r & 1) * 8, col = ks * 16 + (r >> 1) * 8 + 2 * tq;
+                uint32_t pu = 0u;
+                if (row < chunk) {
+                    const float2 q = __bfloat1622float2(
+                        *reinterpret_cast<const __nv_bfloat162 *>(qb + (int64_t)row * a.q_rs + col));
+                    const float2 u = __bfloat1622float2(__ldg(reinterpret_cast<const __nv_bfloat162 *>(bu + col)));
+                    __nv_bfloat162 xu = __floats2bfloat162_rn(q.x + u.x, q.y + u.y);
+                    pu = *reinterpret_cast<uint32_t *>(&xu);
+                }
+                fu[ks][r] = pu;
+            }
+    }
+
     // write those rows into box i (K or V) and into their page in global memory
     auto append_rows = [&](const uint4 &val, int kvi, int i, char *box) {
         if (app_lane) {
@@ -239,8 +327,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         __syncwarp();
     };
 
-    // ---- pass 1: rel-pos blocks -> BD rows, K pages -> S rows
-    for (int n = 0; n < npb + nb; ++n) {
+    // ---- pass 1: K pages -> S rows
+    for (int n = 0; n < nb; ++n) {
         const int s = n % NS;
         if (s_abort) break;
         if (!__all_sync(0xffffffffu, mbar_wait_bounded(&full[s], (n / NS) & 1, kWaitLimitNs))) {
@@ -252,40 +340,21 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         }
         char *box = smem + s * g.stage_bytes + h * kBox;
         const uint32_t abox = smem_u32(box);
-        const bool is_pos = n >= nb;
-        const int pblk = n - nb, kbox = n;
-        if (is_pos) {
+        const int i = n;
+        if (a.k_new) append_rows(knew, 0, i, box);
 #pragma unroll
-            for (int nt = 0; nt < 2; ++nt) {
-                float c[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int nt = 0; nt < 2; ++nt) {
+            float c[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                for (int kp = 0; kp < 4; kp += 2) {
-                    uint32_t bb[4];
-                    ldsm_x4(abox + sw128(nt * 8 + (lane % 8), (kp * 16 + (lane / 8) * 8) * 2), bb);
-                    mma_bf16(c, fv[kp], bb[0], bb[1]);
-                    mma_bf16(c, fv[kp + 1], bb[2], bb[3]);
-                }
-                if (gq < chunk)
-                    *reinterpret_cast<float2 *>(sBD + (h * chunk + gq) * bds + pblk * 16 + nt * 8 + 2 * tq) =
-                        make_float2(c[0], c[1]);
+            for (int kp = 0; kp < 4; kp += 2) {
+                uint32_t bb[4];
+                ldsm_x4(abox + sw128(nt * 8 + (lane % 8), (kp * 16 + (lane / 8) * 8) * 2), bb);
+                mma_bf16(c, fu[kp], bb[0], bb[1]);
+                mma_bf16(c, fu[kp + 1], bb[2], bb[3]);
             }
-        } else {
-            const int i = kbox;
-            if (a.k_new) append_rows(knew, 0, i, box);
-#pragma unroll
-            for (int nt = 0; nt < 2; ++nt) {
-                float c[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-                for (int kp = 0; kp < 4; kp += 2) {
-                    uint32_t bb[4];
-                    ldsm_x4(abox + sw128(nt * 8 + (lane % 8), (kp * 16 + (lane / 8) * 8) * 2), bb);
-                    mma_bf16(c, fu[kp], bb[0], bb[1]);
-                    mma_bf16(c, fu[kp + 1], bb[2], bb[3]);
-                }
-                if (gq < chunk)
-                    *reinterpret_cast<float2 *>(sS + (i * 16 + h * chunk + gq) * 16 + nt * 8 + 2 * tq) =
-                        make_float2(c[0], c[1]);
-            }
+            if (gq < chunk)
+                *reinterpret_cast<float2 *>(sS + (i * 16 + h * chunk + gq) * 16 + nt * 8 + 2 * tq) =
+                    make_float2(c[0], c[1]);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
@@ -343,8 +412,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         for (int k = 0; k < 2; ++k)
 #pragma unroll
             for (int e = 0; e < 4; ++e) o[np][k][e] = 0.f;
-    for (int n = npb + nb; n < nblocks; ++n) {
-        const int s = n % NS, i = n - npb - nb;
+    for (int n = nb; n < nblocks; ++n) {
+        const int s = n % NS, i = n - nb;
         if (s_abort) break;
         if (!__all_sync(0xffffffffu, mbar_wait_bounded(&full[s], (n / NS) & 1, kWaitLimitNs))) {
             if (lane == 0) {
@@ -388,24 +457,86 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     }
 }
 
-}  // namespace
+// grid (num_layers, num_heads, ceil(batch * chunk / 64)), 128 threads: warp w
+// computes BD of the (stream, query) rows [64 z + 16 w, 64 z + 16 w + 16) of one
+// (layer, head) - every stream of a layer uses the same rel-pos rows, read once
+// per CTA here instead of once per (stream, head group) in the attention kernel.
+__global__ void __launch_bounds__(128)
+    relpos_bd_kernel(const pk_paged_kv_desc d, const AttnArgs a, int bds, float *bd) {
+    using T = __nv_bfloat16;
+    const int lrel = blockIdx.x, hh = blockIdx.y;
+    const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+    const int gq = lane / 4, tq = lane % 4;
+    const int chunk = d.chunk, rows = a.batch * chunk;
+    const int m0 = blockIdx.z * 64 + warp * 16;
+    grid_dep_wait();     // q may come from the previous kernel
+    grid_dep_launch();   // the attention kernel waits for all of us
+    if (m0 >= rows) return;
+    const __nv_bfloat162 *bv2 = reinterpret_cast<const __nv_bfloat162 *>(
+        static_cast<const T *>(a.bias_v) + (int64_t)lrel * a.bias_ls + hh * 64 + 16 * tq);
+    auto q_row = [&](int m) -> const T * {
+        if (m >= rows) return nullptr;
+        const int b = m / chunk, t = m - b * chunk;
+        return static_cast<const T *>(a.q) + (int64_t)lrel * a.q_ls + (int64_t)b * a.q_bs +
+               (int64_t)t * a.q_rs + hh * 64 + 16 * tq;
+    };
+    uint32_t xa[8], xb[8];
+    bd_a_words(q_row(m0 + gq), bv2, xa);
+    bd_a_words(q_row(m0 + gq + 8), bv2, xb);
+    const T *p_base = static_cast<const T *>(a.pos) + (int64_t)lrel * a.pos_ls + hh * 64 + 16 * tq;
+    float *out = bd + (int64_t)lrel * rows * d.num_heads * bds;   // [batch][heads][chunk][bds]
+    bd_tile<kBdBatchPrepass>(xa, xb, p_base, d.dim, a.pos_rows, bds / 8, gq,
+                             [&](int nt, const float (&c)[4]) {
+#pragma unroll
+        for (int rh = 0; rh < 2; ++rh) {
+            const int m = m0 + gq + 8 * rh;
+            if (m < rows) {
+                const int b = m / chunk, t = m - b * chunk;
+                *reinterpret_cast<float2 *>(out + ((int64_t)(b * d.num_heads + hh) * chunk + t) * bds +
+                                            nt * 8 + 2 * tq) = make_float2(c[2 * rh], c[2 * rh + 1]);
+            }
+        }
+    });
+}
 
-int launch_attention_stacked(const pk_paged_kv *kv, const CUtensorMap &pos_map16,
-                             const AttnArgs &a, cudaStream_t s) {
+bool stacked_shape(const pk_paged_kv *kv, SGeom *g) {
     const pk_paged_kv_desc &d = kv->d;
     if (d.dtype != PK_DTYPE_BF16 || kv->head_dim != 64 || d.num_heads % kH != 0 ||
         kH * d.chunk > 16 || d.page_size != 16)
-        return PK_ENOTSUP;
+        return false;
+    g->num_layers = d.num_layers;
+    g->left = d.left;
+    g->chunk = d.chunk;
+    g->W = d.left + d.chunk;
+    g->R = g->W + d.chunk - 1;
+    g->npb = (g->R + 15) / 16;
+    g->max_boxes = pk_pages_per_stream(d.left, d.chunk, d.page_size);
+    return g->max_boxes <= kMaxBoxes && g->npb <= kMaxPosBlocks;
+}
+
+}  // namespace
+
+int relpos_bd_cols(const pk_paged_kv *kv) {
+    SGeom g;
+    return stacked_shape(kv, &g) ? g.npb * 16 : 0;
+}
+
+int launch_relpos_bd(const pk_paged_kv *kv, const AttnArgs &a, float *bd, cudaStream_t s) {
+    SGeom g;
+    if (!stacked_shape(kv, &g)) return PK_ENOTSUP;
+    if (a.batch == 0 || a.nlayers == 0) return PK_OK;
+    dim3 grid(a.nlayers, kv->d.num_heads, (a.batch * kv->d.chunk + 63) / 64);
+    return cuda_status(launch_pdl(relpos_bd_kernel, grid, dim3(128), 0, s, kv->d, a, g.npb * 16, bd),
+                       "relpos_bd_kernel");
+}
+
+int launch_attention_stacked(const pk_paged_kv *kv, const CUtensorMap &pos_map16,
+                             const AttnArgs &a, cudaStream_t s) {
+    (void)pos_map16;   // the rel-pos rows are read through a.pos (or a.bd)
+    const pk_paged_kv_desc &d = kv->d;
     constexpr int NS = kStages;
     SGeom g;
-    g.num_layers = d.num_layers;
-    g.left = d.left;
-    g.chunk = d.chunk;
-    g.W = d.left + d.chunk;
-    g.R = g.W + d.chunk - 1;
-    g.npb = (g.R + 15) / 16;
-    g.max_boxes = pk_pages_per_stream(d.left, d.chunk, d.page_size);
-    if (g.max_boxes > kMaxBoxes || g.npb > kMaxPosBlocks) return PK_ENOTSUP;
+    if (!stacked_shape(kv, &g)) return PK_ENOTSUP;
     g.stage_bytes = kH * kBox;
     g.off_s = NS * g.stage_bytes;
     g.off_bd = g.off_s + kMaxBoxes * 16 * 16 * 4;
@@ -421,7 +552,7 @@ int launch_attention_stacked(const pk_paged_kv *kv, const CUtensorMap &pos_map16
     }
     dim3 grid(a.batch, a.nlayers, d.num_heads / kH);
     return cuda_status(launch_pdl(paged_attn_stacked_kernel<NS>, grid, dim3(kThreads), smem, s,
-                                  kv->kv_map, pos_map16, g, d, a),
+                                  kv->kv_map, g, d, a),
                        "paged_attn_stacked_kernel");
 }
 

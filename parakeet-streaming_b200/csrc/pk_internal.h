@@ -67,6 +67,10 @@ struct AttnArgs {
     const void *k_new, *v_new;   // optional: this step's K/V rows (q's strides) to append
     const void *bias_u, *bias_v;
     int64_t bias_ls;
+    const void *pos;             // pos_proj rows (l, p, c) at l * pos_ls + p * dim + c
+    int64_t pos_ls;
+    int pos_rows;                // 2 * (left + chunk) - 1
+    const float *bd;             // optional: rel-pos term from launch_relpos_bd (replaces pos)
     const int32_t *slots, *lengths;
     int batch;
     void *out;
@@ -82,6 +86,11 @@ int launch_attention_bf16(const pk_paged_kv *kv, const CUtensorMap &pos_map, con
 // returns PK_ENOTSUP for other shapes.  pos_map16 has 16-row boxes.
 int launch_attention_stacked(const pk_paged_kv *kv, const CUtensorMap &pos_map16,
                              const AttnArgs &a, cudaStream_t s);
+// pk_attn_stacked.cu: the rel-pos term of every (layer, stream, head, query) of a
+// step, bd[l][b][h][t][relpos_bd_cols], for the shapes launch_attention_stacked
+// handles (PK_ENOTSUP otherwise); reads a.q, a.bias_v, a.pos.
+int relpos_bd_cols(const pk_paged_kv *kv);
+int launch_relpos_bd(const pk_paged_kv *kv, const AttnArgs &a, float *bd, cudaStream_t s);
 // pk_attn_heads.cu: head_dim 128, chunks of 8..16 frames, K/V appended before;
 // returns PK_ENOTSUP for other shapes.  pos_map16 has 16-row boxes of 64 columns.
 int launch_attention_heads(const pk_paged_kv *kv, const CUtensorMap &pos_map16,

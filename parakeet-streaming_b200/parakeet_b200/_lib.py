@@ -92,6 +92,10 @@ SIGNATURES = {
     "pk_pre_encode_window": [_P, _I32, _P, _P, _I32, _I32, _I32, _I32, _I32, _P, _I32, _P, _P],
     "pk_paged_attention": [_P, _I32, _I32, _P, _I64, _I64, _I64, _P, _P, _P, _I64, _P, _P,
                            _I64, _P, _P, _I32, _P, _I64, _I64, _I64, _P],
+    "pk_relpos_bd_cols": [_P],
+    "pk_relpos_bd": [_P, _I32, _I32, _P, _I64, _I64, _I64, _P, _I64, _P, _I64, _I32, _P, _P],
+    "pk_paged_attention_bd": [_P, _I32, _I32, _P, _I64, _I64, _I64, _P, _P, _P, _P, _I64, _P, _P,
+                              _I32, _P, _I64, _I64, _I64, _P],
     "pk_conv_step": [_P, _I32, _I32, _I32, _I32, _I32, _I32, _I32, _P, _I64, _I64, _P, _P, _P,
                      ctypes.c_float, _P, _P, _I32, _P, _P, _P],
     "pk_gemm_bf16": [_P, _I64, _P, _I64, _I32, _I32, _I32, _P, _I64, _I32, _P, _I64, _P,

@@ -285,31 +285,79 @@ class PagedKVPool:
                                       _stream(self.device)), "pk_gather_windows")
         return k, v
 
-    def attention(self, layer: int, query: torch.Tensor, pos_proj: torch.Tensor,
-                  bias_u: torch.Tensor, bias_v: torch.Tensor, slots: torch.Tensor,
-                  lengths: torch.Tensor, out: torch.Tensor | None = None,
-                  key: torch.Tensor | None = None, value: torch.Tensor | None = None):
-        """query [B, T, D] or [nl, B, T, D]; pos_proj [P, D] or [nl, P, D];
-        bias_u/v [H, dh] or [nl, H, dh]; lengths int32 [B].  With key/value
-        (this step's new rows, the query's shape and strides) the append is
-        part of the call.  Returns out with the query's leading shape."""
-        squeeze = query.dim() == 3
-        if squeeze:
-            query, pos_proj = query.unsqueeze(0), pos_proj.unsqueeze(0)
-            bias_u, bias_v = bias_u.unsqueeze(0), bias_v.unsqueeze(0)
-        self._check_rows(query, "query")
+    @property
+    def relpos_bd_cols(self) -> int:
+        """Row length of ``relpos_bd``'s output; 0 when this pool's shape has no
+        all-stream rel-pos pre-pass."""
+        return int(lib().pk_relpos_bd_cols(self._h))
+
+    def _check_attn_inputs(self, query, pos_proj, biases):
         nl, B, T, D = query.shape
         P = 2 * self.window - 1
         if T != self.chunk or D != self.dim:
             raise ValueError(f"query shape {tuple(query.shape)} vs chunk {self.chunk}, dim {self.dim}")
-        if tuple(pos_proj.shape) != (nl, P, D) or not pos_proj[0].is_contiguous():
+        if pos_proj is not None and (tuple(pos_proj.shape) != (nl, P, D) or not pos_proj[0].is_contiguous()):
             raise ValueError(f"pos_proj must be [{nl}, {P}, {D}] with contiguous rows")
         dh = D // self.num_heads
-        for t, n in ((bias_u, "bias_u"), (bias_v, "bias_v")):
+        for t, n in biases:
             if tuple(t.shape) != (nl, self.num_heads, dh) or not t[0].is_contiguous() or t.dtype != self.dtype:
                 raise ValueError(f"{n} must be [{nl}, {self.num_heads}, {dh}] {self.dtype}")
-        if bias_u.stride(0) != bias_v.stride(0):
-            raise ValueError("bias_u/bias_v layer strides differ")
+
+    def relpos_bd(self, layer: int, query: torch.Tensor, pos_proj: torch.Tensor,
+                  bias_v: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """The rel-pos term (q + pos_bias_v) pos_proj^T of every (layer, stream,
+        head, query row), fp32 [nl, B, H, T, relpos_bd_cols], for
+        ``attention(..., bd=...)``: one pass over all streams, which share the
+        layer's pos_proj rows.  Shapes as in ``attention``."""
+        squeeze = query.dim() == 3
+        if squeeze:
+            query, pos_proj, bias_v = query.unsqueeze(0), pos_proj.unsqueeze(0), bias_v.unsqueeze(0)
+        self._check_rows(query, "query")
+        self._check_attn_inputs(query, pos_proj, ((bias_v, "bias_v"),))
+        nl, B, T, _ = query.shape
+        cols = self.relpos_bd_cols
+        if cols == 0:
+            raise _lib.PKError("relpos_bd: no all-stream pre-pass for this pool's shape")
+        shape = (nl, B, self.num_heads, T, cols)
+        if out is None:
+            out = torch.empty(shape, dtype=torch.float32, device=self.device)
+        elif tuple(out.shape) != shape or out.dtype != torch.float32 or not out.is_contiguous():
+            raise ValueError(f"out must be contiguous float32 {shape}")
+        check(lib().pk_relpos_bd(
+            self._h, layer, nl, query.data_ptr(), query.stride(0), query.stride(1), query.stride(2),
+            pos_proj.data_ptr(), pos_proj.stride(0), bias_v.data_ptr(), bias_v.stride(0), B,
+            out.data_ptr(), _stream(self.device)), "pk_relpos_bd")
+        return out
+
+    def attention(self, layer: int, query: torch.Tensor, pos_proj: torch.Tensor | None,
+                  bias_u: torch.Tensor, bias_v: torch.Tensor | None, slots: torch.Tensor,
+                  lengths: torch.Tensor, out: torch.Tensor | None = None,
+                  key: torch.Tensor | None = None, value: torch.Tensor | None = None,
+                  bd: torch.Tensor | None = None):
+        """query [B, T, D] or [nl, B, T, D]; pos_proj [P, D] or [nl, P, D];
+        bias_u/v [H, dh] or [nl, H, dh]; lengths int32 [B].  With key/value
+        (this step's new rows, the query's shape and strides) the append is
+        part of the call.  With ``bd`` (``relpos_bd``'s output for the same
+        query) pos_proj and bias_v are not read.  Returns out with the query's
+        leading shape."""
+        squeeze = query.dim() == 3
+        if squeeze:
+            query, bias_u = query.unsqueeze(0), bias_u.unsqueeze(0)
+            if bd is None:
+                pos_proj, bias_v = pos_proj.unsqueeze(0), bias_v.unsqueeze(0)
+            elif bd.dim() == 4:
+                bd = bd.unsqueeze(0)
+        self._check_rows(query, "query")
+        nl, B, T, D = query.shape
+        if bd is None:
+            self._check_attn_inputs(query, pos_proj, ((bias_u, "bias_u"), (bias_v, "bias_v")))
+            if bias_u.stride(0) != bias_v.stride(0):
+                raise ValueError("bias_u/bias_v layer strides differ")
+        else:
+            self._check_attn_inputs(query, None, ((bias_u, "bias_u"),))
+            shape = (nl, B, self.num_heads, T, self.relpos_bd_cols)
+            if tuple(bd.shape) != shape or bd.dtype != torch.float32 or not bd.is_contiguous():
+                raise ValueError(f"bd must be contiguous float32 {shape} (relpos_bd's output)")
         if out is None:
             out = torch.empty((nl, B, T, D), dtype=self.dtype, device=self.device)
         elif out.dim() == 3:
@@ -323,6 +371,13 @@ class PagedKVPool:
             if key.shape != query.shape or key.stride() != query.stride() or value.stride() != query.stride():
                 raise ValueError("key/value must have the query's shape and strides")
             kp, vp = key.data_ptr(), value.data_ptr()
+        if bd is not None:
+            check(lib().pk_paged_attention_bd(
+                self._h, layer, nl, query.data_ptr(), query.stride(0), query.stride(1),
+                query.stride(2), kp, vp, bd.data_ptr(), bias_u.data_ptr(), bias_u.stride(0),
+                slots.data_ptr(), lengths.data_ptr(), B, out.data_ptr(), out.stride(0),
+                out.stride(1), out.stride(2), _stream(self.device)), "pk_paged_attention_bd")
+            return out[0] if squeeze else out
         check(lib().pk_paged_attention(
             self._h, layer, nl, query.data_ptr(), query.stride(0), query.stride(1),
             query.stride(2), kp, vp, pos_proj.data_ptr(), pos_proj.stride(0), bias_u.data_ptr(),

@@ -93,9 +93,10 @@ def test_pool_exhaustion_sets_error_bit_and_allocates_nothing():
 
 
 def run_stream_steps(shape, dtype, steps, n_slots, seed, check_every=1, short_last=True,
-                     fused=False):
+                     fused=False, prepass=False):
     """Staggered streams through append + gather + attention, against the
-    oracle's dense slot pool (pack -> update_attn_cache -> unpack) and masks."""
+    oracle's dense slot pool (pack -> update_attn_cache -> unpack) and masks.
+    prepass: the rel-pos term comes from the all-stream pre-pass (relpos_bd)."""
     cfg = SHAPES[shape]
     att, D, H = cfg["att"], cfg["dim"], cfg["heads"]
     left, T = att[0], att[1] + 1
@@ -127,7 +128,10 @@ def run_stream_steps(shape, dtype, steps, n_slots, seed, check_every=1, short_la
             qkv = to(rng.standard_normal((len(batch), T, 3 * D)) / 8)
             q, k, v = qkv[..., :D], qkv[..., D:2 * D], qkv[..., 2 * D:]
             kw_ref, vw_ref = st.cache.update_attn_cache(l, rd(k), rd(v))
-            if fused:   # the append happens inside the attention call
+            if prepass:
+                bd = pool.relpos_bd(l, q, pos_t[l], bv_t[l])
+                out = pool.attention(l, q, None, bu_t[l], None, sl, ln, key=k, value=v, bd=bd)
+            elif fused:   # the append happens inside the attention call
                 out = pool.attention(l, q, pos_t[l], bu_t[l], bv_t[l], sl, ln, key=k, value=v)
             else:
                 pool.append(l, k, v, sl)
@@ -167,6 +171,50 @@ def test_append_gather_attention_small(dtype, fused):
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_append_gather_attention_large(dtype, fused):
     run_stream_steps("large", dtype, steps=9, n_slots=3, seed=4, fused=fused)
+
+
+def test_append_gather_attention_small_relpos_prepass():
+    run_stream_steps("small", torch.bfloat16, steps=44, n_slots=5, seed=3, check_every=5,
+                     prepass=True)
+
+
+def test_relpos_prepass_matches_in_kernel_term():
+    """All layers in one call: relpos_bd + attention(bd=) gives the attention
+    output of the in-kernel rel-pos term bit for bit (both run the same
+    fragment code), and the pre-pass term itself matches float64 on the
+    bf16-rounded operands."""
+    cfg = SHAPES["small"]
+    att, D, H = cfg["att"], cfg["dim"], cfg["heads"]
+    left, T = att[0], att[1] + 1
+    L, n_slots, dh = 3, 7, D // H
+    P = 2 * (left + T) - 1
+    rng = np.random.default_rng(21)
+    order = rng.permutation(n_slots * pages.pages_per_stream(left, T, 16))
+    pa, pb = (PagedKVPool(L, D, H, att, n_slots, dtype=torch.bfloat16, device=DEV, page_order=order)
+              for _ in range(2))
+    assert pa.relpos_bd_cols == 80
+    to = lambda a: torch.tensor(np.asarray(a), dtype=torch.bfloat16, device=DEV)  # noqa: E731
+    pos = to(rng.standard_normal((L, P, D)) / 8)
+    bu, bv = to(rng.standard_normal((L, H, dh)) / 8), to(rng.standard_normal((L, H, dh)) / 8)
+    slots = torch.tensor([4, 0, 6, 2, 5], dtype=torch.int32, device=DEV)
+    B = slots.numel()
+    ln = torch.full((B,), T, dtype=torch.int32, device=DEV)
+    for step in range(7):
+        qkv = to(rng.standard_normal((L, B, T, 3 * D)) / 8)
+        q, k, v = qkv[..., :D], qkv[..., D:2 * D], qkv[..., 2 * D:]
+        pa.begin_step(slots, ln)
+        pb.begin_step(slots, ln)
+        oa = pa.attention(0, q, pos, bu, bv, slots, ln, key=k, value=v)
+        bd = pb.relpos_bd(0, q, pos, bv)
+        ob = pb.attention(0, q, None, bu, None, slots, ln, key=k, value=v, bd=bd)
+        pa.end_step(slots, ln)
+        pb.end_step(slots, ln)
+        assert torch.equal(oa, ob), step
+        x = (q.double() + bv.double()[:, None, None].reshape(L, 1, 1, D)).to(torch.bfloat16).double()
+        ref = torch.einsum("lbthd,lrhd->lbhtr", x.reshape(L, B, T, H, dh),
+                           pos.double()[:, :80].reshape(L, 80, H, dh))
+        assert rel_l2(bd.double().cpu().numpy(), ref.cpu().numpy()) <= 1e-5, step
+    assert pa.read_error() == 0 and pb.read_error() == 0
 
 
 def conv_oracle(x2d, cache, w, lengths, g, b, eps=1e-5):
