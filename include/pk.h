@@ -226,6 +226,31 @@ int pk_paged_attention_bd(pk_paged_kv *kv, int32_t layer0, int32_t num_layers,
                           void *out, int64_t out_layer_stride, int64_t out_batch_stride,
                           int64_t out_row_stride, void *stream);
 
+/* Bytes of the static rel-pos scratch that pk_paged_attention_noalloc uses
+ * (one device array per device, part of every context that loads libpk). */
+int64_t pk_relpos_scratch_bytes(void);
+
+/* pk_paged_attention with pk_paged_attention's arguments, outputs and
+ * replaced calls, computed as pk_relpos_bd + pk_paged_attention_bd with the
+ * rel-pos term in a static device array instead of a caller buffer: the call
+ * allocates nothing.  Shapes without the pre-pass run pk_paged_attention
+ * (which needs no scratch).  Returns PK_EINVAL when the term,
+ * num_layers * batch * heads * chunk * pk_relpos_bd_cols * 4 bytes, exceeds
+ * pk_relpos_scratch_bytes().  Calls on one device share the array: order
+ * them on one stream.  Replaces ConformerAttention.forward lines 99-122
+ * (parakeet/modules/attention.py) and ModelCache.update_attn_cache
+ * (cache.py:36-45) as pk_paged_attention does. */
+int pk_paged_attention_noalloc(pk_paged_kv *kv, int32_t layer0, int32_t num_layers,
+                               const void *query, int64_t q_layer_stride,
+                               int64_t q_batch_stride, int64_t q_row_stride,
+                               const void *key, const void *value,
+                               const void *pos_proj, int64_t pos_layer_stride,
+                               const void *bias_u, const void *bias_v,
+                               int64_t bias_layer_stride, const int32_t *slots,
+                               const int32_t *lengths, int32_t batch, void *out,
+                               int64_t out_layer_stride, int64_t out_batch_stride,
+                               int64_t out_row_stride, void *stream);
+
 /* Depthwise causal conv step with its time cache, one layer:
  *   GLU over the pw-conv1 output x (l=0: [batch][chunk][2*dim] with
  *   x_batch_stride / x_row_stride) -> zero rows t >= length -> depthwise conv

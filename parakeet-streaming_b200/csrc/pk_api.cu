@@ -404,6 +404,68 @@ int pk_paged_attention_bd(pk_paged_kv *kv, int32_t layer0, int32_t num_layers, c
     return launch_attention_stacked(kv, unused, a, static_cast<cudaStream_t>(stream));
 }
 
+// Rel-pos scratch of pk_paged_attention_noalloc: a static device array, so
+// the call allocates nothing; every context that loads this library holds one
+// copy per device, and its address is looked up once per device.
+constexpr uint64_t kRelposScratchBytes = 32ull << 20;
+__device__ __align__(256) float g_relpos_scratch[kRelposScratchBytes / sizeof(float)];
+
+static int relpos_scratch(float **out) {
+    constexpr int kMaxDevices = 64;
+    static float *ptrs[kMaxDevices] = {};
+    static std::mutex mu;
+    int dev = -1;
+    int st = cuda_status(cudaGetDevice(&dev), "cudaGetDevice");
+    if (st != PK_OK) return st;
+    if (dev < 0 || dev >= kMaxDevices) {
+        set_error("device %d above the %d the scratch table holds", dev, kMaxDevices);
+        return PK_ENOTSUP;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    if (!ptrs[dev]) {
+        void *p = nullptr;
+        st = cuda_status(cudaGetSymbolAddress(&p, g_relpos_scratch), "cudaGetSymbolAddress");
+        if (st != PK_OK) return st;
+        ptrs[dev] = static_cast<float *>(p);
+    }
+    *out = ptrs[dev];
+    return PK_OK;
+}
+
+int64_t pk_relpos_scratch_bytes(void) { return (int64_t)kRelposScratchBytes; }
+
+int pk_paged_attention_noalloc(pk_paged_kv *kv, int32_t layer0, int32_t num_layers,
+                               const void *query, int64_t q_layer_stride, int64_t q_batch_stride,
+                               int64_t q_row_stride, const void *key, const void *value,
+                               const void *pos_proj, int64_t pos_layer_stride, const void *bias_u,
+                               const void *bias_v, int64_t bias_layer_stride,
+                               const int32_t *slots, const int32_t *lengths, int32_t batch,
+                               void *out, int64_t out_layer_stride, int64_t out_batch_stride,
+                               int64_t out_row_stride, void *stream) {
+    PK_CHECK(kv, "null pool");
+    const int cols = relpos_bd_cols(kv);
+    if (cols == 0 || batch <= 0 || num_layers <= 0)   // the in-kernel rel-pos term needs no scratch
+        return pk_paged_attention(kv, layer0, num_layers, query, q_layer_stride, q_batch_stride,
+                                  q_row_stride, key, value, pos_proj, pos_layer_stride, bias_u,
+                                  bias_v, bias_layer_stride, slots, lengths, batch, out,
+                                  out_layer_stride, out_batch_stride, out_row_stride, stream);
+    const uint64_t need = (uint64_t)num_layers * batch * kv->d.num_heads * kv->d.chunk * cols *
+                          sizeof(float);
+    PK_CHECK(need <= kRelposScratchBytes,
+             "rel-pos term of %d layers x %d streams needs %llu bytes; the static scratch holds %llu",
+             num_layers, batch, (unsigned long long)need, (unsigned long long)kRelposScratchBytes);
+    float *scratch = nullptr;
+    int st = relpos_scratch(&scratch);
+    if (st != PK_OK) return st;
+    st = pk_relpos_bd(kv, layer0, num_layers, query, q_layer_stride, q_batch_stride, q_row_stride,
+                      pos_proj, pos_layer_stride, bias_v, bias_layer_stride, batch, scratch, stream);
+    if (st != PK_OK) return st;
+    return pk_paged_attention_bd(kv, layer0, num_layers, query, q_layer_stride, q_batch_stride,
+                                 q_row_stride, key, value, scratch, bias_u, bias_layer_stride,
+                                 slots, lengths, batch, out, out_layer_stride, out_batch_stride,
+                                 out_row_stride, stream);
+}
+
 int pk_conv_step(void *conv_state, int32_t num_slots, int32_t num_layers, int32_t layer,
                  int32_t dim, int32_t kernel, int32_t chunk, int32_t dtype, const void *x,
                  int64_t x_batch_stride, int64_t x_row_stride, const void *weight,

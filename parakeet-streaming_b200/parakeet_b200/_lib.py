@@ -96,6 +96,9 @@ SIGNATURES = {
     "pk_relpos_bd": [_P, _I32, _I32, _P, _I64, _I64, _I64, _P, _I64, _P, _I64, _I32, _P, _P],
     "pk_paged_attention_bd": [_P, _I32, _I32, _P, _I64, _I64, _I64, _P, _P, _P, _P, _I64, _P, _P,
                               _I32, _P, _I64, _I64, _I64, _P],
+    "pk_relpos_scratch_bytes": [],
+    "pk_paged_attention_noalloc": [_P, _I32, _I32, _P, _I64, _I64, _I64, _P, _P, _P, _I64, _P,
+                                   _P, _I64, _P, _P, _I32, _P, _I64, _I64, _I64, _P],
     "pk_conv_step": [_P, _I32, _I32, _I32, _I32, _I32, _I32, _I32, _P, _I64, _I64, _P, _P, _P,
                      ctypes.c_float, _P, _P, _I32, _P, _P, _P],
     "pk_gemm_bf16": [_P, _I64, _P, _I64, _I32, _I32, _I32, _P, _I64, _I32, _P, _I64, _P,
@@ -111,7 +114,7 @@ SIGNATURES = {
                          _P, _P],
     "pk_last_error": [],
 }
-RESTYPES = {"pk_last_error": ctypes.c_char_p}
+RESTYPES = {"pk_last_error": ctypes.c_char_p, "pk_relpos_scratch_bytes": ctypes.c_int64}
 
 _lib = None
 

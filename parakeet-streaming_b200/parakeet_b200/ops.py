@@ -333,13 +333,15 @@ class PagedKVPool:
                   bias_u: torch.Tensor, bias_v: torch.Tensor | None, slots: torch.Tensor,
                   lengths: torch.Tensor, out: torch.Tensor | None = None,
                   key: torch.Tensor | None = None, value: torch.Tensor | None = None,
-                  bd: torch.Tensor | None = None):
+                  bd: torch.Tensor | None = None, noalloc: bool = False):
         """query [B, T, D] or [nl, B, T, D]; pos_proj [P, D] or [nl, P, D];
         bias_u/v [H, dh] or [nl, H, dh]; lengths int32 [B].  With key/value
         (this step's new rows, the query's shape and strides) the append is
         part of the call.  With ``bd`` (``relpos_bd``'s output for the same
-        query) pos_proj and bias_v are not read.  Returns out with the query's
-        leading shape."""
+        query) pos_proj and bias_v are not read.  ``noalloc``: the rel-pos
+        pre-pass into the library's static device scratch
+        (pk_paged_attention_noalloc; calls on one device share it, so keep
+        them on one stream).  Returns out with the query's leading shape."""
         squeeze = query.dim() == 3
         if squeeze:
             query, bias_u = query.unsqueeze(0), bias_u.unsqueeze(0)
@@ -378,12 +380,13 @@ class PagedKVPool:
                 slots.data_ptr(), lengths.data_ptr(), B, out.data_ptr(), out.stride(0),
                 out.stride(1), out.stride(2), _stream(self.device)), "pk_paged_attention_bd")
             return out[0] if squeeze else out
-        check(lib().pk_paged_attention(
+        name = "pk_paged_attention_noalloc" if noalloc else "pk_paged_attention"
+        check(getattr(lib(), name)(
             self._h, layer, nl, query.data_ptr(), query.stride(0), query.stride(1),
             query.stride(2), kp, vp, pos_proj.data_ptr(), pos_proj.stride(0), bias_u.data_ptr(),
             bias_v.data_ptr(), bias_u.stride(0), slots.data_ptr(), lengths.data_ptr(), B,
             out.data_ptr(), out.stride(0), out.stride(1), out.stride(2), _stream(self.device)),
-            "pk_paged_attention")
+            name)
         return out[0] if squeeze else out
 
     def conv_step(self, layer: int, x: torch.Tensor, weight: torch.Tensor, slots: torch.Tensor,
