@@ -1114,8 +1114,19 @@ def main():
     if world > 1:
         dist.barrier()
     eager_ms = e0.elapsed_time(e1) / K
-    attn_ms = sum(e[0].elapsed_time(e[1]) for e in evs) / K
-    bd_ms = sum(e[2].elapsed_time(e[3]) for e in evs) / K if prepass else 0.0
+    # (a') eager steps queued behind a GPU-side spin: the host enqueues a step
+    # more slowly than the GPU runs it, so in (a) the events around a launch
+    # also time the host's gap before it; queued, the kernels run back to back
+    # and the events time the launches alone (roofline.avg_launch_ms)
+    KQ = min(K, 48)
+    evq = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(4)) for _ in range(KQ)]
+    torch.cuda.synchronize()
+    torch.cuda._sleep(int((2e-3 + 2 * KQ * eager_ms * 1e-3) * 2.0e9))   # cycles at <= 2 GHz
+    for i in range(KQ):
+        step(qkv[i % NBUF], evq[i])
+    torch.cuda.synchronize()
+    attn_ms = sum(e[0].elapsed_time(e[1]) for e in evq) / KQ
+    bd_ms = sum(e[2].elapsed_time(e[3]) for e in evq) / KQ if prepass else 0.0
 
     # (b) the same steps replayed as CUDA graphs (one graph per input buffer): `value`
     ms = eager_ms

@@ -111,46 +111,59 @@ __device__ __forceinline__ void bd_a_words(const __nv_bfloat16 *q_row,
     }
 }
 
-// n-tiles (8 rel-pos rows) whose B fragments one batch of loads brings in:
-// 5 inside the attention kernel (register budget), 10 (all of them at the
-// small config) in the pre-pass
+// n-tiles (8 rel-pos rows) whose B fragments one batch of loads brings in
+// (5: half of the small config's 10, within the attention kernel's registers;
+// the pre-pass gives each warp half of the n-tiles)
 constexpr int kBdBatch = 5;
-constexpr int kBdBatchPrepass = 10;
 
 // BD of the m16 tile's rows gq (xa) and gq + 8 (xb) against rel-pos rows
 // [0, 8 * ntiles) (rows >= pos_rows read as zero); p_base = the layer's P at
 // row 0, offset by the head and by 16 tq, rows dim elements apart.
 // store(nt, c) receives n-tile nt's accumulators (row gq: c[0..1], row gq + 8:
 // c[2..3], columns nt * 8 + 2 tq + {0, 1}).
+// B fragments of n-tiles [nt0, nt0 + NB) (those < ntiles) into pw
+template <int NB>
+__device__ __forceinline__ void bd_load_p(uint4 (&pw)[NB][2], const __nv_bfloat16 *p_base, int dim,
+                                          int pos_rows, int nt0, int ntiles, int gq) {
+#pragma unroll
+    for (int i = 0; i < NB; ++i) {
+        const int r = (nt0 + i) * 8 + gq;
+        pw[i][0] = pw[i][1] = make_uint4(0, 0, 0, 0);
+        if (nt0 + i < ntiles && r < pos_rows) {
+            const uint4 *src = reinterpret_cast<const uint4 *>(p_base + (int64_t)r * dim);
+            pw[i][0] = __ldg(src);
+            pw[i][1] = __ldg(src + 1);
+        }
+    }
+}
+
+// the MMAs of those n-tiles, k-steps in order, each n-tile's result to store
+template <int NB, class Store>
+__device__ __forceinline__ void bd_mma_p(const uint4 (&pw)[NB][2], const uint32_t (&xa)[8],
+                                         const uint32_t (&xb)[8], int nt0, int ntiles, Store store) {
+#pragma unroll
+    for (int i = 0; i < NB; ++i) {
+        if (nt0 + i >= ntiles) break;
+        const uint32_t pv[8] = {pw[i][0].x, pw[i][0].y, pw[i][0].z, pw[i][0].w,
+                                pw[i][1].x, pw[i][1].y, pw[i][1].z, pw[i][1].w};
+        float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+            const uint32_t af[4] = {xa[2 * ks], xb[2 * ks], xa[2 * ks + 1], xb[2 * ks + 1]};
+            mma_bf16(c, af, pv[2 * ks], pv[2 * ks + 1]);
+        }
+        store(nt0 + i, c);
+    }
+}
+
 template <int NB, class Store>
 __device__ __forceinline__ void bd_tile(const uint32_t (&xa)[8], const uint32_t (&xb)[8],
                                         const __nv_bfloat16 *p_base, int dim, int pos_rows,
                                         int ntiles, int gq, Store store) {
     for (int nt0 = 0; nt0 < ntiles; nt0 += NB) {
         uint4 pw[NB][2];
-#pragma unroll
-        for (int i = 0; i < NB; ++i) {
-            const int r = (nt0 + i) * 8 + gq;
-            pw[i][0] = pw[i][1] = make_uint4(0, 0, 0, 0);
-            if (nt0 + i < ntiles && r < pos_rows) {
-                const uint4 *src = reinterpret_cast<const uint4 *>(p_base + (int64_t)r * dim);
-                pw[i][0] = __ldg(src);
-                pw[i][1] = __ldg(src + 1);
-            }
-        }
-#pragma unroll
-        for (int i = 0; i < NB; ++i) {
-            if (nt0 + i >= ntiles) break;
-            const uint32_t pv[8] = {pw[i][0].x, pw[i][0].y, pw[i][0].z, pw[i][0].w,
-                                    pw[i][1].x, pw[i][1].y, pw[i][1].z, pw[i][1].w};
-            float c[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-            for (int ks = 0; ks < 4; ++ks) {
-                const uint32_t af[4] = {xa[2 * ks], xb[2 * ks], xa[2 * ks + 1], xb[2 * ks + 1]};
-                mma_bf16(c, af, pv[2 * ks], pv[2 * ks + 1]);
-            }
-            store(nt0 + i, c);
-        }
+        bd_load_p<NB>(pw, p_base, dim, pos_rows, nt0, ntiles, gq);
+        bd_mma_p<NB>(pw, xa, xb, nt0, ntiles, store);
     }
 }
 
@@ -457,45 +470,54 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     }
 }
 
-// grid (num_layers, num_heads, ceil(batch * chunk / 64)), 128 threads: warp w
-// computes BD of the (stream, query) rows [64 z + 16 w, 64 z + 16 w + 16) of one
-// (layer, head) - every stream of a layer uses the same rel-pos rows, read once
-// per CTA here instead of once per (stream, head group) in the attention kernel.
-__global__ void __launch_bounds__(128)
+// grid (num_layers, num_heads, ceil(batch * chunk / 32)), 128 threads: warp w
+// computes BD of the (stream, query) rows [32 z + 16 (w / 2), +16) of one
+// (layer, head) against the first (w even) or second half of the rel-pos
+// n-tiles - every stream of a layer uses the same rel-pos rows, read once per
+// CTA here instead of once per (stream, head group) in the attention kernel.
+__global__ void __launch_bounds__(128, 5)   // 5 CTAs per SM: the small step in one wave
     relpos_bd_kernel(const pk_paged_kv_desc d, const AttnArgs a, int bds, float *bd) {
     using T = __nv_bfloat16;
     const int lrel = blockIdx.x, hh = blockIdx.y;
     const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
     const int gq = lane / 4, tq = lane % 4;
     const int chunk = d.chunk, rows = a.batch * chunk;
-    const int m0 = blockIdx.z * 64 + warp * 16;
+    const int m0 = blockIdx.z * 32 + (warp >> 1) * 16;
+    const int nt_all = bds / 8, nt_half = (nt_all + 1) / 2;
+    const int nt_begin = (warp & 1) ? nt_half : 0;
+    const int nt_count = (warp & 1) ? nt_all - nt_half : nt_half;   // <= kBdBatch (launch check)
     grid_dep_wait();     // q may come from the previous kernel
     grid_dep_launch();   // the attention kernel waits for all of us
     if (m0 >= rows) return;
+    // the rel-pos rows first: their loads do not wait for the query arithmetic
+    const T *p_base = static_cast<const T *>(a.pos) + (int64_t)lrel * a.pos_ls +
+                      (int64_t)nt_begin * 8 * d.dim + hh * 64 + 16 * tq;
+    const int p_rows = a.pos_rows - nt_begin * 8;
+    uint4 pw[kBdBatch][2];
+    bd_load_p<kBdBatch>(pw, p_base, d.dim, p_rows, 0, nt_count, gq);
     const __nv_bfloat162 *bv2 = reinterpret_cast<const __nv_bfloat162 *>(
         static_cast<const T *>(a.bias_v) + (int64_t)lrel * a.bias_ls + hh * 64 + 16 * tq);
-    auto q_row = [&](int m) -> const T * {
-        if (m >= rows) return nullptr;
-        const int b = m / chunk, t = m - b * chunk;
-        return static_cast<const T *>(a.q) + (int64_t)lrel * a.q_ls + (int64_t)b * a.q_bs +
-               (int64_t)t * a.q_rs + hh * 64 + 16 * tq;
-    };
-    uint32_t xa[8], xb[8];
-    bd_a_words(q_row(m0 + gq), bv2, xa);
-    bd_a_words(q_row(m0 + gq + 8), bv2, xb);
-    const T *p_base = static_cast<const T *>(a.pos) + (int64_t)lrel * a.pos_ls + hh * 64 + 16 * tq;
-    float *out = bd + (int64_t)lrel * rows * d.num_heads * bds;   // [batch][heads][chunk][bds]
-    bd_tile<kBdBatchPrepass>(xa, xb, p_base, d.dim, a.pos_rows, bds / 8, gq,
-                             [&](int nt, const float (&c)[4]) {
+    // rows gq and gq + 8 of the tile: their query rows and their BD output rows
+    const T *qr[2] = {nullptr, nullptr};
+    float *orow[2] = {nullptr, nullptr};
 #pragma unroll
-        for (int rh = 0; rh < 2; ++rh) {
-            const int m = m0 + gq + 8 * rh;
-            if (m < rows) {
-                const int b = m / chunk, t = m - b * chunk;
-                *reinterpret_cast<float2 *>(out + ((int64_t)(b * d.num_heads + hh) * chunk + t) * bds +
-                                            nt * 8 + 2 * tq) = make_float2(c[2 * rh], c[2 * rh + 1]);
-            }
+    for (int rh = 0; rh < 2; ++rh) {
+        const int m = m0 + gq + 8 * rh;
+        if (m < rows) {
+            const int b = m / chunk, t = m - b * chunk;
+            qr[rh] = static_cast<const T *>(a.q) + (int64_t)lrel * a.q_ls + (int64_t)b * a.q_bs +
+                     (int64_t)t * a.q_rs + hh * 64 + 16 * tq;
+            // [layer][batch][heads][chunk][bds], from this warp's first n-tile
+            orow[rh] = bd + (((int64_t)lrel * a.batch + b) * d.num_heads + hh) * chunk * bds +
+                       (int64_t)t * bds + nt_begin * 8 + 2 * tq;
         }
+    }
+    uint32_t xa[8], xb[8];
+    bd_a_words(qr[0], bv2, xa);
+    bd_a_words(qr[1], bv2, xb);
+    bd_mma_p<kBdBatch>(pw, xa, xb, 0, nt_count, [&](int nt, const float (&c)[4]) {
+        if (orow[0]) *reinterpret_cast<float2 *>(orow[0] + nt * 8) = make_float2(c[0], c[1]);
+        if (orow[1]) *reinterpret_cast<float2 *>(orow[1] + nt * 8) = make_float2(c[2], c[3]);
     });
 }
 
@@ -517,15 +539,15 @@ bool stacked_shape(const pk_paged_kv *kv, SGeom *g) {
 }  // namespace
 
 int relpos_bd_cols(const pk_paged_kv *kv) {
-    SGeom g;
-    return stacked_shape(kv, &g) ? g.npb * 16 : 0;
+    SGeom g;   // a pre-pass warp holds half of the 2 * npb n-tiles in registers
+    return stacked_shape(kv, &g) && g.npb <= kBdBatch ? g.npb * 16 : 0;
 }
 
 int launch_relpos_bd(const pk_paged_kv *kv, const AttnArgs &a, float *bd, cudaStream_t s) {
     SGeom g;
-    if (!stacked_shape(kv, &g)) return PK_ENOTSUP;
+    if (!stacked_shape(kv, &g) || g.npb > kBdBatch) return PK_ENOTSUP;
     if (a.batch == 0 || a.nlayers == 0) return PK_OK;
-    dim3 grid(a.nlayers, kv->d.num_heads, (a.batch * kv->d.chunk + 63) / 64);
+    dim3 grid(a.nlayers, kv->d.num_heads, (a.batch * kv->d.chunk + 31) / 32);
     return cuda_status(launch_pdl(relpos_bd_kernel, grid, dim3(128), 0, s, kv->d, a, g.npb * 16, bd),
                        "relpos_bd_kernel");
 }
