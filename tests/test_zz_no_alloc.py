@@ -76,3 +76,35 @@ def test_noalloc_refuses_a_term_above_the_static_scratch():
         pool.attention(0, q, pos, bu, bv, slots, ln, noalloc=True)
     torch.cuda.synchronize()
     assert pool.read_error() == 0
+
+
+@pytest.mark.parametrize("dtype,att,dim", [(torch.float32, (70, 1), 512),
+                                           (torch.bfloat16, (70, 13), 1024)])
+def test_shapes_without_prepass(dtype, att, dim):
+    """fp32 pools and the large shape have no pre-pass: relpos_bd_cols is 0,
+    relpos_bd raises, and the no-allocation entry point runs pk_paged_attention
+    itself (identical output on identical pools)."""
+    left, T = att[0], att[1] + 1
+    P, n_slots, nl = 2 * (left + T) - 1, 3, 2
+    rng = np.random.default_rng(8)
+    order = rng.permutation(n_slots * pages.pages_per_stream(left, T, 16))
+    a, b = (PagedKVPool(nl, dim, H, att, n_slots, dtype=dtype, device=DEV, page_order=order)
+            for _ in range(2))
+    assert a.relpos_bd_cols == 0
+    to = lambda x: torch.tensor(np.asarray(x), dtype=dtype, device=DEV)  # noqa: E731
+    pos = to(rng.standard_normal((nl, P, dim)) / 8)
+    bu, bv = to(rng.standard_normal((nl, H, dim // H)) / 8), to(rng.standard_normal((nl, H, dim // H)) / 8)
+    slots = torch.tensor([2, 0], dtype=torch.int32, device=DEV)
+    ln = torch.full((2,), T, dtype=torch.int32, device=DEV)
+    qkv = to(rng.standard_normal((nl, 2, T, 3 * dim)) / 8)
+    q, k, v = qkv[..., :dim], qkv[..., dim:2 * dim], qkv[..., 2 * dim:]
+    with pytest.raises(_lib.PKError):
+        a.relpos_bd(0, q, pos, bv)
+    outs = []
+    for pool, noalloc in ((a, False), (b, True)):
+        pool.begin_step(slots, ln)
+        outs.append(pool.attention(0, q, pos, bu, bv, slots, ln, key=k, value=v, noalloc=noalloc))
+        pool.end_step(slots, ln)
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])
+    assert a.read_error() == 0 and b.read_error() == 0
