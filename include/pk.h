@@ -226,20 +226,30 @@ int pk_paged_attention_bd(pk_paged_kv *kv, int32_t layer0, int32_t num_layers,
                           void *out, int64_t out_layer_stride, int64_t out_batch_stride,
                           int64_t out_row_stride, void *stream);
 
-/* Bytes of the static rel-pos scratch that pk_paged_attention_noalloc uses
- * (one device array per device, part of every context that loads libpk). */
-int64_t pk_relpos_scratch_bytes(void);
+/* Size of the one static device array pk_paged_attention_noalloc works in. */
+#define PK_NOALLOC_SCRATCH_BYTES (32 * 1024 * 1024)
 
-/* pk_paged_attention with pk_paged_attention's arguments, outputs and
- * replaced calls, computed as pk_relpos_bd + pk_paged_attention_bd with the
- * rel-pos term in a static device array instead of a caller buffer: the call
- * allocates nothing.  Shapes without the pre-pass run pk_paged_attention
- * (which needs no scratch).  Returns PK_EINVAL when the term,
- * num_layers * batch * heads * chunk * pk_relpos_bd_cols * 4 bytes, exceeds
- * pk_relpos_scratch_bytes().  Calls on one device share the array: order
- * them on one stream.  Replaces ConformerAttention.forward lines 99-122
- * (parakeet/modules/attention.py) and ModelCache.update_attn_cache
- * (cache.py:36-45) as pk_paged_attention does. */
+/* pk_paged_attention (same arguments, same output) for callers that cannot
+ * allocate device memory: hosts whose device memory is all reserved up front
+ * and owned by another allocator (a framework's caching pool, a fixed memory
+ * cap per process), and latency-bound serving loops that must not call
+ * cudaMalloc / cudaFree, which can block and synchronise the device.  The
+ * rel-pos term that pk_relpos_bd would write into a caller buffer goes into a
+ * static device array of PK_NOALLOC_SCRATCH_BYTES (32 MiB) that every GPU
+ * loading this library holds until the process exits; the call allocates
+ * nothing, with no allocating library routine either.  It has no counterpart
+ * in the reference.
+ *   - limit: PK_EINVAL before any launch when num_layers * batch * heads *
+ *     chunk * pk_relpos_bd_cols * 4 bytes exceeds PK_NOALLOC_SCRATCH_BYTES
+ *     (split the call by layers or streams);
+ *   - the first call on a device looks up the array's device address
+ *     (cudaGetSymbolAddress, with that device current): make that first call
+ *     before any stream capture; the pool must be on the current device;
+ *   - every call uses the same array: calls whose work overlaps on the GPU
+ *     (other streams, other threads) race; order them on one stream.  Each
+ *     call writes every element it reads, so no clearing is needed;
+ *   - shapes without the pre-pass (pk_relpos_bd_cols == 0) run
+ *     pk_paged_attention, which needs no scratch. */
 int pk_paged_attention_noalloc(pk_paged_kv *kv, int32_t layer0, int32_t num_layers,
                                const void *query, int64_t q_layer_stride,
                                int64_t q_batch_stride, int64_t q_row_stride,

@@ -404,13 +404,15 @@ int pk_paged_attention_bd(pk_paged_kv *kv, int32_t layer0, int32_t num_layers, c
     return launch_attention_stacked(kv, unused, a, static_cast<cudaStream_t>(stream));
 }
 
-// Rel-pos scratch of pk_paged_attention_noalloc: a static device array, so
-// the call allocates nothing; every context that loads this library holds one
-// copy per device, and its address is looked up once per device.
-constexpr uint64_t kRelposScratchBytes = 32ull << 20;
-__device__ __align__(256) float g_relpos_scratch[kRelposScratchBytes / sizeof(float)];
+// Scratch of pk_paged_attention_noalloc, for callers that must not allocate
+// device memory.  A file-scope device array of PK_NOALLOC_SCRATCH_BYTES:
+// every GPU on which this library's code is loaded holds it until the process
+// exits.  In host code its name is only a stand-in for the device copy, so
+// the device address is looked up with cudaGetSymbolAddress, once per device,
+// with that device current, and that address is what the kernels receive.
+static __device__ __align__(256) float g_noalloc_scratch[PK_NOALLOC_SCRATCH_BYTES / sizeof(float)];
 
-static int relpos_scratch(float **out) {
+static int noalloc_scratch(float **out) {
     constexpr int kMaxDevices = 64;
     static float *ptrs[kMaxDevices] = {};
     static std::mutex mu;
@@ -422,17 +424,15 @@ static int relpos_scratch(float **out) {
         return PK_ENOTSUP;
     }
     std::lock_guard<std::mutex> lock(mu);
-    if (!ptrs[dev]) {
+    if (!ptrs[dev]) {   // first call on this device: the set-up
         void *p = nullptr;
-        st = cuda_status(cudaGetSymbolAddress(&p, g_relpos_scratch), "cudaGetSymbolAddress");
+        st = cuda_status(cudaGetSymbolAddress(&p, g_noalloc_scratch), "cudaGetSymbolAddress");
         if (st != PK_OK) return st;
         ptrs[dev] = static_cast<float *>(p);
     }
     *out = ptrs[dev];
     return PK_OK;
 }
-
-int64_t pk_relpos_scratch_bytes(void) { return (int64_t)kRelposScratchBytes; }
 
 int pk_paged_attention_noalloc(pk_paged_kv *kv, int32_t layer0, int32_t num_layers,
                                const void *query, int64_t q_layer_stride, int64_t q_batch_stride,
@@ -451,12 +451,25 @@ int pk_paged_attention_noalloc(pk_paged_kv *kv, int32_t layer0, int32_t num_laye
                                   out_layer_stride, out_batch_stride, out_row_stride, stream);
     const uint64_t need = (uint64_t)num_layers * batch * kv->d.num_heads * kv->d.chunk * cols *
                           sizeof(float);
-    PK_CHECK(need <= kRelposScratchBytes,
-             "rel-pos term of %d layers x %d streams needs %llu bytes; the static scratch holds %llu",
-             num_layers, batch, (unsigned long long)need, (unsigned long long)kRelposScratchBytes);
-    float *scratch = nullptr;
-    int st = relpos_scratch(&scratch);
+    PK_CHECK(need <= (uint64_t)PK_NOALLOC_SCRATCH_BYTES,
+             "rel-pos term of %d layers x %d streams needs %llu bytes; the static scratch "
+             "holds %llu (PK_NOALLOC_SCRATCH_BYTES): split the call by layers or streams",
+             num_layers, batch, (unsigned long long)need,
+             (unsigned long long)PK_NOALLOC_SCRATCH_BYTES);
+    // the scratch address belongs to the current device: the pool must be on it
+    int dev = -1;
+    cudaPointerAttributes attr{};
+    int st = cuda_status(cudaGetDevice(&dev), "cudaGetDevice");
     if (st != PK_OK) return st;
+    st = cuda_status(cudaPointerGetAttributes(&attr, kv->d.kv), "cudaPointerGetAttributes");
+    if (st != PK_OK) return st;
+    PK_CHECK(attr.type == cudaMemoryTypeDevice && attr.device == dev,
+             "the pool is not on the current device (%d): make its device current first", dev);
+    float *scratch = nullptr;
+    st = noalloc_scratch(&scratch);
+    if (st != PK_OK) return st;
+    // every element the attention kernel reads is written by the pre-pass of
+    // the same call, so nothing of the previous call's contents is used
     st = pk_relpos_bd(kv, layer0, num_layers, query, q_layer_stride, q_batch_stride, q_row_stride,
                       pos_proj, pos_layer_stride, bias_v, bias_layer_stride, batch, scratch, stream);
     if (st != PK_OK) return st;

@@ -20,6 +20,7 @@ PK_DEV_POOL_EXHAUSTED, PK_DEV_BAD_PAGE, PK_DEV_TIMEOUT, PK_DEV_BAD_SLOT = 1, 2, 
 PK_DEV_BAD_COUNT = 16
 PK_GEMM_STORE, PK_GEMM_SILU, PK_GEMM_RESIDUAL, PK_GEMM_RESIDUAL_RELU, PK_GEMM_BIAS = 0, 1, 2, 3, 4
 PK_FE_HIST, PK_FE_META_STRIDE, PK_FE_FIRST, PK_FE_FINAL = 512, 4, 1, 2
+PK_NOALLOC_SCRATCH_BYTES = 32 * 1024 * 1024   # pk_paged_attention_noalloc's static scratch
 META_FIRST, META_NEXT, META_WRITTEN, META_PROCESSED, META_CACHE_LEN = 0, 1, 2, 3, 4
 META_STRIDE = 8
 WIN_STRIDE = 128
@@ -96,7 +97,6 @@ SIGNATURES = {
     "pk_relpos_bd": [_P, _I32, _I32, _P, _I64, _I64, _I64, _P, _I64, _P, _I64, _I32, _P, _P],
     "pk_paged_attention_bd": [_P, _I32, _I32, _P, _I64, _I64, _I64, _P, _P, _P, _P, _I64, _P, _P,
                               _I32, _P, _I64, _I64, _I64, _P],
-    "pk_relpos_scratch_bytes": [],
     "pk_paged_attention_noalloc": [_P, _I32, _I32, _P, _I64, _I64, _I64, _P, _P, _P, _I64, _P,
                                    _P, _I64, _P, _P, _I32, _P, _I64, _I64, _I64, _P],
     "pk_conv_step": [_P, _I32, _I32, _I32, _I32, _I32, _I32, _I32, _P, _I64, _I64, _P, _P, _P,
@@ -114,7 +114,7 @@ SIGNATURES = {
                          _P, _P],
     "pk_last_error": [],
 }
-RESTYPES = {"pk_last_error": ctypes.c_char_p, "pk_relpos_scratch_bytes": ctypes.c_int64}
+RESTYPES = {"pk_last_error": ctypes.c_char_p}
 
 _lib = None
 

@@ -338,10 +338,11 @@ class PagedKVPool:
         bias_u/v [H, dh] or [nl, H, dh]; lengths int32 [B].  With key/value
         (this step's new rows, the query's shape and strides) the append is
         part of the call.  With ``bd`` (``relpos_bd``'s output for the same
-        query) pos_proj and bias_v are not read.  ``noalloc``: the rel-pos
-        pre-pass into the library's static device scratch
-        (pk_paged_attention_noalloc; calls on one device share it, so keep
-        them on one stream).  Returns out with the query's leading shape."""
+        query) pos_proj and bias_v are not read.  ``noalloc``: for callers that
+        must not allocate device memory, pk_paged_attention_noalloc keeps the
+        rel-pos term in the library's static 32 MiB device array (larger steps
+        are refused; calls overlapping on the GPU race on it, so keep them on
+        one stream).  Returns out with the query's leading shape."""
         squeeze = query.dim() == 3
         if squeeze:
             query, bias_u = query.unsqueeze(0), bias_u.unsqueeze(0)
