@@ -776,14 +776,16 @@ def streaming_step(model, steps, dev, profile=False):
 
 
 def serve_trial(pipe, N, period, banks, hbufs, dbufs, hslots, dslots, htok, hcnt,
-                warm_periods, meas_periods, seed, max_batch=2048):
+                warm_periods, meas_periods, seed, max_batch=2048, full_graph=None):
     """N streams paced in real time: stream i's chunk k completes at
     t0 + phase_i + k * period (phases uniform over one period).  The loop takes
     every chunk that has completed (one per stream per iteration), groups them
     by push index (first, second, later; batches of at most 2048 streams), copies
     their samples
-    and slots in from pinned host memory, runs ``step_audio`` eagerly and
-    copies the tokens back to pinned host memory; a chunk's latency is the
+    and slots in from pinned host memory, runs ``step_audio`` (a later-chunk
+    batch of exactly ``max_batch`` streams as the replay of ``full_graph`` =
+    (graph, samples, slots, tokens, counts) when given, every other batch
+    eagerly) and copies the tokens back to pinned host memory; a chunk's latency is the
     wall time from its completion to its tokens being on the host (the
     reference's push_samples -> DecodeResult, model_runner.py:150-171).
     Returns latencies (s) of the chunks completed in the measured periods and
@@ -826,11 +828,17 @@ def serve_trial(pipe, N, period, banks, hbufs, dbufs, hslots, dslots, htok, hcnt
                 torch.index_select(bank, 0, torch.from_numpy((part + k[part]) % bank.shape[0]),
                                    out=hbufs[c][rs])
                 hslots[c][rs].numpy()[:] = part
-                dx = dbufs[c][rs]
-                dx.copy_(hbufs[c][rs], non_blocking=True)
-                ds = dslots[c][rs]
-                ds.copy_(hslots[c][rs], non_blocking=True)
-                tok, cnt = pipe.step_audio(dx, ds, c)
+                if full_graph is not None and c == 2 and B == max_batch:
+                    gph, dx, ds, tok, cnt = full_graph
+                    dx.copy_(hbufs[c][rs], non_blocking=True)
+                    ds.copy_(hslots[c][rs], non_blocking=True)
+                    gph.replay()
+                else:
+                    dx = dbufs[c][rs]
+                    dx.copy_(hbufs[c][rs], non_blocking=True)
+                    ds = dslots[c][rs]
+                    ds.copy_(hslots[c][rs], non_blocking=True)
+                    tok, cnt = pipe.step_audio(dx, ds, c)
                 htok[c][rs].copy_(tok.view(B, -1), non_blocking=True)
                 hcnt[c][rs].copy_(cnt, non_blocking=True)
                 rows += B
@@ -852,14 +860,15 @@ def serve_trial(pipe, N, period, banks, hbufs, dbufs, hslots, dslots, htok, hcnt
                  "backlog_chunks_at_end": backlog}
 
 
-def serving_search(model, dev, measure_s=3.0, max_trials=9, limit_ms=160.0):
+def serving_search(model, dev, measure_s=3.0, max_trials=9, limit_ms=160.0, use_graph=True):
     """Metric 1 of the survey: the most concurrent streams one GPU serves with
     p99 chunk latency <= 160 ms, streams paced in real time (configs[2] /
     configs[3] audio, random bf16 weights).  Doubling from 1024 streams until
     a trial fails (p99 above the limit, or chunks left waiting at the end),
     then bisection, a failing trial repeated once; the slot count is capped by
-    85 % of the free device memory (every slot holds its K/V pages).  Eager
-    steps (batch sizes vary from step to step)."""
+    85 % of the free device memory (every slot holds its K/V pages).  Batch
+    sizes vary from step to step: a later-chunk batch of the full 2048 streams
+    replays one CUDA graph, every other batch runs eagerly."""
     import numpy as np
     import torch
 
@@ -904,12 +913,33 @@ def serving_search(model, dev, measure_s=3.0, max_trials=9, limit_ms=160.0):
                 pipe.step_audio(dbufs[c][:B], dslots[c][:B], c)
             pipe.end_streams(sl)
         torch.cuda.synchronize(dev)
+        # A later-chunk step of a full 2048-stream batch as one CUDA graph: the
+        # eager step launches about 300 kernels, whose host cost (about 7.5 ms)
+        # exceeds their GPU time at this batch.  Slots and samples are data in
+        # the graph's input buffers, so one graph serves any 2048 streams.
+        full_graph = None
+        if use_graph and cap >= 2048:
+            Bg = 2048
+            sl = torch.arange(Bg, dtype=torch.int32)
+            gx = torch.empty(Bg, n, dtype=torch.float32, device=dev)
+            gs = sl.to(dev)
+            pipe.start_streams(sl)
+            # one eager first step: it also applies the releases queued above,
+            # so that the captured step carries none
+            pipe.step_audio(dbufs[0][:Bg], gs, 0)
+            gx.copy_(banks[2][torch.arange(Bg) % banks[2].shape[0]])
+            torch.cuda.synchronize(dev)
+            gph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gph):
+                gtok, gcnt = pipe.step_audio(gx, gs, 2)
+            pipe.end_streams(sl)
+            full_graph = (gph, gx, gs, gtok, gcnt)
         serve_trial(pipe, min(64, cap), period, banks, hbufs, dbufs, hslots, dslots, htok, hcnt,
-                    3, 1, seed=0)
+                    3, 1, seed=0, full_graph=full_graph)
 
         def run(N, seed):
             lat, st = serve_trial(pipe, N, period, banks, hbufs, dbufs, hslots, dslots, htok, hcnt,
-                                  3, meas, seed=seed)
+                                  3, meas, seed=seed, full_graph=full_graph)
             p99 = float(np.percentile(lat, 99)) * 1e3 if lat.size else float("inf")
             ok = p99 <= limit_ms and st["backlog_chunks_at_end"] <= 1
             return ok, {"streams": N, "ok": ok, "p50_ms": round(float(np.median(lat)) * 1e3, 2),
@@ -942,7 +972,8 @@ def serving_search(model, dev, measure_s=3.0, max_trials=9, limit_ms=160.0):
             "p99_ms_at_max": best["p99_ms"] if best else None,
             "audio_ms_per_chunk": period * 1e3, "measured_s_per_trial": round(meas * period, 2),
             "trials": trials, "device_error_word": err,
-            "method": "streams paced in real time, eager batched steps over every completed "
+            "full_batch_graph": full_graph is not None,
+            "method": "streams paced in real time, batched steps over every completed "
                       "chunk, latency = chunk completion -> tokens in pinned host memory"}
 
 

@@ -48,7 +48,8 @@ class StreamingPipeline:
         self.dec = BatchedGreedyDecoder(predictor, joiner, blank_id, num_slots, max_symbols)
         self.fe = FeatureExtractor(**{"n_mels": self.pre.feat_in, **(feature_kw or {})},
                                    num_slots=num_slots, device=self.device, out_dtype=self.dtype)
-        self._fe_bufs = {}
+        self._fe_bufs = {}          # recent batch sizes' feature buffers (bounded)
+        self._fe_bufs_graph = {}    # buffers a captured CUDA graph uses: kept for good
 
     def start_streams(self, slots) -> None:
         """Fresh state for new streams in ``slots`` (their pages start empty;
@@ -96,7 +97,10 @@ class StreamingPipeline:
                 first_samples = (1 + 8 * la) * self.fe.hop_length
             prefix = min(self.frames_per_push(first_samples, True), self.pre.cache_size)
         key = (B, n, first)
-        bufs = self._fe_bufs.pop(key, None)
+        capturing = torch.cuda.is_current_stream_capturing()
+        bufs = self._fe_bufs_graph.get(key)
+        if bufs is None:
+            bufs = self._fe_bufs.pop(key, None)
         if bufs is None:
             while len(self._fe_bufs) >= 16:   # batches of many sizes: keep the recent ones
                 self._fe_bufs.pop(next(iter(self._fe_bufs)))
@@ -106,7 +110,12 @@ class StreamingPipeline:
                                device=dev),
                     torch.empty(B, self.fe.n_mels, F, dtype=self.dtype, device=dev),
                     torch.empty(B, dtype=torch.int32, device=dev))
-        self._fe_bufs[key] = bufs
+        if capturing or key in self._fe_bufs_graph:
+            # a graph captured now reads these addresses at every replay: they
+            # must outlive any eviction of the recent-sizes cache
+            self._fe_bufs_graph[key] = bufs
+        else:
+            self._fe_bufs[key] = bufs
         ns, flags, feats, nframes = bufs
         self.fe.launch(samples, ns, flags, slots, feats, F, nframes)
         return self.encode(feats, slots, first, prefix=prefix)

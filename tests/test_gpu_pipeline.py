@@ -212,3 +212,35 @@ def test_overlapped_runner_equals_sequential_steps():
         assert torch.equal(got[k][0], want[k][0]) and torch.equal(got[k][1], want[k][1]), k
     assert sum(int(c.sum()) for _, c in want) > 0
     assert pipe.pool.read_error() == 0 and pipe.fe.error_bits() == 0
+
+
+def test_captured_step_survives_other_batch_sizes():
+    """A step captured as a CUDA graph keeps working after the pipeline has run
+    many other batch sizes eagerly: the feature buffers the graph reads must not
+    be evicted (and their memory reused) by the cache of recent batch sizes."""
+    pipe, ref_pipe = make(24), make(24)
+    slots = torch.tensor([0, 1], dtype=torch.int32, device="cuda")
+    pipe.start_streams([0, 1])
+    ref_pipe.start_streams([0, 1])
+    with torch.inference_mode():
+        for push in range(2):
+            x = torch.cat([audio(push, 0), audio(push, 1)]).cuda()
+            pipe.step_audio(x, slots, push)
+            ref_pipe.step_audio(x, slots, push)
+        x2 = torch.cat([audio(2, 0), audio(2, 1)]).cuda()
+        static_x = x2.clone()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            tok, cnt = pipe.step_audio(static_x, slots, 2)
+        # first chunks of other streams at 20 batch sizes: more than the cache holds
+        for rep in range(2):
+            for B in range(1, 21):
+                other = torch.arange(2, 2 + B, dtype=torch.int32, device="cuda")
+                pipe.start_streams(other)
+                xb = torch.cat([audio(0, 10 + i) for i in range(B)]).cuda()
+                pipe.step_audio(xb, other, 0)
+        want = ref_pipe.step_audio(x2, slots, 2)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(tok, want[0]) and torch.equal(cnt, want[1])
+    assert pipe.fe.error_bits() == 0 and pipe.pool.read_error() == 0
