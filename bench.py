@@ -5,12 +5,13 @@ Workload: one isolated paged-attention step of the
 small model, bf16 - 80 streams x 17 layers, 8 heads of 64, chunk of 2 frames
 over 70 cached left-context frames (window 72), 16-frame pages, the free
 list a random permutation of the pool (seed 1), Q/K/V and the rel-pos
-projection N(0,1)/8.  A step is four launches: the rel-pos term of every
-(layer, stream, head, query) in one pre-pass (each layer's pos rows read
-once, not once per stream) -> step start (page allocator and window
-descriptors) -> paged rel-pos attention for all 17 layers with the chunk's
-K/V append fused in -> counter update (end); ``--relpos in-kernel`` computes
-the rel-pos term inside the attention kernel instead (three launches).
+projection N(0,1)/8.  A step is three launches: step start (page allocator
+and window descriptors) together with the rel-pos term of every (layer,
+stream, head, query) (each layer's pos rows read once, not once per stream)
+-> paged rel-pos attention for all 17 layers with the chunk's K/V append
+fused in -> counter update (end).  ``--relpos prepass`` runs the rel-pos
+term as its own launch (four launches), ``--relpos in-kernel`` inside the
+attention kernel (three).
 Streams are
 independent, so N GPUs run N replicas with no collective on the data path
 (weak scaling): each rank owns its own pool and streams, and the only
@@ -69,9 +70,10 @@ def parse():
     ap.add_argument("--streams", type=int, default=80)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-breakdown", action="store_true")
-    ap.add_argument("--relpos", choices=["prepass", "in-kernel"], default="prepass",
-                    help="rel-pos term: all-stream pre-pass (pk_relpos_bd) or inside the "
-                         "attention kernel")
+    ap.add_argument("--relpos", choices=["fused", "prepass", "in-kernel"], default="fused",
+                    help="rel-pos term: all-stream pre-pass in the step-start launch "
+                         "(pk_pages_begin_step_relpos), as its own launch (pk_relpos_bd), or "
+                         "inside the attention kernel")
     ap.add_argument("--no-serve", action="store_true",
                     help="skip the paced serving search (streams at p99 <= 160 ms)")
     ap.add_argument("--no-graph", action="store_true", help="time eager launches only")
@@ -1050,7 +1052,8 @@ def main():
     # the rel-pos term of every (layer, stream, head, query) in one pre-pass
     # that reads each layer's pos rows once, instead of once per stream inside
     # the attention kernel (where they are L2 traffic 1.5x the K/V bytes' size)
-    prepass = args.relpos == "prepass" and pool.relpos_bd_cols > 0
+    relpos_mode = args.relpos if pool.relpos_bd_cols > 0 else "in-kernel"
+    prepass = relpos_mode != "in-kernel"
     bd_buf = (torch.empty(L, B, H, T, pool.relpos_bd_cols, dtype=torch.float32, device=dev)
               if prepass else None)
 
@@ -1059,11 +1062,14 @@ def main():
         # the join costs the programmatic overlap of step start and attention)
         if ev is not None:
             ev[2].record()
-        if prepass:
+        if relpos_mode == "prepass":
             pool.relpos_bd(0, x[..., :D], pos, bv, out=bd_buf)
         if ev is not None:
             ev[3].record()
-        pool.begin_step(slots, lengths)
+        if relpos_mode == "fused":   # step start and pre-pass in one launch
+            pool.begin_step(slots, lengths, relpos=(0, x[..., :D], pos, bv, bd_buf))
+        else:
+            pool.begin_step(slots, lengths)
         if ev is not None:
             ev[0].record()
         # append of the chunk's K/V rows fused into the attention call
@@ -1157,7 +1163,8 @@ def main():
         step(qkv[i % NBUF], evq[i])
     torch.cuda.synchronize()
     attn_ms = sum(e[0].elapsed_time(e[1]) for e in evq) / KQ
-    bd_ms = sum(e[2].elapsed_time(e[3]) for e in evq) / KQ if prepass else 0.0
+    bd_ms = sum(e[2].elapsed_time(e[3]) for e in evq) / KQ
+    start_ms = sum(e[3].elapsed_time(e[0]) for e in evq) / KQ
 
     # (b) the same steps replayed as CUDA graphs (one graph per input buffer): `value`
     ms = eager_ms
@@ -1338,9 +1345,10 @@ def main():
                     "ms_per_step": round(e2e_ms, 4),
                     "pipeline": "copy-in, compute and copy-out streams, 3 buffer sets, eager API calls"},
             # per step: [rel-pos pre-pass,] allocator+windows, attention+append, counters
-            "gpu_launches": (4 if prepass else 3) * K,
-            "relpos": {"mode": "prepass" if prepass else "in-kernel",
-                       "prepass_ms": round(bd_ms, 4) if prepass else None},
+            "gpu_launches": (4 if relpos_mode == "prepass" else 3) * K,
+            "relpos": {"mode": relpos_mode,
+                       "prepass_ms": round(bd_ms, 4) if relpos_mode == "prepass" else None,
+                       "step_start_ms": round(start_ms, 4)},
             "clocks": clk,
             "device_error_word": err,
             "ops": breakdown,

@@ -213,6 +213,24 @@ int pk_relpos_bd(pk_paged_kv *kv, int32_t layer0, int32_t num_layers,
                  const void *bias_v, int64_t bias_layer_stride, int32_t batch,
                  float *bd, void *stream);
 
+/* pk_pages_begin_step and pk_relpos_bd for the same step in one launch (its
+ * first CTA runs the page allocator and window descriptors, the others the
+ * pre-pass tiles): the same outputs as the two calls, with one link fewer in
+ * the step's launch chain.  Arguments are those of the two calls (the
+ * pre-pass's batch is the step's batch).  Batches above 256 rows run as the
+ * two launches.  Replaces, as those two do, Scheduler.pack_states +
+ * _create_streaming_masks (parakeet/engine/scheduler.py:106-170,
+ * parakeet/modules/encoder.py:167-227) and the (q + pos_bias_v) pos^T product
+ * of ConformerAttention.forward lines 108-110 (parakeet/modules/attention.py). */
+int pk_pages_begin_step_relpos(pk_paged_kv *kv, const int32_t *slots,
+                               const int32_t *lengths, int32_t batch,
+                               const int32_t *released, int32_t num_released,
+                               int32_t layer0, int32_t num_layers, const void *query,
+                               int64_t q_layer_stride, int64_t q_batch_stride,
+                               int64_t q_row_stride, const void *pos_proj,
+                               int64_t pos_layer_stride, const void *bias_v,
+                               int64_t bias_layer_stride, float *bd, void *stream);
+
 /* pk_paged_attention with the rel-pos term taken from pk_relpos_bd's output
  * for the same query, layers and batch (in place of pos_proj and bias_v).
  * Same outputs, same replaced calls; for the shapes pk_relpos_bd_cols

@@ -319,10 +319,11 @@ int32_t pk_relpos_bd_cols(const pk_paged_kv *kv) {
     return kv ? relpos_bd_cols(kv) : 0;
 }
 
-int pk_relpos_bd(pk_paged_kv *kv, int32_t layer0, int32_t num_layers, const void *query,
-                 int64_t q_layer_stride, int64_t q_batch_stride, int64_t q_row_stride,
-                 const void *pos_proj, int64_t pos_layer_stride, const void *bias_v,
-                 int64_t bias_layer_stride, int32_t batch, float *bd, void *stream) {
+// argument checks of the rel-pos pre-pass; fills a (nothing launched)
+static int relpos_args(pk_paged_kv *kv, int32_t layer0, int32_t num_layers, const void *query,
+                       int64_t q_layer_stride, int64_t q_batch_stride, int64_t q_row_stride,
+                       const void *pos_proj, int64_t pos_layer_stride, const void *bias_v,
+                       int64_t bias_layer_stride, int32_t batch, float *bd, AttnArgs *out) {
     PK_CHECK(kv, "null pool");
     PK_CHECK(batch >= 0 && num_layers >= 0 && layer0 >= 0 &&
                  layer0 + num_layers <= kv->d.num_layers,
@@ -354,7 +355,49 @@ int pk_relpos_bd(pk_paged_kv *kv, int32_t layer0, int32_t num_layers, const void
     a.batch = batch;
     a.layer0 = layer0;
     a.nlayers = num_layers;
+    *out = a;
+    return PK_OK;
+}
+
+int pk_relpos_bd(pk_paged_kv *kv, int32_t layer0, int32_t num_layers, const void *query,
+                 int64_t q_layer_stride, int64_t q_batch_stride, int64_t q_row_stride,
+                 const void *pos_proj, int64_t pos_layer_stride, const void *bias_v,
+                 int64_t bias_layer_stride, int32_t batch, float *bd, void *stream) {
+    AttnArgs a{};
+    const int st = relpos_args(kv, layer0, num_layers, query, q_layer_stride, q_batch_stride,
+                               q_row_stride, pos_proj, pos_layer_stride, bias_v,
+                               bias_layer_stride, batch, bd, &a);
+    if (st != PK_OK || batch == 0 || num_layers == 0) return st;
     return launch_relpos_bd(kv, a, bd, static_cast<cudaStream_t>(stream));
+}
+
+int pk_pages_begin_step_relpos(pk_paged_kv *kv, const int32_t *slots, const int32_t *lengths,
+                               int32_t batch, const int32_t *released, int32_t num_released,
+                               int32_t layer0, int32_t num_layers, const void *query,
+                               int64_t q_layer_stride, int64_t q_batch_stride,
+                               int64_t q_row_stride, const void *pos_proj,
+                               int64_t pos_layer_stride, const void *bias_v,
+                               int64_t bias_layer_stride, float *bd, void *stream) {
+    PK_CHECK(kv, "null pool");
+    PK_CHECK(batch >= 0 && num_released >= 0, "negative count");
+    PK_CHECK(batch <= kv->d.num_slots, "batch larger than the pool's slots");
+    PK_CHECK(batch == 0 || slots, "null slots");
+    PK_CHECK(num_released == 0 || released, "null released");
+    PK_CHECK(batch <= 2048, "batch above 2048 rows");
+    AttnArgs a{};
+    int st = relpos_args(kv, layer0, num_layers, query, q_layer_stride, q_batch_stride,
+                         q_row_stride, pos_proj, pos_layer_stride, bias_v, bias_layer_stride,
+                         batch, bd, &a);
+    if (st != PK_OK) return st;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (batch > 0 && num_layers > 0) {
+        st = launch_pages_begin_relpos(kv, slots, lengths, batch, released, num_released, a, bd, s);
+        if (st != PK_ENOTSUP) return st;
+        // a batch too large for the one launch: the same work as two launches
+        st = launch_relpos_bd(kv, a, bd, s);
+        if (st != PK_OK) return st;
+    }
+    return launch_pages_begin(kv, slots, lengths, batch, released, num_released, s);
 }
 
 int pk_paged_attention_bd(pk_paged_kv *kv, int32_t layer0, int32_t num_layers, const void *query,

@@ -91,6 +91,11 @@ int launch_attention_stacked(const pk_paged_kv *kv, const CUtensorMap &pos_map16
 // handles (PK_ENOTSUP otherwise); reads a.q, a.bias_v, a.pos.
 int relpos_bd_cols(const pk_paged_kv *kv);
 int launch_relpos_bd(const pk_paged_kv *kv, const AttnArgs &a, float *bd, cudaStream_t s);
+// pk_pages.cu: launch_pages_begin and launch_relpos_bd in one launch (batch <= 256,
+// shapes with the pre-pass; PK_ENOTSUP otherwise)
+int launch_pages_begin_relpos(const pk_paged_kv *kv, const int32_t *slots,
+                              const int32_t *lengths, int batch, const int32_t *released,
+                              int num_released, const AttnArgs &a, float *bd, cudaStream_t s);
 // pk_attn_heads.cu: head_dim 128, chunks of 8..16 frames, K/V appended before;
 // returns PK_ENOTSUP for other shapes.  pos_map16 has 16-row boxes of 64 columns.
 int launch_attention_heads(const pk_paged_kv *kv, const CUtensorMap &pos_map16,

@@ -12,12 +12,14 @@
 // _create_streaming_masks (parakeet/modules/encoder.py:167-227) as bit rows.
 #include "pk_common.cuh"
 #include "pk_internal.h"
+#include "pk_relpos.cuh"
 
 namespace pk {
 namespace {
 
 constexpr int kAllocThreads = 1024;            // most threads of the step-start CTA
 constexpr int kMaxBatch = 2 * kAllocThreads;
+constexpr int kMaxBatchRelpos = 256;           // step start fused with the rel-pos pre-pass
 
 // Exclusive prefix sum of v over the CTA (blockDim.x a multiple of 32), in batch
 // order of the threads; `total` gets the CTA's sum.  s_warp: 33 ints of scratch.
@@ -130,11 +132,12 @@ __device__ void write_window(const pk_paged_kv_desc &d, const RowState &r, const
     out[1] = make_int4(r.len, nb, nfirst, r.slot);
 }
 
-// One CTA, one thread per batch row (two for batch > 1024).  Every row keeps
-// its owner thread through all phases, so only the scans cross threads.
-__global__ void __launch_bounds__(kAllocThreads)
-    pages_begin_kernel(pk_paged_kv_desc d, const int32_t *slots, const int32_t *lengths,
-                       int batch, const int32_t *released, int num_released) {
+// One CTA, one thread per batch row (several for batches above the CTA's
+// threads).  Every row keeps its owner thread through all phases, so only the
+// scans cross threads.
+__device__ __forceinline__ void pages_begin_body(const pk_paged_kv_desc &d, const int32_t *slots,
+                                                 const int32_t *lengths, int batch,
+                                                 const int32_t *released, int num_released) {
     extern __shared__ __align__(16) int s_dyn[];
     __shared__ int scan_tmp[33];
     __shared__ int64_t s_ctr[2];
@@ -276,6 +279,30 @@ __global__ void __launch_bounds__(kAllocThreads)
     }
 }
 
+__global__ void __launch_bounds__(kAllocThreads)
+    pages_begin_kernel(pk_paged_kv_desc d, const int32_t *slots, const int32_t *lengths,
+                       int batch, const int32_t *released, int num_released) {
+    pages_begin_body(d, slots, lengths, batch, released, num_released);
+}
+
+// The step start and the all-stream rel-pos pre-pass in one launch: CTA 0 runs
+// the allocator and window descriptors, CTAs 1.. one pre-pass tile each.  They
+// touch disjoint memory, so the allocator's serial chain and the tiles overlap
+// instead of being two links of the step's launch chain.
+__global__ void __launch_bounds__(kRelposThreads, 5)
+    pages_begin_relpos_kernel(pk_paged_kv_desc d, const int32_t *slots, const int32_t *lengths,
+                              int batch, const int32_t *released, int num_released,
+                              const AttnArgs a, int bds, float *bd, int tiles_z) {
+    if (blockIdx.x == 0) {
+        pages_begin_body(d, slots, lengths, batch, released, num_released);
+        return;
+    }
+    grid_dep_wait();     // q may come from the previous kernel
+    grid_dep_launch();
+    const int t = blockIdx.x - 1, z = t % tiles_z, lh = t / tiles_z;
+    relpos_tile(d, a, bds, bd, lh / d.num_heads, lh % d.num_heads, z);
+}
+
 __global__ void pages_end_kernel(pk_paged_kv_desc d, const int32_t *slots, const int32_t *lengths,
                                  int batch) {
     const int b = blockIdx.x * blockDim.x + threadIdx.x;
@@ -320,6 +347,22 @@ int launch_pages_begin(const pk_paged_kv *kv, const int32_t *slots, const int32_
     return cuda_status(launch_pdl(pages_begin_kernel, dim3(1), dim3(threads), smem, s, kv->d,
                                   slots, lengths, batch, released, num_released),
                        "pages_begin_kernel");
+}
+
+int launch_pages_begin_relpos(const pk_paged_kv *kv, const int32_t *slots,
+                              const int32_t *lengths, int batch, const int32_t *released,
+                              int num_released, const AttnArgs &a, float *bd, cudaStream_t s) {
+    const int bds = relpos_bd_cols(kv);
+    // the allocator runs in a pre-pass-sized CTA here, and every tile CTA gets
+    // the allocator's shared memory: small batches only
+    if (bds == 0 || batch > kMaxBatchRelpos || kv->d.ring > PK_WIN_MAX_PAGES) return PK_ENOTSUP;
+    const size_t smem = (size_t)batch * (sizeof(RowState) + PK_WIN_MAX_PAGES * sizeof(int));
+    const int tiles_z = (a.batch * kv->d.chunk + kRelposRows - 1) / kRelposRows;
+    const int grid = 1 + (a.batch > 0 ? a.nlayers * kv->d.num_heads * tiles_z : 0);
+    return cuda_status(launch_pdl(pages_begin_relpos_kernel, dim3(grid), dim3(kRelposThreads), smem,
+                                  s, kv->d, slots, lengths, batch, released, num_released, a, bds,
+                                  bd, tiles_z),
+                       "pages_begin_relpos_kernel");
 }
 
 int launch_pages_end(const pk_paged_kv *kv, const int32_t *slots, const int32_t *lengths,

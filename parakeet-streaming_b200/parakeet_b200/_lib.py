@@ -95,6 +95,8 @@ SIGNATURES = {
                            _I64, _P, _P, _I32, _P, _I64, _I64, _I64, _P],
     "pk_relpos_bd_cols": [_P],
     "pk_relpos_bd": [_P, _I32, _I32, _P, _I64, _I64, _I64, _P, _I64, _P, _I64, _I32, _P, _P],
+    "pk_pages_begin_step_relpos": [_P, _P, _P, _I32, _P, _I32, _I32, _I32, _P, _I64, _I64, _I64,
+                                   _P, _I64, _P, _I64, _P, _P],
     "pk_paged_attention_bd": [_P, _I32, _I32, _P, _I64, _I64, _I64, _P, _P, _P, _P, _I64, _P, _P,
                               _I32, _P, _I64, _I64, _I64, _P],
     "pk_paged_attention_noalloc": [_P, _I32, _I32, _P, _I64, _I64, _I64, _P, _P, _P, _I64, _P,

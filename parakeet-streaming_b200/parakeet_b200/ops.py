@@ -212,20 +212,35 @@ class PagedKVPool:
             self.pending_release.append(int(slot))
 
     def begin_step(self, slots: torch.Tensor, lengths: torch.Tensor | None = None,
-                   released: torch.Tensor | None = None):
+                   released: torch.Tensor | None = None, relpos=None):
         """Page releases, frees and allocations for one step of ``slots``
         (int32 [B], distinct), then the step's window descriptors for chunks
         of ``lengths`` (int32 [B]; None = full chunks).  ``released`` defaults
-        to the queued releases."""
+        to the queued releases.  ``relpos`` = (layer, query, pos_proj, bias_v,
+        out or None): the same launch also computes ``relpos_bd`` of this
+        step's rows (pk_pages_begin_step_relpos), which is returned."""
         if released is None:
             with self._lock:
                 rel, self.pending_release = self.pending_release, []
             if rel:
                 released = torch.tensor(rel, dtype=torch.int32).to(self.device)
         n_rel = 0 if released is None else int(released.numel())
-        check(lib().pk_pages_begin_step(self._h, slots.data_ptr(), _ptr(lengths),
-                                        int(slots.numel()), _ptr(released) if n_rel else None,
-                                        n_rel, _stream(self.device)), "pk_pages_begin_step")
+        if relpos is None:
+            check(lib().pk_pages_begin_step(self._h, slots.data_ptr(), _ptr(lengths),
+                                            int(slots.numel()), _ptr(released) if n_rel else None,
+                                            n_rel, _stream(self.device)), "pk_pages_begin_step")
+            return None
+        layer, query, pos_proj, bias_v, out = relpos
+        query, pos_proj, bias_v, out = self._relpos_prep(query, pos_proj, bias_v, out)
+        if query.shape[1] != slots.numel():
+            raise ValueError("the pre-pass's batch must be the step's batch")
+        check(lib().pk_pages_begin_step_relpos(
+            self._h, slots.data_ptr(), _ptr(lengths), int(slots.numel()),
+            _ptr(released) if n_rel else None, n_rel, layer, query.shape[0], query.data_ptr(),
+            query.stride(0), query.stride(1), query.stride(2), pos_proj.data_ptr(),
+            pos_proj.stride(0), bias_v.data_ptr(), bias_v.stride(0), out.data_ptr(),
+            _stream(self.device)), "pk_pages_begin_step_relpos")
+        return out
 
     def end_step(self, slots: torch.Tensor, lengths: torch.Tensor):
         check(lib().pk_pages_end_step(self._h, slots.data_ptr(), lengths.data_ptr(),
@@ -303,14 +318,8 @@ class PagedKVPool:
             if tuple(t.shape) != (nl, self.num_heads, dh) or not t[0].is_contiguous() or t.dtype != self.dtype:
                 raise ValueError(f"{n} must be [{nl}, {self.num_heads}, {dh}] {self.dtype}")
 
-    def relpos_bd(self, layer: int, query: torch.Tensor, pos_proj: torch.Tensor,
-                  bias_v: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
-        """The rel-pos term (q + pos_bias_v) pos_proj^T of every (layer, stream,
-        head, query row), fp32 [nl, B, H, T, relpos_bd_cols], for
-        ``attention(..., bd=...)``: one pass over all streams, which share the
-        layer's pos_proj rows.  Shapes as in ``attention``."""
-        squeeze = query.dim() == 3
-        if squeeze:
+    def _relpos_prep(self, query, pos_proj, bias_v, out):
+        if query.dim() == 3:
             query, pos_proj, bias_v = query.unsqueeze(0), pos_proj.unsqueeze(0), bias_v.unsqueeze(0)
         self._check_rows(query, "query")
         self._check_attn_inputs(query, pos_proj, ((bias_v, "bias_v"),))
@@ -323,6 +332,16 @@ class PagedKVPool:
             out = torch.empty(shape, dtype=torch.float32, device=self.device)
         elif tuple(out.shape) != shape or out.dtype != torch.float32 or not out.is_contiguous():
             raise ValueError(f"out must be contiguous float32 {shape}")
+        return query, pos_proj, bias_v, out
+
+    def relpos_bd(self, layer: int, query: torch.Tensor, pos_proj: torch.Tensor,
+                  bias_v: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """The rel-pos term (q + pos_bias_v) pos_proj^T of every (layer, stream,
+        head, query row), fp32 [nl, B, H, T, relpos_bd_cols], for
+        ``attention(..., bd=...)``: one pass over all streams, which share the
+        layer's pos_proj rows.  Shapes as in ``attention``."""
+        query, pos_proj, bias_v, out = self._relpos_prep(query, pos_proj, bias_v, out)
+        nl, B = query.shape[:2]
         check(lib().pk_relpos_bd(
             self._h, layer, nl, query.data_ptr(), query.stride(0), query.stride(1), query.stride(2),
             pos_proj.data_ptr(), pos_proj.stride(0), bias_v.data_ptr(), bias_v.stride(0), B,

@@ -217,6 +217,47 @@ def test_relpos_prepass_matches_in_kernel_term():
     assert pa.read_error() == 0 and pb.read_error() == 0
 
 
+@pytest.mark.parametrize("n_slots,batch,nl", [(9, 6, 3), (320, 300, 1)])
+def test_step_start_with_relpos_equals_two_launches(n_slots, batch, nl):
+    """pk_pages_begin_step_relpos (step start and rel-pos pre-pass in one launch;
+    above 256 rows as two launches) against pk_relpos_bd + pk_pages_begin_step:
+    the same page tables, counters, free ring and window descriptors, the same
+    term and the same attention output, over steps with a released slot."""
+    cfg = SHAPES["small"]
+    att, D, H = cfg["att"], cfg["dim"], cfg["heads"]
+    left, T = att[0], att[1] + 1
+    P, dh = 2 * (left + T) - 1, D // H
+    rng = np.random.default_rng(31)
+    order = rng.permutation(n_slots * pages.pages_per_stream(left, T, 16))
+    pa, pb = (PagedKVPool(nl, D, H, att, n_slots, dtype=torch.bfloat16, device=DEV, page_order=order)
+              for _ in range(2))
+    to = lambda a: torch.tensor(np.asarray(a), dtype=torch.bfloat16, device=DEV)  # noqa: E731
+    pos = to(rng.standard_normal((nl, P, D)) / 8)
+    bu, bv = to(rng.standard_normal((nl, H, dh)) / 8), to(rng.standard_normal((nl, H, dh)) / 8)
+    slot_list = rng.permutation(n_slots)[:batch].tolist()
+    for step in range(5):
+        if step == 3:   # a stream ends; a new one takes its slot
+            for p_ in (pa, pb):
+                p_.release_slot(slot_list[0])
+        slots = torch.tensor(slot_list, dtype=torch.int32, device=DEV)
+        ln = torch.full((batch,), T, dtype=torch.int32, device=DEV)
+        qkv = to(rng.standard_normal((nl, batch, T, 3 * D)) / 8)
+        q, k, v = qkv[..., :D], qkv[..., D:2 * D], qkv[..., 2 * D:]
+        bd_a = pa.relpos_bd(0, q, pos, bv)
+        pa.begin_step(slots, ln)
+        bd_b = pb.begin_step(slots, ln, relpos=(0, q, pos, bv, None))
+        oa = pa.attention(0, q, None, bu, None, slots, ln, key=k, value=v, bd=bd_a)
+        ob = pb.attention(0, q, None, bu, None, slots, ln, key=k, value=v, bd=bd_b)
+        torch.cuda.synchronize()
+        assert torch.equal(bd_a, bd_b), step
+        assert torch.equal(oa, ob), step
+        for name in ("page_table", "meta", "free_ring", "ring_ctr", "win_desc"):
+            assert torch.equal(getattr(pa, name), getattr(pb, name)), (step, name)
+        pa.end_step(slots, ln)
+        pb.end_step(slots, ln)
+    assert pa.read_error() == 0 and pb.read_error() == 0
+
+
 def conv_oracle(x2d, cache, w, lengths, g, b, eps=1e-5):
     """GLU -> pad mask -> cached depthwise conv -> LayerNorm -> SiLU
     (convolution.py:153-159) on float64."""
