@@ -1158,7 +1158,8 @@ def main():
     KQ = min(K, 48)
     evq = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(4)) for _ in range(KQ)]
     torch.cuda.synchronize()
-    torch.cuda._sleep(int((2e-3 + 2 * KQ * eager_ms * 1e-3) * 2.0e9))   # cycles at <= 2 GHz
+    # cycles at <= 2 GHz; at most 0.1 s (a profiler's serialised launches make eager_ms large)
+    torch.cuda._sleep(int(min(0.1, 2e-3 + 2 * KQ * eager_ms * 1e-3) * 2.0e9))
     for i in range(KQ):
         step(qkv[i % NBUF], evq[i])
     torch.cuda.synchronize()
