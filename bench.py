@@ -70,6 +70,8 @@ def parse():
     ap.add_argument("--streams", type=int, default=80)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-breakdown", action="store_true")
+    ap.add_argument("--pipeline-streams", type=int, default=None,
+                    help="streams of --profile-op streaming (default: the config's 160 / 480)")
     ap.add_argument("--relpos", choices=["fused", "prepass", "in-kernel"], default="fused",
                     help="rel-pos term: all-stream pre-pass in the step-start launch "
                          "(pk_pages_begin_step_relpos), as its own launch (pk_relpos_bd), or "
@@ -694,7 +696,7 @@ def build_streaming_pipeline(model, dev, num_slots, feature_kw=None):
     return StreamingPipeline(*mods, blank_id=V, num_slots=num_slots, feature_kw=feature_kw)
 
 
-def streaming_step(model, steps, dev, profile=False):
+def streaming_step(model, steps, dev, profile=False, streams=None):
     """Audio -> tokens for every stream of configs[2] (small, 160 streams) or
     configs[3] on one GPU (large, 480 streams): batched log-mel features ->
     batched pre-encode -> paged encoder -> batched greedy decode
@@ -704,8 +706,9 @@ def streaming_step(model, steps, dev, profile=False):
     per step / step time."""
     import torch
 
-    pipe = build_streaming_pipeline(model, dev, DECODE_CFG[model]["streams"])
-    att, B = SHAPES[model]["att"], DECODE_CFG[model]["streams"]
+    B = streams or DECODE_CFG[model]["streams"]
+    pipe = build_streaming_pipeline(model, dev, B)
+    att = SHAPES[model]["att"]
     la = att[1]
     slots = torch.arange(B, dtype=torch.int32, device=dev)
     pipe.start_streams(slots)
@@ -1022,7 +1025,8 @@ def main():
         print(json.dumps(profile_gemm(args.model, args.steps, dev)))
         return
     if args.profile_op == "streaming":  # --steps audio -> tokens steps inside a profiler range
-        print(json.dumps(streaming_step(args.model, args.steps, dev, profile=True)))
+        print(json.dumps(streaming_step(args.model, args.steps, dev, profile=True,
+                                        streams=args.pipeline_streams)))
         return
     c = SHAPES[args.model]
     L, D, H, att = c["layers"], c["dim"], c["heads"], c["att"]
