@@ -21,6 +21,22 @@ def test_library_exports_every_declared_symbol():
     assert set(_lib.SIGNATURES) == set(names)
 
 
+def test_ctypes_signatures_match_header_arity():
+    """Every entry point's ctypes argument list has as many entries as its
+    declaration in include/pk.h has parameters (an argument added on one side
+    only would shift every later one)."""
+    import re
+    text = re.sub(r"/\*.*?\*/", "", open(_lib.HEADER).read(), flags=re.S)
+    decls = dict(re.findall(r"\b(pk_[a-z_0-9]+)\s*\(([^;{]*?)\)\s*;", text, flags=re.S))
+    checked = 0
+    for name, args in _lib.SIGNATURES.items():
+        params = decls[name].strip()
+        n = 0 if params in ("", "void") else params.count(",") + 1
+        assert len(args) == n, (name, len(args), n)
+        checked += 1
+    assert checked == len(_lib.declared_functions())
+
+
 @pytest.mark.parametrize("left,chunk,ps", [(70, 2, 16), (70, 14, 16), (70, 2, 8), (33, 5, 16)])
 def test_page_geometry_matches_model(left, chunk, ps):
     lib = _lib.lib()
