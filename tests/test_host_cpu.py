@@ -21,18 +21,30 @@ def test_library_exports_every_declared_symbol():
     assert set(_lib.SIGNATURES) == set(names)
 
 
-def test_ctypes_signatures_match_header_arity():
-    """Every entry point's ctypes argument list has as many entries as its
-    declaration in include/pk.h has parameters (an argument added on one side
-    only would shift every later one)."""
+def test_ctypes_signatures_match_header_declarations():
+    """Every entry point's ctypes argument list matches its declaration in
+    include/pk.h parameter by parameter: the same count, pointers as pointers,
+    and the same integer or float width (an int32 passed where int64 is
+    declared leaves garbage in the upper half; an argument added on one side
+    only shifts every later one)."""
+    import ctypes
     import re
     text = re.sub(r"/\*.*?\*/", "", open(_lib.HEADER).read(), flags=re.S)
     decls = dict(re.findall(r"\b(pk_[a-z_0-9]+)\s*\(([^;{]*?)\)\s*;", text, flags=re.S))
+    scalar = {"int32_t": ctypes.c_int32, "int64_t": ctypes.c_int64, "float": ctypes.c_float,
+              "double": ctypes.c_double, "int": ctypes.c_int}
     checked = 0
     for name, args in _lib.SIGNATURES.items():
         params = decls[name].strip()
-        n = 0 if params in ("", "void") else params.count(",") + 1
-        assert len(args) == n, (name, len(args), n)
+        plist = [] if params in ("", "void") else [p.strip() for p in params.split(",")]
+        assert len(args) == len(plist), (name, len(args), len(plist))
+        for i, (c_param, ct) in enumerate(zip(plist, args)):
+            if "*" in c_param:
+                assert ct is ctypes.c_void_p or ct is ctypes.c_char_p or \
+                    issubclass(ct, ctypes._Pointer), (name, i, c_param, ct)
+            else:
+                ctype = c_param.replace("const ", "").split()[0]
+                assert ct is scalar[ctype], (name, i, c_param, ct)
         checked += 1
     assert checked == len(_lib.declared_functions())
 
