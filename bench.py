@@ -81,6 +81,9 @@ def parse():
     ap.add_argument("--no-graph", action="store_true", help="time eager launches only")
     ap.add_argument("--profile", action="store_true",
                     help="prefill + warmup + --steps steps only (for ncu), no report")
+    ap.add_argument("--install-reference", metavar="CHECKOUT", default=None,
+                    help="install the reference from a source checkout into baseline/_ref and exit")
+    ap.add_argument("--wheelhouse", default=None, help="offline wheel directory for pip")
     ap.add_argument("--profile-op", default=None,
                     choices=["append", "attention", "attention+append", "gather",
                              "gather_all_layers", "conv", "features", "streaming", "gemm"],
@@ -159,6 +162,30 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- reference arm
+def install_reference(src, wheelhouse=None):
+    """Installs the reference into baseline/_ref (git-ignored; it travels with
+    the working tree to the GPU box).  pip first, offline; the reference
+    builds with hatchling, which no offline wheelhouse here carries, so when
+    pip cannot build it the install is what its wheel would hold: the
+    reference's pure-Python ``parakeet`` package tree (pyproject's
+    ``[tool.hatch.build.targets.wheel] packages = ["parakeet"]``), copied
+    unmodified.  Returns the method used."""
+    import shutil
+    dst = os.path.join(REPO, "baseline", "_ref")
+    os.makedirs(dst, exist_ok=True)
+    cmd = [sys.executable, "-m", "pip", "install", "--no-index", "--no-build-isolation",
+           "--no-deps", "--target", dst, src]
+    if wheelhouse:
+        cmd[4:4] = ["--find-links", wheelhouse]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode == 0:
+        return "pip"
+    shutil.copytree(os.path.join(src, "parakeet"), os.path.join(dst, "parakeet"),
+                    ignore=shutil.ignore_patterns("__pycache__", "*.pyc"), dirs_exist_ok=True)
+    last = (r.stderr or r.stdout).strip().splitlines()[-1:] or [""]
+    return f"package tree copied (pip could not build offline: {last[0]})"
+
+
 def cpu_reference(args, seconds, steps=None):
     """Time oracle/baseline.ReferenceStep; returns (GB/s, steps, seconds, threads, sample)."""
     import numpy as np  # noqa: F401
@@ -241,7 +268,9 @@ def encoder_step(model, streams, steps, dev):
                            conv_kernel_size=9, att_context_size=att,
                            subsampling_conv_channels=256, use_bias=False)
     sd = random_encoder_layers(0, L, D, H)
-    enc.load_state_dict({k: torch.from_numpy(v) for k, v in sd.items()}, strict=True)
+    missing, unexpected = enc.load_state_dict({k: torch.from_numpy(v) for k, v in sd.items()},
+                                              strict=False)
+    assert not unexpected and all(k.startswith("pre_encode.") for k in missing)
     enc = enc.to(device=dev, dtype=torch.bfloat16).eval()
     state = enc.init_streaming_state(streams, dev, torch.bfloat16)
     g = torch.Generator(device=dev).manual_seed(7)
@@ -672,7 +701,7 @@ def build_streaming_pipeline(model, dev, num_slots, feature_kw=None):
     import torch
 
     from parakeet_b200.engine import StreamingPipeline
-    from parakeet_b200.modules import ConformerEncoder, ConvSubsampling, Joiner, Predictor
+    from parakeet_b200.modules import ConformerEncoder, Joiner, Predictor
     from parakeet_b200.weights import (random_decoder_state_dict, random_encoder_layers,
                                        random_pre_encode_state_dict)
     c, d = SHAPES[model], DECODE_CFG[model]
@@ -682,10 +711,10 @@ def build_streaming_pipeline(model, dev, num_slots, feature_kw=None):
                            num_heads=H, subsampling_factor=8, pos_emb_max_len=5000,
                            conv_kernel_size=9, att_context_size=att, subsampling_conv_channels=256,
                            use_bias=False)
-    enc.load_state_dict({k: torch.from_numpy(v) for k, v in random_encoder_layers(0, L, D, H).items()})
-    pre = ConvSubsampling(D, 256, 128, 8)
-    pre.load_state_dict({k: torch.from_numpy(v)
-                         for k, v in random_pre_encode_state_dict(6, 128, 256, D).items()})
+    sd = {**random_encoder_layers(0, L, D, H),
+          **{f"pre_encode.{k}": v for k, v in random_pre_encode_state_dict(6, 128, 256, D).items()}}
+    enc.load_state_dict({k: torch.from_numpy(v) for k, v in sd.items()})
+    pre = enc.pre_encode
     sd = random_decoder_state_dict(5, D, 640, 640, V, d["pred_layers"], blank_bias=2.3)
     pred, join = Predictor(640, 640, d["pred_layers"], V), Joiner(D, 640, 640, num_classes=V)
     pred.load_state_dict({k[10:]: torch.from_numpy(v) for k, v in sd.items()
@@ -1002,6 +1031,9 @@ def job_throughput(bytes_per_rank_step, world, ms):
 # ---------------------------------------------------------------- B200 arm
 def main():
     args = parse()
+    if args.install_reference:
+        print(install_reference(args.install_reference, args.wheelhouse))
+        return
     if args.impl == "reference":
         run_reference_arm(args)
         return

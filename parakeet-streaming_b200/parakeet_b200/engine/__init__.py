@@ -1,8 +1,7 @@
 from .decoding import BatchedGreedyDecoder
 from .pipeline import OverlappedStreamingRunner, StreamingPipeline
 from .pre_encode import BatchedPreEncoder
-from .scheduler import Scheduler, SlotAllocator, StreamResult
-from .sequence import Sequence, SequenceStatus
+from .scheduler import Scheduler, SequenceStatus, SlotAllocator, StreamResult
 
-__all__ = ["BatchedGreedyDecoder", "BatchedPreEncoder", "OverlappedStreamingRunner", "Scheduler", "SlotAllocator", "StreamResult", "Sequence",
-           "SequenceStatus", "StreamingPipeline"]
+__all__ = ["BatchedGreedyDecoder", "BatchedPreEncoder", "OverlappedStreamingRunner", "Scheduler",
+           "SequenceStatus", "SlotAllocator", "StreamResult", "StreamingPipeline"]

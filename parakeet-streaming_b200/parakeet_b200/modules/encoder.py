@@ -22,6 +22,7 @@ from .attention import ConformerAttention, PositionalEncoding
 from .cache import PagedModelCache, StreamingState
 from .convolution import ConformerConvolution
 from .feedforward import ConformerFeedForward
+from .subsample import ConvSubsampling
 
 
 class ConformerLayer(nn.Module):
@@ -67,6 +68,8 @@ class ConformerEncoder(nn.Module):
                  use_bias: bool, pre_encode_cache_size=(0, 9), drop_extra_pre_encoded: int = 2):
         super().__init__()
         self.embed_dim = hidden_size
+        self.pre_encode = ConvSubsampling(hidden_size, subsampling_conv_channels, feat_in,
+                                          subsampling_factor, stride=2, kernel_size=3)
         self.num_heads = num_heads
         self.feat_in = feat_in
         self.subsampling_factor = subsampling_factor
@@ -100,9 +103,11 @@ class ConformerEncoder(nn.Module):
         return StreamingState(PagedModelCache(pool, slots))
 
     def forward(self, x: Tensor, state: StreamingState, length: Tensor | None = None,
-                bypass_pre_encode: bool = True):
-        if not bypass_pre_encode:
-            raise NotImplementedError("pass subsampled chunks (bypass_pre_encode=True)")
+                bypass_pre_encode: bool = False):
+        """x [B, T, D]: one chunk of subsampled frames per slot of ``state``.
+        As in the reference (encoder.py:229-267), ``pre_encode`` is never run
+        here whatever ``bypass_pre_encode`` says: the engine runs it per
+        window (model_runner.py:221) and hands the encoder its frames."""
         cache = state.cache
         pool = cache.pool
         B, T = x.shape[:2]

@@ -114,3 +114,16 @@ def random_pre_encode_state_dict(seed, feat_in=128, channels=256, hidden=512, fa
     sd["out.weight"] = _lin(rng, hidden, channels * freq)
     sd["out.bias"] = (0.1 * rng.standard_normal(hidden)).astype(np.float32)
     return sd
+
+
+def random_model_state_dict(seed, layers, dim, heads, vocab_size, pred_layers, feat_in=128,
+                            sub_channels=256, pred_dim=640, joint_dim=640, blank_bias=0.0):
+    """A whole ``Parakeet`` model's parameters (parakeet/model.py:69-102) with
+    its state_dict keys: ``encoder.layers.*`` (seed), ``encoder.pre_encode.*``
+    (seed + 1), ``predictor.*`` and ``joiner.*`` (seed + 2)."""
+    sd = {f"encoder.{k}": v for k, v in random_encoder_layers(seed, layers, dim, heads).items()}
+    sd.update({f"encoder.pre_encode.{k}": v for k, v in
+               random_pre_encode_state_dict(seed + 1, feat_in, sub_channels, dim).items()})
+    sd.update(random_decoder_state_dict(seed + 2, dim, pred_dim, joint_dim, vocab_size,
+                                        pred_layers, blank_bias))
+    return sd

@@ -20,7 +20,6 @@ from __future__ import annotations
 import argparse
 import os
 import sys
-import types
 from types import SimpleNamespace
 
 import numpy as np
@@ -31,35 +30,20 @@ REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, os.path.join(REPO, "parakeet-streaming_b200"))
 from parakeet_b200.weights import random_encoder_layers, seeded_normal  # noqa: E402
 
-
-def install_librosa_stub():
-    import torchaudio
-
-    lib = types.ModuleType("librosa")
-    filters = types.ModuleType("librosa.filters")
-
-    def mel(sr, n_fft, n_mels, fmin, fmax, norm):
-        fb = torchaudio.functional.melscale_fbanks(
-            n_fft // 2 + 1, float(fmin), float(fmax), n_mels, sr,
-            norm=norm, mel_scale="slaney")
-        return fb.T.numpy()
-
-    filters.mel = mel
-    lib.filters = filters
-    sys.modules["librosa"] = lib
-    sys.modules["librosa.filters"] = filters
+sys.path.insert(0, os.path.join(REPO, "baseline"))
+from harness import install_librosa_stub  # noqa: E402,F401  (also used by the other generators)
 
 
 # Streams used by the encoder fixtures: (name, acquire step, release step or
 # None, step whose chunk is short).  A stream runs in steps acquire <= s < release
 # and is released at the start of step ``release``; a short chunk (length 1 < T)
 # is only ever that stream's last step, like a final chunk.
-SMALL_SCHEDULE = dict(att=(70, 1), dim=512, heads=8, layers=2, steps=40, pool=4,
+SMALL_SCHEDULE = dict(att=(70, 1), dim=512, heads=8, layers=17, steps=40, pool=4,
                       seed=11, events=[("a", 0, None, None), ("b", 0, 21, None),
                                        ("c", 6, None, None), ("d", 22, None, 39),
                                        ("e", 25, None, None)],
                       keep_steps=[0, 1, 2, 17, 34, 35, 36, 38, 39])
-LARGE_SCHEDULE = dict(att=(70, 13), dim=1024, heads=8, layers=1, steps=8, pool=3,
+LARGE_SCHEDULE = dict(att=(70, 13), dim=1024, heads=8, layers=24, steps=8, pool=3,
                       seed=12, events=[("a", 0, None, None), ("b", 2, None, None)],
                       keep_steps=[1, 6, 7])
 
@@ -208,6 +192,40 @@ def scheduler_fixture():
     return {"ops": np.array(ops, np.int64)}
 
 
+def admission_fixture():
+    """The reference Scheduler's admission queue (scheduler.py:35-66) under
+    seeded add / admit_ready / release calls, max_active 3: per call, the
+    sequences admitted, the running sequences in order and every sequence's
+    status.  Sequences are plain objects holding a status of the reference's
+    ``SequenceStatus`` (what ``Sequence.__init__`` sets, sequence.py:33)."""
+    import json
+
+    from parakeet.engine.scheduler import Scheduler
+    from parakeet.engine.sequence import SequenceStatus
+
+    sched = Scheduler(max_active=3)
+    rng = np.random.default_rng(13)
+    seqs, calls = [], []
+    for _ in range(300):
+        u = rng.random()
+        if u < 0.4 or not seqs:
+            seq = SimpleNamespace(status=SequenceStatus.WAITING, name=len(seqs))
+            seqs.append(seq)
+            sched.add(seq)
+            call, arg, admitted = "add", seq.name, []
+        elif u < 0.7:
+            call, arg = "admit", -1
+            admitted = [q.name for q in sched.admit_ready()]
+        else:
+            seq = seqs[int(rng.integers(len(seqs)))]
+            sched.release(seq)
+            call, arg, admitted = "release", seq.name, []
+        calls.append({"call": call, "arg": arg, "admitted": admitted,
+                      "active": [q.name for q in sched.active_sequences()],
+                      "status": [q.status.name for q in seqs]})
+    return {"calls": np.array(json.dumps(calls))}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True)
@@ -222,6 +240,7 @@ def main():
                         **cache_window_fixture((70, 13), 8, 9, 2, 2, 22))
     np.savez_compressed(os.path.join(HERE, "masks.npz"), **masks_fixture())
     np.savez_compressed(os.path.join(HERE, "scheduler_slots.npz"), **scheduler_fixture())
+    np.savez_compressed(os.path.join(HERE, "admission.npz"), **admission_fixture())
     np.savez_compressed(os.path.join(HERE, "encoder_small.npz"),
                         **run_encoder_fixture(None, SMALL_SCHEDULE))
     np.savez_compressed(os.path.join(HERE, "encoder_large.npz"),

@@ -11,7 +11,7 @@ import pytest
 import torch
 
 from parakeet_b200.engine import OverlappedStreamingRunner, StreamingPipeline
-from parakeet_b200.modules import ConformerEncoder, ConvSubsampling, Joiner, Predictor
+from parakeet_b200.modules import ConformerEncoder, Joiner, Predictor
 from parakeet_b200.weights import (random_decoder_state_dict, random_encoder_layers,
                                    random_pre_encode_state_dict)
 
@@ -26,11 +26,10 @@ def make(num_slots, **kw):
                            num_heads=HEADS, subsampling_factor=8, pos_emb_max_len=5000,
                            conv_kernel_size=9, att_context_size=(70, 1),
                            subsampling_conv_channels=256, use_bias=False)
-    enc.load_state_dict({k: torch.from_numpy(v)
-                         for k, v in random_encoder_layers(3, LAYERS, D, HEADS).items()})
-    pre = ConvSubsampling(D, 256, 128, 8)
-    pre.load_state_dict({k: torch.from_numpy(v)
-                         for k, v in random_pre_encode_state_dict(4, 128, 256, D).items()})
+    sd = {**random_encoder_layers(3, LAYERS, D, HEADS),
+          **{f"pre_encode.{k}": v for k, v in random_pre_encode_state_dict(4, 128, 256, D).items()}}
+    enc.load_state_dict({k: torch.from_numpy(v) for k, v in sd.items()})
+    pre = enc.pre_encode
     sd = random_decoder_state_dict(5, D, 640, 640, V, 1, blank_bias=2.3)
     pred, join = Predictor(640, 640, 1, V), Joiner(D, 640, 640, num_classes=V)
     pred.load_state_dict({k[10:]: torch.from_numpy(v) for k, v in sd.items()

@@ -122,3 +122,38 @@ def test_page_model_churn_conserves_pages():
         held = int((pool.next - pool.first).sum())
         assert held + len(pool.free) == pool.num_pages
         assert set(pool.free).isdisjoint(set(pool.table[pool.table >= 0].tolist()))
+
+
+def test_admission_queue_matches_reference_scheduler():
+    """The drop-in Scheduler's add / admit_ready / release against the
+    reference's (golden ``admission.npz`` from tests/golden/make_golden.py):
+    the same sequences admitted per call, the same running order, and every
+    status written with the caller's own enum."""
+    import enum
+    import json
+    from types import SimpleNamespace
+
+    from parakeet_b200.engine.scheduler import Scheduler
+
+    class CallerStatus(enum.Enum):      # stands in for the reference's SequenceStatus
+        WAITING = enum.auto()
+        RUNNING = enum.auto()
+        FINISHED = enum.auto()
+
+    calls = json.loads(str(load("admission.npz")["calls"]))
+    sched = Scheduler(max_active=3)
+    seqs = []
+    for c in calls:
+        admitted = []
+        if c["call"] == "add":
+            seqs.append(SimpleNamespace(status=CallerStatus.WAITING, name=c["arg"]))
+            sched.add(seqs[-1])
+        elif c["call"] == "admit":
+            admitted = [q.name for q in sched.admit_ready()]
+        else:
+            sched.release(seqs[c["arg"]])
+        assert admitted == c["admitted"]
+        assert [q.name for q in sched.active_sequences()] == c["active"]
+        assert all(type(q.status) is CallerStatus for q in seqs)
+        assert [q.status.name for q in seqs] == c["status"]
+    assert any(c["admitted"] for c in calls) and sched.num_waiting >= 0
