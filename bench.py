@@ -79,6 +79,8 @@ def parse():
     ap.add_argument("--no-serve", action="store_true",
                     help="skip the paced serving search (streams at p99 <= 160 ms)")
     ap.add_argument("--no-graph", action="store_true", help="time eager launches only")
+    ap.add_argument("--no-reference-engine", action="store_true",
+                    help="skip timing the reference's own engine in the serving search")
     ap.add_argument("--profile", action="store_true",
                     help="prefill + warmup + --steps steps only (for ncu), no report")
     ap.add_argument("--install-reference", metavar="CHECKOUT", default=None,
@@ -162,6 +164,24 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- reference arm
+def workload_config(model, streams, world):
+    """The ``config`` of both arms' JSON lines (the same workload)."""
+    c = SHAPES[model]
+    L, D, H, att = c["layers"], c["dim"], c["heads"], c["att"]
+    T = att[1] + 1
+    per = -(-(att[0] + T - 1) // PAGE) + 1        # pages a stream's window can touch
+    pool_mb = streams * per * L * 2 * PAGE * D * 2 / 1e6
+    b = alg_bytes(model)
+    step_mb = (b["append"] + b["attention"]) * streams * L / 1e6
+    return {"workload": f"configs[1] isolated paged-attention step, {model} model",
+            "streams_per_gpu": streams, "layers": L, "heads": H, "head_dim": D // H,
+            "chunk": T, "left_context": att[0], "page_size": PAGE,
+            "page_order": "randperm seed 1",
+            "l2": f"inputs > L2: {pool_mb:.0f} MB page pool, {step_mb:.0f} MB read+written "
+                  f"per step",
+            "parallelism": f"{world} independent replicas (stream sharding)"}
+
+
 def install_reference(src, wheelhouse=None):
     """Installs the reference into baseline/_ref (git-ignored; it travels with
     the working tree to the GPU box).  pip first, offline; the reference
@@ -186,21 +206,127 @@ def install_reference(src, wheelhouse=None):
     return f"package tree copied (pip could not build offline: {last[0]})"
 
 
-def cpu_reference(args, seconds, steps=None):
-    """Time oracle/baseline.ReferenceStep; returns (GB/s, steps, seconds, threads, sample)."""
-    import numpy as np  # noqa: F401
+class ReferenceTorchStep:
+    """configs[1]'s step through the reference's own code on the host cores
+    (torch CPU, fp32), from the install under baseline/_ref: its ``Scheduler``
+    (pack_states / unpack_states over a ``ModelCache`` slot pool,
+    parakeet/engine/scheduler.py:68-201), ``ConformerEncoder._create_streaming_masks``
+    (parakeet/modules/encoder.py:167-227), ``ConformerAttention.forward`` per
+    layer (parakeet/modules/attention.py:85-125: ``update_attn_cache``,
+    ``linear_pos``, ``rel_shift``, the masked fill and SDPA) and the counter
+    update of encoder.py:257-260.  The step's Q/K/V are inputs here, so each
+    layer's ``qkv`` projection is replaced by a module that hands the forward
+    that layer's given rows, and ``linear_out`` by the identity (the metric's
+    output is the attention output); everything between runs unmodified."""
 
+    def __init__(self, num_layers, dim, heads, att_context, num_streams, seed=1):
+        import torch
+        from types import SimpleNamespace
+        sys.path.insert(0, os.path.join(REPO, "baseline"))
+        import harness
+        harness.import_reference()
+        from parakeet.engine.scheduler import Scheduler
+        from parakeet.modules import ConformerAttention, ModelCache, PositionalEncoding
+        from parakeet.modules.cache import StreamingState
+        from parakeet.modules.encoder import ConformerEncoder
+
+        self.torch = torch
+        self.L, self.D, self.H, self.att, self.B = num_layers, dim, heads, att_context, num_streams
+        self.T = att_context[1] + 1
+
+        class Pool:                    # what init_state_pool asks of an encoder
+            @staticmethod
+            def init_streaming_state(batch_size, device, dtype):
+                z = torch.zeros(batch_size, dtype=torch.int64)
+                return StreamingState(ModelCache(num_layers, att_context, dim, 9, batch_size,
+                                                 device, dtype), z, z.clone())
+
+        self.sched = Scheduler(max_active=num_streams)
+        self.sched.init_state_pool(Pool(), torch.device("cpu"), torch.float32, num_streams)
+        self.seqs = [SimpleNamespace(encoder_state=self.sched.acquire_state_slot())
+                     for _ in range(num_streams)]
+        self.masks = lambda *a: ConformerEncoder._create_streaming_masks(
+            SimpleNamespace(att_context_size=att_context), *a)
+        g = torch.Generator().manual_seed(seed)
+        s = (dim // heads) ** -0.5
+        self.given = [None] * num_layers
+
+        class Given(torch.nn.Module):   # hands forward() this layer's Q/K/V rows
+            def __init__(self, owner, l):
+                super().__init__()
+                self.owner, self.l = owner, l
+
+            def forward(self, x):
+                return self.owner.given[self.l]
+
+        self.attn = []
+        for l in range(num_layers):
+            a = ConformerAttention(l, heads, dim, use_bias=False)
+            with torch.no_grad():
+                a.linear_pos.weight.copy_(torch.randn(dim, dim, generator=g) * dim ** -0.5)
+                a.pos_bias_u.copy_(torch.randn(heads, dim // heads, generator=g) * s)
+                a.pos_bias_v.copy_(torch.randn(heads, dim // heads, generator=g) * s)
+            a.qkv, a.linear_out = Given(self, l), torch.nn.Identity()
+            self.attn.append(a.eval())
+        pe = PositionalEncoding(dim, 0.0, 5000, 0.0)
+        pe.extend_pe(5000, torch.device("cpu"))
+        self.pos_enc = pe
+        self.g = g
+
+    def inputs(self):
+        s = (self.D // self.H) ** -0.5
+        return self.torch.randn(self.L, self.B, self.T, 3 * self.D, generator=self.g) * s
+
+    def step(self, qkv, lengths=None):
+        torch = self.torch
+        T = self.T
+        length = torch.full((self.B,), T, dtype=torch.int64) if lengths is None else lengths
+        with torch.inference_mode():
+            st, idx = self.sched.pack_states(self.seqs)
+            x = torch.empty(self.B, T, self.D)
+            x, pos_emb = self.pos_enc(x, cache_len=self.att[0])
+            _, att_mask = self.masks(T, st.cache_lengths, st.processed_frames,
+                                     torch.device("cpu"), length)
+            out = []
+            for l, a in enumerate(self.attn):
+                self.given[l] = qkv[l]
+                out.append(a(x, pos_emb, att_mask, st.cache))
+            st.processed_frames.add_(length)
+            st.cache_lengths.add_(length)
+            st.cache_lengths.clamp_(max=self.att[0])
+            self.sched.unpack_states(st, idx)
+        return out
+
+
+def reference_step_class():
+    """The reference's own code (``ReferenceTorchStep``) when baseline/_ref
+    holds it, else the float32 numpy restatement (oracle/baseline.py)."""
+    sys.path.insert(0, os.path.join(REPO, "baseline"))
+    import harness
+    if harness.available():
+        return ReferenceTorchStep, "reference"
     from oracle.baseline import ReferenceStep
-    try:
-        from threadpoolctl import threadpool_info
-        threads = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
-    except Exception:
-        threads = os.cpu_count() or 1
+    return ReferenceStep, "port"
+
+
+def cpu_reference(args, seconds, steps=None):
+    """Time the reference's step on the host cores (``reference_step_class``);
+    returns (GB/s, steps, seconds, threads, sample, kind)."""
+    cls, kind = reference_step_class()
+    if kind == "reference":
+        import torch
+        torch.set_num_threads(os.cpu_count() or 1)
+        threads = torch.get_num_threads()
+    else:
+        try:
+            from threadpoolctl import threadpool_info
+            threads = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
+        except Exception:
+            threads = os.cpu_count() or 1
     c = SHAPES[args.model]
-    ref = ReferenceStep(c["layers"], c["dim"], c["heads"], c["att"], args.streams)
-    left, T = c["att"][0], c["att"][1] + 1
+    ref = cls(c["layers"], c["dim"], c["heads"], c["att"], args.streams)
     x = ref.inputs()
-    ref.step(x)  # warm (allocations, BLAS threads)
+    ref.step(x)  # warm (allocations, thread pools)
     done, t0 = 0, time.perf_counter()
     while True:
         ref.step(x)
@@ -210,9 +336,11 @@ def cpu_reference(args, seconds, steps=None):
             break
     b = alg_bytes(args.model, es=2)
     per_step = (b["append"] + b["attention"]) * args.streams * c["layers"]
-    sample = (f"{done} steps x {args.streams} streams x {c['layers']} layers "
-              f"(pack, mask loop, shift-append, attention, unpack), float32 numpy")
-    return per_step * done / el / 1e9, done, el, threads, sample
+    what = ("the reference's own Scheduler / ModelCache / masks / ConformerAttention, torch "
+            "CPU float32" if kind == "reference" else
+            "pack, mask loop, shift-append, attention, unpack; float32 numpy restatement")
+    sample = f"{done} steps x {args.streams} streams x {c['layers']} layers ({what})"
+    return per_step * done / el / 1e9, done, el, threads, sample, kind
 
 
 def run_reference_arm(args):
@@ -220,12 +348,16 @@ def run_reference_arm(args):
     if rank != 0:
         return
     K, W = args.steps, args.warmup
-    # each step is a bounded sample: at most ~1.5 s of CPU work per step
-    from oracle.baseline import ReferenceStep
+    # each step is a bounded sample: at most ~150 s of CPU work for the whole run
+    cls, kind = reference_step_class()
+    if kind == "reference":
+        import torch
+        torch.set_num_threads(os.cpu_count() or 1)
     c = SHAPES[args.model]
     streams = args.streams
-    probe = ReferenceStep(c["layers"], c["dim"], c["heads"], c["att"], streams)
+    probe = cls(c["layers"], c["dim"], c["heads"], c["att"], streams)
     x = probe.inputs()
+    probe.step(x)
     t0 = time.perf_counter()
     probe.step(x)
     one = time.perf_counter() - t0
@@ -233,19 +365,19 @@ def run_reference_arm(args):
     sample_streams = streams
     while one * sample_streams / streams > budget and sample_streams > 1:
         sample_streams = max(1, sample_streams // 2)
+    del probe
     args2 = argparse.Namespace(**vars(args))
     args2.streams = sample_streams
-    gbs, done, el, threads, sample = cpu_reference(args2, 0, steps=K + W)
+    gbs, done, el, threads, sample, kind = cpu_reference(args2, 0, steps=K + W)
     b = alg_bytes(args.model)
     print(json.dumps({
         "impl": "reference", "metric": "paged-attn HBM GB/s (append + attention, algorithmic bytes)",
         "value": round(gbs, 4), "unit": "GB/s", "n_gpus": args.gpus, "steps": K, "warmup": W,
         "ms_per_step": round(1e3 * el / done, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"configs[1] isolated paged-attention step, {args.model} model",
-                   "streams": sample_streams, "layers": c["layers"]},
+        "config": workload_config(args.model, streams, args.gpus),
         "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": threads,
-                         "kind": "port", "sample": sample},
+                         "kind": kind, "sample": sample},
         "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
         "bytes_per_stream_layer": {"append": b["append"], "attention": b["attention"]},
@@ -809,40 +941,107 @@ def streaming_step(model, steps, dev, profile=False, streams=None):
     return out
 
 
-def serve_trial(pipe, N, period, banks, hbufs, dbufs, hslots, dslots, htok, hcnt,
-                warm_periods, meas_periods, seed, max_batch=2048, full_graph=None):
-    """N streams paced in real time: stream i's chunk k completes at
-    t0 + phase_i + k * period (phases uniform over one period).  The loop takes
-    every chunk that has completed (one per stream per iteration), groups them
-    by push index (first, second, later; batches of at most 2048 streams), copies
-    their samples
-    and slots in from pinned host memory, runs ``step_audio`` (a later-chunk
-    batch of exactly ``max_batch`` streams as the replay of ``full_graph`` =
-    (graph, samples, slots, tokens, counts) when given, every other batch
-    eagerly) and copies the tokens back to pinned host memory; a chunk's latency is the
-    wall time from its completion to its tokens being on the host (the
-    reference's push_samples -> DecodeResult, model_runner.py:150-171).
-    Returns latencies (s) of the chunks completed in the measured periods and
-    the loop's statistics."""
+class ServePositions:
+    """Stream positions of the paced serving trials on one GPU, one slot each.
+    A position always holds a live stream of ``life`` chunks (configs[2]: 30 s
+    of audio); when it ends, its slot is released and a new stream starts there
+    at the position's next chunk time, so streams join and leave every period
+    (about N / life of them).  Positions persist across trials: trial N runs
+    positions 0..N-1, whose streams keep their age.  ``age`` is the chunk
+    index of each position's current stream; streams start at ages uniform in
+    [0, life), and before the first trial every position is stepped through
+    min(age, fill) chunks, ``fill`` covering the 70-frame left context and
+    then some (36 small, 7 large), so trials run on full windows from their
+    first chunk, as steady-state serving does."""
+
+    def __init__(self, cap, period, life, fill, seed):
+        import numpy as np
+        rng = np.random.default_rng(seed)
+        self.cap, self.period, self.life, self.fill = cap, period, life, fill
+        self.phase = rng.uniform(0.0, period, cap)
+        self.age = rng.integers(0, life, cap).astype(np.int64)
+        self.joined = 0
+
+
+def _serve_batch(pipe, c, part, k, banks, hbufs, dbufs, hslots, dslots, htok, hcnt, off,
+                 full_graph, max_batch):
+    """Copies the samples and slots of rows ``part`` (push class c: first,
+    second, later) in from pinned host memory, runs their step (a later-chunk
+    batch of exactly ``max_batch`` rows as the captured graph), and queues the
+    tokens' copy back to pinned host memory."""
+    import torch
+    B = part.size
+    rs = slice(off, off + B)
+    bank = banks[c]
+    torch.index_select(bank, 0, torch.from_numpy((part + k[part]) % bank.shape[0]),
+                       out=hbufs[c][rs])
+    hslots[c][rs].numpy()[:] = part
+    if full_graph is not None and c == 2 and B == max_batch:
+        gph, dx, ds, tok, cnt = full_graph
+        dx.copy_(hbufs[c][rs], non_blocking=True)
+        ds.copy_(hslots[c][rs], non_blocking=True)
+        gph.replay()
+    else:
+        dx = dbufs[c][rs]
+        dx.copy_(hbufs[c][rs], non_blocking=True)
+        ds = dslots[c][rs]
+        ds.copy_(hslots[c][rs], non_blocking=True)
+        tok, cnt = pipe.step_audio(dx, ds, c)
+    htok[c][rs].copy_(tok.view(B, -1), non_blocking=True)
+    hcnt[c][rs].copy_(cnt, non_blocking=True)
+
+
+def serve_prefill(pipe, pos, bufs, full_graph, max_batch=2048):
+    """Steps every position through min(age, fill) chunks as fast as the GPU
+    runs them (no pacing), so that each stream's pages, conv cache, feature
+    history and prediction state are those of a stream of that age."""
+    import numpy as np
+    import torch
+    pipe.start_streams(torch.arange(pos.cap, dtype=torch.int32))
+    target = np.minimum(pos.age, pos.fill)
+    k = np.zeros(pos.cap, np.int64)
+    for c in range(int(target.max(initial=0))):
+        sel = np.flatnonzero(target > c)
+        cls = min(c, 2)
+        for off in range(0, sel.size, max_batch):
+            part = sel[off:off + max_batch]
+            _serve_batch(pipe, cls, part, k, *bufs, 0, full_graph, max_batch)
+        k[sel] += 1
+    torch.cuda.synchronize(pipe.device)
+
+
+def serve_trial(pipe, N, pos, bufs, warm_periods, meas_periods, max_batch=2048,
+                full_graph=None):
+    """Positions 0..N-1 paced in real time: position i's next chunk completes
+    at t0 + phase_i + m * period (m = chunks it has pushed in this trial).
+    The loop takes every chunk that has completed (one per position per
+    iteration), groups them by push class of their stream (first, second,
+    later; batches of at most 2048 rows), copies their samples and slots in
+    from pinned host memory, runs ``step_audio`` (a later-chunk batch of exactly
+    ``max_batch`` rows as the replay of ``full_graph`` = (graph, samples, slots,
+    tokens, counts) when given, every other batch eagerly) and copies the
+    tokens back to pinned host memory; a chunk's latency is the wall time from
+    its completion to its tokens being on the host (the reference's
+    push_samples -> DecodeResult, model_runner.py:150-171).  Streams that
+    reach their last chunk are released (pages back to the pool at the next
+    step) and a new stream starts in their slot.  Returns latencies (s) of
+    the chunks completed in the measured periods and the loop's statistics."""
     import numpy as np
     import torch
 
-    dev = pipe.device
-    rng = np.random.default_rng(seed)
-    phase = rng.uniform(0.0, period, N)
-    k = np.zeros(N, np.int64)
-    slots_all = torch.arange(N, dtype=torch.int32)
-    pipe.start_streams(slots_all)
-    torch.cuda.synchronize(dev)
+    period = pos.period
+    k = pos.age[:N].copy()
+    m = np.zeros(N, np.int64)
+    phase = pos.phase[:N]
     t0 = time.perf_counter() + 0.02
     t_meas, t_end = t0 + warm_periods * period, t0 + (warm_periods + meas_periods) * period
-    lats, steps, rows, launches = [], 0, 0, 0
+    lats, steps, rows, launches, joins = [], 0, 0, 0, 0
     ev = torch.cuda.Event()
     while True:
         now = time.perf_counter()
         if now >= t_end:
             break
-        arr = t0 + phase + k * period
+        arr = t0 + phase + m * period
         ready = np.flatnonzero(arr <= now)
         if ready.size == 0:
             time.sleep(max(0.0, min(float(arr.min()), t_end) - now))
@@ -852,30 +1051,12 @@ def serve_trial(pipe, N, period, banks, hbufs, dbufs, hslots, dslots, htok, hcnt
         for c in (0, 1, 2):
             sel = ready[cls == c]
             sel = sel[np.argsort(arr[sel], kind="stable")]
-            # batches of at most 2048 rows (the step's allocator), oldest first,
-            # each in its own rows of the buffers (copies are still in flight)
+            # batches of at most 2048 rows, oldest first, each in its own rows
+            # of the buffers (copies are still in flight)
             for off in range(0, sel.size, max_batch):
                 part = sel[off:off + max_batch]
-                B = part.size
-                rs = slice(off, off + B)
-                bank = banks[c]
-                torch.index_select(bank, 0, torch.from_numpy((part + k[part]) % bank.shape[0]),
-                                   out=hbufs[c][rs])
-                hslots[c][rs].numpy()[:] = part
-                if full_graph is not None and c == 2 and B == max_batch:
-                    gph, dx, ds, tok, cnt = full_graph
-                    dx.copy_(hbufs[c][rs], non_blocking=True)
-                    ds.copy_(hslots[c][rs], non_blocking=True)
-                    gph.replay()
-                else:
-                    dx = dbufs[c][rs]
-                    dx.copy_(hbufs[c][rs], non_blocking=True)
-                    ds = dslots[c][rs]
-                    ds.copy_(hslots[c][rs], non_blocking=True)
-                    tok, cnt = pipe.step_audio(dx, ds, c)
-                htok[c][rs].copy_(tok.view(B, -1), non_blocking=True)
-                hcnt[c][rs].copy_(cnt, non_blocking=True)
-                rows += B
+                _serve_batch(pipe, c, part, k, *bufs, off, full_graph, max_batch)
+                rows += part.size
                 launches += 1
             if sel.size:
                 launched.append((sel, arr[sel]))
@@ -885,39 +1066,104 @@ def serve_trial(pipe, N, period, banks, hbufs, dbufs, hslots, dslots, htok, hcnt
         for sel, a in launched:
             lats.append(t_done - a[a >= t_meas])
             k[sel] += 1
+            m[sel] += 1
+        ended = ready[k[ready] >= pos.life]
+        if ended.size:               # streams leave, new ones take their slots
+            sl = torch.from_numpy(ended.astype(np.int32))
+            pipe.end_streams(sl)
+            pipe.start_streams(sl)
+            k[ended] = 0
+            joins += ended.size
         steps += 1
-    backlog = int(np.max(np.floor((t_end - t0 - phase) / period) + 1 - k))
-    pipe.end_streams(slots_all)
+    pos.age[:N] = k
+    pos.joined += joins
+    backlog = int(np.max(np.floor((t_end - t0 - phase) / period) + 1 - m))
     lat = np.concatenate(lats) if lats else np.zeros(0)
     return lat, {"iterations": steps, "steps": launches,
                  "mean_batch": round(rows / max(launches, 1), 1),
-                 "backlog_chunks_at_end": backlog}
+                 "streams_joined": joins, "backlog_chunks_at_end": backlog}
 
 
-def serving_search(model, dev, measure_s=3.0, max_trials=9, limit_ms=160.0, use_graph=True):
-    """Metric 1 of the survey: the most concurrent streams one GPU serves with
+def reduce_over_ranks(vals, op, world, dev):
+    """All-reduce of a few host scalars over the process group (control plane
+    of the multi-GPU serving search; identity on one rank)."""
+    if world == 1:
+        return list(vals)
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor(list(vals), dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=op)
+    return t.tolist()
+
+
+def job_trial(total, world, rank, cap, dev, limit_ms, local_trial):
+    """One serving trial of ``total`` streams over the job: ``StreamRouter``
+    places them (least loaded; every rank computes the same placement, its
+    share is a prefix of its positions), ``local_trial(n)`` serves this rank's
+    n and returns (latencies s, stats); the job passes when every rank's p99
+    is within the limit and no rank is left behind by more than one chunk."""
+    import numpy as np
+    import torch.distributed as dist
+
+    from parakeet_b200.engine import StreamRouter
+    router = StreamRouter(world, capacity=cap)
+    mine = sum(router.place(p) == rank for p in range(total))
+    lat, st = local_trial(mine)
+    p99 = float(np.percentile(lat, 99)) * 1e3 if lat.size else float("inf")
+    p50 = float(np.median(lat)) * 1e3 if lat.size else float("inf")
+    mx = dist.ReduceOp.MAX if world > 1 else None
+    sm = dist.ReduceOp.SUM if world > 1 else None
+    p99, p50m, backlog = reduce_over_ranks([p99, p50, st["backlog_chunks_at_end"]], mx, world, dev)
+    chunks, joined, served = reduce_over_ranks(
+        [float(lat.size), float(st.get("streams_joined", 0)), float(mine)], sm, world, dev)
+    ok = p99 <= limit_ms and backlog <= 1
+    return ok, {"streams": total, "streams_per_gpu": round(total / world, 1),
+                "streams_served": int(served), "ok": ok, "p50_ms": round(p50m, 2),
+                "p99_ms": round(p99, 2), "chunks": int(chunks), "streams_joined": int(joined),
+                "backlog_chunks_at_end": int(backlog),
+                "iterations": st.get("iterations"), "mean_batch": st.get("mean_batch")}
+
+
+def serving_search(model, dev, measure_s=3.0, max_trials=9, limit_ms=160.0, use_graph=True,
+                   lifetime_s=30.0, start_per_gpu=1024, fixed_total=None):
+    """Metric 1 of the survey: the most concurrent streams per GPU served with
     p99 chunk latency <= 160 ms, streams paced in real time (configs[2] /
-    configs[3] audio, random bf16 weights).  Doubling from 1024 streams until
-    a trial fails (p99 above the limit, or chunks left waiting at the end),
-    then bisection, a failing trial repeated once; the slot count is capped by
-    85 % of the free device memory (every slot holds its K/V pages).  Batch
-    sizes vary from step to step: a later-chunk batch of the full 2048 streams
-    replays one CUDA graph, every other batch runs eagerly."""
+    configs[3] audio, random bf16 weights), each stream living ``lifetime_s``
+    (streams join and leave every period), every window full (positions
+    prefilled, ``ServePositions``).  On N GPUs (one process each) the job's
+    streams are placed by ``StreamRouter`` (least loaded), each rank serves its
+    share, and a trial passes when every rank's p99 and backlog pass (the
+    job's p99 is the largest rank p99).  The total doubles from
+    ``start_per_gpu`` x N until a trial fails (p99 above the limit, or chunks
+    left waiting at the end; a failing trial is repeated once), then
+    bisects; slots per GPU are capped by 85 % of its free memory (every slot
+    holds its K/V pages).  ``fixed_total``: one trial at that many streams
+    (configs[3]: 480 large streams over the job) before the search."""
     import numpy as np
     import torch
+    import torch.distributed as dist
 
     from parakeet_b200.ops import pages_per_stream
+    world = dist.get_world_size() if dist.is_available() and dist.is_initialized() else 1
+    rank = dist.get_rank() if world > 1 else 0
+
+    def reduce(vals, op):
+        return reduce_over_ranks(vals, op, world, dev)
+
     c = SHAPES[model]
     L, D, att = c["layers"], c["dim"], c["att"]
     la = att[1]
     T = la + 1
     period = (la + 1) * 0.08
     n0, n = (1 + 8 * la) * 160, (8 + 8 * la) * 160
+    life = int(round(lifetime_s / period))
+    fill = -(-att[0] // T) + 1
     per_slot = (pages_per_stream(att[0], T, PAGE) * L * 2 * PAGE * D * 2 + L * D * 8 * 2
                 + 128 * 9 * 2 + 4096)
     torch.cuda.empty_cache()
     free = torch.cuda.mem_get_info(dev)[0]
     cap = int(min(65536, 0.85 * free / per_slot)) // 256 * 256
+    cap = int(reduce([cap], dist.ReduceOp.MIN if world > 1 else None)[0])
     pipe = build_streaming_pipeline(model, dev, cap)
     S = pipe.dec.max_symbols
     audio = synth_audio_batch(64, n0 + 2 * n, seed=11)
@@ -929,9 +1175,11 @@ def serving_search(model, dev, measure_s=3.0, max_trials=9, limit_ms=160.0, use_
     dslots = [torch.empty(cap, dtype=torch.int32, device=dev) for _ in range(3)]
     htok = [torch.empty(cap, T * S, dtype=torch.int32).pin_memory() for _ in range(3)]
     hcnt = [torch.empty(cap, T, dtype=torch.int32).pin_memory() for _ in range(3)]
+    bufs = (banks, hbufs, dbufs, hslots, dslots, htok, hcnt)
     meas = max(3, int(round(measure_s / period)))
+    warm = 3 if period < 0.5 else 2
     trials, ok_n, bad_n = [], 0, None
-    N = min(1024, cap)
+    t_start = time.perf_counter()
     with torch.inference_mode():
         # Warm-up: one first, second and later step at batch sizes 1 ... wcap
         # (ratio 1.5), so that every kernel the trials' batch sizes select is
@@ -941,10 +1189,10 @@ def serving_search(model, dev, measure_s=3.0, max_trials=9, limit_ms=160.0, use_
         for B in sizes:
             sl = torch.arange(B, dtype=torch.int32)
             pipe.start_streams(sl)
-            for c in range(3):
-                dbufs[c][:B].copy_(banks[c][torch.arange(B) % banks[c].shape[0]])
-                dslots[c][:B].copy_(sl)
-                pipe.step_audio(dbufs[c][:B], dslots[c][:B], c)
+            for cc in range(3):
+                dbufs[cc][:B].copy_(banks[cc][torch.arange(B) % banks[cc].shape[0]])
+                dslots[cc][:B].copy_(sl)
+                pipe.step_audio(dbufs[cc][:B], dslots[cc][:B], cc)
             pipe.end_streams(sl)
         torch.cuda.synchronize(dev)
         # A later-chunk step of a full 2048-stream batch as one CUDA graph: the
@@ -968,21 +1216,25 @@ def serving_search(model, dev, measure_s=3.0, max_trials=9, limit_ms=160.0, use_
                 gtok, gcnt = pipe.step_audio(gx, gs, 2)
             pipe.end_streams(sl)
             full_graph = (gph, gx, gs, gtok, gcnt)
-        serve_trial(pipe, min(64, cap), period, banks, hbufs, dbufs, hslots, dslots, htok, hcnt,
-                    3, 1, seed=0, full_graph=full_graph)
+        pos = ServePositions(cap, period, life, fill, seed=1000 + rank)
+        t_pf = time.perf_counter()
+        serve_prefill(pipe, pos, bufs, full_graph)
+        prefill_s = time.perf_counter() - t_pf
+        serve_trial(pipe, min(64, cap), pos, bufs, 2, 1, full_graph=full_graph)
 
-        def run(N, seed):
-            lat, st = serve_trial(pipe, N, period, banks, hbufs, dbufs, hslots, dslots, htok, hcnt,
-                                  3, meas, seed=seed, full_graph=full_graph)
-            p99 = float(np.percentile(lat, 99)) * 1e3 if lat.size else float("inf")
-            ok = p99 <= limit_ms and st["backlog_chunks_at_end"] <= 1
-            return ok, {"streams": N, "ok": ok, "p50_ms": round(float(np.median(lat)) * 1e3, 2),
-                        "p99_ms": round(p99, 2), "chunks": int(lat.size), **st}
+        def run(total):
+            return job_trial(total, world, rank, cap, dev, limit_ms,
+                             lambda mine: serve_trial(pipe, mine, pos, bufs, warm, meas,
+                                                      full_graph=full_graph))
 
+        fixed = None
+        if fixed_total:
+            _, fixed = run(min(fixed_total, cap * world))
+        N = min(start_per_gpu, cap) * world
         while len(trials) < max_trials:
-            ok, rec = run(N, len(trials) + 1)
+            ok, rec = run(N)
             if not ok:   # a trial fails only if its repeat fails too
-                ok, rec2 = run(N, 100 + len(trials))
+                ok, rec2 = run(N)
                 rec = {**rec2, "first_attempt_p99_ms": rec["p99_ms"]}
             trials.append(rec)
             if ok:
@@ -990,25 +1242,59 @@ def serving_search(model, dev, measure_s=3.0, max_trials=9, limit_ms=160.0, use_
             else:
                 bad_n = N
             if bad_n is None:
-                if N >= cap:
+                if N >= cap * world:
                     break
-                N = min(2 * N, cap)
+                N = min(2 * N, cap * world)
             else:
-                if bad_n - ok_n <= max(64, ok_n // 16):
+                if bad_n - ok_n <= max(64 * world, ok_n // 16):
                     break
-                N = (ok_n + bad_n) // 2 // 32 * 32
+                N = (ok_n + bad_n) // 2 // (32 * world) * (32 * world)
     err = pipe.pool.read_error() | pipe.fe.error_bits()
+    err = int(reduce([float(err)], dist.ReduceOp.MAX if world > 1 else None)[0])
     del pipe
     torch.cuda.empty_cache()
     best = next((t for t in trials if t["streams"] == ok_n), None)
-    return {"model": model, "limit_ms": limit_ms, "streams_max": ok_n,
-            "capped_by_memory": bad_n is None and ok_n == cap, "slot_cap": cap,
-            "p99_ms_at_max": best["p99_ms"] if best else None,
-            "audio_ms_per_chunk": period * 1e3, "measured_s_per_trial": round(meas * period, 2),
-            "trials": trials, "device_error_word": err,
-            "full_batch_graph": full_graph is not None,
-            "method": "streams paced in real time, batched steps over every completed "
-                      "chunk, latency = chunk completion -> tokens in pinned host memory"}
+    out = {"model": model, "limit_ms": limit_ms, "n_gpus": world,
+           "streams_max": ok_n, "streams_per_gpu": round(ok_n / world, 1),
+           "capped_by_memory": bad_n is None and ok_n == cap * world, "slot_cap_per_gpu": cap,
+           "p99_ms_at_max": best["p99_ms"] if best else None,
+           "audio_ms_per_chunk": period * 1e3, "measured_s_per_trial": round(meas * period, 2),
+           "stream_life_s": lifetime_s, "prefill_chunks": fill,
+           "prefill_s": round(prefill_s, 1), "search_s": round(time.perf_counter() - t_start, 1),
+           "trials": trials, "device_error_word": err,
+           "full_batch_graph": full_graph is not None,
+           "method": "streams paced in real time, full windows (prefilled), 30 s lifetimes "
+                     "(streams leave and new ones join), batched steps over every completed "
+                     "chunk, latency = chunk completion -> tokens in pinned host memory"
+                     + ("; job streams placed least-loaded across GPUs" if world > 1 else "")}
+    if fixed is not None:
+        out["fixed_load"] = fixed
+    return out
+
+
+def serve_lines(args, dev, world):
+    """Streams per GPU at p99 <= 160 ms.  One GPU: this package's engine for
+    configs[2] (small) and configs[3] (large), each beside the reference's own
+    engine on the same GPU (``reference_engine_search``).  N GPUs: configs[3],
+    480 large streams placed across the N engines, then the search for the
+    most the job serves."""
+    if world == 1:
+        out = {}
+        for model in ("small", "large"):
+            ours = serving_search(model, dev, measure_s=3.0 if model == "small" else 4.0,
+                                  max_trials=9 if model == "small" else 7,
+                                  fixed_total=480 if model == "large" else 160)
+            ref = None
+            if not args.no_reference_engine:
+                ref = reference_engine_search(model, dev, max_trials=8 if model == "small" else 6,
+                                              measure_s=3.0 if model == "small" else 4.0)
+            if ref and ref.get("streams_max"):
+                ours["vs_reference_engine"] = round(ours["streams_max"] / ref["streams_max"], 1)
+            ours["reference_engine"] = ref
+            out[model] = ours
+        return out
+    return {"large": serving_search("large", dev, measure_s=4.0, max_trials=6,
+                                    fixed_total=480)}
 
 
 def max_over_ranks(vals, device):
@@ -1237,8 +1523,8 @@ def main():
         fe_line = feature_step(args.model, 50, dev)
         gemm_line = {m: gemm_step(m, 20, dev) for m in ("small", "large")}
         pipe_line = streaming_step(args.model, 10, dev)
-        if not args.no_serve:
-            serve_line = serving_search(args.model, dev)
+    if not args.no_serve:
+        serve_line = serve_lines(args, dev, world)
     err = pool.read_error()
 
     # ---- end to end through the public API, as a serving loop runs it: every step
@@ -1353,8 +1639,8 @@ def main():
                     traffic = tj.get("dram_bytes_per_launch")
         cpu = None
         if world == 1:
-            gbs, done, el, threads, sample = cpu_reference(args, args.cpu_seconds)
-            cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+            gbs, done, el, threads, sample, ckind = cpu_reference(args, args.cpu_seconds)
+            cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": ckind,
                    "sample": sample}
         value = job_throughput(step_bytes, world, ms)
         e2e = job_throughput(step_bytes, world, e2e_ms)
@@ -1364,14 +1650,8 @@ def main():
             "warmup": args.warmup, "ms_per_step": round(ms, 4),
             "ms_per_step_eager": round(eager_ms, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": f"configs[1] isolated paged-attention step, {args.model} model",
-                       "streams_per_gpu": B, "layers": L, "heads": H, "head_dim": dh,
-                       "chunk": T, "left_context": left, "page_size": PAGE,
-                       "page_order": "randperm seed 1",
-                       "l2": f"inputs > L2: {pool.kv.numel() * 2 / 1e6:.0f} MB page pool, "
-                             f"{step_bytes / 1e6:.0f} MB read+written per step",
-                       "parallelism": f"{world} independent replicas (stream sharding)",
-                       "launch": "CUDA graph per step" if graphs else "eager"},
+            "config": workload_config(args.model, B, world),
+            "launch": "CUDA graph per step" if graphs else "eager",
             "roofline": {"bound": "hbm", "kernel": kernel_name,
                          "achieved": round(achieved, 1), "peak": hbm, "peak_kind": kind,
                          "unit": "GB/s", "frac": round(achieved / hbm, 3), "traffic": traffic,

@@ -38,14 +38,23 @@ from harness import install_librosa_stub  # noqa: E402,F401  (also used by the o
 # None, step whose chunk is short).  A stream runs in steps acquire <= s < release
 # and is released at the start of step ``release``; a short chunk (length 1 < T)
 # is only ever that stream's last step, like a final chunk.
-SMALL_SCHEDULE = dict(att=(70, 1), dim=512, heads=8, layers=17, steps=40, pool=4,
+SMALL_SCHEDULE = dict(att=(70, 1), dim=512, heads=8, layers=2, steps=40, pool=4,
                       seed=11, events=[("a", 0, None, None), ("b", 0, 21, None),
                                        ("c", 6, None, None), ("d", 22, None, 39),
                                        ("e", 25, None, None)],
                       keep_steps=[0, 1, 2, 17, 34, 35, 36, 38, 39])
-LARGE_SCHEDULE = dict(att=(70, 13), dim=1024, heads=8, layers=24, steps=8, pool=3,
+LARGE_SCHEDULE = dict(att=(70, 13), dim=1024, heads=8, layers=1, steps=8, pool=3,
                       seed=12, events=[("a", 0, None, None), ("b", 2, None, None)],
                       keep_steps=[1, 6, 7])
+
+
+# The same schedules through the whole stack (17 layers small, 24 large:
+# parakeet/config.py:7,27).  Their fixtures also hold how far the reference's
+# own bf16 run lands from its fp32 run at each kept step: bf16 rounding alone
+# moves a 17-24 layer stack of random weights by 2-3 % rel-L2, which is the
+# scale a bf16 implementation is held to at full depth.
+SMALL_FULL = dict(SMALL_SCHEDULE, layers=17)
+LARGE_FULL = dict(LARGE_SCHEDULE, layers=24)
 
 
 def encoder_stream_inputs(seed, step, batch, T, dim):
@@ -64,7 +73,7 @@ def schedule_batches(cfg):
     return steps
 
 
-def run_encoder_fixture(ref, cfg):
+def run_encoder_fixture(ref, cfg, dtype=torch.float32):
     from parakeet.modules import ConformerEncoder
     from parakeet.engine.scheduler import Scheduler
 
@@ -80,9 +89,9 @@ def run_encoder_fixture(ref, cfg):
     missing, unexpected = enc.load_state_dict({k: torch.from_numpy(v) for k, v in sd.items()},
                                               strict=False)
     assert not unexpected and all(not k.startswith("layers.") for k in missing), missing
-    enc.eval()
+    enc = enc.to(dtype).eval()
     sched = Scheduler(max_active=cfg["pool"])
-    sched.init_state_pool(enc, torch.device("cpu"), torch.float32, cfg["pool"])
+    sched.init_state_pool(enc, torch.device("cpu"), dtype, cfg["pool"])
     slot_of, acquired, released = {}, [], []
     outs, lens, slots = {}, {}, {}
     batches = schedule_batches(cfg)
@@ -97,13 +106,14 @@ def run_encoder_fixture(ref, cfg):
                 acquired.append((s, slot_of[name]))
         seqs = [SimpleNamespace(encoder_state=slot_of[n]) for n, _ in batch]
         x = torch.from_numpy(encoder_stream_inputs(cfg["seed"], s, len(batch), T, cfg["dim"]))
+        x = x.to(dtype)
         length = torch.tensor([n for _, n in batch], dtype=torch.int64)
         st, idx = sched.pack_states(seqs)
         with torch.inference_mode():
             y, st = enc(x, st, length=length, bypass_pre_encode=True)
         sched.unpack_states(st, idx)
         if s in cfg["keep_steps"]:
-            outs[s] = y.numpy().astype(np.float32)
+            outs[s] = y.float().numpy()
             lens[s] = length.numpy()
             slots[s] = idx.numpy()
     fx = {"keep_steps": np.array(cfg["keep_steps"]),
@@ -111,8 +121,8 @@ def run_encoder_fixture(ref, cfg):
           "released": np.array(released, np.int64).reshape(-1, 2),
           "final_processed": sched._pool_state.processed_frames.numpy(),
           "final_cache_len": sched._pool_state.cache_lengths.numpy(),
-          "final_conv_l0": sched._pool_state.cache.conv[:, 0].numpy(),
-          "final_k_l0_last": sched._pool_state.cache.attn_k[:, 0, -T:].numpy()}
+          "final_conv_l0": sched._pool_state.cache.conv[:, 0].float().numpy(),
+          "final_k_l0_last": sched._pool_state.cache.attn_k[:, 0, -T:].float().numpy()}
     for s in cfg["keep_steps"]:
         fx[f"out_{s}"] = outs[s]
         fx[f"len_{s}"] = lens[s]
@@ -245,6 +255,15 @@ def main():
                         **run_encoder_fixture(None, SMALL_SCHEDULE))
     np.savez_compressed(os.path.join(HERE, "encoder_large.npz"),
                         **run_encoder_fixture(None, LARGE_SCHEDULE))
+    for cfg, name in ((SMALL_FULL, "encoder_small_full.npz"), (LARGE_FULL, "encoder_large_full.npz")):
+        fx = run_encoder_fixture(None, cfg)
+        bf = run_encoder_fixture(None, cfg, torch.bfloat16)
+        for s in cfg["keep_steps"]:
+            n = fx[f"len_{s}"]
+            a = np.concatenate([fx[f"out_{s}"][b, :, :k].ravel() for b, k in enumerate(n)])
+            b = np.concatenate([bf[f"out_{s}"][b, :, :k].ravel() for b, k in enumerate(n)])
+            fx[f"ref_bf16_err_{s}"] = np.array(np.linalg.norm(a - b) / np.linalg.norm(a))
+        np.savez_compressed(os.path.join(HERE, name), **fx)
     print("golden vectors written to", HERE)
 
 

@@ -15,6 +15,8 @@ _spec.loader.exec_module(make_golden)
 
 SMALL = make_golden.SMALL_SCHEDULE
 LARGE = make_golden.LARGE_SCHEDULE
+SMALL_FULL = make_golden.SMALL_FULL
+LARGE_FULL = make_golden.LARGE_FULL
 
 
 def load(name):

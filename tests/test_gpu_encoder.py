@@ -1,7 +1,11 @@
 """The paged encoder (drop-in modules + scheduler) against the reference's
 own outputs: the golden stream schedules of tests/golden/make_golden.py,
 replayed through Scheduler.pack_states -> ConformerEncoder.forward ->
-unpack_states.  fp32: rel-L2 <= 1e-5; bf16: rel-L2 <= 1e-2 (valid frames)."""
+unpack_states, on valid frames.  fp32: rel-L2 <= 1e-5 at every depth.  bf16:
+rel-L2 <= 1e-2 over 2 layers (small) / 1 layer (large); over the whole stack
+(17 / 24 layers) bf16 rounding alone moves the reference's own bf16 run 2-3 %
+from its fp32 run (recorded per step in the fixture), so there the bound is
+1e-2 or 1.25 x the reference's own bf16 error, whichever is larger."""
 from types import SimpleNamespace
 
 import numpy as np
@@ -11,7 +15,7 @@ import torch
 from parakeet_b200.engine.scheduler import Scheduler
 from parakeet_b200.modules import ConformerEncoder
 from parakeet_b200.weights import random_encoder_layers
-from replay import LARGE, SMALL, load, rel_l2, schedule, valid_rows
+from replay import LARGE, LARGE_FULL, SMALL, SMALL_FULL, load, rel_l2, schedule, valid_rows
 
 pytestmark = pytest.mark.gpu
 
@@ -48,7 +52,9 @@ def replay_encoder(cfg, dtype):
     return outs, sched
 
 
-@pytest.mark.parametrize("cfg,name", [(SMALL, "encoder_small.npz"), (LARGE, "encoder_large.npz")])
+@pytest.mark.parametrize("cfg,name", [(SMALL, "encoder_small.npz"), (LARGE, "encoder_large.npz"),
+                                      (SMALL_FULL, "encoder_small_full.npz"),
+                                      (LARGE_FULL, "encoder_large_full.npz")])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_paged_encoder_matches_reference(cfg, name, dtype):
     torch.backends.cuda.matmul.allow_tf32 = False
@@ -60,7 +66,10 @@ def test_paged_encoder_matches_reference(cfg, name, dtype):
         assert np.array_equal(idx, g[f"slots_{s}"])
         lens = g[f"len_{s}"]
         err = rel_l2(valid_rows(y, lens), valid_rows(g[f"out_{s}"], lens))
-        assert err <= tol, (int(s), err)
+        bound = tol
+        if dtype == torch.bfloat16 and f"ref_bf16_err_{s}" in g:
+            bound = max(tol, 1.25 * float(g[f"ref_bf16_err_{s}"]))
+        assert err <= bound, (int(s), err, bound)
     pool = sched.pool
     assert pool.read_error() == 0
     slots = torch.arange(cfg["pool"], dtype=torch.int32, device="cuda")

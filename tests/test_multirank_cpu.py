@@ -66,3 +66,57 @@ def test_reference_arm_only_rank0_reports():
                        env=env, capture_output=True, text=True, timeout=120)
     assert r.returncode == 0
     assert r.stdout.strip() == ""
+
+
+def _serve_rank_main(rank, world, port, out_dir):
+    """Two engines behind the router: every rank places the same 1001 streams,
+    serves its share (a fake trial whose latencies depend on the rank) and
+    reduces the result with the other rank."""
+    import numpy as np
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=__import__("datetime").timedelta(seconds=30))
+    try:
+        from parakeet_b200.engine import StreamRouter
+        router = StreamRouter(world)
+        where = [router.place(s) for s in range(1001)]
+        served = []
+
+        def local(n):
+            served.append(n)
+            lat = np.full(n, 0.010 * (rank + 1))           # rank 1 is slower
+            return lat, {"backlog_chunks_at_end": rank, "streams_joined": 3}
+
+        ok, rec = bench.job_trial(1001, world, rank, 10_000, torch.device("cpu"), 160.0, local)
+        with open(os.path.join(out_dir, f"serve{rank}.json"), "w") as f:
+            json.dump({"where": where, "served": served, "ok": ok, "rec": rec}, f)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_job_serving_trial_gloo_two_ranks(tmp_path):
+    world, port = 2, _free_port()
+    mp.start_processes(_serve_rank_main, args=(world, port, str(tmp_path)), nprocs=world,
+                       join=True, start_method="spawn")
+    res = [json.load(open(tmp_path / f"serve{r}.json")) for r in range(world)]
+    assert res[0]["where"] == res[1]["where"]            # same placement on every rank
+    assert res[0]["served"] == [501] and res[1]["served"] == [500]
+    for r in res:                                         # both ranks see the job's result
+        assert r["ok"] is True
+        assert r["rec"]["p99_ms"] == pytest.approx(20.0)   # the slower rank's p99
+        assert r["rec"]["chunks"] == 1001 and r["rec"]["streams_served"] == 1001
+        assert r["rec"]["backlog_chunks_at_end"] == 1 and r["rec"]["streams_joined"] == 6
+    assert res[0]["rec"] == res[1]["rec"]
+
+
+def test_router_least_loaded_with_capacity_and_release():
+    from parakeet_b200.engine import StreamRouter
+    r = StreamRouter(3, capacity=2)
+    assert [r.place(i) for i in range(6)] == [0, 1, 2, 0, 1, 2]
+    assert r.place(6) is None                              # every engine full
+    assert r.release(4) == 1 and r.place(7) == 1           # the freed engine takes the next
+    r.release(0)
+    r.release(3)
+    assert r.load == [0, 2, 2] and r.place(8) == 0 and r.streams_of(1) == [1, 7]
+    with pytest.raises(ValueError):
+        r.place(8)

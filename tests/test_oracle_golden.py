@@ -4,7 +4,7 @@ import pytest
 
 from oracle import pages, streaming
 from parakeet_b200.weights import random_encoder_layers
-from replay import LARGE, SMALL, load, rel_l2, schedule, valid_rows
+from replay import LARGE, SMALL, SMALL_FULL, load, rel_l2, schedule, valid_rows
 
 
 @pytest.mark.parametrize("name,att", [("cache_window_small.npz", (70, 1)),
@@ -88,7 +88,8 @@ def run_oracle_schedule(cfg):
     return outs, sched
 
 
-@pytest.mark.parametrize("cfg,name", [(SMALL, "encoder_small.npz"), (LARGE, "encoder_large.npz")])
+@pytest.mark.parametrize("cfg,name", [(SMALL, "encoder_small.npz"), (LARGE, "encoder_large.npz"),
+                                      (SMALL_FULL, "encoder_small_full.npz")])
 def test_oracle_encoder_matches_reference_fp32(cfg, name):
     g = load(name)
     outs, sched = run_oracle_schedule(cfg)
