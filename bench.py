@@ -941,6 +941,147 @@ def streaming_step(model, steps, dev, profile=False, streams=None):
     return out
 
 
+def reference_engine_search(model, dev, limit_ms=160.0, measure_s=3.0, max_trials=8,
+                            start=8, pool=1024):
+    """The survey's metric 1 for the reference's own engine on this GPU: its
+    unmodified ``ModelRunner`` (parakeet/engine/model_runner.py:19-496) in bf16
+    with eager CUDA, its three worker threads (``start_workers``), its
+    ``Scheduler`` slot pool, its host ``FeatureExtractor`` and per-stream
+    pre-encode; random bf16 weights (baseline/harness.py).  One shim: the
+    runner moves features to the device but not to the model's dtype
+    (model_runner.py:196), which fails in bf16, so the extractor's output is
+    cast to bf16.  Streams are paced as ``serve_trial`` paces this package's:
+    stream i pushes its chunk k (the engine's first chunk, then its later
+    chunks) through ``Sequence.push_samples`` at t0 + phase_i + k * period; a
+    chunk's latency is the time from that push to the return of
+    ``_decode_batch`` with its tokens (then put on the results queue).  N
+    doubles from ``start`` until a trial fails (p99 above the limit, or more
+    than one chunk per stream left undecoded at the end; a failing trial is
+    repeated once), then bisects."""
+    import numpy as np
+    import torch
+
+    sys.path.insert(0, os.path.join(REPO, "baseline"))
+    import harness
+    if not harness.available():
+        return {"unavailable": "no reference install under baseline/_ref "
+                               "(python bench.py --install-reference <checkout>)"}
+    harness.import_reference()
+    from parakeet.config import Config
+    from parakeet.engine.model_runner import ModelRunner
+    from parakeet.engine.scheduler import Scheduler
+
+    c = SHAPES[model]
+    la = c["att"][1]
+    period = (la + 1) * 0.08
+    n0, n = (1 + 8 * la) * 160, (8 + 8 * la) * 160
+    net = harness.seeded_parakeet(model, torch.bfloat16)
+    fe = net._feature_extractor
+    fe_push = fe.push
+
+    def push_bf16(samples, state, final=False):       # the dtype shim (model_runner.py:196)
+        f = fe_push(samples, state, final=final)
+        return None if f is None else f.to(torch.bfloat16)
+
+    fe.push = push_bf16
+    harness.patch_from_pretrained(net)
+
+    class TimedRunner(ModelRunner):
+        def _decode_batch(self, seqs, chunks):
+            out = super()._decode_batch(seqs, chunks)
+            t = time.perf_counter()
+            for q in seqs:
+                self.done_at[q.request_id].append(t)
+            return out
+
+    runner = TimedRunner(Config(size=model, max_num_streams=pool), torch.device(dev),
+                         Scheduler(max_active=pool))
+    runner.done_at = {}
+    audio = synth_audio_batch(64, n0 + 2 * n, seed=11)
+    banks = [audio[:, :n0], audio[:, n0:n0 + n], audio[:, n0 + n:]]
+    meas = max(3, int(round(measure_s / period)))
+
+    def trial(N, seed, warm=3):
+        rng = np.random.default_rng(seed)
+        phase = rng.uniform(0.0, period, N)
+        seqs = []
+        for _ in range(N):
+            q = runner.create_sequence()
+            runner.add_sequence(q)
+            runner.done_at[q.request_id] = []
+            seqs.append(q)
+        pushed = [[] for _ in range(N)]
+        k = np.zeros(N, np.int64)
+        if torch.device(dev).type == "cuda":
+            torch.cuda.synchronize(dev)
+        runner.start_workers()
+        t0 = time.perf_counter() + 0.02
+        t_meas, t_end = t0 + warm * period, t0 + (warm + meas) * period
+        try:
+            while True:
+                now = time.perf_counter()
+                if now >= t_end:
+                    break
+                due = t0 + phase + k * period
+                i = int(np.argmin(due))
+                if due[i] > now:
+                    time.sleep(min(due[i], t_end) - now)
+                    continue
+                b = banks[min(int(k[i]), 2)]
+                x = b[(i + int(k[i])) % b.shape[0]]
+                q = seqs[i]
+                with q.lock:
+                    q.push_samples(x)
+                pushed[i].append(time.perf_counter())
+                k[i] += 1
+        finally:
+            runner.stop_workers()
+        lats, backlog = [], 0
+        for i, q in enumerate(seqs):
+            done = runner.done_at.pop(q.request_id)
+            backlog = max(backlog, len(pushed[i]) - len(done))
+            lats += [d - p for p, d in zip(pushed[i], done) if p >= t_meas]
+            runner._release_sequence(q)
+        lat = np.array(lats)
+        p99 = float(np.percentile(lat, 99)) * 1e3 if lat.size else float("inf")
+        ok = p99 <= limit_ms and backlog <= 1
+        return ok, {"streams": N, "ok": ok,
+                    "p50_ms": round(float(np.median(lat)) * 1e3, 2) if lat.size else None,
+                    "p99_ms": round(p99, 2), "chunks": int(lat.size),
+                    "backlog_chunks_at_end": backlog}
+
+    t_start = time.perf_counter()
+    trial(min(4, start), seed=0, warm=2)              # module loads, allocator, threads
+    trials, ok_n, bad_n, N = [], 0, None, start
+    while len(trials) < max_trials:
+        ok, rec = trial(N, len(trials) + 1)
+        if not ok:
+            ok, rec2 = trial(N, 100 + len(trials))
+            rec = {**rec2, "first_attempt_p99_ms": rec["p99_ms"]}
+        trials.append(rec)
+        if ok:
+            ok_n = N
+        else:
+            bad_n = N
+        if bad_n is None:
+            if 2 * N > pool:
+                break
+            N *= 2
+        else:
+            if bad_n - ok_n <= max(2, ok_n // 16):
+                break
+            N = (ok_n + bad_n) // 2
+    best = next((t for t in trials if t["streams"] == ok_n), None)
+    del runner, net
+    torch.cuda.empty_cache()
+    return {"model": model, "limit_ms": limit_ms, "streams_max": ok_n,
+            "p99_ms_at_max": best["p99_ms"] if best else None,
+            "audio_ms_per_chunk": period * 1e3, "measured_s_per_trial": round(meas * period, 2),
+            "search_s": round(time.perf_counter() - t_start, 1), "trials": trials,
+            "engine": "reference ModelRunner (unmodified, eager CUDA, bf16, worker threads), "
+                      "from baseline/_ref"}
+
+
 class ServePositions:
     """Stream positions of the paced serving trials on one GPU, one slot each.
     A position always holds a live stream of ``life`` chunks (configs[2]: 30 s
