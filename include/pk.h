@@ -260,9 +260,12 @@ int pk_paged_attention_bd(pk_paged_kv *kv, int32_t layer0, int32_t num_layers,
  *   - limit: PK_EINVAL before any launch when num_layers * batch * heads *
  *     chunk * pk_relpos_bd_cols * 4 bytes exceeds PK_NOALLOC_SCRATCH_BYTES
  *     (split the call by layers or streams);
- *   - the first call on a device looks up the array's device address
- *     (cudaGetSymbolAddress, with that device current): make that first call
- *     before any stream capture; the pool must be on the current device;
+ *   - the first call on a device, and the first after a pool is created on
+ *     that device, looks up the array's device address (cudaGetSymbolAddress,
+ *     with that device current): make those calls before any stream capture;
+ *     the pool must be on the current device.  A device reset
+ *     (cudaDeviceReset) loads the array anew at another address; the pools
+ *     made after the reset (the old ones lost their memory) renew it;
  *   - every call uses the same array: calls whose work overlaps on the GPU
  *     (other streams, other threads) race; order them on one stream.  Each
  *     call writes every element it reads, so no clearing is needed;

@@ -109,6 +109,31 @@ int32_t pk_ring_size(int32_t left, int32_t chunk, int32_t page_size) {
     return r;
 }
 
+// Device addresses of the no-allocation entry point's static scratch array
+// (g_noalloc_scratch, below), one per device, looked up on first use.
+namespace {
+constexpr int kNoallocMaxDevices = 64;
+float *g_noalloc_ptrs[kNoallocMaxDevices] = {};
+std::mutex g_noalloc_mu;
+
+// A pool created on a device makes the next no-allocation call on that device
+// look the scratch address up again.  After a device reset (cudaDeviceReset)
+// the library's device code is loaded anew, at a new address, and the pools
+// made before it are gone with their memory: the pools made after it renew
+// the address.
+void noalloc_forget(const void *dev_ptr) {
+    cudaPointerAttributes attr{};
+    if (cudaPointerGetAttributes(&attr, dev_ptr) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return;
+    }
+    if (attr.type == cudaMemoryTypeDevice && attr.device >= 0 && attr.device < kNoallocMaxDevices) {
+        std::lock_guard<std::mutex> lock(g_noalloc_mu);
+        g_noalloc_ptrs[attr.device] = nullptr;
+    }
+}
+}  // namespace
+
 int pk_paged_kv_create(const pk_paged_kv_desc *desc, pk_paged_kv **out) {
     PK_CHECK(desc && out, "null argument");
     const pk_paged_kv_desc &d = *desc;
@@ -146,6 +171,7 @@ int pk_paged_kv_create(const pk_paged_kv_desc *desc, pk_paged_kv **out) {
         free(kv);
         return st;
     }
+    noalloc_forget(d.kv);
     *out = kv;
     return PK_OK;
 }
@@ -456,24 +482,21 @@ int pk_paged_attention_bd(pk_paged_kv *kv, int32_t layer0, int32_t num_layers, c
 static __device__ __align__(256) float g_noalloc_scratch[PK_NOALLOC_SCRATCH_BYTES / sizeof(float)];
 
 static int noalloc_scratch(float **out) {
-    constexpr int kMaxDevices = 64;
-    static float *ptrs[kMaxDevices] = {};
-    static std::mutex mu;
     int dev = -1;
     int st = cuda_status(cudaGetDevice(&dev), "cudaGetDevice");
     if (st != PK_OK) return st;
-    if (dev < 0 || dev >= kMaxDevices) {
-        set_error("device %d above the %d the scratch table holds", dev, kMaxDevices);
+    if (dev < 0 || dev >= kNoallocMaxDevices) {
+        set_error("device %d above the %d the scratch table holds", dev, kNoallocMaxDevices);
         return PK_ENOTSUP;
     }
-    std::lock_guard<std::mutex> lock(mu);
-    if (!ptrs[dev]) {   // first call on this device: the set-up
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptrs[dev]) {   // first call on this device since a pool was made: the set-up
         void *p = nullptr;
         st = cuda_status(cudaGetSymbolAddress(&p, g_noalloc_scratch), "cudaGetSymbolAddress");
         if (st != PK_OK) return st;
-        ptrs[dev] = static_cast<float *>(p);
+        g_noalloc_ptrs[dev] = static_cast<float *>(p);
     }
-    *out = ptrs[dev];
+    *out = g_noalloc_ptrs[dev];
     return PK_OK;
 }
 

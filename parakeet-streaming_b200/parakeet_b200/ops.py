@@ -361,7 +361,8 @@ class PagedKVPool:
         must not allocate device memory, pk_paged_attention_noalloc keeps the
         rel-pos term in the library's static 32 MiB device array (larger steps
         are refused; calls overlapping on the GPU race on it, so keep them on
-        one stream).  Returns out with the query's leading shape."""
+        one stream) and ``out`` must be given.  Returns out with the query's
+        leading shape."""
         squeeze = query.dim() == 3
         if squeeze:
             query, bias_u = query.unsqueeze(0), bias_u.unsqueeze(0)
@@ -381,6 +382,8 @@ class PagedKVPool:
             if tuple(bd.shape) != shape or bd.dtype != torch.float32 or not bd.is_contiguous():
                 raise ValueError(f"bd must be contiguous float32 {shape} (relpos_bd's output)")
         if out is None:
+            if noalloc:
+                raise ValueError("noalloc=True allocates nothing: pass `out`")
             out = torch.empty((nl, B, T, D), dtype=self.dtype, device=self.device)
         elif out.dim() == 3:
             out = out.unsqueeze(0)

@@ -121,10 +121,12 @@ def test_shapes_without_prepass(dtype, att, dim):
     q, k, v = qkv[..., :dim], qkv[..., dim:2 * dim], qkv[..., 2 * dim:]
     with pytest.raises(_lib.PKError):
         a.relpos_bd(0, q, pos, bv)
-    outs = []
-    for pool, noalloc in ((a, False), (b, True)):
+    outs = [torch.empty(nl, 2, T, dim, dtype=dtype, device=DEV) for _ in range(2)]
+    with pytest.raises(ValueError):       # allocating nothing: the caller passes `out`
+        b.attention(0, q, pos, bu, bv, slots, ln, key=k, value=v, noalloc=True)
+    for pool, noalloc, out in ((a, False, outs[0]), (b, True, outs[1])):
         pool.begin_step(slots, ln)
-        outs.append(pool.attention(0, q, pos, bu, bv, slots, ln, key=k, value=v, noalloc=noalloc))
+        pool.attention(0, q, pos, bu, bv, slots, ln, key=k, value=v, noalloc=noalloc, out=out)
         pool.end_step(slots, ln)
     torch.cuda.synchronize()
     assert torch.equal(outs[0], outs[1])
