@@ -469,6 +469,17 @@ int pk_features_push(const pk_features_desc *fe, const float *samples, int64_t s
                      int32_t batch, void *out, int32_t out_dtype, int32_t max_frames,
                      int32_t *num_frames, void *stream);
 
+/* Self-test of the failure path of every TMA pipeline here: the bounded
+ * mbarrier wait that gives up after a time limit and records PK_DEV_TIMEOUT in
+ * *error (instead of hanging the GPU), leaving the context usable.  One CTA
+ * waits on an mbarrier's first phase for at most limit_ns (0 < limit_ns <=
+ * 10 s); with arrive != 0 it arrives first (the wait returns at once, no error
+ * bit), with arrive == 0 nothing arrives and no copy is issued, so the wait
+ * runs out.  *waited_ns receives the time the wait took.  Asynchronous on
+ * `stream`.  No counterpart in the reference, which has no device waits. */
+int pk_selftest_bounded_wait(int32_t *error, int32_t arrive, int64_t limit_ns, int64_t *waited_ns,
+                             void *stream);
+
 /* Text of the last PK_ECUDA / PK_EINVAL cause seen by this thread. */
 const char *pk_last_error(void);
 

@@ -851,3 +851,11 @@ int pk_features_push(const pk_features_desc *fe, const float *samples, int64_t s
 }
 
 }  // extern "C"
+
+int pk_selftest_bounded_wait(int32_t *error, int32_t arrive, int64_t limit_ns, int64_t *waited_ns,
+                             void *stream) {
+    PK_CHECK(error && waited_ns, "null argument");
+    PK_CHECK(limit_ns > 0 && limit_ns <= 10ll * 1000 * 1000 * 1000, "limit_ns must be in (0, 10 s]");
+    return pk::launch_selftest_wait(error, arrive, static_cast<uint64_t>(limit_ns), waited_ns,
+                                    static_cast<cudaStream_t>(stream));
+}

@@ -19,6 +19,9 @@ namespace pk {
 
 void set_error(const char *fmt, ...);
 int cuda_status(cudaError_t e, const char *what);
+// pk_selftest.cu: one CTA waits on an mbarrier with the shared bounded wait
+int launch_selftest_wait(int32_t *error, int32_t arrive, uint64_t limit_ns, int64_t *waited_ns,
+                         cudaStream_t stream);
 // Encode a tiled TMA descriptor (driver entry point fetched once via cudart).
 int encode_tmap(CUtensorMap *map, int dtype, const void *base, int rank, const uint64_t *dims,
                 const uint64_t *strides_bytes, const uint32_t *box);

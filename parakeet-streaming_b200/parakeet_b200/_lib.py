@@ -114,6 +114,7 @@ SIGNATURES = {
                            ctypes.POINTER(_I64), ctypes.POINTER(_I32)],
     "pk_features_push": [ctypes.POINTER(FeaturesDesc), _P, _I64, _P, _P, _P, _I32, _P, _I32, _I32,
                          _P, _P],
+    "pk_selftest_bounded_wait": [_P, _I32, _I64, _P, _P],
     "pk_last_error": [],
 }
 RESTYPES = {"pk_last_error": ctypes.c_char_p}

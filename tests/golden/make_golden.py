@@ -57,6 +57,90 @@ SMALL_FULL = dict(SMALL_SCHEDULE, layers=17)
 LARGE_FULL = dict(LARGE_SCHEDULE, layers=24)
 
 
+# 256 streams arriving as a Poisson process (mean 20 per second)
+# with lengths uniform in 2-120 s, one 160 ms chunk per stream per step; the
+# page pool holds 60 % of the full demand (256 streams x 6 pages), which admits
+# floor(0.6 * 256) = 153 streams at once; the others wait in arrival order.
+CHURN = dict(streams=256, rate=20.0, min_s=2.0, max_s=120.0, period=0.16, cap=0.6,
+             pages_per_stream=6, seed=41)
+
+
+def churn_schedule(cfg=CHURN):
+    """(arrival step, chunks) per stream, seeded."""
+    rng = np.random.default_rng(cfg["seed"])
+    t = np.cumsum(rng.exponential(1.0 / cfg["rate"], cfg["streams"]))
+    secs = rng.uniform(cfg["min_s"], cfg["max_s"], cfg["streams"])
+    return (np.floor(t / cfg["period"]).astype(np.int64),
+            np.maximum(1, np.round(secs / cfg["period"])).astype(np.int64))
+
+
+def churn_replay(acquire, release, cfg=CHURN, on_step=None):
+    """The engine's admission loop over ``churn_schedule``: each step, the
+    streams that sent their last chunk in the previous step are released (in
+    admission order), the step's arrivals join the waiting queue, waiting
+    streams are admitted in arrival order while ``acquire()`` gives a slot,
+    and every live stream sends one chunk (its last one of length 1, a short
+    final chunk).  ``on_step(step, slots, lengths, released)`` sees each step.
+    Returns the slot operations [(step, op 0 = acquire / 1 = release, stream,
+    slot)]."""
+    from collections import deque
+    arrive, chunks = churn_schedule(cfg)
+    waiting, live, ops = deque(), {}, []          # live: stream -> [slot, chunks left]
+    step, nxt = 0, 0
+    while nxt < len(arrive) or waiting or live:
+        released = []
+        for sid in [s for s, (_, left) in live.items() if left == 0]:
+            slot = live.pop(sid)[0]
+            release(slot)
+            ops.append((step, 1, sid, slot))
+            released.append(slot)
+        while nxt < len(arrive) and arrive[nxt] <= step:
+            waiting.append(nxt)
+            nxt += 1
+        while waiting:
+            slot = acquire()
+            if slot is None:
+                break
+            sid = waiting.popleft()
+            live[sid] = [slot, int(chunks[sid])]
+            ops.append((step, 0, sid, slot))
+        slots, lengths = [], []
+        for sid, rec in live.items():
+            slots.append(rec[0])
+            lengths.append(1 if rec[1] == 1 else None)
+            rec[1] -= 1
+        if on_step is not None:
+            on_step(step, slots, lengths, released)
+        step += 1
+    return ops
+
+
+def churn_fixture():
+    """The reference Scheduler's slot ids (scheduler.py:86-104, a pool of the
+    153 streams the capped page pool admits) under configs[4]'s churn."""
+    from parakeet.engine.scheduler import Scheduler
+    from parakeet.modules.cache import ModelCache, StreamingState
+
+    class TinyEncoder:
+        def init_streaming_state(self, batch_size, device, dtype):
+            return StreamingState(ModelCache(1, (70, 1), 4, 9, batch_size, device, dtype),
+                                  torch.zeros(batch_size, dtype=torch.int64),
+                                  torch.zeros(batch_size, dtype=torch.int64))
+
+    sched = Scheduler()
+    n = int(CHURN["cap"] * CHURN["streams"])
+    sched.init_state_pool(TinyEncoder(), torch.device("cpu"), torch.float32, n)
+    live = [0, 0]
+
+    def count(step, slots, lengths, released):
+        live[0] = max(live[0], len(slots))
+        live[1] = step + 1
+
+    ops = churn_replay(sched.acquire_state_slot, sched.release_state_slot, on_step=count)
+    return {"ops": np.array(ops, np.int64), "max_live": np.array(live[0]),
+            "steps": np.array(live[1])}
+
+
 def encoder_stream_inputs(seed, step, batch, T, dim):
     """Chunk input of one step: N(0,1) [batch, T, dim] from seed*1000+step."""
     return seeded_normal(seed * 1000 + step, (batch, T, dim))
@@ -251,6 +335,7 @@ def main():
     np.savez_compressed(os.path.join(HERE, "masks.npz"), **masks_fixture())
     np.savez_compressed(os.path.join(HERE, "scheduler_slots.npz"), **scheduler_fixture())
     np.savez_compressed(os.path.join(HERE, "admission.npz"), **admission_fixture())
+    np.savez_compressed(os.path.join(HERE, "churn_configs4.npz"), **churn_fixture())
     np.savez_compressed(os.path.join(HERE, "encoder_small.npz"),
                         **run_encoder_fixture(None, SMALL_SCHEDULE))
     np.savez_compressed(os.path.join(HERE, "encoder_large.npz"),
