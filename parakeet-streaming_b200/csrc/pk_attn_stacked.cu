@@ -73,7 +73,7 @@ __device__ __forceinline__ void consumer_sync() {
     asm volatile("bar.sync 1, %0;" ::"n"(kH * 32) : "memory");
 }
 
-template <int NS>
+template <int NS, bool kRows16>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     paged_attn_stacked_kernel(const __grid_constant__ CUtensorMap kv_map, const SGeom g,
                               const pk_paged_kv_desc d, const AttnArgs a) {
@@ -282,8 +282,11 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     if (s_abort) return;
 
     // ---- dense softmax over the stacked rows: 16 threads per row
-    {
-        const int row = tid / 16, sub = tid % 16;
+    // (a chunk of 3 or 4 frames stacks 12 or 16 rows: the 128 consumer threads
+    // then take rows 8-15 in a second pass)
+#pragma unroll
+    for (int pass = 0; pass < (kRows16 ? 2 : 1); ++pass) {
+        const int row = tid / 16 + pass * 8, sub = tid % 16;
         const int rows = kH * chunk;
         const int iq = row % chunk;
         float sv[kMaxBoxes];
@@ -429,16 +432,19 @@ int launch_attention_stacked(const pk_paged_kv *kv, const CUtensorMap &pos_map16
     g.bd_stride = g.npb * 16;
     g.off_p = g.off_bd + 16 * g.bd_stride * 4;
     const size_t smem = g.off_p + kMaxBoxes * 16 * kPStride + 1024;
-    static size_t limit = 48 * 1024;
-    if (smem > limit) {
-        cudaError_t e = cudaFuncSetAttribute(paged_attn_stacked_kernel<NS>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    // more than 8 stacked query rows (chunks of 3 or 4) take a second softmax pass
+    auto kernel = kH * d.chunk > 8 ? paged_attn_stacked_kernel<NS, true>
+                                   : paged_attn_stacked_kernel<NS, false>;
+    static size_t limit[2] = {48 * 1024, 48 * 1024};
+    size_t &lim = limit[kH * d.chunk > 8];
+    if (smem > lim) {
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem);
         if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(paged_attn_stacked)");
-        limit = smem;
+        lim = smem;
     }
     dim3 grid(a.batch, a.nlayers, d.num_heads / kH);
-    return cuda_status(launch_pdl(paged_attn_stacked_kernel<NS>, grid, dim3(kThreads), smem, s,
-                                  kv->kv_map, g, d, a),
+    return cuda_status(launch_pdl(kernel, grid, dim3(kThreads), smem, s, kv->kv_map, g, d, a),
                        "paged_attn_stacked_kernel");
 }
 

@@ -19,7 +19,10 @@ pytestmark = pytest.mark.gpu
 
 DEV = "cuda"
 TOL = {torch.float32: 1e-5, torch.bfloat16: 1e-2}
-SHAPES = {"small": dict(att=(70, 1), dim=512, heads=8), "large": dict(att=(70, 13), dim=1024, heads=8)}
+SHAPES = {"small": dict(att=(70, 1), dim=512, heads=8), "large": dict(att=(70, 13), dim=1024, heads=8),
+          # head_dim 64 with chunks of 3 and 4 frames: 12 and 16 stacked query rows of
+          # the 4-head CTA (the small model stacks 8)
+          "small_t3": dict(att=(70, 2), dim=512, heads=8), "small_t4": dict(att=(70, 3), dim=512, heads=8)}
 
 
 def pool_state(pool):
@@ -171,6 +174,12 @@ def test_append_gather_attention_small(dtype, fused):
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_append_gather_attention_large(dtype, fused):
     run_stream_steps("large", dtype, steps=9, n_slots=3, seed=4, fused=fused)
+
+
+@pytest.mark.parametrize("shape", ["small_t3", "small_t4"])
+@pytest.mark.parametrize("fused", [False, True])
+def test_append_gather_attention_stacked_rows_above_8(shape, fused):
+    run_stream_steps(shape, torch.bfloat16, steps=30, n_slots=4, seed=5, check_every=3, fused=fused)
 
 
 def test_append_gather_attention_small_relpos_prepass():
