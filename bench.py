@@ -88,7 +88,9 @@ def parse():
     ap.add_argument("--wheelhouse", default=None, help="offline wheel directory for pip")
     ap.add_argument("--profile-op", default=None,
                     choices=["append", "attention", "attention+append", "gather",
-                             "gather_all_layers", "conv", "features", "streaming", "gemm"],
+                             "gather_all_layers", "conv", "features", "streaming", "gemm",
+                             "scale_append", "scale_gather", "scale_attention+append",
+                             "scale_conv"],
                     help="prefill + warmup, then --steps runs of one breakdown op (for ncu)")
     return ap.parse_args()
 
@@ -382,6 +384,66 @@ def run_reference_arm(args):
                 "d2h_bytes_per_step": 0},
         "bytes_per_stream_layer": {"append": b["append"], "attention": b["attention"]},
     }), flush=True)
+
+
+def ops_at_scale(model, dev, timeit, hbm, streams=2048, layers=2, only=None):
+    """One layer's append, gather, attention (+ append) and conv-cache step over
+    the 2048 streams of a full serving batch (the largest step the allocator
+    takes), where a launch moves tens to hundreds of MB; the configs[1]
+    breakdown beside it (80 streams) shows the launch- and latency-bound end.
+    Full windows (36 steps of prefill), pages a random permutation, bf16."""
+    import torch
+
+    from parakeet_b200.ops import PagedKVPool, pages_per_stream
+    c = SHAPES[model]
+    D, H, att = c["dim"], c["heads"], c["att"]
+    left, T = att[0], att[1] + 1
+    W, P = left + T, 2 * (left + T) - 1
+    dt = torch.bfloat16
+    g = torch.Generator(device=dev).manual_seed(3)
+    rnd = lambda *sh: (torch.randn(*sh, generator=g, device=dev) / 8).to(dt)  # noqa: E731
+    n_pages = streams * pages_per_stream(left, T, PAGE)
+    order = torch.randperm(n_pages, generator=torch.Generator().manual_seed(1))
+    pool = PagedKVPool(layers, D, H, att, streams, dtype=dt, device=dev, page_order=order)
+    slots = torch.arange(streams, dtype=torch.int32, device=dev)
+    lengths = torch.full((streams,), T, dtype=torch.int32, device=dev)
+    qkv = rnd(streams, T, 3 * D)
+    q, k, v = qkv[..., :D], qkv[..., D:2 * D], qkv[..., 2 * D:]
+    for _ in range(-(-left // T) + 1):
+        pool.begin_step(slots, lengths)
+        for l in range(layers):
+            pool.append(l, k, v, slots)
+        pool.end_step(slots, lengths)
+    pos, bu, bv = rnd(P, D), rnd(H, D // H), rnd(H, D // H)
+    out = torch.empty(streams, T, D, dtype=dt, device=dev)
+    kw, vw = (torch.empty(streams, W, D, dtype=dt, device=dev) for _ in range(2))
+    x2, wconv = rnd(streams, T, 2 * D), rnd(D, 1, 9)
+    lnw, lnb = rnd(D) + 1, rnd(D)
+    yconv = torch.empty(streams, T, D, dtype=dt, device=dev)
+    nb = alg_bytes(model)
+    ops = {
+        "append": (lambda: pool.append(0, k, v, slots), nb["append"]),
+        "gather": (lambda: pool.gather(0, slots, kw, vw), nb["gather"]),
+        "attention+append": (lambda: pool.attention(0, q, pos, bu, bv, slots, lengths, out,
+                                                    key=k, value=v),
+                             nb["attention"] + nb["append"]),
+        "conv": (lambda: pool.conv_step(0, x2, wconv, slots, lengths, lnw, lnb, 1e-5, yconv),
+                 nb["conv"]),
+    }
+    pool.begin_step(slots, lengths)
+    res = {"streams": streams}
+    for name, (fn, per) in ops.items():
+        if only is not None and name != only:
+            continue
+        t = timeit(fn)
+        nbytes = per * streams
+        res[name] = {"ms": round(t, 4), "GB/s": round(nbytes / t / 1e6, 1),
+                     "frac": round(nbytes / t / 1e6 / hbm, 3), "bytes_per_launch": nbytes}
+    torch.cuda.synchronize()
+    res["device_error_word"] = pool.read_error()
+    del pool
+    torch.cuda.empty_cache()
+    return res
 
 
 def encoder_step(model, streams, steps, dev):
@@ -1483,6 +1545,20 @@ def main():
     if args.profile_op == "gemm":       # the projection GEMMs alone, for ncu
         print(json.dumps(profile_gemm(args.model, args.steps, dev)))
         return
+    if args.profile_op and args.profile_op.startswith("scale_"):   # one op at 2048 streams, for ncu
+        import torch
+        dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+        torch.cuda.set_device(dev)
+
+        def run_only(fn):
+            for _ in range(args.steps):
+                fn()
+            torch.cuda.synchronize()
+            return 1.0
+        r = ops_at_scale(args.model, dev, run_only, 1.0, only=args.profile_op[len("scale_"):])
+        print(json.dumps({"profile_run": args.model, "op": args.profile_op, "steps": args.steps,
+                          "device_error_word": r["device_error_word"]}))
+        return
     if args.profile_op == "streaming":  # --steps audio -> tokens steps inside a profiler range
         print(json.dumps(streaming_step(args.model, args.steps, dev, profile=True,
                                         streams=args.pipeline_streams)))
@@ -1762,6 +1838,7 @@ def main():
             breakdown[name] = {"ms": round(t, 4), "GB/s": round(nbytes / t / 1e6, 1),
                                "frac": round(nbytes / t / 1e6 / hbm, 3), "launches": launches,
                                "bytes_per_stream_layer": nbytes // units}
+        breakdown["at_2048_streams"] = ops_at_scale(args.model, dev, timeit, hbm)
 
     ms, e2e_ms, attn_ms, eager_ms = max_over_ranks([ms, e2e_ms, attn_ms, eager_ms], dev)
 

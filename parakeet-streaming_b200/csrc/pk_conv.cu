@@ -13,6 +13,8 @@
 // there is no gather/scatter (scheduler.py:162-168,196-201) around it.
 #include <math.h>
 
+#include <type_traits>
+
 #include "pk_common.cuh"
 #include "pk_internal.h"
 
@@ -205,6 +207,140 @@ __global__ void __launch_bounds__(512) conv_step_kernel(const ConvArgs a) {
     }
 }
 
+// Short chunks (the small model's 2 frames): everything in registers, no shared
+// memory but the LayerNorm's cross-warp partial sums.  Thread i owns channels
+// 2i and 2i + 1 of one stream (NT = D / 2 threads per CTA); the chunk length
+// and the width are compile-time constants, so every loop below is unrolled
+// and the next cache is plain register moves.  The two channels' weights (18
+// contiguous values, loaded as 9 words) and LayerNorm parameters are read
+// before the wait on the previous kernel (no kernel of the stream writes
+// them); then the slot and the GLU inputs; then both 8-frame caches at once
+// (16 bytes each in bf16).  The frames' LayerNorm statistics are block
+// reductions (exact two passes: the mean, then the sum of squared
+// deviations): each warp's partial sums meet in shared memory and are summed
+// by the lanes of every warp with shuffles, so each thread normalises its own
+// channels.
+template <typename T, int CH, int NT>
+__global__ void __launch_bounds__(NT) conv_step_reg_kernel(const ConvArgs a) {
+    constexpr int K = 9, KC = K - 1, D = 2 * NT, NW = NT / 32;
+    static_assert(NW <= 32, "one lane per warp in the cross-warp sums");
+    __shared__ float red[2][NW][CH];   // per-warp partial sums
+    const int b = blockIdx.x;
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int c0 = 2 * threadIdx.x;
+    const bool ln = a.ln_w != nullptr;
+    float wk[2][K], gw[2] = {0.f, 0.f}, gb[2] = {0.f, 0.f};
+    {
+        const T *wt = static_cast<const T *>(a.w) + c0 * K;   // 2K values, 4-byte aligned
+        if constexpr (sizeof(T) == 2) {
+            const uint32_t *w32 = reinterpret_cast<const uint32_t *>(wt);
+#pragma unroll
+            for (int i = 0; i < K; ++i) {
+                const uint32_t u = __ldg(w32 + i);
+                const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&u));
+                wk[(2 * i) / K][(2 * i) % K] = f.x;
+                wk[(2 * i + 1) / K][(2 * i + 1) % K] = f.y;
+            }
+        } else {
+            const float2 *w2 = reinterpret_cast<const float2 *>(wt);
+#pragma unroll
+            for (int i = 0; i < K; ++i) {
+                const float2 f = __ldg(w2 + i);
+                wk[(2 * i) / K][(2 * i) % K] = f.x;
+                wk[(2 * i + 1) / K][(2 * i + 1) % K] = f.y;
+            }
+        }
+        if (ln) {
+            load2<T>(static_cast<const T *>(a.ln_w) + c0, gw);
+            load2<T>(static_cast<const T *>(a.ln_b) + c0, gb);
+        }
+    }
+    grid_dep_wait();     // x and the cache may come from the previous kernel
+    grid_dep_launch();   // the next kernel may be scheduled (it waits for us)
+    const int s = a.slots[b];
+    const int n = a.lengths[b];
+    float xa[CH][2], xg[CH][2];
+    {
+        const T *xb = static_cast<const T *>(a.x) + (int64_t)b * a.x_bs + c0;
+#pragma unroll
+        for (int t = 0; t < CH; ++t) {
+            load2<T>(xb + (int64_t)t * a.x_rs, xa[t]);
+            load2<T>(xb + (int64_t)t * a.x_rs + D, xg[t]);
+        }
+    }
+    if (s < 0 || s >= a.num_slots) {   // block-uniform
+        if (threadIdx.x == 0) raise(a.error, PK_DEV_BAD_SLOT);
+        return;
+    }
+    T *cache = static_cast<T *>(a.state) + (((int64_t)s * a.num_layers + a.layer) * D + c0) * KC;
+    float hist[2][KC + CH];
+    load_cache<T, KC>(cache, hist[0]);
+    load_cache<T, KC>(cache + KC, hist[1]);
+    float y[CH][2];
+#pragma unroll
+    for (int ch = 0; ch < 2; ++ch) {
+#pragma unroll
+        for (int t = 0; t < CH; ++t) {
+            // F.glu then masked_fill(pad_mask, 0) (convolution.py:153-155)
+            const float v = round_to(xa[t][ch] * sigmoid(xg[t][ch]), static_cast<const T *>(nullptr));
+            hist[ch][KC + t] = t < n ? v : 0.f;
+        }
+#pragma unroll
+        for (int t = 0; t < CH; ++t) {
+            float acc = 0.f;
+#pragma unroll
+            for (int k = 0; k < K; ++k) acc = fmaf(wk[ch][k], hist[ch][t + k], acc);
+            y[t][ch] = round_to(acc, static_cast<const T *>(nullptr));   // the conv output's dtype
+        }
+    }
+    // next cache: the last K-1 entries of cat(cache, x)
+    store_cache<T, KC>(cache, hist[0] + CH);
+    store_cache<T, KC>(cache + KC, hist[1] + CH);
+    T *yb = static_cast<T *>(a.y) + (int64_t)b * CH * D + c0;
+    if (!ln) {
+#pragma unroll
+        for (int t = 0; t < CH; ++t) store2<T>(yb + t * D, y[t]);
+        return;
+    }
+    // LayerNorm over channels (the module's "batch_norm", convolution.py:138,157), then SiLU
+    auto block_sum = [&](float (&v)[CH], int which) {
+#pragma unroll
+        for (int t = 0; t < CH; ++t)
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) v[t] += __shfl_xor_sync(0xffffffffu, v[t], o);
+        if (lane == 0)
+#pragma unroll
+            for (int t = 0; t < CH; ++t) red[which][warp][t] = v[t];
+        __syncthreads();
+#pragma unroll
+        for (int t = 0; t < CH; ++t) {
+            float u = lane < NW ? red[which][lane][t] : 0.f;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) u += __shfl_xor_sync(0xffffffffu, u, o);
+            v[t] = u;
+        }
+    };
+    float part[CH], mean[CH];
+#pragma unroll
+    for (int t = 0; t < CH; ++t) part[t] = y[t][0] + y[t][1];
+    block_sum(part, 0);
+#pragma unroll
+    for (int t = 0; t < CH; ++t) {
+        mean[t] = part[t] / D;
+        const float d0 = y[t][0] - mean[t], d1 = y[t][1] - mean[t];
+        part[t] = d0 * d0 + d1 * d1;
+    }
+    block_sum(part, 1);
+#pragma unroll
+    for (int t = 0; t < CH; ++t) {
+        const float inv = rsqrtf(part[t] / D + a.eps);
+        const float z0 = (y[t][0] - mean[t]) * inv * gw[0] + gb[0];
+        const float z1 = (y[t][1] - mean[t]) * inv * gw[1] + gb[1];
+        const float o[2] = {z0 * sigmoid(z0), z1 * sigmoid(z1)};
+        store2<T>(yb + t * D, o);
+    }
+}
+
 }  // namespace
 
 int launch_conv(const ConvArgs &a, cudaStream_t s) {
@@ -213,6 +349,25 @@ int launch_conv(const ConvArgs &a, cudaStream_t s) {
         return PK_ENOTSUP;
     const int threads = ((a.dim / kCpt + 31) / 32) * 32;
     const int tm = a.chunk <= 2 ? 2 : a.chunk <= 4 ? 4 : a.chunk <= 8 ? 8 : 16;
+    // chunks of 1 to 4 frames at widths 512 and 1024: the register form (no
+    // staging, one load round after the slot)
+    if (a.chunk <= 4 && (a.dim == 512 || a.dim == 1024)) {
+        auto pick = [&](auto tag) {
+            using T = decltype(tag);
+            auto by_chunk = [&](auto nt) {
+                constexpr int NT = decltype(nt)::value;
+                void (*k)(const ConvArgs) = a.chunk == 1   ? conv_step_reg_kernel<T, 1, NT>
+                                          : a.chunk == 2 ? conv_step_reg_kernel<T, 2, NT>
+                                          : a.chunk == 3 ? conv_step_reg_kernel<T, 3, NT>
+                                                         : conv_step_reg_kernel<T, 4, NT>;
+                return launch_pdl(k, dim3(a.batch), dim3(NT), 0, s, a);
+            };
+            return a.dim == 512 ? by_chunk(std::integral_constant<int, 256>())
+                                : by_chunk(std::integral_constant<int, 512>());
+        };
+        const cudaError_t e = a.dtype == PK_DTYPE_BF16 ? pick(__nv_bfloat16()) : pick(float());
+        return cuda_status(e, "conv_step_reg_kernel");
+    }
     auto pick = [&](auto tag) {
         using T = decltype(tag);
         auto kernel = tm == 2 ? conv_step_kernel<T, 9, 2> : tm == 4 ? conv_step_kernel<T, 9, 4>

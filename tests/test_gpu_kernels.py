@@ -22,7 +22,9 @@ TOL = {torch.float32: 1e-5, torch.bfloat16: 1e-2}
 SHAPES = {"small": dict(att=(70, 1), dim=512, heads=8), "large": dict(att=(70, 13), dim=1024, heads=8),
           # head_dim 64 with chunks of 3 and 4 frames: 12 and 16 stacked query rows of
           # the 4-head CTA (the small model stacks 8)
-          "small_t3": dict(att=(70, 2), dim=512, heads=8), "small_t4": dict(att=(70, 3), dim=512, heads=8)}
+          "small_t3": dict(att=(70, 2), dim=512, heads=8), "small_t4": dict(att=(70, 3), dim=512, heads=8),
+          # the conv-cache step's register form at the large width, and a 1-frame chunk
+          "wide_t2": dict(att=(70, 1), dim=1024, heads=8), "small_t1": dict(att=(70, 0), dim=512, heads=8)}
 
 
 def pool_state(pool):
@@ -280,7 +282,7 @@ def conv_oracle(x2d, cache, w, lengths, g, b, eps=1e-5):
     return z, y.transpose(0, 2, 1), nxt
 
 
-@pytest.mark.parametrize("shape", ["small", "large"])
+@pytest.mark.parametrize("shape", ["small", "large", "small_t1", "small_t3", "small_t4", "wide_t2"])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_conv_step_matches_oracle(shape, dtype):
     cfg = SHAPES[shape]
