@@ -73,7 +73,7 @@ __device__ __forceinline__ void consumer_sync() {
     asm volatile("bar.sync 1, %0;" ::"n"(kH * 32) : "memory");
 }
 
-template <int NS, bool kRows16>
+template <int NS, bool kRows16, int MB>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     paged_attn_stacked_kernel(const __grid_constant__ CUtensorMap kv_map, const SGeom g,
                               const pk_paged_kv_desc d, const AttnArgs a) {
@@ -85,6 +85,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     __shared__ int s_ok, s_w, s_nfirst, s_nb;
     __shared__ volatile int s_abort;
     __shared__ int s_page[kMaxBoxes], s_start[kMaxBoxes];
+    // per page box: its first window column (jbase) and the box rows [lo, hi)
+    // that hold window frames (inside the page, at or after frame 0, in the window)
+    __shared__ int s_jbase[kMaxBoxes], s_lo[kMaxBoxes], s_hi[kMaxBoxes];
     __shared__ uint32_t s_mask[16 * 4];
     __shared__ float s_rowsum[16];
 
@@ -116,10 +119,20 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         s_mask[32 + lane] = (uint32_t)wd[PK_WIN_MASK + 32 + lane];
         if (lane == 0) {
             const int nb = wd[PK_WIN_NB];
-            s_ok = wd[PK_WIN_OK] && nb <= g.max_boxes && nb <= kMaxBoxes;
+            s_ok = wd[PK_WIN_OK] && nb <= g.max_boxes && nb <= MB;
             s_w = wd[PK_WIN_W];
             s_nfirst = wd[PK_WIN_NFIRST];
             s_nb = nb;
+        }
+        if (lane < kMaxBoxes) {
+            // row r of box `lane` is window column jbase + r when it is a real frame:
+            // 0 <= start + r < 16 (inside the page), abs frame >= 0, 0 <= column < W
+            const int st = wd[PK_WIN_START + lane];
+            const int abs0 = ((wd[PK_WIN_NFIRST] + lane) << 4) + st;
+            const int jb = abs0 - (wd[PK_WIN_W] - g.left);
+            s_jbase[lane] = jb;
+            s_lo[lane] = max(max(-st, -abs0), -jb);
+            s_hi[lane] = min(16 - st, g.W - jb);
         }
     }
     __syncthreads();
@@ -289,16 +302,14 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         const int row = tid / 16 + pass * 8, sub = tid % 16;
         const int rows = kH * chunk;
         const int iq = row % chunk;
-        float sv[kMaxBoxes];
+        float sv[MB];
         float mx = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < kMaxBoxes; ++i) {
+        for (int i = 0; i < MB; ++i) {
             sv[i] = -INFINITY;
             if (i < nb && row < rows) {
-                const int pr = s_start[i] + sub;
-                const int av = ((nfirst + i) << 4) + pr;
-                const int j = av - (w - g.left);
-                if (pr >= 0 && pr < 16 && av >= 0 && j >= 0 && j < W) {
+                if (sub >= s_lo[i] && sub < s_hi[i]) {
+                    const int j = s_jbase[i] + sub;
                     const float c = sS[(i * 16 + row) * 16 + sub] * scale;
                     const bool allowed = (s_mask[iq * 4 + (j >> 5)] >> (j & 31)) & 1u;
                     sv[i] = allowed ? c + sBD[row * bds + chunk - 1 - iq + j] * scale
@@ -311,7 +322,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
         float sum = 0.f;
 #pragma unroll
-        for (int i = 0; i < kMaxBoxes; ++i) {
+        for (int i = 0; i < MB; ++i) {
             if (i < nb) {
                 const float p = sv[i] == -INFINITY ? 0.f : __expf(sv[i] - mx);
                 sum += p;
@@ -433,10 +444,12 @@ int launch_attention_stacked(const pk_paged_kv *kv, const CUtensorMap &pos_map16
     g.off_p = g.off_bd + 16 * g.bd_stride * 4;
     const size_t smem = g.off_p + kMaxBoxes * 16 * kPStride + 1024;
     // more than 8 stacked query rows (chunks of 3 or 4) take a second softmax pass
-    auto kernel = kH * d.chunk > 8 ? paged_attn_stacked_kernel<NS, true>
-                                   : paged_attn_stacked_kernel<NS, false>;
-    static size_t limit[2] = {48 * 1024, 48 * 1024};
-    size_t &lim = limit[kH * d.chunk > 8];
+    // and the softmax loops run over at most MB page boxes (6 for the small model)
+    const bool r16 = kH * d.chunk > 8, mb6 = g.max_boxes <= 6;
+    auto kernel = r16 ? (mb6 ? paged_attn_stacked_kernel<NS, true, 6> : paged_attn_stacked_kernel<NS, true, kMaxBoxes>)
+                      : (mb6 ? paged_attn_stacked_kernel<NS, false, 6> : paged_attn_stacked_kernel<NS, false, kMaxBoxes>);
+    static size_t limit[4] = {48 * 1024, 48 * 1024, 48 * 1024, 48 * 1024};
+    size_t &lim = limit[2 * r16 + mb6];
     if (smem > lim) {
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)smem);
