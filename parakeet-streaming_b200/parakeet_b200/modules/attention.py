@@ -89,10 +89,17 @@ class ConformerAttention(nn.Module):
         D = x.shape[-1]
         qkv = self.qkv(x)                                             # attention.py:94
         query, key, value = qkv[..., :D], qkv[..., D:2 * D], qkv[..., 2 * D:]
+        pool, pos = cache.pool, self.pos_projection(pos_emb)
         # cache append (attention.py:98) fused into the paged attention call
-        return cache.pool.attention(self.layer_idx, query, self.pos_projection(pos_emb),
-                                    self.pos_bias_u, self.pos_bias_v, cache.slots, cache.lengths,
-                                    key=key, value=value)
+        if pool.relpos_bd_cols:
+            # shapes with the all-stream pre-pass (bf16, 4 heads x chunk <= 16): the
+            # rel-pos term of every stream in one pass over the layer's pos rows,
+            # then attention over it (the same output, bit for bit)
+            bd = pool.relpos_bd(self.layer_idx, query, pos, self.pos_bias_v)
+            return pool.attention(self.layer_idx, query, None, self.pos_bias_u, None, cache.slots,
+                                  cache.lengths, key=key, value=value, bd=bd)
+        return pool.attention(self.layer_idx, query, pos, self.pos_bias_u, self.pos_bias_v,
+                              cache.slots, cache.lengths, key=key, value=value)
 
     def forward(self, x: Tensor, pos_emb: Tensor, attn_mask=None, cache: PagedModelCache = None):
         return self.linear_out(self._context(x, pos_emb, cache))      # attention.py:123
