@@ -755,6 +755,15 @@ GEMM_SHAPES = {   # (name, M, N, K, epilogue): the GEMMs of one encoder layer at
               ("qkv", 6720, 3072, 1024, "store"),
               ("out_proj+residual", 6720, 1024, 1024, "residual"),
               ("pointwise_conv1", 6720, 2048, 1024, "store")],
+    # a 2048-stream small-model serving step: the encoder layer's at 4096 rows,
+    # the greedy decode's per symbol step at 2048 rows
+    "serving": [("ff_linear1+silu", 4096, 2048, 512, "silu"),
+                ("ff_linear2+residual", 4096, 512, 2048, "residual"),
+                ("qkv", 4096, 1536, 512, "store"),
+                ("pointwise_conv1", 4096, 1024, 512, "store"),
+                ("joint_pred+relu", 2048, 640, 640, "residual_relu"),
+                ("joint_out+bias", 2048, 1088, 640, "bias"),
+                ("lstm_recurrent", 2048, 2560, 640, "store")],
 }
 
 
@@ -774,16 +783,23 @@ def gemm_step(model, steps, dev):
         a = torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16)
         w = (torch.randn(N, K, generator=g, device=dev) / K ** 0.5).to(torch.bfloat16)
         r = torch.randn(M, N, generator=g, device=dev).to(torch.bfloat16)
+        bias = torch.randn(N, generator=g, device=dev).to(torch.bfloat16)
+        alpha = 1.0 if epi == "residual_relu" else 0.5
 
         def ours():
-            return gemm(a, w, epi, residual=r if epi == "residual" else None, alpha=0.5)
+            return gemm(a, w, epi, residual=r if epi.startswith("residual") else None,
+                        alpha=alpha, bias=bias if epi == "bias" else None)
 
         def cublas():
+            if epi == "bias":
+                return torch.addmm(bias, a, w.t())
             y = a @ w.t()
             if epi == "silu":
                 return torch.nn.functional.silu(y)
             if epi == "residual":
                 return r + 0.5 * y
+            if epi == "residual_relu":
+                return torch.relu(r + y)
             return y
 
         row = {"name": name, "M": M, "N": N, "K": K}
@@ -1738,7 +1754,7 @@ def main():
         dec_line = rnnt_decode_step(args.model, 10, dev)
         pre_line = pre_encode_step(args.model, 10, dev)
         fe_line = feature_step(args.model, 50, dev)
-        gemm_line = {m: gemm_step(m, 20, dev) for m in ("small", "large")}
+        gemm_line = {m: gemm_step(m, 20, dev) for m in ("small", "large", "serving")}
         pipe_line = streaming_step(args.model, 10, dev)
     if not args.no_serve:
         serve_line = serve_lines(args, dev, world)

@@ -545,6 +545,16 @@ int launch_gemm(const GemmArgs &g, cudaStream_t s) {
     if (st != PK_OK) return st;
     if (pbn == 256) return launch_gemm_persistent<256, 4>(g, ta, tw, num_sms, s);
     if (pbn == 128) return launch_gemm_persistent<128, 6>(g, ta, tw, num_sms, s);
+    // more tiles than SMs but not two waves of them: a shallower ring (96 KB of
+    // stages) lets two CTAs share an SM, so the grid runs as one wave
+    const int ctas = mtiles * (g.N / bn);
+    if (ctas > num_sms && ctas <= 2 * num_sms) {
+        switch (bn) {
+            case 256: return launch_gemm_epi<256, 2>(g, ta, tw, s);
+            case 128: return launch_gemm_epi<128, 3>(g, ta, tw, s);
+            default: return launch_gemm_epi<64, 4>(g, ta, tw, s);
+        }
+    }
     switch (bn) {
         case 256: return launch_gemm_epi<256, 3>(g, ta, tw, s);
         case 128: return launch_gemm_epi<128, 4>(g, ta, tw, s);
