@@ -875,7 +875,8 @@ def stage_times(pipe, samples, slots, reps):
     from parakeet_b200.modules.cache import PagedModelCache, StreamingState
     B, n = samples.shape
     F = pipe.frames_per_push(n, False)
-    ns, flags, feats, nframes = pipe._fe_bufs[(B, n, False)]
+    key = (B, n, False)   # the buffers of this batch size (kept for good once a graph used them)
+    ns, flags, feats, nframes = pipe._fe_bufs_graph.get(key) or pipe._fe_bufs[key]
     graphs, res = [], {}
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
