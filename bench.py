@@ -1816,6 +1816,24 @@ def main():
     f0, f1 = e2e_loop(K)
     torch.cuda.synchronize()
     e2e_ms = f0.elapsed_time(f1) / K
+    # the copy-in alone, every rank at once (as in the loop): this rank's host
+    # link rate, to read the e2e figure against (ranks share the host's links)
+    if world > 1:
+        dist.barrier()
+    h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(s_in):
+        h0.record(s_in)
+        for i in range(K):
+            dq[i % NB2].copy_(hq[i % NBUF], non_blocking=True)
+        h1.record(s_in)
+    torch.cuda.synchronize()
+    h2d_gbs_rank = hq[0].numel() * hq[0].element_size() * K / (h0.elapsed_time(h1) * 1e-3) / 1e9
+    h2d_ranks = [h2d_gbs_rank]
+    if world > 1:
+        t = torch.zeros(world, dtype=torch.float64, device=dev)
+        t[rank] = h2d_gbs_rank
+        dist.all_reduce(t)
+        h2d_ranks = t.tolist()
     if world > 1:
         dist.barrier()
 
@@ -1895,7 +1913,9 @@ def main():
             "e2e": {"value": round(e2e, 1), "unit": "GB/s",
                     "h2d_bytes_per_step": qkv[0].numel() * 2, "d2h_bytes_per_step": out.numel() * 2,
                     "ms_per_step": round(e2e_ms, 4),
-                    "pipeline": "copy-in, compute and copy-out streams, 3 buffer sets, eager API calls"},
+                    "pipeline": "copy-in, compute and copy-out streams, 3 buffer sets, eager API calls",
+                    # the copy-in alone on every rank at once: the host-link rate per rank
+                    "h2d_gbs_per_rank": [round(v, 1) for v in h2d_ranks]},
             # per step: [rel-pos pre-pass,] allocator+windows, attention+append, counters
             "gpu_launches": (4 if relpos_mode == "prepass" else 3) * K,
             "relpos": {"mode": relpos_mode,
