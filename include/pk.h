@@ -69,6 +69,8 @@ extern "C" {
 #define PK_WIN_MASK 40
 #define PK_WIN_MAX_PAGES 16
 #define PK_WIN_STRIDE 128
+/* most batch rows of one step (pk_pages_begin_step) */
+#define PK_MAX_BATCH 6144
 
 /*
  * Paged K/V window of every stream slot.  Replaces ModelCache.attn_k /
@@ -114,7 +116,8 @@ int32_t pk_ring_size(int32_t left, int32_t chunk, int32_t page_size);
  * like deque(range(pool)) in scheduler.py:84. */
 int pk_pages_reset(pk_paged_kv *kv, const int32_t *init_order, void *stream);
 
-/* Start of one batched step (one CTA, deterministic order; batch <= 2048):
+/* Start of one batched step (one CTA, deterministic order;
+ * batch <= PK_MAX_BATCH):
  *  0. return every page of the `released` slots (finished streams,
  *     parakeet/engine/scheduler.py:101-104) and zero their counters;
  *  1. per batch row, in order: free pages wholly left of the window;

@@ -194,7 +194,7 @@ int pk_pages_begin_step(pk_paged_kv *kv, const int32_t *slots, const int32_t *le
     PK_CHECK(batch <= kv->d.num_slots, "batch larger than the pool's slots");
     PK_CHECK(batch == 0 || slots, "null slots");
     PK_CHECK(num_released == 0 || released, "null released");
-    PK_CHECK(batch <= 2048, "batch above 2048 rows");
+    PK_CHECK(batch <= PK_MAX_BATCH, "batch above PK_MAX_BATCH rows");
     return launch_pages_begin(kv, slots, lengths, batch, released, num_released,
                               static_cast<cudaStream_t>(stream));
 }
@@ -409,7 +409,7 @@ int pk_pages_begin_step_relpos(pk_paged_kv *kv, const int32_t *slots, const int3
     PK_CHECK(batch <= kv->d.num_slots, "batch larger than the pool's slots");
     PK_CHECK(batch == 0 || slots, "null slots");
     PK_CHECK(num_released == 0 || released, "null released");
-    PK_CHECK(batch <= 2048, "batch above 2048 rows");
+    PK_CHECK(batch <= PK_MAX_BATCH, "batch above PK_MAX_BATCH rows");
     AttnArgs a{};
     int st = relpos_args(kv, layer0, num_layers, query, q_layer_stride, q_batch_stride,
                          q_row_stride, pos_proj, pos_layer_stride, bias_v, bias_layer_stride,

@@ -94,7 +94,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     const int b = blockIdx.x, lrel = blockIdx.y, hg0 = blockIdx.z * kH;   // first head of the group
     const int layer = a.layer0 + lrel;
     const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
-    const int chunk = g.chunk, W = g.W, npb = g.npb;
+    const int chunk = g.chunk, npb = g.npb;
     float *sS = reinterpret_cast<float *>(smem + g.off_s);    // [box][16 rows][16]
     float *sBD = reinterpret_cast<float *>(smem + g.off_bd);  // [16 rows][bd_stride]
     char *sP = smem + g.off_p;                                // [box][16 rows][kPStride B]

@@ -18,7 +18,12 @@ namespace pk {
 namespace {
 
 constexpr int kAllocThreads = 1024;            // most threads of the step-start CTA
-constexpr int kMaxBatch = 2 * kAllocThreads;
+// Rows of one step: up to 2048 the rows keep a copy of their page-table rings in
+// shared memory (96 bytes a row); up to 6144 the rings stay in global memory
+// (32 bytes of shared memory a row).  Both fit the CTA's 192 KB.
+constexpr int kMaxBatchShared = 2 * kAllocThreads;
+constexpr int kMaxBatch = 6 * kAllocThreads;
+static_assert(kMaxBatch == PK_MAX_BATCH, "step rows");
 constexpr int kMaxBatchRelpos = 256;           // step start fused with the rel-pos pre-pass
 
 // Exclusive prefix sum of v over the CTA (blockDim.x a multiple of 32), in batch
@@ -134,7 +139,10 @@ __device__ void write_window(const pk_paged_kv_desc &d, const RowState &r, const
 
 // One CTA, one thread per batch row (several for batches above the CTA's
 // threads).  Every row keeps its owner thread through all phases, so only the
-// scans cross threads.
+// scans cross threads.  kSharedRings: each row's page-table ring is copied to
+// shared memory and written to both copies; otherwise the owner thread reads
+// and writes the slot's ring in global memory.
+template <bool kSharedRings>
 __device__ __forceinline__ void pages_begin_body(const pk_paged_kv_desc &d, const int32_t *slots,
                                                  const int32_t *lengths, int batch,
                                                  const int32_t *released, int num_released) {
@@ -142,7 +150,11 @@ __device__ __forceinline__ void pages_begin_body(const pk_paged_kv_desc &d, cons
     __shared__ int scan_tmp[33];
     __shared__ int64_t s_ctr[2];
     RowState *rows = reinterpret_cast<RowState *>(s_dyn);
-    int *rings = s_dyn + batch * (int)(sizeof(RowState) / sizeof(int));
+    int *rings = s_dyn + batch * (int)(sizeof(RowState) / sizeof(int));   // kSharedRings only
+    // ring of row b (slot s): shared copy or the page table itself
+    auto ring_of = [&](int b, int s) -> int32_t * {
+        return kSharedRings ? rings + b * PK_WIN_MAX_PAGES : d.page_table + (int64_t)s * d.ring;
+    };
     const int tid = threadIdx.x;
     const int N = d.num_pages, rmask = d.ring - 1;
     const int nthreads = blockDim.x;
@@ -196,9 +208,11 @@ __device__ __forceinline__ void pages_begin_body(const pk_paged_kv_desc &d, cons
             r.w = m[PK_META_WRITTEN];
             r.proc = m[PK_META_PROCESSED];
             r.clen = m[PK_META_CACHE_LEN];
+            if (kSharedRings) {
 #pragma unroll
-            for (int p = 0; p < PK_WIN_MAX_PAGES; ++p)
-                if (p <= rmask) rings[b * PK_WIN_MAX_PAGES + p] = pt[p];
+                for (int p = 0; p < PK_WIN_MAX_PAGES; ++p)
+                    if (p <= rmask) rings[b * PK_WIN_MAX_PAGES + p] = pt[p];
+            }
         } else {
             r.len = d.chunk;
             raise(d.error, PK_DEV_BAD_SLOT);
@@ -219,11 +233,12 @@ __device__ __forceinline__ void pages_begin_body(const pk_paged_kv_desc &d, cons
         if (nfree > 0) {
             RowState &r = rows[b];
             int32_t *pt = d.page_table + (int64_t)r.slot * d.ring;
+            int32_t *rg = ring_of(b, r.slot);
             for (int j = 0; j < nfree; ++j) {
                 const int pos = (r.first + j) & rmask;
-                d.free_ring[(tail + off + j) % N] = rings[b * PK_WIN_MAX_PAGES + pos];
-                rings[b * PK_WIN_MAX_PAGES + pos] = -1;
-                pt[pos] = -1;
+                d.free_ring[(tail + off + j) % N] = rg[pos];
+                rg[pos] = -1;
+                if (kSharedRings) pt[pos] = -1;
             }
             r.first += nfree;
             d.meta[(int64_t)r.slot * PK_META_STRIDE + PK_META_FIRST] = r.first;
@@ -254,11 +269,12 @@ __device__ __forceinline__ void pages_begin_body(const pk_paged_kv_desc &d, cons
             if (need > 0) {
                 RowState &r = rows[b];
                 int32_t *pt = d.page_table + (int64_t)r.slot * d.ring;
+                int32_t *rg = ring_of(b, r.slot);
                 for (int j = 0; j < need; ++j) {
                     const int pos = (r.next + j) & rmask;
                     const int page = d.free_ring[(head + off + j) % N];
-                    rings[b * PK_WIN_MAX_PAGES + pos] = page;
-                    pt[pos] = page;
+                    rg[pos] = page;
+                    if (kSharedRings) pt[pos] = page;
                 }
                 r.next += need;
                 d.meta[(int64_t)r.slot * PK_META_STRIDE + PK_META_NEXT] = r.next;
@@ -275,14 +291,15 @@ __device__ __forceinline__ void pages_begin_body(const pk_paged_kv_desc &d, cons
     // 3. window descriptors: each thread its own rows
     for (int k = 0; k < nk; ++k) {
         const int b = tid + k * nthreads;
-        if (b < batch) write_window(d, rows[b], rings + b * PK_WIN_MAX_PAGES, b);
+        if (b < batch) write_window(d, rows[b], ring_of(b, rows[b].slot), b);
     }
 }
 
+template <bool kSharedRings>
 __global__ void __launch_bounds__(kAllocThreads)
     pages_begin_kernel(pk_paged_kv_desc d, const int32_t *slots, const int32_t *lengths,
                        int batch, const int32_t *released, int num_released) {
-    pages_begin_body(d, slots, lengths, batch, released, num_released);
+    pages_begin_body<kSharedRings>(d, slots, lengths, batch, released, num_released);
 }
 
 // The step start and the all-stream rel-pos pre-pass in one launch: CTA 0 runs
@@ -294,7 +311,7 @@ __global__ void __launch_bounds__(kRelposThreads, 5)
                               int batch, const int32_t *released, int num_released,
                               const AttnArgs a, int bds, float *bd, int tiles_z) {
     if (blockIdx.x == 0) {
-        pages_begin_body(d, slots, lengths, batch, released, num_released);
+        pages_begin_body<true>(d, slots, lengths, batch, released, num_released);
         return;
     }
     grid_dep_wait();     // q may come from the previous kernel
@@ -331,21 +348,26 @@ int launch_pages_reset(const pk_paged_kv *kv, const int32_t *init_order, cudaStr
 int launch_pages_begin(const pk_paged_kv *kv, const int32_t *slots, const int32_t *lengths,
                        int batch, const int32_t *released, int num_released, cudaStream_t s) {
     if (batch > kMaxBatch || kv->d.ring > PK_WIN_MAX_PAGES) return PK_ENOTSUP;
-    const size_t smem = (size_t)batch * (sizeof(RowState) + PK_WIN_MAX_PAGES * sizeof(int));
-    static size_t limit = 48 * 1024;
-    if (smem > limit) {
-        cudaError_t e = cudaFuncSetAttribute(pages_begin_kernel,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)(kMaxBatch * (sizeof(RowState) +
-                                                                PK_WIN_MAX_PAGES * sizeof(int))));
+    const bool shared_rings = batch <= kMaxBatchShared;
+    const size_t row_bytes = sizeof(RowState) + (shared_rings ? PK_WIN_MAX_PAGES * sizeof(int) : 0);
+    const size_t smem = (size_t)batch * row_bytes;
+    auto kernel = shared_rings ? pages_begin_kernel<true> : pages_begin_kernel<false>;
+    static size_t limit[2] = {48 * 1024, 48 * 1024};
+    size_t &lim = limit[shared_rings];
+    if (smem > lim) {
+        const size_t most = shared_rings
+                                ? kMaxBatchShared * (sizeof(RowState) + PK_WIN_MAX_PAGES * sizeof(int))
+                                : kMaxBatch * sizeof(RowState);
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)most);
         if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(pages_begin)");
-        limit = kMaxBatch * (sizeof(RowState) + PK_WIN_MAX_PAGES * sizeof(int));
+        lim = most;
     }
     // one thread per row up to 1024 rows: small batches scan over a few warps only
     int threads = batch >= kAllocThreads ? kAllocThreads : (batch + 31) / 32 * 32;
     if (threads == 0) threads = 32;
-    return cuda_status(launch_pdl(pages_begin_kernel, dim3(1), dim3(threads), smem, s, kv->d,
-                                  slots, lengths, batch, released, num_released),
+    return cuda_status(launch_pdl(kernel, dim3(1), dim3(threads), smem, s, kv->d, slots, lengths,
+                                  batch, released, num_released),
                        "pages_begin_kernel");
 }
 

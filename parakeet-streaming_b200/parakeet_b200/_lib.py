@@ -24,6 +24,7 @@ PK_NOALLOC_SCRATCH_BYTES = 32 * 1024 * 1024   # pk_paged_attention_noalloc's sta
 META_FIRST, META_NEXT, META_WRITTEN, META_PROCESSED, META_CACHE_LEN = 0, 1, 2, 3, 4
 META_STRIDE = 8
 WIN_STRIDE = 128
+PK_MAX_BATCH = 6144   # most rows of one step (pk_pages_begin_step)
 
 
 class PKError(RuntimeError):

@@ -46,12 +46,16 @@ def assert_pool_equals_model(pool, model):
     assert free == list(model.free)
 
 
-@pytest.mark.parametrize("att,cap,n_slots,arrivals", [((70, 1), 0.6, 24, 4), ((70, 13), 0.6, 24, 4),
-                                                      ((70, 1), 1.0, 24, 4),
-                                                      ((70, 1), 0.8, 1100, 120)])
-def test_page_allocator_matches_cpu_model(att, cap, n_slots, arrivals):
+@pytest.mark.parametrize("att,cap,n_slots,arrivals,steps", [((70, 1), 0.6, 24, 4, 160),
+                                                            ((70, 13), 0.6, 24, 4, 160),
+                                                            ((70, 1), 1.0, 24, 4, 160),
+                                                            ((70, 1), 0.8, 1100, 120, 160),
+                                                            ((70, 1), 1.0, 6144, 1200, 64)])
+def test_page_allocator_matches_cpu_model(att, cap, n_slots, arrivals, steps):
     """Device allocator vs the CPU model, op for op; the 1100-slot case runs
-    batches above 1024 rows (two rows per thread of the step-start CTA)."""
+    batches above 1024 rows (two rows per thread of the step-start CTA), the
+    6144-slot case batches above 2048 rows (page-table rings read in place, up
+    to six rows per thread)."""
     rng = np.random.default_rng(7)
     left, T, ps = att[0], att[1] + 1, 16
     per = pages.pages_per_stream(left, T, ps)
@@ -62,7 +66,7 @@ def test_page_allocator_matches_cpu_model(att, cap, n_slots, arrivals):
     model = pages.PagePoolModel(n_pages, n_slots, left, T, ps, init_order=order)
     alloc = SlotAllocator(n_slots, per, n_pages)
     live = []
-    for step in range(160):
+    for step in range(steps):
         for _ in range(int(rng.integers(0, 3))):
             if live and rng.random() < 0.3:
                 s = live.pop(int(rng.integers(len(live))))
@@ -81,10 +85,45 @@ def test_page_allocator_matches_cpu_model(att, cap, n_slots, arrivals):
         pool.begin_step(sl, ln)
         model.end_step(batch, lengths)
         pool.end_step(sl, ln)
-        if step % 8 == 0 or step > 150:
+        if step % 8 == 0 or step > steps - 10:
             assert_pool_equals_model(pool, model)
     assert pool.read_error() == 0
     assert_pool_equals_model(pool, model)
+
+
+def test_append_gather_above_2048_rows_matches_model():
+    """Steps of 2600 rows (the step-start CTA's global-ring form): the window
+    descriptors it writes drive the append and gather, bit-exact against the
+    CPU page model's pool contents."""
+    att, n_slots, D, steps = (70, 1), 2600, 128, 48
+    left, T, ps = att[0], att[1] + 1, 16
+    rng = np.random.default_rng(11)
+    n_pages = n_slots * pages.pages_per_stream(left, T, ps)
+    order = rng.permutation(n_pages)
+    pool = PagedKVPool(1, D, 2, att, n_slots, num_pages=n_pages, dtype=torch.float32,
+                       device=DEV, page_order=order)
+    model = pages.PagedKVModel(pages.PagePoolModel(n_pages, n_slots, left, T, ps, init_order=order),
+                               1, D, dtype=np.float32)
+    start = np.where(np.arange(n_slots) < 2200, 0, rng.integers(1, 8, n_slots))
+    for step in range(steps):
+        batch = [int(s) for s in rng.permutation(n_slots) if start[s] <= step]
+        sl = torch.tensor(batch, dtype=torch.int32, device=DEV)
+        ln = torch.full((len(batch),), T, dtype=torch.int32, device=DEV)
+        k = rng.standard_normal((len(batch), T, D)).astype(np.float32)
+        v = rng.standard_normal((len(batch), T, D)).astype(np.float32)
+        assert model.pool.begin_step(batch)
+        pool.begin_step(sl, ln)
+        model.append(0, batch, k, v)
+        pool.append(0, torch.from_numpy(k).to(DEV), torch.from_numpy(v).to(DEV), sl)
+        if step % 12 == 11 or step == steps - 1:
+            kw, vw = pool.gather(0, sl)
+            km, vm = model.gather(0, batch)
+            assert np.array_equal(kw.cpu().numpy(), km), step
+            assert np.array_equal(vw.cpu().numpy(), vm), step
+        model.pool.end_step(batch, [T] * len(batch))
+        pool.end_step(sl, ln)
+    assert pool.read_error() == 0
+    assert_pool_equals_model(pool, model.pool)
 
 
 def test_pool_exhaustion_sets_error_bit_and_allocates_nothing():
