@@ -444,6 +444,301 @@ __global__ void __launch_bounds__(kPThreads, 1)
     }
 }
 
+// ---------------------------------------------------------------------------
+// CTA-pair form (tcgen05.mma.cta_group::2): a cluster of two CTAs on two SMs
+// computes a 256 x BN tile with M = 256 MMAs.  CTA r of the pair loads rows
+// m0 + 128 r .. + 127 of A and rows n0 + (BN/2) r .. of W into its own shared
+// memory (plain TMA tile loads, no multicast); the MMA issued by the pair's
+// even CTA reads A from each CTA's own stage and B from both, and writes rows
+// 128 r .. of the tile to CTA r's TMEM.  Each SM thus streams 128 + BN/2
+// operand rows per K block for a 128 x BN product, where a one-CTA tile streams
+// 128 + BN.  Both CTAs' loads complete on the even CTA's full[s] barrier (the
+// .cta_group::2 form of the TMA load may signal the peer's barrier); the MMA
+// commits release stage s in both CTAs (commit multicast to both empty[s]) and
+// hand each accumulator to both CTAs' epilogue warps (tmem_full[a]); all eight
+// epilogue warps of the pair return an accumulator on the even CTA's
+// tmem_empty[a].  Tiles are walked persistently, row tiles fastest.
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// shared::cluster address of the same shared-memory object in CTA `rank`
+__device__ __forceinline__ uint32_t mapa_rank(uint32_t saddr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+// arrive on an mbarrier of either CTA of the cluster (release at cluster scope)
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "n"(kSuspendNs)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cluster_bounded(uint64_t *bar, uint32_t parity,
+                                                          uint64_t limit_ns) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait_cluster(bar, parity)) {
+        if (globaltimer_ns() - t0 > limit_ns) return false;
+    }
+    return true;
+}
+// 2-D tile load into this CTA's shared memory, completion on an mbarrier of
+// either CTA of the pair (bar: shared::cluster address)
+__device__ __forceinline__ void tma_load_2d_pair(void *dst, const CUtensorMap *map, uint32_t bar,
+                                                 int32_t c0, int32_t c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ void umma_bf16_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                               uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// arrive on `bar` (same offset) in both CTAs of the pair when the MMAs issued so
+// far by this thread are done
+__device__ __forceinline__ void umma_commit_pair(uint64_t *bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+        " [%0], %1;" ::"r"(smem_u32(bar)),
+        "h"((uint16_t)0x3)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t *dst, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(dst)),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+                 : "memory");
+}
+
+template <int BN, int NS, int EPI>
+__global__ void __launch_bounds__(kPThreads, 1)
+    gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tm_a,
+                          const __grid_constant__ CUtensorMap tm_w, int M, int N, int K,
+                          __nv_bfloat16 *C, int64_t ldc, const __nv_bfloat16 *R, int64_t ldr,
+                          const __nv_bfloat16 *bias, float alpha, int32_t *error) {
+    constexpr int kHalfB = BN / 2;                  // W rows per CTA
+    constexpr int kBBytes = kHalfB * kBK * 2;
+    constexpr uint32_t kStageTx = 2 * (kABytes + kBBytes);   // both CTAs' loads
+    extern __shared__ uint8_t gemm_smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(gemm_smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *sA = smem, *sB = smem + NS * kABytes;
+    __shared__ __align__(8) uint64_t full[NS], empty[NS], tmem_full[2], tmem_empty[2];
+    __shared__ uint32_t tmem_base;
+    __shared__ volatile int failed;
+
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const int pair = blockIdx.x / 2, npairs = gridDim.x / 2;
+    const int mtiles = (M + 2 * kBM - 1) / (2 * kBM), tiles = mtiles * (N / BN), nk = K / kBK;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tmem_full[a], 1);
+            mbar_init(&tmem_empty[a], 8);   // 4 epilogue warps in each CTA of the pair
+        }
+        failed = 0;
+        fence_mbar_init();
+        prefetch_tmap(&tm_a);
+        prefetch_tmap(&tm_w);
+    }
+    if (warp == 0) {
+        tmem_alloc_pair(&tmem_base, 2 * BN);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync_all();   // both CTAs' barriers initialised and TMEM allocated
+    tc_fence_after();
+    const uint32_t tmem = tmem_base;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // producer: this CTA's halves of every K block of the pair's tiles
+            grid_dep_wait();
+            int g = 0;
+            for (int tile = pair; tile < tiles && !failed; tile += npairs) {
+                const int m0 = (tile % mtiles) * 2 * kBM + (int)rank * kBM;
+                const int n0 = (tile / mtiles) * BN + (int)rank * kHalfB;
+                for (int kb = 0; kb < nk; ++kb, ++g) {
+                    const int s = g % NS, u = g / NS;
+                    if (u >= 1 && !mbar_wait_bounded(&empty[s], (u - 1) & 1, kWaitLimitNs)) {
+                        raise(error, PK_DEV_TIMEOUT);
+                        failed = 1;
+                        break;
+                    }
+                    const uint32_t fb = mapa_rank(smem_u32(&full[s]), 0);
+                    if (leader) mbar_arrive_expect_tx(&full[s], kStageTx);
+                    tma_load_2d_pair(sB + s * kBBytes, &tm_w, fb, kb * kBK, n0);
+                    tma_load_2d_pair(sA + s * kABytes, &tm_a, fb, kb * kBK, m0);
+                }
+            }
+            if (leader) {   // leave none of the pair's loads in flight
+                for (int s = 0; s < NS; ++s)
+                    if (g > s) {
+                        const int last = g - 1 - (g - 1 - s) % NS;
+                        mbar_wait_bounded(&full[s], (last / NS) & 1, kWaitLimitNs);
+                    }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && leader) {
+            // MMA issuer of the pair: accumulator t & 1 for the pair's t-th tile
+            constexpr uint32_t idesc = idesc_bf16(2 * kBM, BN);
+            int g = 0, t = 0;
+            for (int tile = pair; tile < tiles && !failed; tile += npairs, ++t) {
+                const int acc = t & 1, use = t >> 1;
+                if (use >= 1 &&
+                    !mbar_wait_cluster_bounded(&tmem_empty[acc], (use - 1) & 1, kWaitLimitNs)) {
+                    raise(error, PK_DEV_TIMEOUT);
+                    failed = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem + acc * BN;
+                for (int kb = 0; kb < nk; ++kb, ++g) {
+                    const int s = g % NS;
+                    if (!mbar_wait_bounded(&full[s], (g / NS) & 1, kWaitLimitNs)) {
+                        raise(error, PK_DEV_TIMEOUT);
+                        failed = 1;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(sA + s * kABytes), b0 = smem_u32(sB + s * kBBytes);
+#pragma unroll
+                    for (int kk = 0; kk < kBK / 16; ++kk)
+                        umma_bf16_pair(d, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32), idesc,
+                                       (kb | kk) != 0);
+                    umma_commit_pair(&empty[s]);
+                }
+                if (failed) break;
+                umma_commit_pair(&tmem_full[acc]);
+            }
+        }
+    } else {
+        // epilogue warps 2..5: TMEM lanes 32 (w % 4) .. = tile rows 128 rank + 32 (w % 4) ..
+        grid_dep_wait();   // the residual rows may come from the previous kernel
+        const int q = warp & 3;
+        const uint32_t empty0 = mapa_rank(smem_u32(&tmem_empty[0]), 0),
+                       empty1 = mapa_rank(smem_u32(&tmem_empty[1]), 0);
+        int t = 0;
+        for (int tile = pair; tile < tiles; tile += npairs, ++t) {
+            const int acc = t & 1, use = t >> 1;
+            const bool ok = __all_sync(0xffffffffu,
+                                       mbar_wait_bounded(&tmem_full[acc], use & 1, kWaitLimitNs));
+            if (!ok) {
+                if (lane == 0) raise(error, PK_DEV_TIMEOUT);
+                failed = 1;
+                break;
+            }
+            tc_fence_after();
+            if (tile + npairs >= tiles) grid_dep_launch();
+            const int m0 = (tile % mtiles) * 2 * kBM + (int)rank * kBM, n0 = (tile / mtiles) * BN;
+            const int row = m0 + q * 32 + lane;
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                float v[32];
+                __syncwarp();
+                tmem_ld32(tmem + acc * BN + ((uint32_t)(q * 32) << 16) + c * 32, v);
+                if (row < M) epilogue_store<EPI>(v, row, n0 + c * 32, C, ldc, R, ldr, bias, alpha);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(acc ? empty1 : empty0);
+        }
+    }
+    // every thread of both CTAs gets here: the pair's MMAs, loads and TMEM reads
+    // are done before either CTA frees its TMEM columns or leaves
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync_all();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem, 2 * BN);
+    }
+}
+
+template <int BN, int NS, int EPI>
+int launch_gemm_pair_t(const GemmArgs &g, const CUtensorMap &ta, const CUtensorMap &tw,
+                       int num_sms, cudaStream_t s) {
+    auto k = gemm_bf16_pair_kernel<BN, NS, EPI>;
+    const size_t smem = (size_t)NS * (kABytes + (BN / 2) * kBK * 2) + 1024;
+    static bool attr = false;
+    if (!attr) {
+        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(gemm pair)");
+        attr = true;
+    }
+    const int tiles = ((g.M + 2 * kBM - 1) / (2 * kBM)) * (g.N / BN);
+    const int pairs = tiles < num_sms / 2 ? tiles : num_sms / 2;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * pairs);
+    cfg.blockDim = dim3(kPThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attrs[2];
+    attrs[0].id = cudaLaunchAttributeClusterDimension;
+    attrs[0].val.clusterDim.x = 2;
+    attrs[0].val.clusterDim.y = 1;
+    attrs[0].val.clusterDim.z = 1;
+    attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attrs;
+    cfg.numAttrs = 2;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, k, ta, tw, g.M, g.N, g.K,
+                                       static_cast<__nv_bfloat16 *>(g.C), g.ldc,
+                                       static_cast<const __nv_bfloat16 *>(g.R), g.ldr,
+                                       static_cast<const __nv_bfloat16 *>(g.bias), g.alpha, g.error);
+    return cuda_status(e, "gemm_bf16_pair_kernel");
+}
+
+template <int BN, int NS>
+int launch_gemm_pair(const GemmArgs &g, const CUtensorMap &ta, const CUtensorMap &tw, int num_sms,
+                     cudaStream_t s) {
+    switch (g.epilogue) {
+        case PK_GEMM_SILU: return launch_gemm_pair_t<BN, NS, PK_GEMM_SILU>(g, ta, tw, num_sms, s);
+        case PK_GEMM_RESIDUAL:
+            return launch_gemm_pair_t<BN, NS, PK_GEMM_RESIDUAL>(g, ta, tw, num_sms, s);
+        case PK_GEMM_RESIDUAL_RELU:
+            return launch_gemm_pair_t<BN, NS, PK_GEMM_RESIDUAL_RELU>(g, ta, tw, num_sms, s);
+        case PK_GEMM_BIAS: return launch_gemm_pair_t<BN, NS, PK_GEMM_BIAS>(g, ta, tw, num_sms, s);
+        default: return launch_gemm_pair_t<BN, NS, PK_GEMM_STORE>(g, ta, tw, num_sms, s);
+    }
+}
+
 template <int BN, int NS, int EPI>
 int launch_gemm_persistent_t(const GemmArgs &g, const CUtensorMap &ta, const CUtensorMap &tw,
                              int num_sms, cudaStream_t s) {
@@ -543,6 +838,19 @@ int launch_gemm(const GemmArgs &g, cudaStream_t s) {
     if (st != PK_OK) return st;
     st = encode_tmap(&tw, PK_DTYPE_BF16, g.W, 2, wdims, wstr, wbox);
     if (st != PK_OK) return st;
+    // CTA pairs (256 x 256 tiles on two SMs) when the pair tiles fill a wave of
+    // pairs and either their waves are at least 80 % full or K is long (measured:
+    // a 1.3- or 1.46-wave grid of short-K pair tiles is slower than one-CTA tiles)
+    const int mt2 = (g.M + 2 * kBM - 1) / (2 * kBM), pairs = num_sms / 2;
+    const int t2 = g.N % 256 == 0 ? mt2 * (g.N / 256) : 0;
+    const bool full_waves = t2 >= pairs && 5 * t2 >= 4 * pairs * ((t2 + pairs - 1) / pairs);
+    if (t2 >= pairs && (full_waves || g.K >= 2048)) {
+        CUtensorMap tw2;
+        const uint32_t wbox2[2] = {kBK, 128};
+        st = encode_tmap(&tw2, PK_DTYPE_BF16, g.W, 2, wdims, wstr, wbox2);
+        if (st != PK_OK) return st;
+        return launch_gemm_pair<256, 6>(g, ta, tw2, num_sms, s);
+    }
     if (pbn == 256) return launch_gemm_persistent<256, 4>(g, ta, tw, num_sms, s);
     if (pbn == 128) return launch_gemm_persistent<128, 6>(g, ta, tw, num_sms, s);
     // more tiles than SMs but not two waves of them: a shallower ring (96 KB of

@@ -1,6 +1,7 @@
 """pk_gemm_bf16 (tcgen05 tensor cores, TMEM accumulator; through the C ABI;
-the persistent two-accumulator form takes the shapes with more than two waves
-of 128 x 256 tiles)
+the CTA-pair form (256 x 256 tiles over two SMs) takes the shapes whose pair
+tiles fill a wave, the persistent one-CTA form other shapes with more than two
+waves of 128 x 256 tiles)
 against an fp32 matmul of the same bf16 operands: the output is the fp32
 result rounded once to bf16, so each element is within 2^-8 relative (plus
 the accumulation-order difference, far below that) of the reference."""
@@ -31,7 +32,8 @@ def check_close(out, ref):
 @pytest.mark.parametrize("M,N,K", [(1, 64, 64), (7, 512, 512), (128, 128, 64), (320, 2048, 512),
                                    (320, 512, 2048), (320, 1536, 512), (1000, 1024, 1024),
                                    (6720, 4096, 1024), (6720, 1024, 4096), (6720, 3072, 1024),
-                                   (6720, 2048, 1024), (6700, 2048, 128)])
+                                   (6720, 2048, 1024), (6700, 2048, 128), (4096, 2048, 512),
+                                   (4096, 1536, 512), (4000, 1024, 512)])
 def test_gemm_store(M, N, K):
     a, w, _ = operands(M, N, K, M + N + K)
     ref = a.float() @ w.float().t()
@@ -39,7 +41,8 @@ def test_gemm_store(M, N, K):
     assert gemm_error_word("cuda") == 0
 
 
-@pytest.mark.parametrize("M,N,K", [(320, 2048, 512), (6720, 4096, 1024), (33, 192, 128)])
+@pytest.mark.parametrize("M,N,K", [(320, 2048, 512), (6720, 4096, 1024), (33, 192, 128),
+                                   (4096, 2048, 512)])
 def test_gemm_silu(M, N, K):
     a, w, _ = operands(M, N, K, 7 * M + N)
     acc = a.float() @ w.float().t()
@@ -47,7 +50,7 @@ def test_gemm_silu(M, N, K):
 
 
 @pytest.mark.parametrize("M,N,K", [(320, 512, 2048), (6720, 1024, 4096), (5, 64, 64),
-                                   (6720, 3072, 1024)])
+                                   (6720, 3072, 1024), (6720, 1024, 1024), (4096, 512, 2048)])
 def test_gemm_residual(M, N, K):
     a, w, r = operands(M, N, K, 3 * M + K)
     ref = r.float() + 0.5 * (a.float() @ w.float().t())
