@@ -117,6 +117,102 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Epilogue staging: each epilogue warp owns a 32-row tile of 64 bf16 columns
+// in shared memory (rows padded to 144 bytes: a row-per-lane 16-byte access
+// and a row-segment access are both free of bank conflicts).
+constexpr int kStageRow = 144;
+constexpr int kStageBytes = 32 * kStageRow;
+
+// The epilogue of accumulator columns [col, col + 64) of the warp's tile rows
+// row0 .. row0 + 31 (TMEM lane l of taddr = row row0 + l).  The arithmetic runs
+// a row per lane, as the accumulator comes out of TMEM; the residual rows are
+// read and the output rows written through the warp's staging tile as whole
+// 128-byte row segments (four rows per warp access), where a row per lane would
+// touch 32 rows per access.
+constexpr bool is_residual(int epi) {
+    return epi == PK_GEMM_RESIDUAL || epi == PK_GEMM_RESIDUAL_RELU;
+}
+
+// This lane's share of the residual rows of the same 64 columns, as row
+// segments (piece i: row row0 + 4 i + lane / 8, bytes (lane % 8) * 16 ..):
+// loaded ahead of the columns' epilogue so that the load latency overlaps work.
+__device__ __forceinline__ void load_residual64(uint4 (&rv)[8], int row0, int M, int col,
+                                                const __nv_bfloat16 *R, int64_t ldr) {
+    const int lane = threadIdx.x & 31;
+    const int sr = lane >> 3, sb = (lane & 7) * 16;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int r = i * 4 + sr;
+        rv[i] = make_uint4(0u, 0u, 0u, 0u);
+        if (row0 + r < M)
+            rv[i] = *reinterpret_cast<const uint4 *>(
+                reinterpret_cast<const char *>(R + (int64_t)(row0 + r) * ldr + col) + sb);
+    }
+}
+
+template <int EPI>
+__device__ __forceinline__ void epilogue_tile64(uint32_t taddr, int row0, int M, int col,
+                                                __nv_bfloat16 *C, int64_t ldc,
+                                                const uint4 (&rv)[8], const __nv_bfloat16 *bias,
+                                                float alpha, uint8_t *stage) {
+    constexpr bool kRes = is_residual(EPI);
+    const int lane = threadIdx.x & 31;
+    const int sr = lane >> 3, sb = (lane & 7) * 16;   // row-segment phase: row in 4, byte
+    if (kRes) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            *reinterpret_cast<uint4 *>(stage + (i * 4 + sr) * kStageRow + sb) = rv[i];
+    }
+    float v[64];
+    tmem_ld32(taddr, *reinterpret_cast<float(*)[32]>(v));
+    tmem_ld32(taddr + 32, *reinterpret_cast<float(*)[32]>(v + 32));
+    __syncwarp();   // residual rows staged
+    uint8_t *mine = stage + lane * kStageRow;
+    if (EPI == PK_GEMM_SILU) {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) v[i] = __fdividef(v[i], 1.f + __expf(-v[i]));
+    } else if (kRes) {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            float f[8];
+            unpack16(*reinterpret_cast<const uint4 *>(mine + q * 16), f, bias);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float t = f[i] + alpha * v[q * 8 + i];
+                v[q * 8 + i] = EPI == PK_GEMM_RESIDUAL_RELU ? fmaxf(t, 0.f) : t;
+            }
+        }
+    } else if (EPI == PK_GEMM_BIAS) {
+        const uint4 *bp = reinterpret_cast<const uint4 *>(bias + col);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            float f[8];
+            unpack16(bp[q], f, bias);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[q * 8 + i] += f[i];
+        }
+    }
+    __syncwarp();   // every lane's residual row read
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+        uint4 o;
+        __nv_bfloat162 *h = reinterpret_cast<__nv_bfloat162 *>(&o);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            h[i] = __floats2bfloat162_rn(v[q * 8 + 2 * i], v[q * 8 + 2 * i + 1]);
+        *reinterpret_cast<uint4 *>(mine + q * 16) = o;
+    }
+    __syncwarp();   // output rows staged
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int r = i * 4 + sr;
+        if (row0 + r < M)
+            *reinterpret_cast<uint4 *>(reinterpret_cast<char *>(C + (int64_t)(row0 + r) * ldc + col) +
+                                       sb) = *reinterpret_cast<const uint4 *>(stage + r * kStageRow + sb);
+    }
+    __syncwarp();   // staging tile free again
+}
+
 template <int BN, int NS, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w,
@@ -201,56 +297,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
 
-    // epilogue: warp w owns TMEM lanes (tile rows) 32w .. 32w + 31
+    // epilogue: warp w owns TMEM lanes (tile rows) 32w .. 32w + 31; the first
+    // residual columns are requested while the MMAs still run
+    uint4 rv[8], rn[8];
+    if (is_residual(EPI)) load_residual64(rn, m0 + warp * 32, M, n0, R, ldr);
     const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(&done, 0, kWaitLimitNs));
     if (!ok && lane == 0) raise(error, PK_DEV_TIMEOUT);
     tc_fence_after();
     grid_dep_launch();
-    const int row = m0 + warp * 32 + lane;
     if (ok && !failed) {
+        // the stage ring is idle now (every MMA is done): it holds the staging tiles
+        uint8_t *stage = smem + warp * kStageBytes;
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-            float v[32];
-            __syncwarp();
-            tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + c * 32, v);
-            if (row < M) {
-                const int col = n0 + c * 32;
-                if (EPI == PK_GEMM_SILU) {
+        for (int c = 0; c < BN / 64; ++c) {
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) v[i] = __fdividef(v[i], 1.f + __expf(-v[i]));
-                } else if (EPI == PK_GEMM_RESIDUAL || EPI == PK_GEMM_RESIDUAL_RELU) {
-                    const uint4 *rp = reinterpret_cast<const uint4 *>(R + (int64_t)row * ldr + col);
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        float f[8];
-                        unpack16(rp[q], f, R);
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            const float t = f[i] + alpha * v[q * 8 + i];
-                            v[q * 8 + i] = EPI == PK_GEMM_RESIDUAL_RELU ? fmaxf(t, 0.f) : t;
-                        }
-                    }
-                } else if (EPI == PK_GEMM_BIAS) {
-                    const uint4 *bp = reinterpret_cast<const uint4 *>(bias + col);
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        float f[8];
-                        unpack16(bp[q], f, bias);
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) v[q * 8 + i] += f[i];
-                    }
-                }
-                uint4 *cp = reinterpret_cast<uint4 *>(C + (int64_t)row * ldc + col);
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    uint4 o;
-                    __nv_bfloat162 *h = reinterpret_cast<__nv_bfloat162 *>(&o);
-#pragma unroll
-                    for (int i = 0; i < 4; ++i)
-                        h[i] = __floats2bfloat162_rn(v[q * 8 + 2 * i], v[q * 8 + 2 * i + 1]);
-                    cp[q] = o;
-                }
-            }
+            for (int i = 0; i < 8; ++i) rv[i] = rn[i];
+            if (is_residual(EPI) && c + 1 < BN / 64)
+                load_residual64(rn, m0 + warp * 32, M, n0 + (c + 1) * 64, R, ldr);
+            epilogue_tile64<EPI>(tmem + ((uint32_t)(warp * 32) << 16) + c * 64, m0 + warp * 32, M,
+                                 n0 + c * 64, C, ldc, rv, bias, alpha, stage);
         }
     }
     tc_fence_before();
@@ -258,48 +323,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 0) {
         tc_fence_after();
         tmem_dealloc(tmem, BN);
-    }
-}
-
-// apply the epilogue to 32 accumulator columns of one row and store them as bf16
-template <int EPI>
-__device__ __forceinline__ void epilogue_store(float (&v)[32], int row, int col, __nv_bfloat16 *C,
-                                               int64_t ldc, const __nv_bfloat16 *R, int64_t ldr,
-                                               const __nv_bfloat16 *bias, float alpha) {
-    if (EPI == PK_GEMM_SILU) {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = __fdividef(v[i], 1.f + __expf(-v[i]));
-    } else if (EPI == PK_GEMM_RESIDUAL || EPI == PK_GEMM_RESIDUAL_RELU) {
-        const uint4 *rp = reinterpret_cast<const uint4 *>(R + (int64_t)row * ldr + col);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            float f[8];
-            unpack16(rp[q], f, R);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const float t = f[i] + alpha * v[q * 8 + i];
-                v[q * 8 + i] = EPI == PK_GEMM_RESIDUAL_RELU ? fmaxf(t, 0.f) : t;
-            }
-        }
-    } else if (EPI == PK_GEMM_BIAS) {
-        const uint4 *bp = reinterpret_cast<const uint4 *>(bias + col);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            float f[8];
-            unpack16(bp[q], f, bias);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) v[q * 8 + i] += f[i];
-        }
-    }
-    uint4 *cp = reinterpret_cast<uint4 *>(C + (int64_t)row * ldc + col);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-        uint4 o;
-        __nv_bfloat162 *h = reinterpret_cast<__nv_bfloat162 *>(&o);
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-            h[i] = __floats2bfloat162_rn(v[q * 8 + 2 * i], v[q * 8 + 2 * i + 1]);
-        cp[q] = o;
     }
 }
 
@@ -330,6 +353,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
     __shared__ volatile int failed;
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    uint8_t *stage = sB + NS * kBBytes + (warp & 3) * kStageBytes;   // epilogue warps
     const int mtiles = (M + kBM - 1) / kBM, tiles = mtiles * (N / BN), nk = K / kBK;
     if (threadIdx.x == 0) {
         for (int s = 0; s < NS; ++s) {
@@ -411,8 +435,12 @@ __global__ void __launch_bounds__(kPThreads, 1)
         grid_dep_wait();   // the residual rows may come from the previous kernel
         const int q = warp & 3;
         int t = 0;
+        uint4 rv[8], rn[8];
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
             const int acc = t & 1, use = t >> 1;
+            const int m0 = (tile % mtiles) * kBM, n0 = (tile / mtiles) * BN;
+            // the tile's first residual columns are requested while its MMAs run
+            if (is_residual(EPI)) load_residual64(rn, m0 + q * 32, M, n0, R, ldr);
             const bool ok = __all_sync(0xffffffffu,
                                        mbar_wait_bounded(&tmem_full[acc], use & 1, kWaitLimitNs));
             if (!ok) {
@@ -422,14 +450,14 @@ __global__ void __launch_bounds__(kPThreads, 1)
             }
             tc_fence_after();
             if (tile + (int)gridDim.x >= tiles) grid_dep_launch();
-            const int m0 = (tile % mtiles) * kBM, n0 = (tile / mtiles) * BN;
-            const int row = m0 + q * 32 + lane;
 #pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
-                float v[32];
-                __syncwarp();
-                tmem_ld32(tmem + acc * BN + ((uint32_t)(q * 32) << 16) + c * 32, v);
-                if (row < M) epilogue_store<EPI>(v, row, n0 + c * 32, C, ldc, R, ldr, bias, alpha);
+            for (int c = 0; c < BN / 64; ++c) {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) rv[i] = rn[i];
+                if (is_residual(EPI) && c + 1 < BN / 64)
+                    load_residual64(rn, m0 + q * 32, M, n0 + (c + 1) * 64, R, ldr);
+                epilogue_tile64<EPI>(tmem + acc * BN + ((uint32_t)(q * 32) << 16) + c * 64,
+                                     m0 + q * 32, M, n0 + c * 64, C, ldc, rv, bias, alpha, stage);
             }
             tc_fence_before();
             __syncwarp();
@@ -558,6 +586,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
     __shared__ volatile int failed;
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    uint8_t *stage = sB + NS * kBBytes + (warp & 3) * kStageBytes;   // epilogue warps
     const uint32_t rank = cluster_ctarank();
     const bool leader = rank == 0;
     const int pair = blockIdx.x / 2, npairs = gridDim.x / 2;
@@ -655,8 +684,12 @@ __global__ void __launch_bounds__(kPThreads, 1)
         const uint32_t empty0 = mapa_rank(smem_u32(&tmem_empty[0]), 0),
                        empty1 = mapa_rank(smem_u32(&tmem_empty[1]), 0);
         int t = 0;
+        uint4 rv[8], rn[8];
         for (int tile = pair; tile < tiles; tile += npairs, ++t) {
             const int acc = t & 1, use = t >> 1;
+            const int m0 = (tile % mtiles) * 2 * kBM + (int)rank * kBM, n0 = (tile / mtiles) * BN;
+            // the tile's first residual columns are requested while its MMAs run
+            if (is_residual(EPI)) load_residual64(rn, m0 + q * 32, M, n0, R, ldr);
             const bool ok = __all_sync(0xffffffffu,
                                        mbar_wait_bounded(&tmem_full[acc], use & 1, kWaitLimitNs));
             if (!ok) {
@@ -666,14 +699,14 @@ __global__ void __launch_bounds__(kPThreads, 1)
             }
             tc_fence_after();
             if (tile + npairs >= tiles) grid_dep_launch();
-            const int m0 = (tile % mtiles) * 2 * kBM + (int)rank * kBM, n0 = (tile / mtiles) * BN;
-            const int row = m0 + q * 32 + lane;
 #pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
-                float v[32];
-                __syncwarp();
-                tmem_ld32(tmem + acc * BN + ((uint32_t)(q * 32) << 16) + c * 32, v);
-                if (row < M) epilogue_store<EPI>(v, row, n0 + c * 32, C, ldc, R, ldr, bias, alpha);
+            for (int c = 0; c < BN / 64; ++c) {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) rv[i] = rn[i];
+                if (is_residual(EPI) && c + 1 < BN / 64)
+                    load_residual64(rn, m0 + q * 32, M, n0 + (c + 1) * 64, R, ldr);
+                epilogue_tile64<EPI>(tmem + acc * BN + ((uint32_t)(q * 32) << 16) + c * 64,
+                                     m0 + q * 32, M, n0 + c * 64, C, ldc, rv, bias, alpha, stage);
             }
             tc_fence_before();
             __syncwarp();
@@ -695,7 +728,7 @@ template <int BN, int NS, int EPI>
 int launch_gemm_pair_t(const GemmArgs &g, const CUtensorMap &ta, const CUtensorMap &tw,
                        int num_sms, cudaStream_t s) {
     auto k = gemm_bf16_pair_kernel<BN, NS, EPI>;
-    const size_t smem = (size_t)NS * (kABytes + (BN / 2) * kBK * 2) + 1024;
+    const size_t smem = (size_t)NS * (kABytes + (BN / 2) * kBK * 2) + 4 * kStageBytes + 1024;
     static bool attr = false;
     if (!attr) {
         cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -743,7 +776,7 @@ template <int BN, int NS, int EPI>
 int launch_gemm_persistent_t(const GemmArgs &g, const CUtensorMap &ta, const CUtensorMap &tw,
                              int num_sms, cudaStream_t s) {
     auto k = gemm_bf16_persistent_kernel<BN, NS, EPI>;
-    const size_t smem = (size_t)NS * (kABytes + BN * kBK * 2) + 1024;
+    const size_t smem = (size_t)NS * (kABytes + BN * kBK * 2) + 4 * kStageBytes + 1024;
     static bool attr = false;
     if (!attr) {
         cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
