@@ -770,8 +770,9 @@ GEMM_SHAPES = {   # (name, M, N, K, epilogue): the GEMMs of one encoder layer at
 def gemm_step(model, steps, dev):
     """The encoder's projection GEMMs at the streaming batch (160 small / 480
     large streams): pk_gemm_bf16 (tcgen05, epilogue fused) against cuBLAS
-    (torch.matmul, epilogue as separate elementwise launches), each replayed
-    as a CUDA graph of `steps` launches after an L2 flush."""
+    (torch.matmul, epilogue as separate elementwise launches) and, for the
+    residual epilogues, cuBLAS with the residual in its own epilogue (addmm),
+    each replayed as a CUDA graph of `steps` launches after an L2 flush."""
     import torch
 
     from parakeet_b200.ops import gemm
@@ -802,8 +803,17 @@ def gemm_step(model, steps, dev):
                 return torch.relu(r + y)
             return y
 
+        def cublas_addmm():   # the residual or bias inside cuBLAS's own epilogue
+            if epi == "bias":
+                return torch.addmm(bias, a, w.t())
+            y = torch.addmm(r, a, w.t(), beta=1, alpha=alpha)
+            return y.relu_() if epi == "residual_relu" else y
+
         row = {"name": name, "M": M, "N": N, "K": K}
-        for label, fn in (("tcgen05", ours), ("cublas", cublas)):
+        arms = [("tcgen05", ours), ("cublas", cublas)]
+        if epi.startswith("residual"):
+            arms.append(("cublas_addmm", cublas_addmm))
+        for label, fn in arms:
             for _ in range(3):
                 fn()
             s = torch.cuda.Stream()
