@@ -85,8 +85,8 @@ class BatchedGreedyDecoder:
         x = None
         for k in range(self.layers):
             if k == 0:   # the token's half comes from the table, in the cell kernel
-                gates = (gemm(h[0], self.w_hh[0]) if self.fast
-                         else torch.mm(h[0], self.w_hh[0].t()))
+                # (cuBLAS: at 2048 rows 8.9 us against the tcgen05 kernel's 12.8)
+                gates = torch.mm(h[0], self.w_hh[0].t())
                 xtab, xld = self.xtab, 4 * H
             else:
                 gates = torch.addmm(self.b[k], x, self.w_ih[k].t())
