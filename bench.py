@@ -388,8 +388,8 @@ def run_reference_arm(args):
 
 def ops_at_scale(model, dev, timeit, hbm, streams=2048, layers=2, only=None):
     """One layer's append, gather, attention (+ append) and conv-cache step over
-    the 2048 streams of a full serving batch (the largest step the allocator
-    takes), where a launch moves tens to hundreds of MB; the configs[1]
+    the 2048 streams of a full serving batch (the serving loop's largest
+    step), where a launch moves tens to hundreds of MB; the configs[1]
     breakdown beside it (80 streams) shows the launch- and latency-bound end.
     Full windows (36 steps of prefill), pages a random permutation, bf16."""
     import torch
