@@ -1193,12 +1193,72 @@ class ServePositions:
         self.joined = 0
 
 
+STEP_BUCKETS = (2048, 1024, 512, 256, 128)   # batch sizes of the captured serving steps
+
+
+class StepGraphs:
+    """A CUDA graph of one ``step_audio`` per push class (first, second,
+    later chunk) and batch size in ``STEP_BUCKETS``: slots and samples are
+    data in each graph's input buffers, so one graph serves any streams of its
+    class.  A batch is cut into bucket-sized pieces, largest first; the last
+    piece is padded to the smallest bucket with rows of ``dummy`` slots (pool
+    slots no served stream uses, started once as streams of their own), so
+    every step runs as a graph replay instead of about 300 eager launches
+    (about 7.5 ms of host time each)."""
+
+    def __init__(self, pipe, cap, spare, banks, dev):
+        import torch
+        self.dummy = torch.arange(cap, cap + spare, dtype=torch.int32, device=dev)
+        self.g = {}
+        pool = torch.cuda.graph_pool_handle()
+        for c in (0, 1, 2):
+            for Bg in STEP_BUCKETS:
+                if Bg > cap:
+                    continue
+                sl = torch.arange(Bg, dtype=torch.int32)
+                gs = sl.to(dev)
+                gx = torch.empty(Bg, banks[c].shape[1], dtype=torch.float32, device=dev)
+                gx.copy_(banks[c][torch.arange(Bg) % banks[c].shape[0]])
+                x0 = banks[0][torch.arange(Bg) % banks[0].shape[0]].to(dev)
+                pipe.start_streams(sl)
+                # one eager first step: it also applies the releases queued so far,
+                # so that the captured step carries none
+                pipe.step_audio(x0, gs, 0)
+                torch.cuda.synchronize(dev)
+                gph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gph, pool=pool):
+                    tok, cnt = pipe.step_audio(gx, gs, c)
+                pipe.end_streams(sl)
+                self.g[(c, Bg)] = (gph, gx, gs, tok, cnt)
+        pipe.start_streams(self.dummy.cpu())
+        self.sizes = sorted({Bg for _, Bg in self.g}, reverse=True)
+
+    def pieces(self, B):
+        """(rows, bucket) of the graph replays that serve a batch of B rows."""
+        out, done = [], 0
+        while done < B:
+            left = B - done
+            Bg = next((g for g in self.sizes if g <= left), self.sizes[-1])
+            r = min(Bg, left)
+            out.append((r, Bg))
+            done += r
+        return out
+
+
+def _flush_releases(pipe):
+    """Return the pages of streams ended since the last step: a captured step
+    carries no releases, so they go in a step start of no rows."""
+    import torch
+    if pipe.pool.pending_release:
+        pipe.pool.begin_step(torch.empty(0, dtype=torch.int32, device=pipe.device))
+
+
 def _serve_batch(pipe, c, part, k, banks, hbufs, dbufs, hslots, dslots, htok, hcnt, off,
-                 full_graph, max_batch):
+                 graphs):
     """Copies the samples and slots of rows ``part`` (push class c: first,
-    second, later) in from pinned host memory, runs their step (a later-chunk
-    batch of exactly ``max_batch`` rows as the captured graph), and queues the
-    tokens' copy back to pinned host memory."""
+    second, later) in from pinned host memory, runs their step (replays of
+    ``graphs``, a StepGraphs, when given; else eagerly), and queues the tokens'
+    copy back to pinned host memory."""
     import torch
     B = part.size
     rs = slice(off, off + B)
@@ -1206,22 +1266,31 @@ def _serve_batch(pipe, c, part, k, banks, hbufs, dbufs, hslots, dslots, htok, hc
     torch.index_select(bank, 0, torch.from_numpy((part + k[part]) % bank.shape[0]),
                        out=hbufs[c][rs])
     hslots[c][rs].numpy()[:] = part
-    if full_graph is not None and c == 2 and B == max_batch:
-        gph, dx, ds, tok, cnt = full_graph
-        dx.copy_(hbufs[c][rs], non_blocking=True)
-        ds.copy_(hslots[c][rs], non_blocking=True)
-        gph.replay()
-    else:
+    if graphs is None:
         dx = dbufs[c][rs]
         dx.copy_(hbufs[c][rs], non_blocking=True)
         ds = dslots[c][rs]
         ds.copy_(hslots[c][rs], non_blocking=True)
         tok, cnt = pipe.step_audio(dx, ds, c)
-    htok[c][rs].copy_(tok.view(B, -1), non_blocking=True)
-    hcnt[c][rs].copy_(cnt, non_blocking=True)
+        htok[c][rs].copy_(tok.view(B, -1), non_blocking=True)
+        hcnt[c][rs].copy_(cnt, non_blocking=True)
+        return
+    _flush_releases(pipe)
+    done = 0
+    for r, Bg in graphs.pieces(B):
+        gph, gx, gs, tok, cnt = graphs.g[(c, Bg)]
+        sub = slice(off + done, off + done + r)
+        gx[:r].copy_(hbufs[c][sub], non_blocking=True)
+        gs[:r].copy_(hslots[c][sub], non_blocking=True)
+        if r < Bg:
+            gs[r:].copy_(graphs.dummy[:Bg - r])
+        gph.replay()
+        htok[c][sub].copy_(tok[:r].view(r, -1), non_blocking=True)
+        hcnt[c][sub].copy_(cnt[:r], non_blocking=True)
+        done += r
 
 
-def serve_prefill(pipe, pos, bufs, full_graph, max_batch=2048):
+def serve_prefill(pipe, pos, bufs, graphs, max_batch=2048):
     """Steps every position through min(age, fill) chunks as fast as the GPU
     runs them (no pacing), so that each stream's pages, conv cache, feature
     history and prediction state are those of a stream of that age."""
@@ -1235,21 +1304,20 @@ def serve_prefill(pipe, pos, bufs, full_graph, max_batch=2048):
         cls = min(c, 2)
         for off in range(0, sel.size, max_batch):
             part = sel[off:off + max_batch]
-            _serve_batch(pipe, cls, part, k, *bufs, 0, full_graph, max_batch)
+            _serve_batch(pipe, cls, part, k, *bufs, 0, graphs)
         k[sel] += 1
     torch.cuda.synchronize(pipe.device)
 
 
 def serve_trial(pipe, N, pos, bufs, warm_periods, meas_periods, max_batch=2048,
-                full_graph=None):
+                graphs=None):
     """Positions 0..N-1 paced in real time: position i's next chunk completes
     at t0 + phase_i + m * period (m = chunks it has pushed in this trial).
     The loop takes every chunk that has completed (one per position per
     iteration), groups them by push class of their stream (first, second,
     later; batches of at most 2048 rows), copies their samples and slots in
-    from pinned host memory, runs ``step_audio`` (a later-chunk batch of exactly
-    ``max_batch`` rows as the replay of ``full_graph`` = (graph, samples, slots,
-    tokens, counts) when given, every other batch eagerly) and copies the
+    from pinned host memory, runs ``step_audio`` (as replays of the captured
+    steps of ``graphs``, a StepGraphs, when given; else eagerly) and copies the
     tokens back to pinned host memory; a chunk's latency is the wall time from
     its completion to its tokens being on the host (the reference's
     push_samples -> DecodeResult, model_runner.py:150-171).  Streams that
@@ -1285,7 +1353,7 @@ def serve_trial(pipe, N, pos, bufs, warm_periods, meas_periods, max_batch=2048,
             # of the buffers (copies are still in flight)
             for off in range(0, sel.size, max_batch):
                 part = sel[off:off + max_batch]
-                _serve_batch(pipe, c, part, k, *bufs, off, full_graph, max_batch)
+                _serve_batch(pipe, c, part, k, *bufs, off, graphs)
                 rows += part.size
                 launches += 1
             if sel.size:
@@ -1394,7 +1462,9 @@ def serving_search(model, dev, measure_s=3.0, max_trials=9, limit_ms=160.0, use_
     free = torch.cuda.mem_get_info(dev)[0]
     cap = int(min(65536, 0.85 * free / per_slot)) // 256 * 256
     cap = int(reduce([cap], dist.ReduceOp.MIN if world > 1 else None)[0])
-    pipe = build_streaming_pipeline(model, dev, cap)
+    # the pool holds STEP_BUCKETS[-1] more slots: the rows that pad a step graph
+    spare = STEP_BUCKETS[-1] if use_graph else 0
+    pipe = build_streaming_pipeline(model, dev, cap + spare)
     S = pipe.dec.max_symbols
     audio = synth_audio_batch(64, n0 + 2 * n, seed=11)
     banks = [torch.from_numpy(np.ascontiguousarray(a))
@@ -1425,37 +1495,20 @@ def serving_search(model, dev, measure_s=3.0, max_trials=9, limit_ms=160.0, use_
                 pipe.step_audio(dbufs[cc][:B], dslots[cc][:B], cc)
             pipe.end_streams(sl)
         torch.cuda.synchronize(dev)
-        # A later-chunk step of a full 2048-stream batch as one CUDA graph: the
-        # eager step launches about 300 kernels, whose host cost (about 7.5 ms)
-        # exceeds their GPU time at this batch.  Slots and samples are data in
-        # the graph's input buffers, so one graph serves any 2048 streams.
-        full_graph = None
-        if use_graph and cap >= 2048:
-            Bg = 2048
-            sl = torch.arange(Bg, dtype=torch.int32)
-            gx = torch.empty(Bg, n, dtype=torch.float32, device=dev)
-            gs = sl.to(dev)
-            pipe.start_streams(sl)
-            # one eager first step: it also applies the releases queued above,
-            # so that the captured step carries none
-            pipe.step_audio(dbufs[0][:Bg], gs, 0)
-            gx.copy_(banks[2][torch.arange(Bg) % banks[2].shape[0]])
-            torch.cuda.synchronize(dev)
-            gph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(gph):
-                gtok, gcnt = pipe.step_audio(gx, gs, 2)
-            pipe.end_streams(sl)
-            full_graph = (gph, gx, gs, gtok, gcnt)
+        # Every step as a CUDA graph replay (StepGraphs): the eager step
+        # launches about 300 kernels, whose host cost (about 7.5 ms) exceeds
+        # their GPU time even at 2048 streams.
+        graphs = StepGraphs(pipe, cap, spare, banks, dev) if use_graph else None
         pos = ServePositions(cap, period, life, fill, seed=1000 + rank)
         t_pf = time.perf_counter()
-        serve_prefill(pipe, pos, bufs, full_graph)
+        serve_prefill(pipe, pos, bufs, graphs)
         prefill_s = time.perf_counter() - t_pf
-        serve_trial(pipe, min(64, cap), pos, bufs, 2, 1, full_graph=full_graph)
+        serve_trial(pipe, min(64, cap), pos, bufs, 2, 1, graphs=graphs)
 
         def run(total):
             return job_trial(total, world, rank, cap, dev, limit_ms,
                              lambda mine: serve_trial(pipe, mine, pos, bufs, warm, meas,
-                                                      full_graph=full_graph))
+                                                      graphs=graphs))
 
         fixed = None
         if fixed_total:
@@ -1492,7 +1545,7 @@ def serving_search(model, dev, measure_s=3.0, max_trials=9, limit_ms=160.0, use_
            "stream_life_s": lifetime_s, "prefill_chunks": fill,
            "prefill_s": round(prefill_s, 1), "search_s": round(time.perf_counter() - t_start, 1),
            "trials": trials, "device_error_word": err,
-           "full_batch_graph": full_graph is not None,
+           "step_graphs": sorted(graphs.sizes) if graphs is not None else None,
            "method": "streams paced in real time, full windows (prefilled), 30 s lifetimes "
                      "(streams leave and new ones join), batched steps over every completed "
                      "chunk, latency = chunk completion -> tokens in pinned host memory"

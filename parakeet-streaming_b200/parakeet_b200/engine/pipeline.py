@@ -110,13 +110,19 @@ class StreamingPipeline:
                                device=dev),
                     torch.empty(B, self.fe.n_mels, F, dtype=self.dtype, device=dev),
                     torch.empty(B, dtype=torch.int32, device=dev))
+        ns, flags, feats, nframes = bufs
         if capturing or key in self._fe_bufs_graph:
             # a graph captured now reads these addresses at every replay: they
-            # must outlive any eviction of the recent-sizes cache
+            # must outlive any eviction of the recent-sizes cache.  Graphs of
+            # different push indices share them (same batch, samples and
+            # first flag), so each graph, and each eager step on them, sets the
+            # two constants itself: the fill that made them may sit in another
+            # graph that has not been replayed yet.
             self._fe_bufs_graph[key] = bufs
+            ns.fill_(n)
+            flags.fill_(_lib.PK_FE_FIRST if first else 0)
         else:
             self._fe_bufs[key] = bufs
-        ns, flags, feats, nframes = bufs
         self.fe.launch(samples, ns, flags, slots, feats, F, nframes)
         return self.encode(feats, slots, first, prefix=prefix)
 

@@ -4,9 +4,10 @@ prefill steps every position through min(age, fill) chunks; in a trial every
 stream's chunks are stepped in order (first, second, later push), one chunk
 per position per loop iteration; a stream that reaches its last chunk is
 released and a new stream starts in its slot with a first chunk; batches never
-exceed the allocator's limit; a later-chunk batch of exactly the limit goes to
-the captured graph and every other batch eagerly; each measured chunk gets a
-latency from its completion time."""
+exceed the loop's limit; with step graphs every batch is cut into bucket-sized
+replays, the last padded with spare slots, and the released streams' pages are
+returned (a step start of no rows) before the next replay; each measured chunk
+gets a latency from its completion time."""
 import os
 import sys
 import time
@@ -35,23 +36,40 @@ class _Dec:
     max_symbols = S
 
 
+class FakePool:
+    def __init__(self):
+        self.pending_release = []
+        self.flushes = 0
+
+    def begin_step(self, slots, *a, **k):
+        assert slots.numel() == 0
+        self.pending_release = []
+        self.flushes += 1
+
+
 class FakePipe:
     device = torch.device("cpu")
     dec = _Dec()
 
-    def __init__(self):
+    def __init__(self, check_flushed=False):
         self.calls = []          # (push class, slots)
         self.pushes = {}         # slot -> one list of push classes per stream it held
         self.ended = []
+        self.pool = FakePool()
+        self.check_flushed = check_flushed
 
     def start_streams(self, slots):
         for s in torch.as_tensor(slots).tolist():
             self.pushes.setdefault(int(s), []).append([])
 
     def end_streams(self, slots):
-        self.ended += [int(s) for s in torch.as_tensor(slots).tolist()]
+        sl = [int(s) for s in torch.as_tensor(slots).tolist()]
+        self.ended += sl
+        self.pool.pending_release += sl
 
     def step_audio(self, x, slots, push):
+        if self.check_flushed:   # a replayed step carries no releases
+            assert not self.pool.pending_release
         sl = slots.tolist()
         self.calls.append((push, sl))
         for s in sl:
@@ -64,13 +82,29 @@ class FakePipe:
 class FakeGraph:
     """Replays 'step_audio' over its own input buffers, as a captured graph does."""
 
-    def __init__(self, pipe, xs, ss):
-        self.pipe, self.xs, self.ss = pipe, xs, ss
+    def __init__(self, pipe, xs, ss, push):
+        self.pipe, self.xs, self.ss, self.push = pipe, xs, ss, push
         self.replays = 0
 
     def replay(self):
         self.replays += 1
-        self.pipe.step_audio(self.xs, self.ss, 2)
+        self.pipe.step_audio(self.xs, self.ss, self.push)
+
+
+class FakeStepGraphs(bench.StepGraphs):
+    """bench.StepGraphs' batching over fake graphs of small buckets."""
+
+    def __init__(self, pipe, sizes, dummy, widths):
+        self.dummy = torch.tensor(dummy, dtype=torch.int32)
+        self.sizes = sorted(sizes, reverse=True)
+        self.g = {}
+        for c in range(3):
+            for Bg in sizes:
+                gx, gs = torch.zeros(Bg, widths[c]), torch.zeros(Bg, dtype=torch.int32)
+                self.g[(c, Bg)] = (FakeGraph(pipe, gx, gs, c), gx, gs,
+                                   torch.zeros(Bg, T, S, dtype=torch.int32),
+                                   torch.zeros(Bg, T, dtype=torch.int32))
+        pipe.start_streams(self.dummy)
 
 
 def _bufs(cap, widths):
@@ -93,18 +127,13 @@ def _stream_ok(seg):
 def test_serve_trial_steps_every_chunk_in_order(monkeypatch, use_graph):
     monkeypatch.setattr(torch.cuda, "Event", _Event)
     monkeypatch.setattr(torch.cuda, "synchronize", lambda *a: None)
-    N, period, warm, meas, max_batch, life, fill = 120, 0.04, 2, 5, 2, 5, 3
+    N, period, warm, meas, max_batch, life, fill = 120, 0.04, 2, 5, 5, 5, 3
     widths = (9, 16, 16)
     banks = [torch.randn(8, w) for w in widths]
     hb, db, hs, ds, ht, hc = _bufs(N, widths)
     bufs = (banks, hb, db, hs, ds, ht, hc)
-    pipe = FakePipe()
-    graph = None
-    if use_graph:
-        gx = torch.zeros(max_batch, widths[2])
-        gs = torch.zeros(max_batch, dtype=torch.int32)
-        graph = (FakeGraph(pipe, gx, gs), gx, gs, torch.zeros(max_batch, T, S, dtype=torch.int32),
-                 torch.zeros(max_batch, T, dtype=torch.int32))
+    pipe = FakePipe(check_flushed=use_graph)
+    graph = FakeStepGraphs(pipe, (4, 2), [N, N + 1], widths) if use_graph else None
     pos = bench.ServePositions(N, period, life, fill, seed=3)
     age0 = pos.age.copy()
     bench.serve_prefill(pipe, pos, bufs, graph, max_batch=max_batch)
@@ -112,9 +141,10 @@ def test_serve_trial_steps_every_chunk_in_order(monkeypatch, use_graph):
         assert len(pipe.pushes[s]) == 1
         assert pipe.pushes[s][0] == [min(j, 2) for j in range(min(age0[s], fill))]
     pipe.calls.clear()
+    replays0 = sum(g[0].replays for g in graph.g.values()) if use_graph else 0
     t0 = time.perf_counter()
     lat, st = bench.serve_trial(pipe, N, pos, bufs, warm, meas, max_batch=max_batch,
-                                full_graph=graph)
+                                graphs=graph)
     elapsed = time.perf_counter() - t0
     assert elapsed < (warm + meas) * period + 2.0
     stepped = 0
@@ -139,10 +169,19 @@ def test_serve_trial_steps_every_chunk_in_order(monkeypatch, use_graph):
     assert 0 < lat.size <= N * (meas + 1)
     assert (lat >= 0).all()
     assert st["backlog_chunks_at_end"] >= 0
-    assert st["steps"] == len(pipe.calls)
-    full = [sl for c, sl in pipe.calls if c == 2 and len(sl) == max_batch]
-    assert full, "the trial should have made full later-chunk batches"
-    if use_graph:   # exactly those went through the graph (its input buffers)
-        assert graph[0].replays >= len(full)
+    if use_graph:
+        # every step a replay of a bucket-sized graph: pieces of 4, then 2, the
+        # last padded with the spare slots N, N + 1
+        assert all(len(sl) in (4, 2) for _, sl in pipe.calls)
+        assert st["steps"] <= len(pipe.calls)
+        assert sum(g[0].replays for g in graph.g.values()) - replays0 == len(pipe.calls)
+        padded = [sl for _, sl in pipe.calls if N in sl or N + 1 in sl]
+        assert padded, "odd batches should have been padded"
+        for sl in padded:
+            real = [x for x in sl if x < N]
+            assert sl[len(real):] == [N, N + 1][:len(sl) - len(real)]
+        assert pipe.pool.flushes > 0   # (streams ended in the last iteration wait for a next step)
     else:
-        assert all(c != 2 or len(sl) <= max_batch for c, sl in pipe.calls)
+        assert st["steps"] == len(pipe.calls)
+        full = [sl for c, sl in pipe.calls if c == 2 and len(sl) == max_batch]
+        assert full, "the trial should have made full later-chunk batches"
