@@ -243,3 +243,35 @@ def test_captured_step_survives_other_batch_sizes():
     torch.cuda.synchronize()
     assert torch.equal(tok, want[0]) and torch.equal(cnt, want[1])
     assert pipe.fe.error_bits() == 0 and pipe.pool.read_error() == 0
+
+
+def test_graphs_of_two_push_indices_share_buffers_in_any_replay_order():
+    """Steps of push 1 and of push 2 captured at one batch size share the
+    feature buffers (same samples, not first); replaying the push-2 graph
+    before the push-1 graph ever ran still counts the right samples."""
+    pipe, ref_pipe = make(3), make(3)
+    sl = [0, 1, 2]
+    slots = torch.tensor(sl, dtype=torch.int32, device="cuda")
+    pipe.start_streams(sl)
+    ref_pipe.start_streams(sl)
+    with torch.inference_mode():
+        x0 = torch.cat([audio(0, i) for i in sl]).cuda()
+        x1 = torch.cat([audio(1, i) for i in sl]).cuda()
+        x2 = torch.cat([audio(2, i) for i in sl]).cuda()
+        pipe.step_audio(x0, slots, 0)
+        for p, x in enumerate((x0, x1)):
+            ref_pipe.step_audio(x, slots, p)
+        want = ref_pipe.step_audio(x2, slots, 2)
+        gx1, gx2 = x1.clone(), x2.clone()
+        g1, g2 = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g1):
+            pipe.step_audio(gx1, slots, 1)
+        with torch.cuda.graph(g2):
+            tok, cnt = pipe.step_audio(gx2, slots, 2)
+        # push 1 eagerly at other batch sizes (g1 never replays)
+        pipe.step_audio(x1[:2], slots[:2], 1)
+        pipe.step_audio(x1[2:], slots[2:], 1)
+    g2.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(tok, want[0]) and torch.equal(cnt, want[1])
+    assert pipe.fe.error_bits() == 0 and pipe.pool.read_error() == 0
