@@ -1561,17 +1561,33 @@ def serve_lines(args, dev, world):
     engine on the same GPU (``reference_engine_search``).  N GPUs: configs[3],
     480 large streams placed across the N engines, then the search for the
     most the job serves."""
+    import torch
+
+    def guarded(fn, model, **kw):
+        # one GPU: a search that fails (out of memory, say) is reported in its
+        # entry instead of costing the bench line
+        try:
+            return fn(model, dev, **kw)
+        except Exception as e:   # noqa: BLE001
+            try:
+                torch.cuda.synchronize(dev)
+                torch.cuda.empty_cache()
+            except Exception:   # noqa: BLE001  (a device error: the line reports it)
+                pass
+            return {"model": model, "error": f"{type(e).__name__}: {e}"[:400]}
+
     if world == 1:
         out = {}
         for model in ("small", "large"):
-            ours = serving_search(model, dev, measure_s=3.0 if model == "small" else 4.0,
-                                  max_trials=9 if model == "small" else 7,
-                                  fixed_total=480 if model == "large" else 160)
+            ours = guarded(serving_search, model, measure_s=3.0 if model == "small" else 4.0,
+                           max_trials=9 if model == "small" else 7,
+                           fixed_total=480 if model == "large" else 160)
             ref = None
             if not args.no_reference_engine:
-                ref = reference_engine_search(model, dev, max_trials=8 if model == "small" else 6,
-                                              measure_s=3.0 if model == "small" else 4.0)
-            if ref and ref.get("streams_max"):
+                ref = guarded(reference_engine_search, model,
+                              max_trials=8 if model == "small" else 6,
+                              measure_s=3.0 if model == "small" else 4.0)
+            if ref and ref.get("streams_max") and ours.get("streams_max"):
                 ours["vs_reference_engine"] = round(ours["streams_max"] / ref["streams_max"], 1)
             ours["reference_engine"] = ref
             out[model] = ours
