@@ -45,6 +45,10 @@ SHAPES = {
     "large": dict(layers=24, dim=1024, heads=8, att=(70, 13)),
 }
 PAGE = 16
+# K/V page size of the serving engines: the small model's stacked attention
+# kernel also takes pages of 8 frames (a 72-frame window then reserves 80 rows
+# per stream instead of 96); the large model's kernel takes 16
+SERVE_PAGE = {"small": 8, "large": 16}
 
 
 def alg_bytes(shape, es=2):
@@ -86,6 +90,8 @@ def parse():
     ap.add_argument("--install-reference", metavar="CHECKOUT", default=None,
                     help="install the reference from a source checkout into baseline/_ref and exit")
     ap.add_argument("--wheelhouse", default=None, help="offline wheel directory for pip")
+    ap.add_argument("--serve-page-small", type=int, choices=[8, 16], default=None,
+                    help="K/V page size of the small model's serving engine (default 8)")
     ap.add_argument("--profile-op", default=None,
                     choices=["append", "attention", "attention+append", "gather",
                              "gather_all_layers", "conv", "features", "streaming", "gemm",
@@ -916,9 +922,10 @@ def stage_times(pipe, samples, slots, reps):
     return res
 
 
-def build_streaming_pipeline(model, dev, num_slots, feature_kw=None):
+def build_streaming_pipeline(model, dev, num_slots, feature_kw=None, page_size=PAGE):
     """StreamingPipeline of configs[2] (small) / configs[3] (large) with random
-    bf16 weights over ``num_slots`` stream slots."""
+    bf16 weights over ``num_slots`` stream slots, K/V pages of ``page_size``
+    frames."""
     import torch
 
     from parakeet_b200.engine import StreamingPipeline
@@ -943,7 +950,8 @@ def build_streaming_pipeline(model, dev, num_slots, feature_kw=None):
     join.load_state_dict({k[7:]: torch.from_numpy(v) for k, v in sd.items()
                           if k.startswith("joiner.")})
     mods = [m.to(dev, torch.bfloat16).eval() for m in (enc, pre, pred, join)]
-    return StreamingPipeline(*mods, blank_id=V, num_slots=num_slots, feature_kw=feature_kw)
+    return StreamingPipeline(*mods, blank_id=V, num_slots=num_slots, feature_kw=feature_kw,
+                             page_size=page_size)
 
 
 def streaming_step(model, steps, dev, profile=False, streams=None):
@@ -1423,7 +1431,7 @@ def job_trial(total, world, rank, cap, dev, limit_ms, local_trial):
 
 
 def serving_search(model, dev, measure_s=3.0, max_trials=9, limit_ms=160.0, use_graph=True,
-                   lifetime_s=30.0, start_per_gpu=1024, fixed_total=None):
+                   lifetime_s=30.0, start_per_gpu=1024, fixed_total=None, page_size=None):
     """Metric 1 of the survey: the most concurrent streams per GPU served with
     p99 chunk latency <= 160 ms, streams paced in real time (configs[2] /
     configs[3] audio, random bf16 weights), each stream living ``lifetime_s``
@@ -1456,7 +1464,8 @@ def serving_search(model, dev, measure_s=3.0, max_trials=9, limit_ms=160.0, use_
     n0, n = (1 + 8 * la) * 160, (8 + 8 * la) * 160
     life = int(round(lifetime_s / period))
     fill = -(-att[0] // T) + 1
-    per_slot = (pages_per_stream(att[0], T, PAGE) * L * 2 * PAGE * D * 2 + L * D * 8 * 2
+    ps = page_size or SERVE_PAGE[model]
+    per_slot = (pages_per_stream(att[0], T, ps) * L * 2 * ps * D * 2 + L * D * 8 * 2
                 + 128 * 9 * 2 + 4096)
     torch.cuda.empty_cache()
     free = torch.cuda.mem_get_info(dev)[0]
@@ -1464,7 +1473,7 @@ def serving_search(model, dev, measure_s=3.0, max_trials=9, limit_ms=160.0, use_
     cap = int(reduce([cap], dist.ReduceOp.MIN if world > 1 else None)[0])
     # the pool holds STEP_BUCKETS[-1] more slots: the rows that pad a step graph
     spare = STEP_BUCKETS[-1] if use_graph else 0
-    pipe = build_streaming_pipeline(model, dev, cap + spare)
+    pipe = build_streaming_pipeline(model, dev, cap + spare, page_size=ps)
     S = pipe.dec.max_symbols
     audio = synth_audio_batch(64, n0 + 2 * n, seed=11)
     banks = [torch.from_numpy(np.ascontiguousarray(a))
@@ -1540,6 +1549,7 @@ def serving_search(model, dev, measure_s=3.0, max_trials=9, limit_ms=160.0, use_
     out = {"model": model, "limit_ms": limit_ms, "n_gpus": world,
            "streams_max": ok_n, "streams_per_gpu": round(ok_n / world, 1),
            "capped_by_memory": bad_n is None and ok_n == cap * world, "slot_cap_per_gpu": cap,
+           "page_size": ps,
            "p99_ms_at_max": best["p99_ms"] if best else None,
            "audio_ms_per_chunk": period * 1e3, "measured_s_per_trial": round(meas * period, 2),
            "stream_life_s": lifetime_s, "prefill_chunks": fill,
@@ -1576,6 +1586,8 @@ def serve_lines(args, dev, world):
                 pass
             return {"model": model, "error": f"{type(e).__name__}: {e}"[:400]}
 
+    if args.serve_page_small:
+        SERVE_PAGE["small"] = args.serve_page_small
     if world == 1:
         out = {}
         for model in ("small", "large"):

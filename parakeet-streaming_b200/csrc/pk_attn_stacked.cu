@@ -38,8 +38,13 @@ namespace {
 
 constexpr int kH = 4;                    // heads per CTA = consumer warps
 constexpr int kThreads = (kH + 1) * 32;  // + producer warp
-constexpr int kBox = 2048;               // one head's 16 rows x 128 bytes
-constexpr int kMaxBoxes = 8;             // pages per window handled
+// Pages of PS = 16 or 8 rows: a head's page box is PS rows x 128 bytes (one or
+// two 1 KB 128B-swizzle atoms); a window spans at most 8 boxes of 16 rows or
+// 16 of 8.  The softmax and P V walk "virtual boxes" of 16 window columns: one
+// 16-row box, or two consecutive 8-row boxes.
+template <int PS> constexpr int box_bytes() { return PS * 128; }
+template <int PS> constexpr int max_boxes() { return PS == 16 ? 8 : 16; }
+constexpr int kMaxBoxes = 16;            // descriptor entries read (either page size)
 constexpr int kMaxPosBlocks = 8;         // rel-pos blocks of 16 rows (R <= 128)
 constexpr int kPStride = 48;             // bytes per row of a 16x16 bf16 probability tile
 // Four CTAs of 4 heads per SM, each with a 4-stage ring of 8 KB blocks (52 KB of
@@ -48,6 +53,8 @@ constexpr int kPStride = 48;             // bytes per row of a 16x16 bf16 probab
 // CTAs: half-size CTAs shorten the last, partly filled wave.
 constexpr int kStages = 4;
 constexpr int kCtasPerSm = 4;
+// stages of 8-row boxes: half the bytes each, so twice as many (same ring bytes)
+template <int PS> constexpr int stages_of() { return PS == 16 ? kStages : 2 * kStages; }
 
 struct SGeom {
     int num_layers, left, chunk, W, R, npb, max_boxes;
@@ -73,7 +80,7 @@ __device__ __forceinline__ void consumer_sync() {
     asm volatile("bar.sync 1, %0;" ::"n"(kH * 32) : "memory");
 }
 
-template <int NS, bool kRows16, int MB>
+template <int NS, bool kRows16, int MB, int PS>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     paged_attn_stacked_kernel(const __grid_constant__ CUtensorMap kv_map, const SGeom g,
                               const pk_paged_kv_desc d, const AttnArgs a) {
@@ -95,9 +102,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     const int layer = a.layer0 + lrel;
     const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
     const int chunk = g.chunk, npb = g.npb;
-    float *sS = reinterpret_cast<float *>(smem + g.off_s);    // [box][16 rows][16]
+    constexpr int kBox = box_bytes<PS>(), kMB = max_boxes<PS>();
+    float *sS = reinterpret_cast<float *>(smem + g.off_s);    // [box][16 rows][PS]
     float *sBD = reinterpret_cast<float *>(smem + g.off_bd);  // [16 rows][bd_stride]
-    char *sP = smem + g.off_p;                                // [box][16 rows][kPStride B]
+    char *sP = smem + g.off_p;                                // [virtual box][16 rows][kPStride B]
 
     if (warp == kH && lane == 0) {
         for (int s = 0; s < NS; ++s) {
@@ -111,7 +119,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     if (warp == kH) {
         // window descriptor of this stream (written by pk_pages_begin_step)
         const int32_t *wd = d.window + (int64_t)b * PK_WIN_STRIDE;
-        if (lane < kMaxBoxes) {
+        if (lane < kMB) {
             s_page[lane] = wd[PK_WIN_PAGE + lane];
             s_start[lane] = wd[PK_WIN_START + lane];
         }
@@ -119,25 +127,26 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         s_mask[32 + lane] = (uint32_t)wd[PK_WIN_MASK + 32 + lane];
         if (lane == 0) {
             const int nb = wd[PK_WIN_NB];
-            s_ok = wd[PK_WIN_OK] && nb <= g.max_boxes && nb <= MB;
+            s_ok = wd[PK_WIN_OK] && nb <= g.max_boxes && (PS == 16 ? nb : (nb + 1) / 2) <= MB;
             s_w = wd[PK_WIN_W];
             s_nfirst = wd[PK_WIN_NFIRST];
             s_nb = nb;
         }
-        if (lane < kMaxBoxes) {
+        if (lane < kMB) {
             // row r of box `lane` is window column jbase + r when it is a real frame:
-            // 0 <= start + r < 16 (inside the page), abs frame >= 0, 0 <= column < W
+            // 0 <= start + r < PS (inside the page), abs frame >= 0, 0 <= column < W
             const int st = wd[PK_WIN_START + lane];
-            const int abs0 = ((wd[PK_WIN_NFIRST] + lane) << 4) + st;
+            const int abs0 = (wd[PK_WIN_NFIRST] + lane) * PS + st;
             const int jb = abs0 - (wd[PK_WIN_W] - g.left);
             s_jbase[lane] = jb;
             s_lo[lane] = max(max(-st, -abs0), -jb);
-            s_hi[lane] = min(16 - st, g.W - jb);
+            s_hi[lane] = min(PS - st, g.W - jb);
         }
     }
     __syncthreads();
     const int nb = s_nb, w = s_w, nfirst = s_nfirst;
     const int nblocks = 2 * nb;   // K pages, then V pages
+    const int nvb = PS == 16 ? nb : (nb + 1) / 2;   // virtual boxes of 16 columns
     T *out_base = static_cast<T *>(a.out) + (int64_t)lrel * a.o_ls + (int64_t)b * a.o_bs + hg0 * 64;
     if (!s_ok) {
         for (int idx = tid; idx < chunk * kH * 64; idx += kThreads)
@@ -247,13 +256,13 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         if (app_lane) {
             const int t = lane / 8, c = lane % 8;
             const int av = w + t;
-            if ((av >> 4) - nfirst == i) {
-                const int pr = av & 15, r = pr - s_start[i];
+            if (av / PS - nfirst == i) {
+                const int pr = av & (PS - 1), r = pr - s_start[i];
                 *reinterpret_cast<uint4 *>(box + sw128(r, c * 16)) = val;
                 T *pool = static_cast<T *>(d.kv);
                 const int64_t plane =
                     ((int64_t)(s_page[i] * d.num_layers + layer) * 2 + kvi) * d.num_heads + hg0 + h;
-                *reinterpret_cast<uint4 *>(pool + (plane * 16 + pr) * 64 + c * 8) = val;
+                *reinterpret_cast<uint4 *>(pool + (plane * PS + pr) * 64 + c * 8) = val;
             }
         }
         __syncwarp();
@@ -275,7 +284,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         const int i = n;
         if (a.k_new) append_rows(knew, 0, i, box);
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
+        for (int nt = 0; nt < PS / 8; ++nt) {   // n-tiles of 8 keys in the box
             float c[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int kp = 0; kp < 4; kp += 2) {
@@ -285,7 +294,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
                 mma_bf16(c, fu[kp + 1], bb[2], bb[3]);
             }
             if (gq < chunk)
-                *reinterpret_cast<float2 *>(sS + (i * 16 + h * chunk + gq) * 16 + nt * 8 + 2 * tq) =
+                *reinterpret_cast<float2 *>(sS + (i * 16 + h * chunk + gq) * PS + nt * 8 + 2 * tq) =
                     make_float2(c[0], c[1]);
         }
         __syncwarp();
@@ -302,31 +311,34 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         const int row = tid / 16 + pass * 8, sub = tid % 16;
         const int rows = kH * chunk;
         const int iq = row % chunk;
+        // column sub of virtual box v: column cs of page box bi
+        const int cs = PS == 16 ? sub : (sub & 7);
         float sv[MB];
         float mx = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < MB; ++i) {
-            sv[i] = -INFINITY;
-            if (i < nb && row < rows) {
-                if (sub >= s_lo[i] && sub < s_hi[i]) {
-                    const int j = s_jbase[i] + sub;
-                    const float c = sS[(i * 16 + row) * 16 + sub] * scale;
+        for (int v = 0; v < MB; ++v) {
+            const int bi = PS == 16 ? v : 2 * v + (sub >> 3);
+            sv[v] = -INFINITY;
+            if (bi < nb && row < rows) {
+                if (cs >= s_lo[bi] && cs < s_hi[bi]) {
+                    const int j = s_jbase[bi] + cs;
+                    const float c = sS[(bi * 16 + row) * PS + cs] * scale;
                     const bool allowed = (s_mask[iq * 4 + (j >> 5)] >> (j & 31)) & 1u;
-                    sv[i] = allowed ? c + sBD[row * bds + chunk - 1 - iq + j] * scale
+                    sv[v] = allowed ? c + sBD[row * bds + chunk - 1 - iq + j] * scale
                                     : c - 1e5f;   // masked_fill(-1e5), attention.py:115
                 }
             }
-            mx = fmaxf(mx, sv[i]);
+            mx = fmaxf(mx, sv[v]);
         }
 #pragma unroll
         for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
         float sum = 0.f;
 #pragma unroll
-        for (int i = 0; i < MB; ++i) {
-            if (i < nb) {
-                const float p = sv[i] == -INFINITY ? 0.f : __expf(sv[i] - mx);
+        for (int v = 0; v < MB; ++v) {
+            if (v < nvb) {   // (keys past the last box get p = 0, which P V needs)
+                const float p = sv[v] == -INFINITY ? 0.f : __expf(sv[v] - mx);
                 sum += p;
-                *reinterpret_cast<__nv_bfloat16 *>(sP + (i * 16 + row) * kPStride + sub * 2) =
+                *reinterpret_cast<__nv_bfloat16 *>(sP + (v * 16 + row) * kPStride + sub * 2) =
                     __float2bfloat16_rn(p);
             }
         }
@@ -345,22 +357,33 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         for (int k = 0; k < 2; ++k)
 #pragma unroll
             for (int e = 0; e < 4; ++e) o[np][k][e] = 0.f;
-    for (int n = nb; n < nblocks; ++n) {
-        const int s = n % NS, i = n - nb;
+    for (int v = 0; v < nvb; ++v) {
+        // virtual box v: page box i0 (and i0 + 1 for 8-row pages), blocks nb + i0 ..
+        const int i0 = PS == 16 ? v : 2 * v;
+        const bool two = PS == 8 && i0 + 1 < nb;
+        const int n0 = nb + i0;
         if (s_abort) break;
-        if (!__all_sync(0xffffffffu, mbar_wait_bounded(&full[s], (n / NS) & 1, kWaitLimitNs))) {
+        bool got = mbar_wait_bounded(&full[n0 % NS], (n0 / NS) & 1, kWaitLimitNs);
+        if (two) got = got && mbar_wait_bounded(&full[(n0 + 1) % NS], ((n0 + 1) / NS) & 1, kWaitLimitNs);
+        if (!__all_sync(0xffffffffu, got)) {
             if (lane == 0) {
                 raise(d.error, PK_DEV_TIMEOUT);
                 s_abort = 1;
             }
             break;
         }
-        char *box = smem + s * g.stage_bytes + h * kBox;
-        const uint32_t abox = smem_u32(box);
-        if (a.v_new) append_rows(vnew, 1, i, box);
+        char *boxa = smem + (n0 % NS) * g.stage_bytes + h * kBox;
+        // (past the last 8-row box the keys have p = 0: any finite rows serve)
+        char *boxb = two ? smem + ((n0 + 1) % NS) * g.stage_bytes + h * kBox : boxa;
+        if (a.v_new) {
+            append_rows(vnew, 1, i0, boxa);
+            if (two) append_rows(vnew, 1, i0 + 1, boxb);
+        }
         uint32_t pa[4];
-        ldsm_x4(smem_u32(sP) + (i * 16 + lane % 16) * kPStride + (lane / 16) * 16, pa);
-        const int key = (lane % 8) + ((lane / 8) & 1) * 8;
+        ldsm_x4(smem_u32(sP) + (v * 16 + lane % 16) * kPStride + (lane / 16) * 16, pa);
+        // keys 0-7 of the virtual box to lanes 0-7 / 16-23, keys 8-15 to 8-15 / 24-31
+        const uint32_t abox = smem_u32(PS == 16 || !(lane & 8) ? boxa : boxb);
+        const int key = PS == 16 ? (lane % 8) + ((lane / 8) & 1) * 8 : (lane % 8);
 #pragma unroll
         for (int np = 0; np < 4; ++np) {
             uint32_t vb[4];
@@ -369,7 +392,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
             mma_bf16(o[np][1], pa, vb[2], vb[3]);
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
+        if (lane == 0) {
+            mbar_arrive(&empty[n0 % NS]);
+            if (two) mbar_arrive(&empty[(n0 + 1) % NS]);
+        }
     }
     if (s_abort) return;
 
@@ -401,7 +427,7 @@ __global__ void __launch_bounds__(kRelposThreads, 5)   // 5 CTAs per SM: the sma
 bool stacked_shape(const pk_paged_kv *kv, SGeom *g) {
     const pk_paged_kv_desc &d = kv->d;
     if (d.dtype != PK_DTYPE_BF16 || kv->head_dim != 64 || d.num_heads % kH != 0 ||
-        kH * d.chunk > 16 || d.page_size != 16)
+        kH * d.chunk > 16 || (d.page_size != 16 && d.page_size != 8))
         return false;
     g->num_layers = d.num_layers;
     g->left = d.left;
@@ -410,7 +436,8 @@ bool stacked_shape(const pk_paged_kv *kv, SGeom *g) {
     g->R = g->W + d.chunk - 1;
     g->npb = (g->R + 15) / 16;
     g->max_boxes = pk_pages_per_stream(d.left, d.chunk, d.page_size);
-    return g->max_boxes <= kMaxBoxes && g->npb <= kMaxPosBlocks;
+    return g->max_boxes <= (d.page_size == 16 ? max_boxes<16>() : max_boxes<8>()) &&
+           g->npb <= kMaxPosBlocks;
 }
 
 }  // namespace
@@ -430,24 +457,26 @@ int launch_relpos_bd(const pk_paged_kv *kv, const AttnArgs &a, float *bd, cudaSt
                        "relpos_bd_kernel");
 }
 
-int launch_attention_stacked(const pk_paged_kv *kv, const CUtensorMap &pos_map16,
-                             const AttnArgs &a, cudaStream_t s) {
-    (void)pos_map16;   // the rel-pos rows are read through a.pos (or a.bd)
+namespace {
+
+template <int PS>
+int launch_stacked_ps(const pk_paged_kv *kv, SGeom g, const AttnArgs &a, cudaStream_t s) {
     const pk_paged_kv_desc &d = kv->d;
-    constexpr int NS = kStages;
-    SGeom g;
-    if (!stacked_shape(kv, &g)) return PK_ENOTSUP;
-    g.stage_bytes = kH * kBox;
+    constexpr int NS = stages_of<PS>();
+    constexpr int kVirt = max_boxes<PS>() * PS / 16;   // virtual boxes of 16 columns (8)
+    g.stage_bytes = kH * box_bytes<PS>();
     g.off_s = NS * g.stage_bytes;
-    g.off_bd = g.off_s + kMaxBoxes * 16 * 16 * 4;
+    g.off_bd = g.off_s + max_boxes<PS>() * 16 * PS * 4;
     g.bd_stride = g.npb * 16;
     g.off_p = g.off_bd + 16 * g.bd_stride * 4;
-    const size_t smem = g.off_p + kMaxBoxes * 16 * kPStride + 1024;
+    const size_t smem = g.off_p + kVirt * 16 * kPStride + 1024;
     // more than 8 stacked query rows (chunks of 3 or 4) take a second softmax pass
-    // and the softmax loops run over at most MB page boxes (6 for the small model)
-    const bool r16 = kH * d.chunk > 8, mb6 = g.max_boxes <= 6;
-    auto kernel = r16 ? (mb6 ? paged_attn_stacked_kernel<NS, true, 6> : paged_attn_stacked_kernel<NS, true, kMaxBoxes>)
-                      : (mb6 ? paged_attn_stacked_kernel<NS, false, 6> : paged_attn_stacked_kernel<NS, false, kMaxBoxes>);
+    // and the softmax loops run over at most MB virtual boxes (6 for the small model)
+    const bool r16 = kH * d.chunk > 8, mb6 = (g.max_boxes * PS + 15) / 16 <= 6;
+    auto kernel = r16 ? (mb6 ? paged_attn_stacked_kernel<NS, true, 6, PS>
+                             : paged_attn_stacked_kernel<NS, true, kVirt, PS>)
+                      : (mb6 ? paged_attn_stacked_kernel<NS, false, 6, PS>
+                             : paged_attn_stacked_kernel<NS, false, kVirt, PS>);
     static size_t limit[4] = {48 * 1024, 48 * 1024, 48 * 1024, 48 * 1024};
     size_t &lim = limit[2 * r16 + mb6];
     if (smem > lim) {
@@ -459,6 +488,17 @@ int launch_attention_stacked(const pk_paged_kv *kv, const CUtensorMap &pos_map16
     dim3 grid(a.batch, a.nlayers, d.num_heads / kH);
     return cuda_status(launch_pdl(kernel, grid, dim3(kThreads), smem, s, kv->kv_map, g, d, a),
                        "paged_attn_stacked_kernel");
+}
+
+}  // namespace
+
+int launch_attention_stacked(const pk_paged_kv *kv, const CUtensorMap &pos_map16,
+                             const AttnArgs &a, cudaStream_t s) {
+    (void)pos_map16;   // the rel-pos rows are read through a.pos (or a.bd)
+    SGeom g;
+    if (!stacked_shape(kv, &g)) return PK_ENOTSUP;
+    return kv->d.page_size == 16 ? launch_stacked_ps<16>(kv, g, a, s)
+                                 : launch_stacked_ps<8>(kv, g, a, s);
 }
 
 }  // namespace pk

@@ -32,10 +32,10 @@ def build_encoder(cfg, dtype):
     return enc.to(device="cuda", dtype=dtype).eval()
 
 
-def replay_encoder(cfg, dtype):
+def replay_encoder(cfg, dtype, page_size=16):
     enc = build_encoder(cfg, dtype)
     sched = Scheduler(max_active=cfg["pool"])
-    sched.init_state_pool(enc, torch.device("cuda"), dtype, cfg["pool"])
+    sched.init_state_pool(enc, torch.device("cuda"), dtype, cfg["pool"], page_size=page_size)
     slot_of, outs = {}, {}
     for s, rel, acq, names, x, length in schedule(cfg):
         for n in rel:
@@ -56,10 +56,10 @@ def replay_encoder(cfg, dtype):
                                       (SMALL_FULL, "encoder_small_full.npz"),
                                       (LARGE_FULL, "encoder_large_full.npz")])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_paged_encoder_matches_reference(cfg, name, dtype):
+def test_paged_encoder_matches_reference(cfg, name, dtype, page_size=16):
     torch.backends.cuda.matmul.allow_tf32 = False
     g = load(name)
-    outs, sched = replay_encoder(cfg, dtype)
+    outs, sched = replay_encoder(cfg, dtype, page_size)
     tol = 1e-5 if dtype == torch.float32 else 1e-2
     for s in g["keep_steps"]:
         y, idx = outs[int(s)]
@@ -76,3 +76,11 @@ def test_paged_encoder_matches_reference(cfg, name, dtype):
     proc, clen = pool.counters(slots)
     assert np.array_equal(proc.cpu().numpy(), g["final_processed"])
     assert np.array_equal(clen.cpu().numpy(), g["final_cache_len"])
+
+
+@pytest.mark.parametrize("cfg,name", [(SMALL, "encoder_small.npz"),
+                                      (SMALL_FULL, "encoder_small_full.npz")])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_paged_encoder_8_frame_pages_matches_reference(cfg, name, dtype):
+    """The same replay over pages of 8 frames (the small serving engine's pool)."""
+    test_paged_encoder_matches_reference(cfg, name, dtype, page_size=8)

@@ -24,7 +24,10 @@ SHAPES = {"small": dict(att=(70, 1), dim=512, heads=8), "large": dict(att=(70, 1
           # the 4-head CTA (the small model stacks 8)
           "small_t3": dict(att=(70, 2), dim=512, heads=8), "small_t4": dict(att=(70, 3), dim=512, heads=8),
           # the conv-cache step's register form at the large width, and a 1-frame chunk
-          "wide_t2": dict(att=(70, 1), dim=1024, heads=8), "small_t1": dict(att=(70, 0), dim=512, heads=8)}
+          "wide_t2": dict(att=(70, 1), dim=1024, heads=8), "small_t1": dict(att=(70, 0), dim=512, heads=8),
+          # pages of 8 frames (10 boxes per window; odd box counts at some alignments)
+          "small_p8": dict(att=(70, 1), dim=512, heads=8, page=8),
+          "small_t3_p8": dict(att=(70, 2), dim=512, heads=8, page=8)}
 
 
 def pool_state(pool):
@@ -145,9 +148,11 @@ def run_stream_steps(shape, dtype, steps, n_slots, seed, check_every=1, short_la
     att, D, H = cfg["att"], cfg["dim"], cfg["heads"]
     left, T = att[0], att[1] + 1
     W, P, L = left + T, 2 * (left + T) - 1, 2
+    ps = cfg.get("page", 16)
     rng = np.random.default_rng(seed)
-    order = rng.permutation(n_slots * pages.pages_per_stream(left, T, 16))
-    pool = PagedKVPool(L, D, H, att, n_slots, dtype=dtype, device=DEV, page_order=order)
+    order = rng.permutation(n_slots * pages.pages_per_stream(left, T, ps))
+    pool = PagedKVPool(L, D, H, att, n_slots, page_size=ps, dtype=dtype, device=DEV,
+                       page_order=order)
     dense = streaming.SlotSchedulerModel(L, att, D, 9, n_slots)
     start = {s: int(rng.integers(0, steps // 2)) if s else 0 for s in range(n_slots)}
     pos = [rng.standard_normal((P, D)) / 8 for _ in range(L)]
@@ -226,6 +231,15 @@ def test_append_gather_attention_stacked_rows_above_8(shape, fused):
 def test_append_gather_attention_small_relpos_prepass():
     run_stream_steps("small", torch.bfloat16, steps=44, n_slots=5, seed=3, check_every=5,
                      prepass=True)
+
+
+@pytest.mark.parametrize("shape", ["small_p8", "small_t3_p8"])
+@pytest.mark.parametrize("fused,prepass", [(False, False), (True, False), (False, True)])
+def test_append_gather_attention_8_frame_pages(shape, fused, prepass):
+    """The stacked kernel over pages of 8 frames (two page boxes per 16 keys of
+    P V), with the append fused or not and the rel-pos term from the pre-pass."""
+    run_stream_steps(shape, torch.bfloat16, steps=44, n_slots=5, seed=8, check_every=3,
+                     fused=fused, prepass=prepass)
 
 
 def test_relpos_prepass_matches_in_kernel_term():
