@@ -92,6 +92,8 @@ def parse():
     ap.add_argument("--wheelhouse", default=None, help="offline wheel directory for pip")
     ap.add_argument("--serve-page-small", type=int, choices=[8, 16], default=None,
                     help="K/V page size of the small model's serving engine (default 8)")
+    ap.add_argument("--serve-page-large", type=int, choices=[8, 16], default=None,
+                    help="K/V page size of the large model's serving engine (default 16)")
     ap.add_argument("--profile-op", default=None,
                     choices=["append", "attention", "attention+append", "gather",
                              "gather_all_layers", "conv", "features", "streaming", "gemm",
@@ -1588,6 +1590,8 @@ def serve_lines(args, dev, world):
 
     if args.serve_page_small:
         SERVE_PAGE["small"] = args.serve_page_small
+    if args.serve_page_large:
+        SERVE_PAGE["large"] = args.serve_page_large
     if world == 1:
         out = {}
         for model in ("small", "large"):

@@ -79,7 +79,9 @@ def test_paged_encoder_matches_reference(cfg, name, dtype, page_size=16):
 
 
 @pytest.mark.parametrize("cfg,name", [(SMALL, "encoder_small.npz"),
-                                      (SMALL_FULL, "encoder_small_full.npz")])
+                                      (SMALL_FULL, "encoder_small_full.npz"),
+                                      (LARGE, "encoder_large.npz"),
+                                      (LARGE_FULL, "encoder_large_full.npz")])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_paged_encoder_8_frame_pages_matches_reference(cfg, name, dtype):
     """The same replay over pages of 8 frames (the small serving engine's pool)."""

@@ -27,7 +27,9 @@ SHAPES = {"small": dict(att=(70, 1), dim=512, heads=8), "large": dict(att=(70, 1
           "wide_t2": dict(att=(70, 1), dim=1024, heads=8), "small_t1": dict(att=(70, 0), dim=512, heads=8),
           # pages of 8 frames (10 boxes per window; odd box counts at some alignments)
           "small_p8": dict(att=(70, 1), dim=512, heads=8, page=8),
-          "small_t3_p8": dict(att=(70, 2), dim=512, heads=8, page=8)}
+          "small_t3_p8": dict(att=(70, 2), dim=512, heads=8, page=8),
+          # the large model over 8-frame pages (the general bf16 kernel)
+          "large_p8": dict(att=(70, 13), dim=1024, heads=8, page=8)}
 
 
 def pool_state(pool):
@@ -220,6 +222,11 @@ def test_append_gather_attention_small(dtype, fused):
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_append_gather_attention_large(dtype, fused):
     run_stream_steps("large", dtype, steps=9, n_slots=3, seed=4, fused=fused)
+
+
+@pytest.mark.parametrize("fused", [False, True])
+def test_append_gather_attention_large_8_frame_pages(fused):
+    run_stream_steps("large_p8", torch.bfloat16, steps=9, n_slots=3, seed=9, fused=fused)
 
 
 @pytest.mark.parametrize("shape", ["small_t3", "small_t4"])
