@@ -45,10 +45,11 @@ SHAPES = {
     "large": dict(layers=24, dim=1024, heads=8, att=(70, 13)),
 }
 PAGE = 16
-# K/V page size of the serving engines: the small model's stacked attention
-# kernel also takes pages of 8 frames (a 72-frame window then reserves 80 rows
-# per stream instead of 96); the large model's kernel takes 16
-SERVE_PAGE = {"small": 8, "large": 16}
+# K/V page size of the serving engines: pages of 8 frames reserve 80 rows per
+# stream for the small model's 72-frame window (16-frame pages: 96) and 96 for
+# the large model's 84-frame window (112); the large model then runs the general
+# bf16 attention kernel, which time allows at these loads
+SERVE_PAGE = {"small": 8, "large": 8}
 
 
 def alg_bytes(shape, es=2):
@@ -93,7 +94,7 @@ def parse():
     ap.add_argument("--serve-page-small", type=int, choices=[8, 16], default=None,
                     help="K/V page size of the small model's serving engine (default 8)")
     ap.add_argument("--serve-page-large", type=int, choices=[8, 16], default=None,
-                    help="K/V page size of the large model's serving engine (default 16)")
+                    help="K/V page size of the large model's serving engine (default 8)")
     ap.add_argument("--profile-op", default=None,
                     choices=["append", "attention", "attention+append", "gather",
                              "gather_all_layers", "conv", "features", "streaming", "gemm",
