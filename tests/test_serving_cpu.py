@@ -185,3 +185,18 @@ def test_serve_trial_steps_every_chunk_in_order(monkeypatch, use_graph):
         assert st["steps"] == len(pipe.calls)
         full = [sl for c, sl in pipe.calls if c == 2 and len(sl) == max_batch]
         assert full, "the trial should have made full later-chunk batches"
+
+
+@pytest.mark.parametrize("B", [1, 127, 128, 129, 300, 1024, 1500, 2047, 2048])
+def test_step_graph_pieces_cover_the_batch_with_little_padding(B):
+    """StepGraphs.pieces: bucket-sized replays, largest first, covering the
+    batch's rows once; only the last is padded, to the smallest bucket."""
+    g = bench.StepGraphs.__new__(bench.StepGraphs)
+    g.sizes = sorted(bench.STEP_BUCKETS, reverse=True)
+    pieces = g.pieces(B)
+    assert sum(r for r, _ in pieces) == B
+    assert all(r == Bg for r, Bg in pieces[:-1])
+    r, Bg = pieces[-1]
+    assert r == Bg or (Bg == min(bench.STEP_BUCKETS) and r < Bg)
+    assert [Bg for _, Bg in pieces] == sorted((Bg for _, Bg in pieces), reverse=True)
+    assert Bg - r < min(bench.STEP_BUCKETS)   # padding fits the spare slots
