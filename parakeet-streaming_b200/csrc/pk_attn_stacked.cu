@@ -8,11 +8,11 @@
 // head, a per-head CTA spends most of its instructions on setup and on the
 // 14 padding rows of every m16 tile.  Here:
 //
-// * a producer warp streams 8 KB blocks through an NS-stage ring with
-//   128B-swizzled TMA tile loads (cp.async.bulk.tensor, one box per head,
-//   L2 evict-first): the stream's K pages, then its V pages - each page box
-//   shifted so that rows outside the window are zero-filled without being
-//   read;
+// * a producer warp streams blocks of one page box per head (8 KB for pages
+//   of 16 frames, 4 KB for pages of 8) through an NS-stage ring with
+//   128B-swizzled TMA tile loads (cp.async.bulk.tensor, L2 evict-first): the
+//   stream's K pages, then its V pages - each page box shifted so that rows
+//   outside the window are zero-filled without being read;
 // * meanwhile consumer warp h computes its head's BD = (q+v) P^T from the
 //   rel-pos rows P read straight from global memory (L2-resident: every
 //   stream of the layer reads the same rows), so they take no turns of the
@@ -20,7 +20,8 @@
 //   (mma.sync m16n8k16, bf16 in, fp32 accumulate), written to shared memory
 //   in the stacked [head * T + query] row order;
 // * one dense softmax over the group's rows (16 threads per row) with the
-//   reference's -1e5 masked fill, probabilities kept as bf16 per page box;
+//   reference's -1e5 masked fill, probabilities kept as bf16 per 16 window
+//   columns (one 16-frame page box, or two 8-frame ones);
 // * O_h = P V_h on tensor cores, normalised by the row sums;
 // * optionally the step's new K/V rows are appended here as well: each
 //   warp writes its head's rows to the page in global memory and over the
