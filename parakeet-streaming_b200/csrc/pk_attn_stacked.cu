@@ -54,8 +54,10 @@ constexpr int kPStride = 48;             // bytes per row of a 16x16 bf16 probab
 // CTAs: half-size CTAs shorten the last, partly filled wave.
 constexpr int kStages = 4;
 constexpr int kCtasPerSm = 4;
-// stages of 8-row boxes: half the bytes each, so twice as many (same ring bytes)
-template <int PS> constexpr int stages_of() { return PS == 16 ? kStages : 2 * kStages; }
+// A ring stage holds one 16-row slot per head: one 16-frame page box, or two
+// 8-frame ones back to back (two 1 KB swizzle atoms: the same bytes and
+// swizzle as one 16-row box), so both page sizes run the same ring.
+constexpr int kSlot = 2048;
 
 struct SGeom {
     int num_layers, left, chunk, W, R, npb, max_boxes;
@@ -103,7 +105,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     const int layer = a.layer0 + lrel;
     const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
     const int chunk = g.chunk, npb = g.npb;
-    constexpr int kBox = box_bytes<PS>(), kMB = max_boxes<PS>();
+    constexpr int kMB = max_boxes<PS>(), kVB = 16 / PS;   // page boxes per 16-row slot
     float *sS = reinterpret_cast<float *>(smem + g.off_s);    // [box][16 rows][PS]
     float *sBD = reinterpret_cast<float *>(smem + g.off_bd);  // [16 rows][bd_stride]
     char *sP = smem + g.off_p;                                // [virtual box][16 rows][kPStride B]
@@ -146,8 +148,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     }
     __syncthreads();
     const int nb = s_nb, w = s_w, nfirst = s_nfirst;
-    const int nblocks = 2 * nb;   // K pages, then V pages
-    const int nvb = PS == 16 ? nb : (nb + 1) / 2;   // virtual boxes of 16 columns
+    const int nvb = (nb + kVB - 1) / kVB;   // 16-row slots ("virtual boxes") of the window
+    const int nblocks = 2 * nvb;             // K slots, then V slots
     T *out_base = static_cast<T *>(a.out) + (int64_t)lrel * a.o_ls + (int64_t)b * a.o_bs + hg0 * 64;
     if (!s_ok) {
         for (int idx = tid; idx < chunk * kH * 64; idx += kThreads)
@@ -172,12 +174,17 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
                 }
                 break;
             }
-            if (lane == 0) mbar_arrive_expect_tx(&full[s], kH * kBox);
+            if (lane == 0) mbar_arrive_expect_tx(&full[s], kH * kSlot);
             __syncwarp();
-            if (lane < kH) {
-                char *dst = smem + s * g.stage_bytes + lane * kBox;
-                const int i = n < nb ? n : n - nb, kvi = n < nb ? 0 : 1;
-                const int plane = ((s_page[i] * d.num_layers + layer) * 2 + kvi) * d.num_heads + hg0 + lane;
+            if (lane < kH * kVB) {
+                // lane: head lane % kH, half lane / kH of the slot; past the last
+                // page box the half repeats the slot's first box (finite rows that
+                // the softmax gives p = 0)
+                const int hd = lane % kH, half = lane / kH;
+                const int v = n < nvb ? n : n - nvb, kvi = n < nvb ? 0 : 1;
+                const int i = v * kVB + half < nb ? v * kVB + half : v * kVB;
+                char *dst = smem + s * g.stage_bytes + hd * kSlot + half * box_bytes<PS>();
+                const int plane = ((s_page[i] * d.num_layers + layer) * 2 + kvi) * d.num_heads + hg0 + hd;
                 tma_load_3d_hint(dst, &kv_map, &full[s], 0, s_start[i], plane, l2_evict_first());
             }
             last_n[s] = n;
@@ -269,33 +276,38 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         __syncwarp();
     };
 
-    // ---- pass 1: K pages -> S rows
-    for (int n = 0; n < nb; ++n) {
-        const int s = n % NS;
+    // ---- pass 1: K slots -> S rows
+    for (int v = 0; v < nvb; ++v) {
+        const int s = v % NS;
         if (s_abort) break;
-        if (!__all_sync(0xffffffffu, mbar_wait_bounded(&full[s], (n / NS) & 1, kWaitLimitNs))) {
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(&full[s], (v / NS) & 1, kWaitLimitNs))) {
             if (lane == 0) {
                 raise(d.error, PK_DEV_TIMEOUT);
                 s_abort = 1;
             }
             break;
         }
-        char *box = smem + s * g.stage_bytes + h * kBox;
-        const uint32_t abox = smem_u32(box);
-        const int i = n;
-        if (a.k_new) append_rows(knew, 0, i, box);
+        char *slot = smem + s * g.stage_bytes + h * kSlot;
+        const uint32_t aslot = smem_u32(slot);
+        if (a.k_new) {
 #pragma unroll
-        for (int nt = 0; nt < PS / 8; ++nt) {   // n-tiles of 8 keys in the box
+            for (int half = 0; half < kVB; ++half)
+                if (v * kVB + half < nb) append_rows(knew, 0, v * kVB + half, slot + half * box_bytes<PS>());
+        }
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {   // n-tiles of 8 keys: slot rows 8 nt ..
             float c[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int kp = 0; kp < 4; kp += 2) {
                 uint32_t bb[4];
-                ldsm_x4(abox + sw128(nt * 8 + (lane % 8), (kp * 16 + (lane / 8) * 8) * 2), bb);
+                ldsm_x4(aslot + sw128(nt * 8 + (lane % 8), (kp * 16 + (lane / 8) * 8) * 2), bb);
                 mma_bf16(c, fu[kp], bb[0], bb[1]);
                 mma_bf16(c, fu[kp + 1], bb[2], bb[3]);
             }
-            if (gq < chunk)
-                *reinterpret_cast<float2 *>(sS + (i * 16 + h * chunk + gq) * PS + nt * 8 + 2 * tq) =
+            // page box bi, its columns from cb
+            const int bi = PS == 16 ? v : 2 * v + nt, cb = PS == 16 ? nt * 8 : 0;
+            if (gq < chunk && bi < nb)
+                *reinterpret_cast<float2 *>(sS + (bi * 16 + h * chunk + gq) * PS + cb + 2 * tq) =
                     make_float2(c[0], c[1]);
         }
         __syncwarp();
@@ -359,44 +371,34 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 #pragma unroll
             for (int e = 0; e < 4; ++e) o[np][k][e] = 0.f;
     for (int v = 0; v < nvb; ++v) {
-        // virtual box v: page box i0 (and i0 + 1 for 8-row pages), blocks nb + i0 ..
-        const int i0 = PS == 16 ? v : 2 * v;
-        const bool two = PS == 8 && i0 + 1 < nb;
-        const int n0 = nb + i0;
+        const int n = nvb + v, s = n % NS;   // V slot v
         if (s_abort) break;
-        bool got = mbar_wait_bounded(&full[n0 % NS], (n0 / NS) & 1, kWaitLimitNs);
-        if (two) got = got && mbar_wait_bounded(&full[(n0 + 1) % NS], ((n0 + 1) / NS) & 1, kWaitLimitNs);
-        if (!__all_sync(0xffffffffu, got)) {
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(&full[s], (n / NS) & 1, kWaitLimitNs))) {
             if (lane == 0) {
                 raise(d.error, PK_DEV_TIMEOUT);
                 s_abort = 1;
             }
             break;
         }
-        char *boxa = smem + (n0 % NS) * g.stage_bytes + h * kBox;
-        // (past the last 8-row box the keys have p = 0: any finite rows serve)
-        char *boxb = two ? smem + ((n0 + 1) % NS) * g.stage_bytes + h * kBox : boxa;
+        char *slot = smem + s * g.stage_bytes + h * kSlot;
+        const uint32_t aslot = smem_u32(slot);
         if (a.v_new) {
-            append_rows(vnew, 1, i0, boxa);
-            if (two) append_rows(vnew, 1, i0 + 1, boxb);
+#pragma unroll
+            for (int half = 0; half < kVB; ++half)
+                if (v * kVB + half < nb) append_rows(vnew, 1, v * kVB + half, slot + half * box_bytes<PS>());
         }
         uint32_t pa[4];
         ldsm_x4(smem_u32(sP) + (v * 16 + lane % 16) * kPStride + (lane / 16) * 16, pa);
-        // keys 0-7 of the virtual box to lanes 0-7 / 16-23, keys 8-15 to 8-15 / 24-31
-        const uint32_t abox = smem_u32(PS == 16 || !(lane & 8) ? boxa : boxb);
-        const int key = PS == 16 ? (lane % 8) + ((lane / 8) & 1) * 8 : (lane % 8);
+        const int key = (lane % 8) + ((lane / 8) & 1) * 8;   // slot row = window key of the slot
 #pragma unroll
         for (int np = 0; np < 4; ++np) {
             uint32_t vb[4];
-            ldsm_x4_t(abox + sw128(key, (np * 16 + (lane / 16) * 8) * 2), vb);
+            ldsm_x4_t(aslot + sw128(key, (np * 16 + (lane / 16) * 8) * 2), vb);
             mma_bf16(o[np][0], pa, vb[0], vb[1]);
             mma_bf16(o[np][1], pa, vb[2], vb[3]);
         }
         __syncwarp();
-        if (lane == 0) {
-            mbar_arrive(&empty[n0 % NS]);
-            if (two) mbar_arrive(&empty[(n0 + 1) % NS]);
-        }
+        if (lane == 0) mbar_arrive(&empty[s]);
     }
     if (s_abort) return;
 
@@ -463,9 +465,9 @@ namespace {
 template <int PS>
 int launch_stacked_ps(const pk_paged_kv *kv, SGeom g, const AttnArgs &a, cudaStream_t s) {
     const pk_paged_kv_desc &d = kv->d;
-    constexpr int NS = stages_of<PS>();
-    constexpr int kVirt = max_boxes<PS>() * PS / 16;   // virtual boxes of 16 columns (8)
-    g.stage_bytes = kH * box_bytes<PS>();
+    constexpr int NS = kStages;
+    constexpr int kVirt = max_boxes<PS>() * PS / 16;   // 16-row slots of a window (8)
+    g.stage_bytes = kH * kSlot;
     g.off_s = NS * g.stage_bytes;
     g.off_bd = g.off_s + max_boxes<PS>() * 16 * PS * 4;
     g.bd_stride = g.npb * 16;
