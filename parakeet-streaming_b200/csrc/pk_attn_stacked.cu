@@ -8,11 +8,11 @@
 // head, a per-head CTA spends most of its instructions on setup and on the
 // 14 padding rows of every m16 tile.  Here:
 //
-// * a producer warp streams blocks of one page box per head (8 KB for pages
-//   of 16 frames, 4 KB for pages of 8) through an NS-stage ring with
-//   128B-swizzled TMA tile loads (cp.async.bulk.tensor, L2 evict-first): the
-//   stream's K pages, then its V pages - each page box shifted so that rows
-//   outside the window are zero-filled without being read;
+// * a producer warp streams 8 KB blocks (a 16-row slot per head: one page box
+//   of 16 frames, or two of 8) through an NS-stage ring with 128B-swizzled TMA
+//   tile loads (cp.async.bulk.tensor, L2 evict-first): the stream's K pages,
+//   then its V pages - each page box shifted so that rows outside the window
+//   are zero-filled without being read;
 // * meanwhile consumer warp h computes its head's BD = (q+v) P^T from the
 //   rel-pos rows P read straight from global memory (L2-resident: every
 //   stream of the layer reads the same rows), so they take no turns of the
@@ -39,10 +39,10 @@ namespace {
 
 constexpr int kH = 4;                    // heads per CTA = consumer warps
 constexpr int kThreads = (kH + 1) * 32;  // + producer warp
-// Pages of PS = 16 or 8 rows: a head's page box is PS rows x 128 bytes (one or
-// two 1 KB 128B-swizzle atoms); a window spans at most 8 boxes of 16 rows or
-// 16 of 8.  The softmax and P V walk "virtual boxes" of 16 window columns: one
-// 16-row box, or two consecutive 8-row boxes.
+// Pages of PS = 16 or 8 rows: a head's page box is PS rows x 128 bytes (two or
+// one 1 KB 128B-swizzle atoms); a window spans at most 8 boxes of 16 rows or
+// 16 of 8.  S, the softmax and P V walk 16-row slots ("virtual boxes") of the
+// window: one 16-row box, or two consecutive 8-row boxes.
 template <int PS> constexpr int box_bytes() { return PS * 128; }
 template <int PS> constexpr int max_boxes() { return PS == 16 ? 8 : 16; }
 constexpr int kMaxBoxes = 16;            // descriptor entries read (either page size)
