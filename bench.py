@@ -1546,13 +1546,20 @@ def serving_search(model, dev, measure_s=3.0, max_trials=9, limit_ms=160.0, use_
                 N = (ok_n + bad_n) // 2 // (32 * world) * (32 * world)
     err = pipe.pool.read_error() | pipe.fe.error_bits()
     err = int(reduce([float(err)], dist.ReduceOp.MAX if world > 1 else None)[0])
+    # HBM at the end of the search, the engine still resident: how much of the
+    # 15 % left beside the slots the rest of the engine used
+    free_end, total = torch.cuda.mem_get_info(dev)
+    hbm = {"total_gb": round(total / 1e9, 1), "free_before_gb": round(free / 1e9, 1),
+           "slots_gb": round((cap + spare) * per_slot / 1e9, 1),
+           "peak_allocated_gb": round(torch.cuda.max_memory_allocated(dev) / 1e9, 1),
+           "free_at_end_gb": round(free_end / 1e9, 1)}
     del pipe
     torch.cuda.empty_cache()
     best = next((t for t in trials if t["streams"] == ok_n), None)
     out = {"model": model, "limit_ms": limit_ms, "n_gpus": world,
            "streams_max": ok_n, "streams_per_gpu": round(ok_n / world, 1),
            "capped_by_memory": bad_n is None and ok_n == cap * world, "slot_cap_per_gpu": cap,
-           "page_size": ps,
+           "page_size": ps, "hbm": hbm,
            "p99_ms_at_max": best["p99_ms"] if best else None,
            "audio_ms_per_chunk": period * 1e3, "measured_s_per_trial": round(meas * period, 2),
            "stream_life_s": lifetime_s, "prefill_chunks": fill,
