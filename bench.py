@@ -50,6 +50,10 @@ PAGE = 16
 # the large model's 84-frame window (112); the large model then runs the general
 # bf16 attention kernel, which time allows at these loads
 SERVE_PAGE = {"small": 8, "large": 8}
+# share of the free HBM given to stream slots.  Large: 0.90 leaves about 9 GB
+# beside the engine's 11 GB (measured).  Small: at 0.93 (60,160 slots) the step
+# time, not memory, binds (p99 198 ms), so the cap stays where memory binds first
+SLOT_HBM_SHARE = {"small": 0.85, "large": 0.90}
 
 
 def alg_bytes(shape, es=2):
@@ -1445,8 +1449,8 @@ def serving_search(model, dev, measure_s=3.0, max_trials=9, limit_ms=160.0, use_
     job's p99 is the largest rank p99).  The total doubles from
     ``start_per_gpu`` x N until a trial fails (p99 above the limit, or chunks
     left waiting at the end; a failing trial is repeated once), then
-    bisects; slots per GPU are capped by 85 % of its free memory (every slot
-    holds its K/V pages).  ``fixed_total``: one trial at that many streams
+    bisects; slots per GPU are capped by SLOT_HBM_SHARE of its free memory
+    (every slot holds its K/V pages).  ``fixed_total``: one trial at that many streams
     (configs[3]: 480 large streams over the job) before the search."""
     import numpy as np
     import torch
@@ -1472,7 +1476,10 @@ def serving_search(model, dev, measure_s=3.0, max_trials=9, limit_ms=160.0, use_
                 + 128 * 9 * 2 + 4096)
     torch.cuda.empty_cache()
     free = torch.cuda.mem_get_info(dev)[0]
-    cap = int(min(65536, 0.85 * free / per_slot)) // 256 * 256
+    # slots take this share of the free HBM; the rest holds the engine's graphs,
+    # activations and sample buffers (measured at the cap: about 3 GB small,
+    # 11 GB large, the `hbm` entry of the line)
+    cap = int(min(65536, SLOT_HBM_SHARE[model] * free / per_slot)) // 256 * 256
     cap = int(reduce([cap], dist.ReduceOp.MIN if world > 1 else None)[0])
     # the pool holds STEP_BUCKETS[-1] more slots: the rows that pad a step graph
     spare = STEP_BUCKETS[-1] if use_graph else 0
@@ -1547,7 +1554,7 @@ def serving_search(model, dev, measure_s=3.0, max_trials=9, limit_ms=160.0, use_
     err = pipe.pool.read_error() | pipe.fe.error_bits()
     err = int(reduce([float(err)], dist.ReduceOp.MAX if world > 1 else None)[0])
     # HBM at the end of the search, the engine still resident: how much of the
-    # 15 % left beside the slots the rest of the engine used
+    # share left beside the slots the rest of the engine used
     free_end, total = torch.cuda.mem_get_info(dev)
     hbm = {"total_gb": round(total / 1e9, 1), "free_before_gb": round(free / 1e9, 1),
            "slots_gb": round((cap + spare) * per_slot / 1e9, 1),
