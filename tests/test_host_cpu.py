@@ -157,3 +157,19 @@ def test_admission_queue_matches_reference_scheduler():
         assert all(type(q.status) is CallerStatus for q in seqs)
         assert [q.status.name for q in seqs] == c["status"]
     assert any(c["admitted"] for c in calls) and sched.num_waiting >= 0
+
+
+def test_python_constants_equal_header_defines():
+    """Every integer #define of include/pk.h that _lib mirrors (same name, or
+    without the PK_ prefix) has the same value."""
+    import re
+    text = open(_lib.HEADER).read()
+    checked = 0
+    for name, value in re.findall(r"^#define (PK_\w+) (\d+)\b", text, re.M):
+        for py in (name, name[3:]):
+            if hasattr(_lib, py):
+                assert getattr(_lib, py) == int(value), (name, getattr(_lib, py), value)
+                checked += 1
+                break
+    assert checked >= 20
+    assert _lib.PK_NOALLOC_SCRATCH_BYTES == 32 * 1024 * 1024
